@@ -1,0 +1,397 @@
+"""Benchmark of the B200-native W4A16 path (one JSON line on rank 0).
+
+Workload ``block``: the seven linears of one
+Llama-3.2-1B-shaped decoder block (q/k/v/o 2048-wide, gate/up 8192, down
+K=8192), weights N(0, 0.02) with 0.1% of entries x10, INT4 G=128, bf16
+activations.  A step runs them as the tensor-parallel dataflow of the block:
+
+    q, k, v = x @ Wq/k/v^T          (column shards, N / world)
+    o = q @ Wo^T ; all-reduce(o)    (row shard, K / world; NCCL when world > 1)
+    g, u = o @ Wgate/up^T           (column shards)
+    d = g @ Wdown^T ; all-reduce(d) (row shard)
+
+At M = 1 this is one decoder block's decode-step GEMV work (32.4 MB of packed
+weights).  Steps are captured in one CUDA graph and cycle through enough
+copies of the weights that the working set exceeds the 126 MB L2, so every
+step streams its weights from HBM.  ``value`` is the block time in
+microseconds (max over ranks); ``roofline`` relates the algorithmic bytes
+(N*K/2 + 4*N*K/G + 2*M*K + 2*M*N per linear) to the measured HBM peak.
+
+``--impl reference`` times the reference's CPU path (the numpy restatement
+of ``x.float() @ dequantize_int4_ref(...).t()`` in ``oracle/``) on the same
+configuration with all host threads, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "itmo-final-project_b200"), os.path.join(ROOT, "tests", "golden")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+BLOCK = [  # name, N, K, column-parallel?
+    ("q_proj", 2048, 2048, True),
+    ("k_proj", 512, 2048, True),
+    ("v_proj", 512, 2048, True),
+    ("o_proj", 2048, 2048, False),
+    ("gate_proj", 8192, 2048, True),
+    ("up_proj", 8192, 2048, True),
+    ("down_proj", 2048, 8192, False),
+]
+GROUP = 128
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def alg_bytes(M, N, K, G=GROUP) -> int:
+    return N * K // 2 + 4 * N * K // G + 2 * M * K + 2 * M * N
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = max(smax, float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- distributed
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- block workload
+
+
+def block_weights(rank: int, world: int, copies: int, dev):
+    """Per-rank shards of the seven linears, quantized on the GPU, ``copies`` rotating copies."""
+    import cases
+    import int4_b200 as ib
+
+    layers = []
+    for li, (name, N, K, colpar) in enumerate(BLOCK):
+        w = cases.weight((N, K), "bfloat16", seed=100 + li, outlier_frac=1e-3)
+        if colpar:
+            n0, n1 = rank * N // world, (rank + 1) * N // world
+            w = w[n0:n1]
+        else:
+            k0, k1 = rank * K // world, (rank + 1) * K // world
+            w = w[:, k0:k1]
+        qs = [ib.quantize_int4(w.contiguous().to(dev), GROUP)]
+        for _ in range(copies - 1):
+            qs.append(tuple(t.clone() for t in qs[0]))
+        layers.append((name, w.shape[0], w.shape[1], qs))
+    return layers
+
+
+def block_step(x, layers, copy: int, world: int):
+    import int4_b200 as ib
+
+    def mm(i, inp):
+        qw, s, z = layers[i][3][copy]
+        return ib.w4a16_matmul(inp, qw, s, z)
+
+    q = mm(0, x)
+    mm(1, x)
+    mm(2, x)
+    o = mm(3, q)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(o)
+    g = mm(4, o)
+    mm(5, o)
+    d = mm(6, g)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(d)
+    return d
+
+
+def run_block(args, world, rank, local):
+    import int4_b200 as ib
+    from int4_b200 import _lib
+
+    dev = torch.device("cuda", local)
+    M = args.m
+    shard_bytes = sum(alg_bytes(M, N, K) for (_, N, K, _) in
+                      [(n, (N // world if c else N), (K if c else K // world), c) for (n, N, K, c) in BLOCK])
+    copies = max(2, math.ceil(2 * L2_BYTES / max(1, shard_bytes - 2 * M * 2048)))
+    copies = min(copies, 64)
+    layers = block_weights(rank, world, copies, dev)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn((M, 2048), generator=g).to(torch.bfloat16).to(dev)
+
+    # One graph holds `chunk` steps (a divisor of K, at most 200); the timed
+    # region replays it K / chunk times, i.e. exactly K steps.
+    chunk = max(d for d in range(1, min(args.steps, 200) + 1) if args.steps % d == 0)
+    reps = args.steps // chunk
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):  # warm-up (eager) on the capture stream: workspace, module load
+        for i in range(args.warmup):
+            block_step(x, layers, i % copies, world)
+    torch.cuda.synchronize()
+
+    def capture(fn):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            for i in range(chunk):
+                fn(i)
+        gr.replay()  # upload / first replay, untimed
+        torch.cuda.synchronize()
+        return gr
+
+    def timed(gr, clocks=None):
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        barrier(world)
+        return e0.elapsed_time(e1) * 1e-3, wall
+
+    graph = capture(lambda i: block_step(x, layers, i % copies, world))
+    with ClockSampler(local) as clk:
+        t_dev, _ = timed(graph)
+    us_per_step = max_over_ranks(t_dev, world) * 1e6 / args.steps
+
+    # L2-hot variant (the reference's timing method: the same weights every step)
+    graph_hot = capture(lambda i: block_step(x, layers, 0, world))
+    hot_us = max_over_ranks(timed(graph_hot)[0], world) * 1e6 / args.steps
+
+    # End to end through the public API: pinned host x in, block output back to the host, every step.
+    x_host = torch.randn((M, 2048), generator=g).to(torch.bfloat16).pin_memory()
+    y_host = torch.empty((M, 2048), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        d = block_step(x_dev, layers, i % copies, world)
+        y_host.copy_(d, non_blocking=True)
+
+    graph_e2e = capture(e2e_step)
+    t_dev, wall = timed(graph_e2e)
+    e2e_us = max_over_ranks(max(t_dev, wall), world) * 1e6 / args.steps
+
+    flags = _lib.device_error_flags(local)
+    total_bytes = sum(alg_bytes(M, l[1], l[2]) for l in layers)
+    total_flops = sum(2 * M * l[1] * l[2] for l in layers)
+    del graph, graph_hot, graph_e2e
+    return {
+        "us_per_step": us_per_step, "hot_us": hot_us, "e2e_us": e2e_us, "clocks": clk.summary(),
+        "bytes_per_step_rank": total_bytes, "flops_per_step_rank": total_flops, "copies": copies,
+        "launches_per_step": len(BLOCK), "device_error_flags": flags,
+        "h2d": M * 2048 * 2, "d2h": M * 2048 * 2,
+    }
+
+
+def cpu_block_sample(M: int, threads: int, steps: int = 1) -> tuple[float, str]:
+    """Reference CPU path (oracle port) for the whole block at M tokens; seconds per block."""
+    import cases
+    from oracle import int4_oracle as orc
+
+    qs = []
+    for li, (name, N, K, _) in enumerate(BLOCK):
+        w = cases.weight((N, K), "bfloat16", seed=100 + li, outlier_frac=1e-3)
+        qs.append(orc.quantize_int4(w.view(torch.int16).numpy().view(np.uint16), GROUP, "bfloat16"))
+    x = cases.activations(M, 2048, "bfloat16", seed=1).view(torch.int16).numpy().view(np.uint16)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        h = x
+        q = orc.w4a16_matmul_threaded(h, *qs[0], threads=threads)
+        orc.w4a16_matmul_threaded(h, *qs[1], threads=threads)
+        orc.w4a16_matmul_threaded(h, *qs[2], threads=threads)
+        o = orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(q), *qs[3], threads=threads)
+        gg = orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(o), *qs[4], threads=threads)
+        orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(o), *qs[5], threads=threads)
+        orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(gg), *qs[6], threads=threads)
+    dt = (time.perf_counter() - t0) / steps
+    return dt, f"{steps} full block step(s) at M={M}: 7 dequantize-then-matmul linears, numpy fp32"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["block"], default="block")
+    ap.add_argument("--m", type=int, default=1, help="tokens per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    config = {"workload": f"llama-3.2-1b decoder block, 7 linears, W4 G={GROUP}, M={args.m}",
+              "model": "Llama-3.2-1B-shaped (random-init)", "group_size": GROUP, "tokens_per_step": args.m,
+              "parallelism": f"tp{args.gpus}", "global_batch": args.m, "seq_len": 1,
+              "l2": "inputs larger than L2: weights rotate over copies whose total exceeds 2x L2"}
+    metric = "per-block W4A16 GEMM us (Llama-3.2-1B decoder block, decode step)"
+    threads = os.cpu_count() or 1
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        ref_steps = min(args.steps, 5)
+        dt, sample = cpu_block_sample(args.m, threads, ref_steps)
+        v = dt * 1e6
+        print(json.dumps({
+            "impl": "reference", "metric": metric, "value": v, "unit": "us", "n_gpus": world,
+            "steps": ref_steps, "steps_requested": args.steps, "warmup": 0, "ms_per_step": dt * 1e3,
+            "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "w4a16-bf16", "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": v, "unit": "us", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    world, rank, local = dist_setup()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    r = run_block(args, world, rank, local)
+    pk = peaks()
+    us = r["us_per_step"]
+    achieved = r["bytes_per_step_rank"] / (us * 1e-6) / 1e9  # per rank, GB/s
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        dt, sample = cpu_block_sample(args.m, threads, 1)
+        cpu = {"value": dt * 1e6, "unit": "us", "cores": threads, "kind": "port", "sample": sample}
+    if rank == 0:
+        prof_traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            with open(tp) as f:
+                prof_traffic = json.load(f).get(f"block_m{args.m}")
+        line = {
+            "metric": metric, "value": us, "unit": "us", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "w4a16-bf16", "data": "synthetic (seeded N(0,0.02) weights, 0.1% x10)",
+            "config": config,
+            "block_gbs_per_gpu": achieved, "block_us_l2_hot": r["hot_us"],
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "traffic": prof_traffic,
+                         "kernel": "skinny_kernel<1,INT4,bf16> (decode GEMV), all 7 launches of a step",
+                         "peak_source": pk["source"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": r["e2e_us"], "unit": "us", "h2d_bytes_per_step": r["h2d"],
+                    "d2h_bytes_per_step": r["d2h"]},
+            "gpu_launches": r["launches_per_step"] * args.steps,
+            "clocks": r["clocks"], "device_error_flags": r["device_error_flags"],
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

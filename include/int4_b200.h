@@ -1,0 +1,134 @@
+/* int4_b200 -- C ABI of the B200-native (sm_100a) INT4 W4A16 path.
+ *
+ * Drop-in boundary for the hot path of homomorfism/itmo-final-project
+ * (Python package `int4_triton`): group-wise asymmetric INT4 quantize/pack and
+ * the W4A16 matmul that consumes the packed weights.  Plain pointers, sizes
+ * and strides; no torch types.  Every entry point is asynchronous on the
+ * given CUDA stream (cudaStream_t passed as void*, NULL = legacy default),
+ * allocates nothing, never synchronises the device, and returns an
+ * I4B_STATUS code (0 = success).
+ *
+ * Storage format (identical to the reference, int4_triton/quantize.py:1-13):
+ *   W        [N, K]     weights of an nn.Linear (out_features N, in_features K)
+ *   qweight  int32[K/8, N]   word [k8, n] holds W[n, 8*k8 + i] in bits 4i..4i+3
+ *   scales   fp16 [K/G, N]   per-group scale
+ *   zeros    fp16 [K/G, N]   per-group integer zero point 0..15
+ *   W_hat[n, k] = (q - zero) * scale      (fp32, exact)
+ *
+ * Element-type codes: I4B_F16, I4B_BF16, I4B_F32.  fp16 / bf16 buffers are
+ * passed as raw 16-bit patterns.
+ */
+#ifndef INT4_B200_H
+#define INT4_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define I4B_ABI_VERSION 1
+
+enum { I4B_F16 = 0, I4B_BF16 = 1, I4B_F32 = 2 };
+
+enum {
+  I4B_OK = 0,
+  I4B_ERR_INVALID_ARG = 1, /* null pointer where data is required, unknown dtype, negative size */
+  I4B_ERR_SHAPE = 2,       /* K not a multiple of 8 / of G, qweight rows != K/8, ... */
+  I4B_ERR_GROUP = 3,       /* group size not supported by this entry point */
+  I4B_ERR_LAYOUT = 4,      /* a stride or alignment the entry point does not accept */
+  I4B_ERR_WORKSPACE = 5,   /* workspace smaller than the matching *_workspace_size() */
+  I4B_ERR_CUDA = 6,        /* a CUDA runtime / driver call failed (see i4b_last_cuda_error) */
+  I4B_ERR_ARCH = 7         /* current device is not sm_100 */
+};
+
+/* Human-readable name of a status code. */
+const char* i4b_status_string(int status);
+/* I4B_ABI_VERSION of the loaded library. */
+int i4b_abi_version(void);
+/* cudaError_t of the last call that returned I4B_ERR_CUDA on this host thread. */
+int i4b_last_cuda_error(void);
+
+/* Quantize W[N, K] group-wise to INT4.
+ * Replaces int4_triton.quantize_int4 (int4_triton/quantize.py:67-96) and is bit
+ * exact with its torch reference quantize_int4_ref (quantize.py:102-117),
+ * including all-zero groups (scale 1) and non-finite inputs (x86 NaN rules).
+ * w: element (n, k) at w + n*stride_wn + k*stride_wk (strides in elements),
+ *    dtype I4B_F16, I4B_BF16 or I4B_F32.
+ * group_size: G, or -1 for G = K.  Requires K % G == 0 and G % 8 == 0.
+ * Outputs are contiguous: qweight int32[K/8, N], scales/zeros fp16[K/G, N]. */
+int i4b_quantize_int4(const void* w, int w_dtype, int64_t N, int64_t K, int64_t stride_wn, int64_t stride_wk,
+                      int group_size, int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream);
+
+/* W_hat[N, K] = (q - zero) * scale computed in fp32 and rounded once to out_dtype.
+ * Replaces dequantize_int4_ref (int4_triton/quantize.py:128-135).  Inputs and
+ * the output are contiguous; G = K / (rows of scales). */
+int i4b_dequantize_int4(const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros, int64_t N, int64_t K,
+                        int group_size, int out_dtype, void* out, void* stream);
+
+/* Bytes of workspace i4b_w4a16_matmul needs for these sizes (0 is possible).
+ * The workspace must be zero-filled before its first use; every call leaves
+ * its counter area zero again, so a workspace kept per stream needs no
+ * further clearing.  Calls that share a workspace must not overlap in time. */
+size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size);
+
+/* y[M, N] = x[M, K] @ W_hat^T in x's dtype (fp32 accumulation).
+ * Replaces int4_triton.w4a16_matmul (int4_triton/gemm.py:303-309, dispatch
+ * gemm.py:234-300): M == 1 decode GEMV and 2 <= M <= 64 split-K both run the
+ * register-dequant tensor-core kernel with a deterministic in-kernel split-K
+ * reduction; M > 64 runs the TMA + tcgen05/TMEM GEMM.
+ * x: element (m, k) at x + m*stride_xm + k*stride_xk, dtype I4B_BF16 or I4B_F16.
+ * qweight: row k8 at qweight + k8*stride_qk (unit stride along N).
+ * scales/zeros: row g at base + g*stride_sg (unit stride along N).
+ * y: element (m, n) at y + m*stride_ym + n.
+ * group_size G = K / (rows of scales); G must be a multiple of 32. */
+int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
+                     const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales,
+                     const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes for i4b_w16a16_matmul (same zero-fill rule as above). */
+size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/* y[M, N] = x[M, K] @ w[N, K]^T, x and w of the same dtype (bf16 or fp16).
+ * Replaces int4_triton.w16a16_matmul (int4_triton/gemm.py:312-317), the
+ * full-precision baseline with the same kernel structure as the W4 path.
+ * w: element (n, k) at w + n*stride_wn + k*stride_wk. */
+int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
+                      const void* w, int64_t N, int64_t stride_wn, int64_t stride_wk, void* y, int64_t stride_ym,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Programmatic dependent launch for the M <= 64 kernels (default off).
+ * When on, those kernels are launched with programmatic stream
+ * serialization: they start while the previous kernel of the stream drains
+ * and read qweight / scales / zeros BEFORE waiting for it, x only after.
+ * Enable it only where no kernel directly before a matmul writes that
+ * matmul's weights (e.g. a decode loop over fixed weights).  No counterpart
+ * in the reference (its launches are plain Triton launches). */
+void i4b_set_pdl(int enable);
+
+/* Tuning hook for the M <= 64 decomposition: columns per CTA (32*wn),
+ * k-warps per CTA (wk) and K splits; 0 keeps the automatic choice, an
+ * unusable value is ignored.  Process-wide.  No counterpart in the reference
+ * (which autotunes, int4_triton/gemm.py:51-56). */
+void i4b_set_skinny_override(int wn, int wk, int splits);
+
+/* Device-side error flags raised by kernels of this library on `device`
+ * (a bounded wait that expired sets bit 0).  Synchronises that device;
+ * clear != 0 resets the flags.  Returns -1 if the flags cannot be read. */
+int i4b_device_error_flags(int device, int clear);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INT4_B200_H */

@@ -1,0 +1,285 @@
+// extern "C" entry points of libint4_b200.so (declared in include/int4_b200.h).
+//
+// Validation mirrors the reference's preconditions (int4_triton/quantize.py:69-75,
+// int4_triton/gemm.py:305-307) as status codes; dispatch mirrors gemm.py:234-300
+// (small M -> one split-K launch, large M -> tcgen05 GEMM).  Nothing here
+// allocates device memory or synchronises: scratch comes from the caller's
+// workspace, whose layout is
+//   [64 KB split-K tickets, always left zero]
+//   M <= 64 : [fp32 partials S x M x N]
+//   M >  64 : [x copy][qweight copy][scales copy][zeros copy]   (copies only when
+//             an operand breaks the TMA rules: 16-byte base / row stride)
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace i4b;
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+bool g_pdl = false;
+
+int fail_cuda(cudaError_t e) {
+  t_last_cuda_error = int(e);
+  return I4B_ERR_CUDA;
+}
+
+struct DevInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+};
+
+// Per-device properties, read once (the device of the calling thread).
+int current_device_info(DevInfo* out) {
+  static DevInfo cache[64];
+  static bool filled[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  if (dev < 0 || dev >= 64) return I4B_ERR_INVALID_ARG;
+  if (!filled[dev]) {
+    DevInfo d;
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return fail_cuda(e);
+    if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return fail_cuda(e);
+    if ((e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+      return fail_cuda(e);
+    cache[dev] = d;
+    filled[dev] = true;
+  }
+  *out = cache[dev];
+  if (out->major != 10 || out->minor != 0) return I4B_ERR_ARCH;
+  return I4B_OK;
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// Workspace of the large-M INT4 path for the worst case the size query can see.
+size_t tc_w4_workspace(int64_t M, int64_t N, int64_t K, int G) {
+  size_t b = kTicketBytes + align256(size_t(M) * size_t(K) * 2);
+  if (N % 8 != 0) {
+    const int64_t Np = round_up(N, 8);
+    b += align256(size_t(K / 8) * Np * 4) + 2 * align256(size_t(K / G) * Np * 2);
+  }
+  return b;
+}
+
+size_t tc_w16_workspace(int64_t M, int64_t N, int64_t K) {
+  const int64_t Kp = round_up(K, 8);
+  size_t b = kTicketBytes + align256(size_t(M) * size_t(Kp) * 2);
+  if (K % 8 != 0) b += align256(size_t(N) * size_t(Kp) * 2);
+  return b;
+}
+
+// Up to this M the register-dequant kernel runs (the reference switches paths at
+// SMALL_M = 64, gemm.py:17; here tokens 17..64 already fill tcgen05 tiles well).
+constexpr int64_t kSmallM = kSkinnyMaxM;
+
+}  // namespace
+
+extern "C" {
+
+const char* i4b_status_string(int status) {
+  switch (status) {
+    case I4B_OK: return "ok";
+    case I4B_ERR_INVALID_ARG: return "invalid argument";
+    case I4B_ERR_SHAPE: return "unsupported shape";
+    case I4B_ERR_GROUP: return "unsupported group size";
+    case I4B_ERR_LAYOUT: return "unsupported stride or alignment";
+    case I4B_ERR_WORKSPACE: return "workspace too small";
+    case I4B_ERR_CUDA: return "CUDA error";
+    case I4B_ERR_ARCH: return "device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+int i4b_abi_version(void) { return I4B_ABI_VERSION; }
+
+int i4b_last_cuda_error(void) { return t_last_cuda_error; }
+
+void i4b_set_skinny_override(int wn, int wk, int splits) { set_skinny_override(wn, wk, splits); }
+
+void i4b_set_pdl(int enable) { g_pdl = enable != 0; }
+
+int i4b_quantize_int4(const void* w, int w_dtype, int64_t N, int64_t K, int64_t stride_wn, int64_t stride_wk,
+                      int group_size, int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream) {
+  if (w_dtype != I4B_F16 && w_dtype != I4B_BF16 && w_dtype != I4B_F32) return I4B_ERR_INVALID_ARG;
+  if (N < 0 || K < 0) return I4B_ERR_INVALID_ARG;
+  const int64_t G = group_size == -1 ? K : group_size;
+  if (K % 8 != 0) return I4B_ERR_SHAPE;
+  if (G <= 0 || G % 8 != 0 || K % G != 0) return I4B_ERR_GROUP;
+  if (N == 0 || K == 0) return I4B_OK;
+  if (!w || !qweight || !scales || !zeros) return I4B_ERR_INVALID_ARG;
+  if (N > INT32_MAX || K > INT32_MAX) return I4B_ERR_SHAPE;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  cudaError_t e = launch_quantize(w, w_dtype, N, K, stride_wn, stride_wk, int(G), qweight, scales, zeros,
+                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_dequantize_int4(const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros, int64_t N, int64_t K,
+                        int group_size, int out_dtype, void* out, void* stream) {
+  if (out_dtype != I4B_F16 && out_dtype != I4B_BF16 && out_dtype != I4B_F32) return I4B_ERR_INVALID_ARG;
+  if (N < 0 || K < 0 || K % 8 != 0) return I4B_ERR_SHAPE;
+  const int64_t G = group_size == -1 ? K : group_size;
+  if (G <= 0 || G % 8 != 0 || (K > 0 && K % G != 0)) return I4B_ERR_GROUP;
+  if (N == 0 || K == 0) return I4B_OK;
+  if (!qweight || !scales || !zeros || !out) return I4B_ERR_INVALID_ARG;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  cudaError_t e = launch_dequantize(qweight, scales, zeros, N, K, int(G), out_dtype, out,
+                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size) {
+  if (M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || group_size % 32 != 0 || K % group_size != 0) return 0;
+  DevInfo d;
+  if (current_device_info(&d) != I4B_OK) d.sms = 148;
+  if (M <= kSmallM) return skinny_workspace_bytes(plan_skinny(M, N, K, group_size, true, d.sms));
+  return tc_w4_workspace(M, N, K, group_size);
+}
+
+int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
+                     const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales,
+                     const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (x_dtype != I4B_F16 && x_dtype != I4B_BF16) return I4B_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return I4B_ERR_INVALID_ARG;
+  if (K % 8 != 0) return I4B_ERR_SHAPE;
+  const int G = group_size;
+  if (G <= 0 || G % 32 != 0 || K % G != 0) return I4B_ERR_GROUP;
+  if (M == 0 || N == 0) return I4B_OK;
+  if (!x || !qweight || !scales || !zeros || !y) return I4B_ERR_INVALID_ARG;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return I4B_ERR_SHAPE;
+  if (stride_qk < N || stride_sg < N || stride_ym < N) return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool f16 = x_dtype == I4B_F16;
+
+  if (M <= kSmallM) {
+    const SkinnyPlan p = plan_skinny(M, N, K, G, true, d.sms);
+    if (p.mode == 3) return I4B_ERR_SHAPE;
+    if (skinny_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;
+    cudaError_t e = launch_skinny(true, f16, x, M, K, stride_xm, stride_xk, qweight, N, stride_qk, 0, scales, zeros,
+                                  stride_sg, G, y, stride_ym, workspace, p, g_pdl, s);
+    return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+  }
+
+  // Large M: TMA needs 16-byte aligned bases and row strides; copy what does not comply.
+  const bool x_ok = aligned16(x) && stride_xk == 1 && (stride_xm * 2) % 16 == 0;
+  const bool w_ok = aligned16(qweight) && (stride_qk * 4) % 16 == 0 && aligned16(scales) && aligned16(zeros) &&
+                    (stride_sg * 2) % 16 == 0;
+  if (!w_ok && N % 8 == 0) return I4B_ERR_LAYOUT;  // no workspace reserved for this case
+  if (tc_w4_workspace(M, N, K, G) > workspace_bytes || !workspace) return I4B_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace) + kTicketBytes;
+  TcOperands o{x, stride_xm, qweight, stride_qk, scales, zeros, stride_sg};
+  cudaError_t e = cudaSuccess;
+  uint8_t* xcopy = ws;
+  ws += align256(size_t(M) * size_t(K) * 2);
+  if (!x_ok) {
+    if ((e = launch_repack(x, 2, M, K, stride_xm, stride_xk, xcopy, K, s)) != cudaSuccess) return fail_cuda(e);
+    o.x = xcopy;
+    o.sxm = K;
+  }
+  if (!w_ok) {
+    const int64_t Np = round_up(N, 8);
+    uint8_t* qc = ws;
+    ws += align256(size_t(K / 8) * Np * 4);
+    uint8_t* scc = ws;
+    ws += align256(size_t(K / G) * Np * 2);
+    uint8_t* zc = ws;
+    if ((e = launch_repack(qweight, 4, K / 8, N, stride_qk, 1, qc, Np, s)) != cudaSuccess) return fail_cuda(e);
+    if ((e = launch_repack(scales, 2, K / G, N, stride_sg, 1, scc, Np, s)) != cudaSuccess) return fail_cuda(e);
+    if ((e = launch_repack(zeros, 2, K / G, N, stride_sg, 1, zc, Np, s)) != cudaSuccess) return fail_cuda(e);
+    o.w = qc;
+    o.sw = Np;
+    o.sc = reinterpret_cast<const uint16_t*>(scc);
+    o.zr = reinterpret_cast<const uint16_t*>(zc);
+    o.ssg = Np;
+  }
+  e = launch_tc(true, f16, o, M, N, K, G, static_cast<uint16_t*>(y), stride_ym, tc_pick_bn(M, N, d.sms), s);
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  DevInfo d;
+  if (current_device_info(&d) != I4B_OK) d.sms = 148;
+  if (M <= kSmallM) return skinny_workspace_bytes(plan_skinny(M, N, K, 32, false, d.sms));
+  return tc_w16_workspace(M, N, K);
+}
+
+int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
+                      const void* w, int64_t N, int64_t stride_wn, int64_t stride_wk, void* y, int64_t stride_ym,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != I4B_F16 && dtype != I4B_BF16) return I4B_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return I4B_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return I4B_OK;
+  if (!x || !w || !y) return I4B_ERR_INVALID_ARG;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return I4B_ERR_SHAPE;
+  if (stride_ym < N) return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool f16 = dtype == I4B_F16;
+  if (K == 0) {
+    // Empty reduction: y = 0.
+    for (int64_t m = 0; m < M; ++m) {
+      cudaError_t e = cudaMemsetAsync(static_cast<uint16_t*>(y) + m * stride_ym, 0, size_t(N) * 2, s);
+      if (e != cudaSuccess) return fail_cuda(e);
+    }
+    return I4B_OK;
+  }
+  if (M <= kSmallM) {
+    const SkinnyPlan p = plan_skinny(M, N, K, 32, false, d.sms);
+    if (p.mode == 3) return I4B_ERR_SHAPE;
+    if (skinny_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;
+    cudaError_t e = launch_skinny(false, f16, x, M, K, stride_xm, stride_xk, w, N, stride_wn, stride_wk, nullptr,
+                                  nullptr, 0, 0, y, stride_ym, workspace, p, g_pdl, s);
+    return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+  }
+  const int64_t Kp = round_up(K, 8);
+  const bool x_ok = K % 8 == 0 && aligned16(x) && stride_xk == 1 && (stride_xm * 2) % 16 == 0;
+  const bool w_ok = K % 8 == 0 && aligned16(w) && stride_wk == 1 && (stride_wn * 2) % 16 == 0;
+  if (!w_ok && K % 8 == 0) return I4B_ERR_LAYOUT;
+  if (tc_w16_workspace(M, N, K) > workspace_bytes || !workspace) return I4B_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace) + kTicketBytes;
+  TcOperands o{x, stride_xm, w, stride_wn, nullptr, nullptr, 0};
+  cudaError_t e = cudaSuccess;
+  uint8_t* xcopy = ws;
+  ws += align256(size_t(M) * size_t(Kp) * 2);
+  if (!x_ok) {
+    if ((e = launch_repack(x, 2, M, K, stride_xm, stride_xk, xcopy, Kp, s)) != cudaSuccess) return fail_cuda(e);
+    o.x = xcopy;
+    o.sxm = Kp;
+  }
+  if (!w_ok) {
+    if ((e = launch_repack(w, 2, N, K, stride_wn, stride_wk, ws, Kp, s)) != cudaSuccess) return fail_cuda(e);
+    o.w = ws;
+    o.sw = Kp;
+  }
+  e = launch_tc(false, f16, o, M, N, Kp, 0, static_cast<uint16_t*>(y), stride_ym, tc_pick_bn(M, N, d.sms), s);
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_device_error_flags(int device, int clear) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return -1;
+  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  int flags = -1;
+  if (cudaDeviceSynchronize() == cudaSuccess) {
+    flags = int(read_quant_error(clear != 0) | read_tc_error(clear != 0));
+  }
+  cudaSetDevice(prev);
+  return flags;
+}
+
+}  // extern "C"

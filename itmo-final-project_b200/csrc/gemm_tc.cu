@@ -1,0 +1,388 @@
+// Large-M (M > 64) W4A16 / W16A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Replaces the reference's large-M Triton path _matmul_kernel (int4_triton/gemm.py:74-157,
+// launched at gemm.py:270-296).  y[M, N] = x[M, K] @ W_hat[N, K]^T.
+//
+// One CTA computes a 128 x BN output tile (BN = 128 or 256) with 6 warps:
+//   warp 0      TMA producer: per 64-wide k-block loads the activation tile
+//               (128 x 64 bf16, 128-byte swizzle), and either the packed
+//               weight tile (8 k8-rows x BN int32) plus two rows of scales and
+//               zeros (INT4), or the bf16 weight tile BN x 64 (W16);
+//   warp 1      allocates BN TMEM columns and, from one thread, issues four
+//               tcgen05.mma.kind::f16 (K = 16 each) per k-block into the fp32
+//               TMEM accumulator, then tcgen05.commit to free the stage;
+//   warps 2..5  INT4 only: dequantize the packed tile into the K-major,
+//               128-byte-swizzled B operand in shared memory,
+//                 W_hat = bf16_rn((q - z) * s)   (exactly the reference's
+//                 dequantize-then-round, int4_triton/gemm.py:137-140),
+//               using bf16x2 arithmetic: (128+q) - (128+z) is exact, the fp16
+//               scale is split into s_hi (top 8 significant bits, a bf16) and
+//               s_lo (the remaining 3 bits, also an exact bf16), q*s_lo is
+//               exact and fma(qz, s_hi, qz*s_lo) rounds once;
+//               then all four read the accumulator back with tcgen05.ld and
+//               store bf16 / fp16 rows of y.
+// Stages are handed over with mbarriers (TMA transaction bytes, dequant
+// arrivals, tcgen05.commit).  Every wait is bounded; on expiry the kernel
+// records I4B_DEVERR_WAIT_TIMEOUT, drains its own TMA copies, frees TMEM and
+// returns.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace i4b {
+
+static __device__ unsigned int g_tc_err = 0;
+
+template <bool INT4, int BN>
+struct TcCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;              // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;              // BN rows of 128 B
+  static constexpr int P_BYTES = INT4 ? 8 * BN * 4 : 0;    // packed words of one k-block
+  static constexpr int SZ_BYTES = INT4 ? 2 * 2 * BN * 2 : 0;  // scales + zeros, two group rows
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES + SZ_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int TX_BYTES = INT4 ? (A_BYTES + P_BYTES + SZ_BYTES) : (A_BYTES + B_BYTES);
+  static constexpr int BAR_BYTES = (3 * STAGES + 1) * 8 + 8;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + BAR_BYTES;
+};
+
+struct DqParams {
+  uint32_t zz;   // (bias + z) twice
+  uint32_t shi;  // bf16: scale high part twice; fp16: scale twice
+  uint32_t slo;  // bf16: scale low part twice
+};
+
+template <bool F16>
+__device__ __forceinline__ DqParams dq_params(uint16_t s_bits, uint16_t z_bits) {
+  const float s = __half2float(__ushort_as_half(s_bits));
+  const float z = __half2float(__ushort_as_half(z_bits));
+  DqParams p;
+  if constexpr (F16) {
+    const uint32_t zz = __half_as_ushort(__float2half_rn(1024.0f + z));
+    p.zz = zz * 0x10001u;
+    p.shi = uint32_t(s_bits) * 0x10001u;
+    p.slo = 0;
+  } else {
+    const uint32_t hi = __float_as_uint(s) & 0xFFFF0000u;
+    const float lo = isfinite(s) ? (s - __uint_as_float(hi)) : 0.0f;
+    const uint32_t lo16 = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+    const uint32_t zz = __bfloat16_as_ushort(__float2bfloat16_rn(128.0f + z));
+    p.zz = zz * 0x10001u;
+    p.shi = (hi >> 16) * 0x10001u;
+    p.slo = lo16 * 0x10001u;
+  }
+  return p;
+}
+
+// 8 nibbles of one packed word -> 8 dequantized 16-bit values in k order (one 16-byte chunk).
+template <bool F16>
+__device__ __forceinline__ uint4 dequant_word(uint32_t w, const DqParams& p) {
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t q = and_or(w >> (4 * i), 0x000F000Fu, F16 ? 0x64006400u : 0x43004300u);  // (q_i, q_{i+4})
+    uint32_t d;
+    if constexpr (F16) {
+      asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(q), "r"(p.zz));
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[i]) : "r"(d), "r"(p.shi));
+    } else {
+      uint32_t pl;
+      asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(q), "r"(p.zz));
+      asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(pl) : "r"(d), "r"(p.slo));
+      asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r[i]) : "r"(d), "r"(p.shi), "r"(pl));
+    }
+  }
+  // r[i] = (w_i, w_{i+4}); reorder to (w0,w1) (w2,w3) (w4,w5) (w6,w7)
+  return make_uint4(__byte_perm(r[0], r[1], 0x5410), __byte_perm(r[2], r[3], 0x5410),
+                    __byte_perm(r[0], r[1], 0x7632), __byte_perm(r[2], r[3], 0x7632));
+}
+
+template <bool INT4, bool F16, int BN>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z, int M, int N,
+                   int K, int G, uint16_t* __restrict__ y, int64_t sym) {
+  using C = TcCfg<INT4, BN>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + S * C::A_BYTES;
+  uint8_t* sP = sB + S * C::B_BYTES;
+  uint8_t* sSZ = sP + S * C::P_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSZ + S * C::SZ_BYTES);
+  uint64_t* bready = full + S;
+  uint64_t* empty = bready + S;
+  uint64_t* tfull = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * C::BM;
+  const int KB = (K + C::BK - 1) / C::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&bready[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+    if constexpr (INT4) {
+      tma_prefetch_desc(&tm_s);
+      tma_prefetch_desc(&tm_z);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % S, u = kb / S;
+        if (kb >= S && !mbar_wait(&empty[s], (u - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+        tma_load_2d(sA + s * C::A_BYTES, &tm_x, &full[s], kb * C::BK, m0);
+        if constexpr (INT4) {
+          const int g_lo = (kb * C::BK) / G;
+          tma_load_2d(sP + s * C::P_BYTES, &tm_w, &full[s], n0, kb * 8);
+          tma_load_2d(sSZ + s * C::SZ_BYTES, &tm_s, &full[s], n0, g_lo);
+          tma_load_2d(sSZ + s * C::SZ_BYTES + 2 * BN * 2, &tm_z, &full[s], n0, g_lo);
+        } else {
+          tma_load_2d(sB + s * C::B_BYTES, &tm_w, &full[s], kb * C::BK, n0);
+        }
+        ++issued;
+      }
+      // Never leave a bulk copy in flight: wait for the last use of every stage.
+      for (int s = 0; s < S && s < issued; ++s) {
+        const int last = ((issued - 1 - s) / S) * S + s;
+        if (!mbar_wait(&full[s], (last / S) & 1)) ok = false;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(F16 ? 0 : 1, 128, BN);
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % S, u = kb / S;
+        // INT4: the activation tile arrives on full[s], the dequantized weights on bready[s].
+        if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
+        if (INT4 && !mbar_wait(&bready[s], u & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t adesc = umma_desc_sw128(smem_u32(sA + s * C::A_BYTES));
+        const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * C::B_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk)
+          umma_f16_ss(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(tfull);  // also on the error path: completes once issued MMAs are done
+    }
+  } else {
+    if constexpr (INT4) {
+      const int dt = threadIdx.x - 64;  // 0..127
+      for (int kb = 0; kb < KB && ok; ++kb) {
+        const int s = kb % S, u = kb / S;
+        if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
+        const uint32_t* P = reinterpret_cast<const uint32_t*>(sP + s * C::P_BYTES);
+        const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ + s * C::SZ_BYTES);
+        const uint16_t* Zs = Ss + 2 * BN;
+        const int g_lo = (kb * C::BK) / G;
+        uint8_t* Bs = sB + s * C::B_BYTES;
+#pragma unroll
+        for (int rr = 0; rr < BN / 128; ++rr) {
+          const int nl = dt + 128 * rr;
+          const DqParams p0 = dq_params<F16>(Ss[nl], Zs[nl]);
+          const DqParams p1 = dq_params<F16>(Ss[BN + nl], Zs[BN + nl]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int sel = (kb * C::BK + 8 * j) / G - g_lo;
+            const uint4 v = dequant_word<F16>(P[j * BN + nl], sel ? p1 : p0);
+            *reinterpret_cast<uint4*>(Bs + nl * 128 + ((j ^ (nl & 7)) << 4)) = v;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bready[s]);
+      }
+    }
+    // ---- epilogue: TMEM -> registers -> y
+    if (!mbar_wait(tfull, 0)) ok = false;
+    tc_fence_after();
+    const int q = warp & 3;
+    const int m = m0 + 32 * q + lane;
+    const bool vec = (sym % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld_32x32b_x16(tmem + (uint32_t(32 * q) << 16) + uint32_t(c0), v);
+      tmem_ld_wait();
+      if (m < M) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float a = __uint_as_float(v[2 * i]), b = __uint_as_float(v[2 * i + 1]);
+          if constexpr (F16) {
+            const __half2 h = __floats2half2_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+          } else {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+        }
+        const int n = n0 + c0;
+        uint16_t* dst = y + int64_t(m) * sym + n;
+        if (vec && n + 16 <= N) {
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (n + i < N) dst[i] = uint16_t(pk[i >> 1] >> (16 * (i & 1)));
+        }
+      }
+    }
+  }
+  if (!ok) atomicOr(&g_tc_err, I4B_DEVERR_WAIT_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+// ------------------------------------------------------------------ repack (misaligned operands)
+
+// out[r, c] = c < cols_in ? in[r*sr + c*sc] : 0   (element size 2 or 4 bytes)
+template <typename T>
+__global__ void repack2d_kernel(const T* __restrict__ in, int64_t rows, int64_t cols_in, int64_t sr, int64_t sc,
+                                T* __restrict__ out, int64_t cols_out) {
+  const int64_t total = rows * cols_out;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols_out, c = i % cols_out;
+    out[i] = c < cols_in ? in[r * sr + c * sc] : T(0);
+  }
+}
+
+cudaError_t launch_repack(const void* in, int esize, int64_t rows, int64_t cols_in, int64_t sr, int64_t sc, void* out,
+                          int64_t cols_out, cudaStream_t stream) {
+  const int64_t total = rows * cols_out;
+  if (total == 0) return cudaSuccess;
+  const int blocks = int(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  if (esize == 2)
+    repack2d_kernel<uint16_t><<<blocks, 256, 0, stream>>>(static_cast<const uint16_t*>(in), rows, cols_in, sr, sc,
+                                                          static_cast<uint16_t*>(out), cols_out);
+  else
+    repack2d_kernel<uint32_t><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t*>(in), rows, cols_in, sr, sc,
+                                                          static_cast<uint32_t*>(out), cols_out);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ tensor maps + launch
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D row-major tensor: `inner` contiguous elements per row, `rows` rows `row_bytes` apart.
+static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+
+
+template <bool INT4, bool F16, int BN>
+static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
+                                  int64_t sym, cudaStream_t stream) {
+  using C = TcCfg<INT4, BN>;
+  const CUtensorMapDataType act = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap mx{}, mw{}, ms{}, mz{};
+  bool ok = make_map(&mx, act, o.x, uint64_t(K), uint64_t(M), uint64_t(o.sxm) * 2, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if constexpr (INT4) {
+    ok = ok && make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, o.w, uint64_t(N), uint64_t(K / 8), uint64_t(o.sw) * 4, BN,
+                        8, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok = ok && make_map(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.sc, uint64_t(N), uint64_t(K / G), uint64_t(o.ssg) * 2,
+                        BN, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok = ok && make_map(&mz, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.zr, uint64_t(N), uint64_t(K / G), uint64_t(o.ssg) * 2,
+                        BN, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    ok = ok && make_map(&mw, act, o.w, uint64_t(K), uint64_t(N), uint64_t(o.sw) * 2, 64, BN,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    ms = mw;
+    mz = mw;
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  auto kern = tc_gemm_kernel<INT4, F16, BN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM));
+  if (e != cudaSuccess) return e;
+  dim3 grid(unsigned(cdiv(N, BN)), unsigned(cdiv(M, 128)));
+  kern<<<grid, 192, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym);
+  return cudaGetLastError();
+}
+
+int tc_pick_bn(int64_t M, int64_t N, int num_sms) {
+  // 256-wide tiles halve the activation re-reads but only pay off with enough tiles.
+  const int64_t tiles256 = cdiv(M, 128) * cdiv(N, 256);
+  return tiles256 >= num_sms ? 256 : 128;
+}
+
+cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
+                      int64_t sym, int bn, cudaStream_t stream) {
+#define I4B_TC(I, F, B) return launch_tc_impl<I, F, B>(o, M, N, K, G, y, sym, stream)
+  if (int4) {
+    if (f16) { if (bn == 256) I4B_TC(true, true, 256); I4B_TC(true, true, 128); }
+    if (bn == 256) I4B_TC(true, false, 256);
+    I4B_TC(true, false, 128);
+  }
+  if (f16) { if (bn == 256) I4B_TC(false, true, 256); I4B_TC(false, true, 128); }
+  if (bn == 256) I4B_TC(false, false, 256);
+  I4B_TC(false, false, 128);
+#undef I4B_TC
+}
+
+unsigned int read_tc_error(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(v));
+  if (clear) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_tc_err, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace i4b

@@ -1,0 +1,57 @@
+// Host-side declarations of the kernel launchers shared between the .cu files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace i4b {
+
+// quantize.cu
+cudaError_t launch_quantize(const void* w, int dt, int64_t N, int64_t K, int64_t swn, int64_t swk, int G,
+                            int32_t* qw, uint16_t* sc, uint16_t* zr, cudaStream_t stream);
+cudaError_t launch_dequantize(const int32_t* qw, const uint16_t* sc, const uint16_t* zr, int64_t N, int64_t K, int G,
+                              int odt, void* out, cudaStream_t stream);
+unsigned int read_quant_error(bool clear);
+
+// Every workspace starts with a ticket region that only the split-K kernels
+// use and always leave zero; scratch of any other kind starts after it.
+constexpr size_t kTicketBytes = 64 * 1024;
+constexpr int64_t kMaxTickets = int64_t(kTicketBytes / 4);
+
+// skinny.cu (M <= kSkinnyMaxM)
+constexpr int64_t kSkinnyMaxM = 16;
+struct SkinnyPlan {
+  int MT, WN, WK, S, KC, KW, L, xstride;
+  int mode;  // 0: one CTA per column tile; 1: cluster along K; 2: workspace split-K; 3: unsupported
+  size_t smem_bytes;
+  size_t partial_bytes;
+  int64_t ntiles;
+};
+SkinnyPlan plan_skinny(int64_t M, int64_t N, int64_t K, int G, bool int4, int num_sms);
+size_t skinny_workspace_bytes(const SkinnyPlan& p);
+cudaError_t launch_skinny(bool int4, bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk,
+                          const void* w, int64_t N, int64_t sw0, int64_t sw1, const uint16_t* sc,
+                          const uint16_t* zr, int64_t ssg, int G, void* y, int64_t sym, void* ws,
+                          const SkinnyPlan& p, bool pdl, cudaStream_t stream);
+// Tuning override of the automatic decomposition (0 = automatic).
+void set_skinny_override(int wn, int wk, int splits);
+
+// gemm_tc.cu (M > 64)
+struct TcOperands {
+  const void* x;
+  int64_t sxm;
+  const void* w;
+  int64_t sw;
+  const uint16_t* sc;
+  const uint16_t* zr;
+  int64_t ssg;
+};
+int tc_pick_bn(int64_t M, int64_t N, int num_sms);
+cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
+                      int64_t sym, int bn, cudaStream_t stream);
+cudaError_t launch_repack(const void* in, int esize, int64_t rows, int64_t cols_in, int64_t sr, int64_t sc, void* out,
+                          int64_t cols_out, cudaStream_t stream);
+unsigned int read_tc_error(bool clear);
+
+}  // namespace i4b

@@ -169,3 +169,26 @@ def rel_fro_error(out: np.ndarray, ref: np.ndarray) -> float:
     out = np.asarray(out, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     return float(np.linalg.norm(out - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+def w4a16_matmul_threaded(x: np.ndarray, qweight, scales, zeros, x_dtype: str = BF16, threads: int = 1) -> np.ndarray:
+    """``w4a16_matmul`` split over output columns on ``threads`` host threads (numpy releases the GIL).
+
+    Same arithmetic per column as ``w4a16_matmul``; used to time the
+    reference's CPU path with all host cores.
+    """
+    import concurrent.futures as cf
+
+    qw = np.asarray(qweight)
+    N = qw.shape[1]
+    if threads <= 1 or N < 2 * threads:
+        return w4a16_matmul(x, qweight, scales, zeros, x_dtype)
+    xf = to_f32(x, x_dtype)
+    bounds = np.linspace(0, N, threads + 1).astype(int)
+
+    def part(i):
+        a, b = bounds[i], bounds[i + 1]
+        return xf @ dequantize_int4_f32(qw[:, a:b], scales[:, a:b], zeros[:, a:b]).T
+
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        return np.concatenate(list(ex.map(part, range(threads))), axis=1)
