@@ -44,7 +44,8 @@ enum {
   I4B_ERR_LAYOUT = 4,      /* a stride or alignment the entry point does not accept */
   I4B_ERR_WORKSPACE = 5,   /* workspace smaller than the matching *_workspace_size() */
   I4B_ERR_CUDA = 6,        /* a CUDA runtime / driver call failed (see i4b_last_cuda_error) */
-  I4B_ERR_ARCH = 7         /* current device is not sm_100 */
+  I4B_ERR_ARCH = 7,        /* current device is not sm_100 */
+  I4B_ERR_SCRATCH_LIMIT = 8 /* i4b_w4a16_matmul_noalloc: these sizes need more than its built-in scratch */
 };
 
 /* Human-readable name of a status code. */
@@ -117,6 +118,26 @@ void i4b_set_pdl(int enable);
  * unusable value is ignored.  Process-wide.  No counterpart in the reference
  * (which autotunes, int4_triton/gemm.py:51-56). */
 void i4b_set_skinny_override(int wn, int wk, int splits);
+
+/* Bytes of the scratch array built into the library for i4b_w4a16_matmul_noalloc. */
+#define I4B_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* i4b_w4a16_matmul for callers that cannot allocate device memory.
+ * No counterpart in the reference, which always allocates its outputs and
+ * split-K scratch with torch (int4_triton/gemm.py:246,266-268).
+ * Same arguments, result and status codes as i4b_w4a16_matmul, minus the
+ * workspace: a plugin inside a host program that owns all device allocation,
+ * or a caller on a path where cudaMalloc may not run, passes only its inputs
+ * and output.  Scratch comes from one I4B_NOALLOC_SCRATCH_BYTES array compiled
+ * into the library (held by every GPU that loads it, until exit).  Sizes whose
+ * i4b_w4a16_workspace_size exceeds that return I4B_ERR_SCRATCH_LIMIT.  No
+ * cudaMalloc / cudaFree is called.  The first call on a device looks up the
+ * array's device address, so make it before any stream capture.  All calls on
+ * a device share the array: calls that overlap on the GPU race. */
+int i4b_w4a16_matmul_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
+                             const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales,
+                             const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
+                             void* stream);
 
 /* Device-side error flags raised by kernels of this library on `device`
  * (a bounded wait that expired sets bit 0).  Synchronises that device;

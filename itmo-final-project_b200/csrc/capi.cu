@@ -94,6 +94,7 @@ const char* i4b_status_string(int status) {
     case I4B_ERR_WORKSPACE: return "workspace too small";
     case I4B_ERR_CUDA: return "CUDA error";
     case I4B_ERR_ARCH: return "device is not sm_100 (B200)";
+    case I4B_ERR_SCRATCH_LIMIT: return "sizes exceed the built-in scratch of i4b_w4a16_matmul_noalloc";
     default: return "unknown status";
   }
 }
