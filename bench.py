@@ -325,12 +325,14 @@ def main():
     ap.add_argument("--workload", choices=["block"], default="block")
     ap.add_argument("--m", type=int, default=1, help="tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pdl", type=int, default=1,
+                    help="programmatic dependent launch for the small-M kernels (weights fetched before the wait)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     config = {"workload": f"llama-3.2-1b decoder block, 7 linears, W4 G={GROUP}, M={args.m}",
               "model": "Llama-3.2-1B-shaped (random-init)", "group_size": GROUP, "tokens_per_step": args.m,
-              "parallelism": f"tp{args.gpus}", "global_batch": args.m, "seq_len": 1,
+              "parallelism": f"tp{args.gpus}", "global_batch": args.m, "seq_len": 1, "pdl": bool(args.pdl),
               "l2": "inputs larger than L2: weights rotate over copies whose total exceeds 2x L2"}
     metric = "per-block W4A16 GEMM us (Llama-3.2-1B decoder block, decode step)"
     threads = os.cpu_count() or 1
@@ -354,6 +356,10 @@ def main():
         return
 
     world, rank, local = dist_setup()
+    if args.pdl:
+        from int4_b200 import _lib
+
+        _lib.set_pdl(True)
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     r = run_block(args, world, rank, local)

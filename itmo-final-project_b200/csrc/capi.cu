@@ -103,7 +103,10 @@ int i4b_abi_version(void) { return I4B_ABI_VERSION; }
 
 int i4b_last_cuda_error(void) { return t_last_cuda_error; }
 
-void i4b_set_skinny_override(int wn, int wk, int splits) { set_skinny_override(wn, wk, splits); }
+void i4b_set_skinny_override(int wn, int wk, int splits) {
+  set_skinny_override(wn, wk, splits);
+  set_w4_split_override(splits);
+}
 
 void i4b_set_pdl(int enable) { g_pdl = enable != 0; }
 
@@ -143,7 +146,7 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
   if (M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || group_size % 32 != 0 || K % group_size != 0) return 0;
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
-  if (M <= kSmallM) return skinny_workspace_bytes(plan_skinny(M, N, K, group_size, true, d.sms));
+  if (M <= kSmallM) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
   return tc_w4_workspace(M, N, K, group_size);
 }
 
@@ -166,11 +169,11 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
   const bool f16 = x_dtype == I4B_F16;
 
   if (M <= kSmallM) {
-    const SkinnyPlan p = plan_skinny(M, N, K, G, true, d.sms);
+    const W4Plan p = plan_w4(M, N, K, G, d.sms);
     if (p.mode == 3) return I4B_ERR_SHAPE;
-    if (skinny_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;
-    cudaError_t e = launch_skinny(true, f16, x, M, K, stride_xm, stride_xk, qweight, N, stride_qk, 0, scales, zeros,
-                                  stride_sg, G, y, stride_ym, workspace, p, g_pdl, s);
+    if (w4_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;
+    cudaError_t e = launch_w4(f16, x, M, K, stride_xm, stride_xk, qweight, N, stride_qk, scales, zeros, stride_sg, G,
+                              y, stride_ym, workspace, p, g_pdl, s);
     return e == cudaSuccess ? I4B_OK : fail_cuda(e);
   }
 

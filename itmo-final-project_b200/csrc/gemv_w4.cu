@@ -1,0 +1,540 @@
+// Small-M (M <= 16) W4A16 kernel: the M == 1 decode GEMV and the small-batch split-K path.
+//
+// Replaces the reference's _gemv_kernel (int4_triton/gemm.py:185-220) and its
+// small-M split-K pair _matmul_kernel + _reduce_split_k (gemm.py:74-182,
+// launched at gemm.py:265-299) with ONE launch per matmul.
+//
+// Work split.  grid = (ceil(N / 128), S), cluster (1, S, 1) when 1 < S <= 8.
+// A CTA owns 128 output columns and the K range [y*KC, (y+1)*KC), KC <= 1024;
+// warp w owns columns 32w..32w+31.  Every lane puts ALL of the packed words it
+// will use in flight at once (cp.async, 16 bytes per 32-k step, one commit
+// group per stage of 4 steps) into its own slots of shared memory, so no
+// barrier orders copy and use: cp.async.wait_group does.  These copies do not
+// depend on the previous kernel of the stream, so with programmatic dependent
+// launch they are issued before griddepcontrol.wait and overlap that kernel's
+// tail; only the activations, staged once per CTA in shared memory, wait for it.
+//
+// Dequant and MMA.  Per 32-k step, lane (r = lane/4, c = lane%4) holds the 4
+// words of columns 4r..4r+3 at k8 row 4*step + c.  One lop3 turns a nibble
+// pair into the bf16 (fp16) pair (bias + q_i, bias + q_{i+4}), bias = 128
+// (1024), exactly; these pairs ARE the A fragments of mma.m16n8k16 (rows =
+// output columns), the activations, stored pre-permuted to the same k order,
+// are the B fragments; fp32 accumulators.  Zero point and scale are applied once
+// per segment of L = 32*SPS consecutive k inside one group:
+//     sum_k x_k (q_k - z) s  =  s * (D - (bias + z) * X),   D = sum_k x_k (bias + q_k),
+// where X = sum_k x_k over the segment comes from one more MMA with an all-ones
+// A fragment (it lands in exactly the accumulator layout the update needs).
+// This is x . ((q - z) s) with the exact fp32 dequantized weight, up to fp32
+// summation order.
+//
+// Reduction.  K splits inside a cluster add through distributed shared memory
+// in fixed rank order.  More than 8 splits (K > 8192) write fp32 partials to
+// the caller's workspace; the last CTA of a column tile (atomic ticket, no
+// spinning) adds them in split order and resets the ticket.  Every path is
+// bit-identical from run to run.  The kernel has no spin-waits.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace i4b {
+
+namespace {
+
+constexpr int kBN = 128;      // output columns per CTA (4 warps x 32)
+constexpr int kMaxKC = 1024;  // k per CTA
+constexpr int kStageSteps = 4;
+
+struct W4SArgs {
+  const uint16_t* x;
+  int64_t sxm, sxk;
+  const uint32_t* qw;
+  int64_t sqk;  // words between k8 rows
+  const uint16_t* sc;
+  const uint16_t* zr;
+  int64_t ssg;  // elements between group rows of scales / zeros
+  uint16_t* y;
+  int64_t sym;
+  float* partials;
+  unsigned int* tickets;
+  int M, N, K, G;
+  int S, KC, mode;
+  int nstages;     // stages per CTA (the last one padded with zeros)
+  int gpl_shift;   // log2(segments per group), or -1 when that count is not a power of two
+  int gpl;         // segments per group
+  int vec_w, vec_s, vec_x, pdl;
+  int xpitch;
+  int off_sz, off_x, off_part;
+};
+
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i, uint32_t magic) {
+  return and_or(w >> (4 * i), 0x000F000Fu, magic);
+}
+
+template <bool F16>
+__device__ __forceinline__ uint16_t f2h_bits(float v) {
+  if constexpr (F16) return __half_as_ushort(__float2half_rn(v));
+  else return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// Shared-memory accesses by 32-bit address; volatile keeps them ordered after cp.async.wait_group.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void cp16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp8(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp4(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+// cp.async.wait_group with a run-time count (0..7).
+__device__ __forceinline__ void cp_async_wait_upto(int pending) {
+  switch (pending) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    default: cp_async_wait<7>(); break;
+  }
+}
+
+}  // namespace
+
+// Shared memory: weights [step][warp][lane] x 16 B | scales+zeros [segment][warp][r] x 16 B (s0..s3, z0..z3) |
+// activations [token][k/8] x 16 B (pre-permuted) | partial sums [token][128] fp32.  The K range of a CTA is
+// padded to whole stages with zero weights, zero activations and zero scales, which add nothing.
+template <int MT, bool F16, int SPS>
+__global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
+  constexpr int SPST = SPS > 4 ? SPS : 4;  // 32-k steps per stage (one cp.async group); whole segments
+  constexpr int SEGST = SPST / SPS;        // segments per stage
+  constexpr int L = 32 * SPS;              // k per segment
+  constexpr int WSTEP = 4 * 32 * 16;       // shared bytes of one step of weights (4 warps x 32 lanes x 16 B)
+  constexpr int SZSEG = 4 * 8 * 16;        // shared bytes of one segment of scales + zeros
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = lane >> 2, c = lane & 3;
+  const int64_t n0 = int64_t(blockIdx.x) * kBN;
+  const int k0 = int(blockIdx.y) * a.KC;
+  const int nsteps = a.KC / 32;
+  const int nstages = a.nstages;
+  const int M = a.M;
+
+  const uint32_t s_w = smem_u32(smem);
+  const uint32_t s_sz = s_w + a.off_sz;
+  const uint32_t s_x = s_w + a.off_x;
+  float* sP = reinterpret_cast<float*>(smem + a.off_part);
+
+  // ---- weights, scales, zeros: independent of the previous kernel, all put in flight first
+  const int64_t n_lane = n0 + warp * 32 + 4 * r;
+  const bool n_in = n_lane < a.N;
+  {
+    const uint32_t* src = a.qw + int64_t(k0 / 8 + c) * a.sqk + (n_in ? n_lane : 0);
+    const int64_t wstep = 4 * a.sqk;
+    uint32_t dst = s_w + (warp * 32 + lane) * 16;
+    const int nfull = nsteps / SPST;  // stages whose steps all lie inside K
+    // Scales and zeros: the 16-byte record (s0 s1 | s2 s3 | z0 z1 | z2 z3) of a segment is copied 4 bytes
+    // per lane c; a group row advances every gpl segments.
+    const uint16_t* szsrc = (c < 2 ? a.sc : a.zr) + 2 * (c & 1);
+    const int seg0 = k0 / L;
+    int64_t g = a.gpl_shift >= 0 ? (seg0 >> a.gpl_shift) : seg0 / a.gpl;
+    int gcnt = seg0 - int(g) * a.gpl;
+    const bool sz_in = n_in && a.vec_s;
+    uint32_t dst_sz = s_sz + (warp * 8 + r) * 16 + 4 * c;
+    for (int st = 0; st < nstages; ++st) {
+      if (st < nfull && a.vec_w) {
+        const uint32_t bytes = n_in ? 16u : 0u;
+#pragma unroll
+        for (int i = 0; i < SPST; ++i) {
+          cp16(dst + i * WSTEP, src, bytes);
+          src += wstep;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < SPST; ++i) {
+          const bool real = st * SPST + i < nsteps;
+          if (a.vec_w) {
+            cp16(dst + i * WSTEP, real ? src : a.qw, real && n_in ? 16u : 0u);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const bool in = real && n_lane + j < a.N;
+              cp4(dst + i * WSTEP + 4 * j, in ? src + j : a.qw, in ? 4u : 0u);
+            }
+          }
+          if (real) src += wstep;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < SEGST; ++j) {
+        const bool real = (st * SEGST + j) * SPS < nsteps;
+        const uint32_t d = dst_sz + j * SZSEG;
+        if (a.vec_s || !real) {
+          cp4(d, real && sz_in ? szsrc + g * a.ssg + n_lane : a.sc, real && sz_in ? 4u : 0u);
+        } else {
+          // unaligned scales / zeros: two plain loads per lane
+          const bool in0 = n_lane + 2 * (c & 1) < a.N, in1 = n_lane + 2 * (c & 1) + 1 < a.N;
+          const uint16_t* p = szsrc + g * a.ssg + n_lane;
+          const uint32_t v = (in0 ? uint32_t(__ldg(p)) : 0u) | ((in1 ? uint32_t(__ldg(p + 1)) : 0u) << 16);
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(d), "r"(v) : "memory");
+        }
+        if (++gcnt == a.gpl) {
+          gcnt = 0;
+          ++g;
+        }
+      }
+      cp_async_commit();
+      dst += SPST * WSTEP;
+      dst_sz += SEGST * SZSEG;
+    }
+  }
+
+  // ---- activations: produced by the previous kernel of the stream
+  if (a.pdl) {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+  {
+    const int nch = nstages * SPST * 4;  // chunks of 8 k, padded
+    const int nreal = a.KC / 8;
+    for (int t = 0; t < M; ++t) {
+      const uint16_t* xrow = a.x + int64_t(t) * a.sxm + int64_t(k0) * a.sxk;
+      for (int ch = tid; ch < nch; ch += blockDim.x) {
+        uint32_t u[4] = {0u, 0u, 0u, 0u};
+        if (ch < nreal) {
+          const uint16_t* p = xrow + int64_t(8 * ch) * a.sxk;
+          if (a.vec_x) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+            u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+          } else {
+            uint16_t e[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) e[j] = __ldg(p + j * a.sxk);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) u[j] = uint32_t(e[2 * j]) | (uint32_t(e[2 * j + 1]) << 16);
+          }
+        }
+        // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
+                     "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
+                     "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
+                     : "memory");
+      }
+    }
+  }
+  __syncthreads();
+
+  float acc[2][MT][4];
+  float dacc[2][MT][4];
+  float xs[MT][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[t][mt][e] = 0.0f;
+
+  const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
+  const float bias = F16 ? 1024.0f : 128.0f;
+  const uint32_t ones = F16 ? 0x3C003C00u : 0x3F803F80u;
+  const uint32_t one4[4] = {ones, ones, ones, ones};
+  uint32_t wl = s_w + (warp * 32 + lane) * 16;
+  uint32_t szl = s_sz + (warp * 8 + r) * 16;
+  // Token rows past M read a real row instead: their outputs are discarded, and no branch is needed.
+  uint32_t xl[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) xl[mt] = s_x + min(mt * 8 + r, M - 1) * a.xpitch + 16 * c;
+
+  for (int st = 0; st < nstages; ++st) {
+    cp_async_wait_upto(nstages - 1 - st);  // this lane's copies of stage st have landed
+    __syncwarp();                           // and the scales / zeros copied by lanes c == 0
+#pragma unroll
+    for (int i = 0; i < SPST; ++i) {
+      if (i % SPS == 0) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dacc[t][mt][e] = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xs[mt][e] = 0.0f;
+      }
+      const uint4 w4 = lds128(wl + i * WSTEP);
+      const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
+      uint32_t af[2][2][4];  // [row tile][k16 half][reg]
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          af[t][s][0] = nib_pair(wd[2 * t], 2 * s, magic);
+          af[t][s][1] = nib_pair(wd[2 * t + 1], 2 * s, magic);
+          af[t][s][2] = nib_pair(wd[2 * t], 2 * s + 1, magic);
+          af[t][s][3] = nib_pair(wd[2 * t + 1], 2 * s + 1, magic);
+        }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint4 b = lds128(xl[mt] + i * 64);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          mma_16816<F16>(dacc[t][mt], af[t][0], b.x, b.y);
+          mma_16816<F16>(dacc[t][mt], af[t][1], b.z, b.w);
+        }
+        mma_16816<F16>(xs[mt], one4, b.x, b.y);
+        mma_16816<F16>(xs[mt], one4, b.z, b.w);
+      }
+      if (i % SPS == SPS - 1) {  // segment complete: acc += s * (D - (bias + z) * X)
+        const uint4 sz = lds128(szl + (i / SPS) * SZSEG);
+        float sv[4], zv[4];
+        sv[0] = __half2float(__ushort_as_half(uint16_t(sz.x & 0xFFFFu)));
+        sv[1] = __half2float(__ushort_as_half(uint16_t(sz.x >> 16)));
+        sv[2] = __half2float(__ushort_as_half(uint16_t(sz.y & 0xFFFFu)));
+        sv[3] = __half2float(__ushort_as_half(uint16_t(sz.y >> 16)));
+        zv[0] = bias + __half2float(__ushort_as_half(uint16_t(sz.z & 0xFFFFu)));
+        zv[1] = bias + __half2float(__ushort_as_half(uint16_t(sz.z >> 16)));
+        zv[2] = bias + __half2float(__ushort_as_half(uint16_t(sz.w & 0xFFFFu)));
+        zv[3] = bias + __half2float(__ushort_as_half(uint16_t(sz.w >> 16)));
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const float X0 = xs[mt][0], X1 = xs[mt][1];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            acc[t][mt][0] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X0, dacc[t][mt][0]), acc[t][mt][0]);
+            acc[t][mt][1] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X1, dacc[t][mt][1]), acc[t][mt][1]);
+            acc[t][mt][2] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X0, dacc[t][mt][2]), acc[t][mt][2]);
+            acc[t][mt][3] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X1, dacc[t][mt][3]), acc[t][mt][3]);
+          }
+        }
+      }
+    }
+    wl += SPST * WSTEP;
+    szl += SEGST * SZSEG;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) xl[mt] += SPST * 64;
+  }
+
+  // ---- outputs: acc[t][mt][e] is (token mt*8 + 2c + (e & 1), column 32*warp + 4r + 2t + (e >> 1))
+  uint16_t* y = a.y;
+  if (a.mode == 0) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = mt * 8 + 2 * c + (e & 1);
+          const int64_t n = n_lane + 2 * t + (e >> 1);
+          if (tok < M && n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(acc[t][mt][e]);
+        }
+    return;
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = mt * 8 + 2 * c + (e & 1);
+        if (tok < M) sP[tok * kBN + warp * 32 + 4 * r + 2 * t + (e >> 1)] = acc[t][mt][e];
+      }
+  if (a.mode == 1) {
+    // Cluster of S CTAs along K: rank q adds outputs q*128 + tid, (q + S)*128 + tid, ... over all ranks in order.
+    cluster_sync();
+    const uint32_t rank = cluster_ctarank();
+    for (int idx = int(rank) * kBN + tid; idx < M * kBN; idx += a.S * kBN) {
+      const uint32_t addr = smem_u32(sP + idx);
+      float v = ld_shared_cluster_f32(mapa_shared(addr, 0));
+      for (int q = 1; q < a.S; ++q) v += ld_shared_cluster_f32(mapa_shared(addr, uint32_t(q)));
+      const int tok = idx / kBN;
+      const int64_t n = n0 + idx % kBN;
+      if (n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
+    }
+    cluster_sync();  // no CTA leaves while others may still read its shared memory
+    return;
+  }
+  // mode 2: fp32 partials in the workspace; the last CTA of the column tile adds them in split order.
+  __syncthreads();
+  for (int idx = tid; idx < M * kBN; idx += blockDim.x) {
+    const int tok = idx / kBN;
+    const int64_t n = n0 + idx % kBN;
+    if (n < a.N) a.partials[(int64_t(blockIdx.y) * M + tok) * a.N + n] = sP[idx];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned int prev = atomicAdd(a.tickets + blockIdx.x, 1u);
+    s_last = (prev == unsigned(a.S - 1));
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = tid; idx < M * kBN; idx += blockDim.x) {
+    const int tok = idx / kBN;
+    const int64_t n = n0 + idx % kBN;
+    if (n >= a.N) continue;
+    float v = __ldcg(a.partials + int64_t(tok) * a.N + n);
+    for (int s = 1; s < a.S; ++s) v += __ldcg(a.partials + (int64_t(s) * M + tok) * a.N + n);
+    y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
+  }
+  if (tid == 0) atomicExch(a.tickets + blockIdx.x, 0u);
+}
+
+// ------------------------------------------------------------------ planning
+
+static int g_w4_ovr_s = 0;
+
+void set_w4_split_override(int splits) { g_w4_ovr_s = splits; }
+
+static int gcd_i(int a, int b) {
+  while (b) {
+    const int t = a % b;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
+// K is cut into units of L = 32 * gcd(G/32, 8) k (a segment: L divides G, so it lies in one group);
+// a CTA owns KC = K / S consecutive k, a whole number of units, at most kMaxKC.
+W4Plan plan_w4(int64_t M, int64_t N, int64_t K, int G, int num_sms) {
+  W4Plan p{};
+  p.MT = M <= 8 ? 1 : 2;
+  p.SPS = gcd_i(G / 32, 8);
+  p.ntiles = cdiv(N, kBN);
+  const int64_t L = 32 * p.SPS;
+  const int64_t units = K / L;
+  // Split count S (a divisor of the units): within one cluster (S <= 8) the smallest S giving two CTAs
+  // per SM, else the largest S that keeps >= 128 k per CTA, else the smallest that fits; only
+  // K > 8 * kMaxKC needs S > 8 (workspace partials).
+  int64_t S = 0;
+  const int64_t smax = std::min<int64_t>(8, units);
+  auto fits = [&](int64_t s) { return units % s == 0 && K / s <= kMaxKC; };
+  for (int64_t s = 1; s <= smax && !S; ++s)
+    if (fits(s) && p.ntiles * s >= 2 * num_sms) S = s;
+  for (int64_t s = smax; s >= 1 && !S; --s)
+    if (fits(s) && K / s >= 128) S = s;
+  for (int64_t s = 1; s <= smax && !S; ++s)
+    if (fits(s)) S = s;
+  for (int64_t s = 9; s <= units && !S; ++s)
+    if (fits(s)) S = s;
+  if (g_w4_ovr_s > 0 && units % g_w4_ovr_s == 0 && K / g_w4_ovr_s <= kMaxKC) S = g_w4_ovr_s;
+  p.S = int(S);
+  p.KC = int(K / S);
+  p.mode = S == 1 ? 0 : (S <= 8 ? 1 : 2);
+  if (p.mode == 2 && p.ntiles > kMaxTickets) p.mode = 3;  // unsupported: reported as an error
+  p.partial_bytes = p.mode == 2 ? size_t(S) * size_t(M) * size_t(N) * 4 : 0;
+  return p;
+}
+
+size_t w4_workspace_bytes(const W4Plan& p) { return p.mode == 2 ? kTicketBytes + p.partial_bytes : 0; }
+
+template <int MT, bool F16, int SPS>
+static cudaError_t launch_w4_impl(const W4SArgs& a, const W4Plan& p, size_t smem, cudaStream_t stream) {
+  auto kern = w4_skinny_kernel<MT, F16, SPS>;
+  static size_t configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(std::max<size_t>(smem, 48 * 1024)));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    configured = std::max<size_t>(smem, 48 * 1024);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(p.ntiles), unsigned(p.S));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (p.mode == 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = unsigned(p.S);
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (a.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int MT, bool F16>
+static cudaError_t launch_w4_sps(const W4SArgs& a, const W4Plan& p, size_t smem, cudaStream_t stream) {
+  switch (p.SPS) {
+    case 1: return launch_w4_impl<MT, F16, 1>(a, p, smem, stream);
+    case 2: return launch_w4_impl<MT, F16, 2>(a, p, smem, stream);
+    case 4: return launch_w4_impl<MT, F16, 4>(a, p, smem, stream);
+    default: return launch_w4_impl<MT, F16, 8>(a, p, smem, stream);
+  }
+}
+
+cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
+                      int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
+                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream) {
+  if (p.mode == 3) return cudaErrorInvalidConfiguration;
+  W4SArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.sxm = sxm;
+  a.sxk = sxk;
+  a.qw = reinterpret_cast<const uint32_t*>(qw);
+  a.sqk = sqk;
+  a.sc = sc;
+  a.zr = zr;
+  a.ssg = ssg;
+  a.y = static_cast<uint16_t*>(y);
+  a.sym = sym;
+  a.M = int(M);
+  a.N = int(N);
+  a.K = int(K);
+  a.G = G;
+  a.S = p.S;
+  a.KC = p.KC;
+  a.mode = p.mode;
+  a.pdl = pdl ? 1 : 0;
+  if (p.mode == 2) {
+    a.tickets = static_cast<unsigned int*>(ws);
+    a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kTicketBytes);
+  }
+  const auto addr = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr); };
+  a.vec_w = addr(qw) % 16 == 0 && sqk % 4 == 0 && N % 4 == 0;
+  a.vec_s = addr(sc) % 4 == 0 && addr(zr) % 4 == 0 && ssg % 2 == 0 && N % 4 == 0;
+  a.vec_x = addr(x) % 16 == 0 && sxk == 1 && (sxm % 8 == 0 || M == 1);
+  const int spst = p.SPS > 4 ? p.SPS : 4;  // steps per stage, as in the kernel
+  const int nsteps = p.KC / 32;
+  a.nstages = (nsteps + spst - 1) / spst;
+  const int L = 32 * p.SPS;
+  a.gpl = G / L;  // L divides G
+  a.gpl_shift = (a.gpl & (a.gpl - 1)) == 0 ? __builtin_ctz(unsigned(a.gpl)) : -1;
+  // token rows of x in shared memory: 4 mod 8 16-byte units apart (conflict-free fragment reads)
+  const int kcp = a.nstages * spst * 32;  // padded k per CTA
+  a.xpitch = (kcp / 8) % 8 == 0 ? kcp * 2 + 64 : kcp * 2;
+  size_t off = size_t(a.nstages) * spst * 4 * 32 * 16;
+  a.off_sz = int(off);
+  off += size_t(a.nstages) * (spst / p.SPS) * 4 * 8 * 16;
+  a.off_x = int(off);
+  off += size_t(M) * a.xpitch;
+  a.off_part = int(off);
+  off += size_t(M) * kBN * 4;
+  const size_t smem = off;
+  if (p.MT == 1) return f16 ? launch_w4_sps<1, true>(a, p, smem, stream) : launch_w4_sps<1, false>(a, p, smem, stream);
+  return f16 ? launch_w4_sps<2, true>(a, p, smem, stream) : launch_w4_sps<2, false>(a, p, smem, stream);
+}
+
+}  // namespace i4b

@@ -37,6 +37,20 @@ cudaError_t launch_skinny(bool int4, bool f16, const void* x, int64_t M, int64_t
 // Tuning override of the automatic decomposition (0 = automatic).
 void set_skinny_override(int wn, int wk, int splits);
 
+// gemv_w4.cu (INT4, M <= kSkinnyMaxM)
+struct W4Plan {
+  int MT, SPS, S, KC;
+  int mode;  // 0: one CTA per column tile; 1: cluster along K; 2: workspace split-K; 3: unsupported
+  int64_t ntiles;
+  size_t partial_bytes;
+};
+W4Plan plan_w4(int64_t M, int64_t N, int64_t K, int G, int num_sms);
+size_t w4_workspace_bytes(const W4Plan& p);
+cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
+                      int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
+                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream);
+void set_w4_split_override(int splits);
+
 // gemm_tc.cu (M > 64)
 struct TcOperands {
   const void* x;
