@@ -64,7 +64,7 @@ struct W4SArgs {
   int gpl;         // segments per group
   int vec_w, vec_s, vec_x, pdl;
   int xpitch;
-  int off_sz, off_x, off_part;
+  int off_sz, off_x, off_xs, off_part;
 };
 
 __device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i, uint32_t magic) {
@@ -110,7 +110,8 @@ __device__ __forceinline__ void cp_async_wait_upto(int pending) {
 }  // namespace
 
 // Shared memory: weights [step][warp][lane] x 16 B | scales+zeros [segment][warp][r] x 16 B (s0..s3, z0..z3) |
-// activations [token][k/8] x 16 B (pre-permuted) | partial sums [token][128] fp32.  The K range of a CTA is
+// activations [token][k/8] x 16 B (pre-permuted) | segment sums of x [segment][8*MT] fp32 |
+// partial sums [token][128] fp32.  The K range of a CTA is
 // padded to whole stages with zero weights, zero activations and zero scales, which add nothing.
 template <int MT, bool F16, int SPS>
 __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
@@ -205,30 +206,57 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     pdl_wait();
   }
   {
+    // Stage x (permuted) and the per-segment sums X[seg][token] in shared memory.  A segment is C = 4*SPS
+    // consecutive chunks of 8 k held by C consecutive lanes, reduced with xor shuffles in a fixed order.
+    constexpr int C = 4 * SPS;
+    constexpr int XB = 4;  // chunks per thread in flight
     const int nch = nstages * SPST * 4;  // chunks of 8 k, padded
     const int nreal = a.KC / 8;
-    for (int t = 0; t < M; ++t) {
-      const uint16_t* xrow = a.x + int64_t(t) * a.sxm + int64_t(k0) * a.sxk;
-      for (int ch = tid; ch < nch; ch += blockDim.x) {
-        uint32_t u[4] = {0u, 0u, 0u, 0u};
-        if (ch < nreal) {
-          const uint16_t* p = xrow + int64_t(8 * ch) * a.sxk;
+    const int total = M * nch;
+    float* sXS = reinterpret_cast<float*>(smem + a.off_xs);
+    for (int base = 0; base < total; base += XB * 128) {
+      uint4 v[XB];
+#pragma unroll
+      for (int j = 0; j < XB; ++j) {
+        const int idx = base + j * 128 + tid;
+        const int t = idx / nch, ch = idx - t * nch;
+        v[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (idx < total && ch < nreal) {
+          const uint16_t* p = a.x + int64_t(t) * a.sxm + int64_t(k0 + 8 * ch) * a.sxk;
           if (a.vec_x) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
-            u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+            v[j] = __ldg(reinterpret_cast<const uint4*>(p));
           } else {
             uint16_t e[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) e[j] = __ldg(p + j * a.sxk);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) u[j] = uint32_t(e[2 * j]) | (uint32_t(e[2 * j + 1]) << 16);
+            for (int q = 0; q < 8; ++q) e[q] = __ldg(p + q * a.sxk);
+            v[j] = make_uint4(uint32_t(e[0]) | (uint32_t(e[1]) << 16), uint32_t(e[2]) | (uint32_t(e[3]) << 16),
+                              uint32_t(e[4]) | (uint32_t(e[5]) << 16), uint32_t(e[6]) | (uint32_t(e[7]) << 16));
           }
         }
-        // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
-                     "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
-                     "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
-                     : "memory");
+      }
+#pragma unroll
+      for (int j = 0; j < XB; ++j) {
+        const int idx = base + j * 128 + tid;
+        if (base + j * 128 >= total) break;  // uniform over the CTA
+        const int t = idx / nch, ch = idx - t * nch;
+        const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        float sum = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float lo = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] & 0xFFFFu))) : __uint_as_float(u[q] << 16);
+          const float hi = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] >> 16))) : __uint_as_float(u[q] & 0xFFFF0000u);
+          sum += lo + hi;
+        }
+#pragma unroll
+        for (int o = 1; o < C; o <<= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+        if (idx < total) {
+          // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
+                       "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
+                       "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
+                       : "memory");
+          if (ch % C == 0) sXS[(ch / C) * (8 * MT) + t] = sum;
+        }
       }
     }
   }
@@ -236,7 +264,6 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
 
   float acc[2][MT][4];
   float dacc[2][MT][4];
-  float xs[MT][4];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -246,10 +273,9 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
 
   const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
   const float bias = F16 ? 1024.0f : 128.0f;
-  const uint32_t ones = F16 ? 0x3C003C00u : 0x3F803F80u;
-  const uint32_t one4[4] = {ones, ones, ones, ones};
   uint32_t wl = s_w + (warp * 32 + lane) * 16;
   uint32_t szl = s_sz + (warp * 8 + r) * 16;
+  uint32_t xsl = s_w + a.off_xs + 2 * c * 4;  // X[seg][token 2c], X[seg][token 2c + 1]
   // Token rows past M read a real row instead: their outputs are discarded, and no branch is needed.
   uint32_t xl[MT];
 #pragma unroll
@@ -260,18 +286,6 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     __syncwarp();                           // and the scales / zeros copied by lanes c == 0
 #pragma unroll
     for (int i = 0; i < SPST; ++i) {
-      if (i % SPS == 0) {
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) dacc[t][mt][e] = 0.0f;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) xs[mt][e] = 0.0f;
-      }
       const uint4 w4 = lds128(wl + i * WSTEP);
       const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
       uint32_t af[2][2][4];  // [row tile][k16 half][reg]
@@ -289,11 +303,10 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
         const uint4 b = lds128(xl[mt] + i * 64);
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          mma_16816<F16>(dacc[t][mt], af[t][0], b.x, b.y);
+          if (i % SPS == 0) mma_16816_first<F16>(dacc[t][mt], af[t][0], b.x, b.y);
+          else mma_16816<F16>(dacc[t][mt], af[t][0], b.x, b.y);
           mma_16816<F16>(dacc[t][mt], af[t][1], b.z, b.w);
         }
-        mma_16816<F16>(xs[mt], one4, b.x, b.y);
-        mma_16816<F16>(xs[mt], one4, b.z, b.w);
       }
       if (i % SPS == SPS - 1) {  // segment complete: acc += s * (D - (bias + z) * X)
         const uint4 sz = lds128(szl + (i / SPS) * SZSEG);
@@ -308,7 +321,9 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
         zv[3] = bias + __half2float(__ushort_as_half(uint16_t(sz.w >> 16)));
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-          const float X0 = xs[mt][0], X1 = xs[mt][1];
+          float X0, X1;
+          asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(X0), "=f"(X1)
+                       : "r"(xsl + ((i / SPS) * (8 * MT) + mt * 8) * 4));
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             acc[t][mt][0] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X0, dacc[t][mt][0]), acc[t][mt][0]);
@@ -321,6 +336,7 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     }
     wl += SPST * WSTEP;
     szl += SEGST * SZSEG;
+    xsl += SEGST * (8 * MT) * 4;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) xl[mt] += SPST * 64;
   }
@@ -416,13 +432,13 @@ W4Plan plan_w4(int64_t M, int64_t N, int64_t K, int G, int num_sms) {
   const int64_t L = 32 * p.SPS;
   const int64_t units = K / L;
   // Split count S (a divisor of the units): within one cluster (S <= 8) the smallest S giving two CTAs
-  // per SM, else the largest S that keeps >= 128 k per CTA, else the smallest that fits; only
+  // per SM with at most kMaxKC / 2 k each (more CTAs resident per SM), else the largest S that keeps >= 128 k per CTA, else the smallest that fits; only
   // K > 8 * kMaxKC needs S > 8 (workspace partials).
   int64_t S = 0;
   const int64_t smax = std::min<int64_t>(8, units);
   auto fits = [&](int64_t s) { return units % s == 0 && K / s <= kMaxKC; };
   for (int64_t s = 1; s <= smax && !S; ++s)
-    if (fits(s) && p.ntiles * s >= 2 * num_sms) S = s;
+    if (fits(s) && K / s <= kMaxKC / 2 && p.ntiles * s >= 2 * num_sms) S = s;
   for (int64_t s = smax; s >= 1 && !S; --s)
     if (fits(s) && K / s >= 128) S = s;
   for (int64_t s = 1; s <= smax && !S; ++s)
@@ -530,6 +546,8 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   off += size_t(a.nstages) * (spst / p.SPS) * 4 * 8 * 16;
   a.off_x = int(off);
   off += size_t(M) * a.xpitch;
+  a.off_xs = int(off);
+  off += size_t(a.nstages) * (spst / p.SPS) * (8 * p.MT) * 4;
   a.off_part = int(off);
   off += size_t(M) * kBN * 4;
   const size_t smem = off;
