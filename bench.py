@@ -316,19 +316,211 @@ def cpu_block_sample(M: int, threads: int, steps: int = 1) -> tuple[float, str]:
     return dt, f"{steps} full block step(s) at M={M}: 7 dequantize-then-matmul linears, numpy fp32"
 
 
+# ----------------------------------------------------------------------------- model workload
+
+LLAMA_1B = dict(vocab_size=128256, hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
+                num_attention_heads=32, num_key_value_heads=8, head_dim=64, max_position_embeddings=131072,
+                rms_norm_eps=1e-5, tie_word_embeddings=True, rope_theta=500000.0,
+                rope_scaling={"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                              "original_max_position_embeddings": 8192})
+
+
+def build_llama(dev, seed: int = 0):
+    """Random-init Llama-3.2-1B-shaped model (transformers' init: N(0, 0.02) weights, RMSNorm weights 1), bf16."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(seed)
+    with torch.device(dev):
+        model = LlamaForCausalLM(LlamaConfig(**LLAMA_1B))
+    return model.to(torch.bfloat16).eval()
+
+
+def time_decode(m, B: int, prompt: int, steps: int, warmup: int, world: int, dev, vocab: int):
+    """Prefill ``prompt`` random tokens, then time ``steps`` greedy decode steps replayed from a CUDA graph."""
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, vocab, (B, prompt), generator=g).to(dev)
+    m.prefill(ids)  # untimed: module loading, workspaces, library heuristics
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    logits = m.prefill(ids)
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    tok = logits[:, -1].argmax(-1, keepdim=True)
+    first = tok.clone()
+    pos = torch.tensor([prompt], device=dev)
+
+    def step():
+        out = m.decode_step(tok, pos)
+        tok.copy_(out[:, -1].argmax(-1, keepdim=True))
+        pos.add_(1)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step()
+
+    def reset():
+        m.prefill(ids)
+        tok.copy_(first)
+        pos.fill_(prompt)
+        torch.cuda.synchronize()
+
+    reset()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dev_s = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+
+    # end to end: every step copies the input token in from pinned host memory and the next token back out
+    reset()
+    tok_in = torch.empty((B, 1), dtype=torch.long).pin_memory()
+    tok_in.copy_(first.cpu())
+    tok_out = torch.empty((B, 1), dtype=torch.long).pin_memory()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(steps):
+        tok.copy_(tok_in, non_blocking=True)
+        graph.replay()
+        tok_out.copy_(tok, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    e2e_s = max_over_ranks(max(wall, e0.elapsed_time(e1) * 1e-3), world)
+    del graph
+    return {"prefill_ms": prefill_ms, "decode_s": dev_s, "e2e_s": e2e_s, "h2d": B * 8, "d2h": B * 8}
+
+
+def run_model(args, world, rank, local):
+    from int4_b200.decode import LlamaTP
+
+    dev = torch.device("cuda", local)
+    B, prompt, steps = args.m, args.prompt, args.steps
+    hf = build_llama(dev)
+    res = {}
+    for label, w4 in (("w4", True), ("bf16", False)):
+        m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world,
+                    max_seq=prompt + steps + args.warmup + 8, max_batch=B, device=dev)
+        with ClockSampler(local) as clk:
+            r = time_decode(m, B, prompt, steps, args.warmup, world, dev, LLAMA_1B["vocab_size"])
+        r["clocks"] = clk.summary()
+        # bytes one decode step must read on this rank: projection weights + the KV cache up to the mean position
+        mean_pos = prompt + steps / 2
+        kv = 2 * len(m.layers) * m.nkv_l * m.hd * 2 * B * mean_pos
+        r["bytes_per_step_rank"] = m.weight_bytes() + kv
+        res[label] = r
+        del m
+        torch.cuda.empty_cache()
+    del hf
+    torch.cuda.empty_cache()
+    return res
+
+
+def cpu_model_sample(threads: int, B: int = 1, steps: int = 2) -> tuple[float, str]:
+    """The reference's model-level CPU path: fake-quant Llama-3.2-1B (bf16 dequantized W4 weights, G=128,
+    oracle quantizer) in transformers on the host cores; seconds per decode step after a 32-token prompt."""
+    import cases  # noqa: F401
+    from oracle import int4_oracle as orc
+
+    torch.set_num_threads(threads)
+    hf = build_llama("cpu")
+    with torch.no_grad():
+        for mod in hf.model.layers.modules():
+            if isinstance(mod, torch.nn.Linear):
+                w = mod.weight.data
+                qw, s, z = orc.quantize_int4(w.view(torch.int16).numpy().view(np.uint16), GROUP, "bfloat16")
+                mod.weight.data.copy_(torch.from_numpy(orc.dequantize_int4(qw, s, z, "bfloat16").view(np.int16))
+                                      .view(torch.bfloat16))
+        ids = torch.randint(0, LLAMA_1B["vocab_size"], (B, 32), generator=torch.Generator().manual_seed(7))
+        out = hf(ids, use_cache=True)
+        past = out.past_key_values
+        tok = out.logits[:, -1:].argmax(-1)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            out = hf(tok, past_key_values=past, use_cache=True)
+            past = out.past_key_values
+            tok = out.logits[:, -1:].argmax(-1)
+        dt = (time.perf_counter() - t0) / steps
+    return dt, f"{steps} greedy decode steps of the fake-quant (dequantized W4 G={GROUP}) model in transformers, " \
+               f"batch {B}, after a 32-token prompt, {threads} threads"
+
+
+MODEL_METRIC = "W4 decode tokens/s (Llama-3.2-1B shape)"
+
+
+def model_config(args) -> dict:
+    return {"workload": f"llama-3.2-1b random-init, W4 G={GROUP} decoder linears"
+                        f"{' + W4 lm_head' if args.lm_head_w4 else ', bf16 lm_head'}, batch {args.m}, "
+                        f"{args.prompt}-token prompt then greedy decode (CUDA graph per step)",
+            "model": "Llama-3.2-1B-shaped (random-init)", "group_size": GROUP, "global_batch": args.m,
+            "seq_len": args.prompt, "parallelism": f"tp{args.gpus}", "pdl": bool(args.pdl),
+            "l2": "inputs larger than L2: 0.65-1 GB of weights streamed per step"}
+
+
+def main_model(args, world, rank, local, threads):
+    res = run_model(args, world, rank, local)
+    if rank != 0:
+        return
+    pk = peaks()
+    w4, bf = res["w4"], res["bf16"]
+    tps = args.m * args.steps / w4["decode_s"]
+    step_s = w4["decode_s"] / args.steps
+    achieved = w4["bytes_per_step_rank"] / step_s / 1e9
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        dt, sample = cpu_model_sample(threads, args.m, 2)
+        cpu = {"value": args.m / dt, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+    line = {
+        "metric": MODEL_METRIC, "value": tps, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "w4a16-bf16", "data": "synthetic (random-init weights, random token ids)",
+        "config": model_config(args),
+        "bf16_tokens_per_s": args.m * args.steps / bf["decode_s"],
+        "w4_over_bf16": bf["decode_s"] / w4["decode_s"],
+        "prefill_ms": {"w4": w4["prefill_ms"], "bf16": bf["prefill_ms"]},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "whole decode step (projection weights + KV cache bytes / step time)",
+                     "peak_source": pk["source"]},
+        "cpu_baseline": cpu,
+        "e2e": {"value": args.m * args.steps / w4["e2e_s"], "unit": "tokens/s", "h2d_bytes_per_step": w4["h2d"],
+                "d2h_bytes_per_step": w4["d2h"]},
+        "clocks": w4["clocks"],
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 20000 block steps, 256 decode steps for the model workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block"], default="block")
+    ap.add_argument("--workload", choices=["block", "model"], default="block")
+    ap.add_argument("--prompt", type=int, default=512, help="model workload: prompt tokens before decoding")
+    ap.add_argument("--lm-head-w4", type=int, default=0, help="model workload: quantize the lm_head too")
     ap.add_argument("--m", type=int, default=1, help="tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pdl", type=int, default=1,
                     help="programmatic dependent launch for the small-M kernels (weights fetched before the wait)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.steps is None:
+        args.steps = 256 if args.workload == "model" else 20000
 
     config = {"workload": f"llama-3.2-1b decoder block, 7 linears, W4 G={GROUP}, M={args.m}",
               "model": "Llama-3.2-1B-shaped (random-init)", "group_size": GROUP, "tokens_per_step": args.m,
@@ -337,6 +529,22 @@ def main():
     metric = "per-block W4A16 GEMM us (Llama-3.2-1B decoder block, decode step)"
     threads = os.cpu_count() or 1
 
+    if args.impl == "reference" and args.workload == "model":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        ref_steps = min(args.steps, 2)
+        dt, sample = cpu_model_sample(threads, args.m, ref_steps)
+        v = args.m / dt
+        print(json.dumps({
+            "impl": "reference", "metric": MODEL_METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": ref_steps, "steps_requested": args.steps, "warmup": 0, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (fake-quant W4)",
+            "data": "synthetic", "config": model_config(args),
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
@@ -362,6 +570,13 @@ def main():
         _lib.set_pdl(True)
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    if args.workload == "model":
+        main_model(args, world, rank, local, threads)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     r = run_block(args, world, rank, local)
     pk = peaks()
     us = r["us_per_step"]

@@ -1,0 +1,237 @@
+"""Tensor-parallel Llama decoding on the W4A16 kernels: the model-level caller of the path.
+
+The reference measures its kernels inside a Hugging Face ``LlamaForCausalLM``
+whose ``nn.Linear`` layers ``quantize_model_linears`` swapped for
+``Int4Linear`` (``benchmarks/eval_llama.py:121-183``, ``int4_triton/qlinear.py:54-68``),
+one GPU.  ``LlamaTP`` runs the same network from the same HF weights, with
+the projections laid out for the kernels and for tensor parallelism:
+
+* q/k/v are one column-parallel projection per layer (this rank's heads of
+  q, k and v stacked along N), gate/up likewise; o_proj and down_proj are
+  row-parallel (this rank's slice of K) followed by a bf16 all-reduce;
+* the lm_head is vocab-parallel followed by an all-gather of the logits;
+* every INT4 weight is quantized per shard -- for column shards that is the
+  same bits as slicing the fully quantized tensor, and for row shards too as
+  long as the shard width is a multiple of the group size (checked);
+* norms, rotary embedding, attention over a static KV cache, SwiGLU and the
+  residual stream follow ``transformers``' Llama (RMSNorm in fp32, rotary
+  tables rounded to bf16, scaled-dot-product attention), so a one-rank
+  ``LlamaTP`` matches the HF model with the same weights.
+
+``w4=False`` keeps every projection in bf16 (``torch.nn.functional.linear``):
+the same model and decode loop, for the W4-versus-bf16 comparison.  All
+steps are free of host synchronisation and of shape changes, so a decode
+step can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .gemm import w4a16_matmul
+from .quantize import quantize_int4
+
+
+def column_shard(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rows [rank*N/world, (rank+1)*N/world) of W[N, K]: this rank's output features."""
+    n = w.shape[0]
+    assert n % world == 0, (n, world)
+    return w[rank * n // world:(rank + 1) * n // world]
+
+
+def row_shard(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Columns [rank*K/world, (rank+1)*K/world) of W[N, K]: this rank's input features."""
+    k = w.shape[1]
+    assert k % world == 0, (k, world)
+    return w[:, rank * k // world:(rank + 1) * k // world]
+
+
+def head_shard(w: torch.Tensor, heads: int, head_dim: int, rank: int, world: int) -> torch.Tensor:
+    """This rank's heads (rows) of a q/k/v projection W[heads*head_dim, K]."""
+    assert heads % world == 0, (heads, world)
+    h = heads // world
+    return w[rank * h * head_dim:(rank + 1) * h * head_dim]
+
+
+class Projection:
+    """One (possibly stacked) projection y = x @ W^T, INT4 (quantize_int4 layout) or bf16."""
+
+    def __init__(self, w: torch.Tensor, w4: bool, group_size: int):
+        w = w.detach().to(torch.bfloat16).contiguous()
+        self.out_features, self.in_features = w.shape
+        if w4:
+            assert self.in_features % group_size == 0, (self.in_features, group_size)
+            self.q = quantize_int4(w, group_size)
+            self.w = None
+        else:
+            self.q = None
+            self.w = w
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.q is not None:
+            return w4a16_matmul(x, *self.q)
+        return F.linear(x, self.w)
+
+    def weight_bytes(self) -> int:
+        if self.q is not None:
+            return sum(t.numel() * t.element_size() for t in self.q)
+        return self.w.numel() * self.w.element_size()
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """transformers' LlamaRMSNorm: statistics in fp32, result cast back, then scaled."""
+    h = x.float()
+    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+    return weight * h.to(x.dtype)
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    x1, x2 = x.chunk(2, dim=-1)
+    return torch.cat((-x2, x1), dim=-1)
+
+
+class LlamaTP:
+    """Llama decoder for one tensor-parallel rank, built from an HF ``LlamaForCausalLM``.
+
+    ``group`` is the ``torch.distributed`` process group of the ranks (None when
+    ``world == 1``).  ``max_seq`` and ``max_batch`` size the static KV cache.
+    """
+
+    def __init__(self, hf_model, *, w4: bool = True, group_size: int = 128, quantize_lm_head: bool = False,
+                 rank: int = 0, world: int = 1, group=None, max_seq: int = 2048, max_batch: int = 1,
+                 device: torch.device | None = None):
+        cfg = hf_model.config
+        self.cfg = cfg
+        self.rank, self.world, self.group = rank, world, group
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        dev = self.device
+        H = cfg.hidden_size
+        nh, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        hd = getattr(cfg, "head_dim", None) or H // nh
+        inter = cfg.intermediate_size
+        assert nh % world == 0 and nkv % world == 0 and inter % world == 0, "heads / MLP width must split over ranks"
+        if w4:
+            assert (nh // world * hd) % group_size == 0 and (inter // world) % group_size == 0, \
+                "row-parallel shards must hold whole quantization groups"
+        self.hd, self.nh_l, self.nkv_l = hd, nh // world, nkv // world
+        self.eps = cfg.rms_norm_eps
+        self.max_seq, self.max_batch = max_seq, max_batch
+        self.w4 = w4
+
+        def bf(t):
+            return t.detach().to(dev, torch.bfloat16)
+
+        self.embed = bf(hf_model.model.embed_tokens.weight)
+        self.layers = []
+        for layer in hf_model.model.layers:
+            at, mlp = layer.self_attn, layer.mlp
+            qkv = torch.cat([head_shard(bf(at.q_proj.weight), nh, hd, rank, world),
+                             head_shard(bf(at.k_proj.weight), nkv, hd, rank, world),
+                             head_shard(bf(at.v_proj.weight), nkv, hd, rank, world)], 0)
+            gu = torch.cat([column_shard(bf(mlp.gate_proj.weight), rank, world),
+                            column_shard(bf(mlp.up_proj.weight), rank, world)], 0)
+            self.layers.append({
+                "ln1": bf(layer.input_layernorm.weight),
+                "ln2": bf(layer.post_attention_layernorm.weight),
+                "qkv": Projection(qkv, w4, group_size),
+                "o": Projection(row_shard(bf(at.o_proj.weight), rank, world), w4, group_size),
+                "gu": Projection(gu, w4, group_size),
+                "down": Projection(row_shard(bf(mlp.down_proj.weight), rank, world), w4, group_size),
+            })
+            del qkv, gu
+        self.norm = bf(hf_model.model.norm.weight)
+        vocab = hf_model.lm_head.weight.shape[0]
+        assert vocab % world == 0, "vocab must split over ranks"
+        self.vocab = vocab
+        self.lm_head = Projection(column_shard(bf(hf_model.lm_head.weight), rank, world),
+                                  w4 and quantize_lm_head, group_size)
+
+        # rotary tables exactly as transformers computes them (fp32, then cast to the activation dtype)
+        rot = hf_model.model.rotary_emb
+        inv_freq = rot.inv_freq.detach().float().to(dev)
+        pos = torch.arange(max_seq, device=dev, dtype=torch.float32)
+        freqs = pos[:, None] * inv_freq[None, :]
+        emb = torch.cat((freqs, freqs), dim=-1)
+        scale = float(getattr(rot, "attention_scaling", 1.0))
+        self.cos = (emb.cos() * scale).to(torch.bfloat16)
+        self.sin = (emb.sin() * scale).to(torch.bfloat16)
+
+        n_layers = len(self.layers)
+        self.k_cache = torch.zeros(n_layers, max_batch, self.nkv_l, max_seq, hd, device=dev, dtype=torch.bfloat16)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.positions = torch.arange(max_seq, device=dev)
+
+    # ------------------------------------------------------------------ collectives
+
+    def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            torch.distributed.all_reduce(x, group=self.group)
+        return x
+
+    def _gather_vocab(self, logits: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return logits
+        parts = [torch.empty_like(logits) for _ in range(self.world)]
+        torch.distributed.all_gather(parts, logits.contiguous(), group=self.group)
+        return torch.cat(parts, dim=-1)
+
+    # ------------------------------------------------------------------ forward
+
+    def weight_bytes(self) -> int:
+        """Bytes of the projection weights this rank streams per decode step (embedding excluded)."""
+        b = sum(L[k].weight_bytes() for L in self.layers for k in ("qkv", "o", "gu", "down"))
+        return b + self.lm_head.weight_bytes()
+
+    def _layer(self, i: int, h: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, pos0, mask) -> torch.Tensor:
+        L = self.layers[i]
+        B, S, _ = h.shape
+        hd, nq, nkv = self.hd, self.nh_l, self.nkv_l
+        x = rms_norm(h, L["ln1"], self.eps)
+        qkv = L["qkv"](x)
+        q, k, v = qkv.split([nq * hd, nkv * hd, nkv * hd], dim=-1)
+        q = q.view(B, S, nq, hd).transpose(1, 2)
+        k = k.view(B, S, nkv, hd).transpose(1, 2)
+        v = v.view(B, S, nkv, hd).transpose(1, 2)
+        q = q * cos + _rotate_half(q) * sin
+        k = k * cos + _rotate_half(k) * sin
+        kc, vc = self.k_cache[i, :B], self.v_cache[i, :B]
+        if mask is None:  # prefill from position 0: attend causally within the prompt
+            kc[:, :, :S] = k
+            vc[:, :, :S] = v
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=hd ** -0.5, enable_gqa=True)
+        else:  # one token at device-side position pos0: write the cache, attend to positions <= pos0
+            kc.index_copy_(2, pos0, k)
+            vc.index_copy_(2, pos0, v)
+            a = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, scale=hd ** -0.5, enable_gqa=True)
+        a = a.transpose(1, 2).reshape(B, S, nq * hd)
+        h = h + self._all_reduce(L["o"](a))
+        x = rms_norm(h, L["ln2"], self.eps)
+        g, u = L["gu"](x).chunk(2, dim=-1)
+        h = h + self._all_reduce(L["down"](F.silu(g) * u))
+        return h
+
+    def _head(self, h: torch.Tensor) -> torch.Tensor:
+        return self._gather_vocab(self.lm_head(rms_norm(h, self.norm, self.eps)))
+
+    @torch.no_grad()
+    def prefill(self, ids: torch.Tensor, all_logits: bool = False) -> torch.Tensor:
+        """Run the prompt ids[B, S] from position 0 and fill the KV cache; logits of the last (or every) token."""
+        B, S = ids.shape
+        assert B <= self.max_batch and S <= self.max_seq
+        h = F.embedding(ids, self.embed)
+        cos, sin = self.cos[:S], self.sin[:S]
+        for i in range(len(self.layers)):
+            h = self._layer(i, h, cos, sin, None, None)
+        return self._head(h if all_logits else h[:, -1:])
+
+    @torch.no_grad()
+    def decode_step(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """One token per sequence: ids[B, 1] at position ``pos`` (a one-element device tensor); logits [B, 1, V]."""
+        B = ids.shape[0]
+        h = F.embedding(ids, self.embed)
+        cos = self.cos.index_select(0, pos)
+        sin = self.sin.index_select(0, pos)
+        mask = (self.positions <= pos)[None, None, None, :]
+        for i in range(len(self.layers)):
+            h = self._layer(i, h, cos, sin, pos, mask)
+        return self._head(h)
