@@ -348,13 +348,15 @@ def time_decode(m, B: int, prompt: int, steps: int, warmup: int, world: int, dev
     e1.record()
     torch.cuda.synchronize()
     prefill_ms = max_over_ranks(e0.elapsed_time(e1), world)
-    tok = logits[:, -1].argmax(-1, keepdim=True)
+    from int4_b200.decode import argmax_last
+
+    tok = argmax_last(logits[:, -1])
     first = tok.clone()
     pos = torch.tensor([prompt], device=dev)
 
     def step():
         out = m.decode_step(tok, pos)
-        tok.copy_(out[:, -1].argmax(-1, keepdim=True))
+        tok.copy_(argmax_last(out[:, -1]))
         pos.add_(1)
 
     side = torch.cuda.Stream(dev)

@@ -139,6 +139,35 @@ int i4b_w4a16_matmul_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, i
                              const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
                              void* stream);
 
+/* ---- Decode-step glue of a Llama layer (bf16, head_dim 64), for the model-level caller of the
+ * matmuls.  No counterpart in the reference, which runs these steps as transformers' torch ops
+ * (benchmarks/eval_llama.py:121-183); each reproduces transformers' bf16 rounding points.
+ * `pos` is a device int64 holding the decode position, so the calls can be captured in a CUDA graph. */
+
+/* h[rows, H] = bf16(h + delta) (delta may be NULL); out = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))).
+ * Rows contiguous, H % 8 == 0, 16-byte aligned (LlamaRMSNorm after the residual add). */
+int i4b_add_rmsnorm(void* h, const void* delta, const void* weight, void* out, int64_t rows, int64_t H, float eps,
+                    void* stream);
+
+/* Rotary embedding of one token per sequence.  qkv[B, (nq + 2 nkv) * 64] holds q, k, v heads in that order;
+ * cos/sin tables [max_seq, 64]; writes rotated q to q_out[B, nq, 64] and rotated k / raw v to
+ * k_cache / v_cache[B, nkv, max_seq, 64] at position *pos (apply_rotary_pos_emb + cache update). */
+int i4b_rope_kv_cache(const void* qkv, const void* cos_table, const void* sin_table, const int64_t* pos, void* q_out,
+                      void* k_cache, void* v_cache, int64_t B, int64_t nq, int64_t nkv, int64_t head_dim,
+                      int64_t max_seq, void* stream);
+
+/* out[B, nq * 64] = softmax(q . K^T * scale) . V over cache positions 0..*pos, query head h reading kv head
+ * h / (nq / nkv) (grouped-query attention); fp32 softmax.  max_seq <= 49152. */
+int i4b_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                         int64_t B, int64_t nq, int64_t nkv, int64_t head_dim, int64_t max_seq, float scale,
+                         void* stream);
+
+/* y[B, I] = bf16(bf16(silu(g)) * u) with gate_up[B, 2I] = (g | u); I % 8 == 0, 16-byte aligned. */
+int i4b_silu_mul(const void* gate_up, void* y, int64_t B, int64_t I, void* stream);
+
+/* out[r] = index of the first maximum of bf16 row x[r, 0..n) (greedy decoding, as torch.argmax). */
+int i4b_argmax_rows(const void* x, int64_t rows, int64_t n, int64_t* out, void* stream);
+
 /* Device-side error flags raised by kernels of this library on `device`
  * (a bounded wait that expired sets bit 0).  Synchronises that device;
  * clear != 0 resets the flags.  Returns -1 if the flags cannot be read. */

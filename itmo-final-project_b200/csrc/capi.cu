@@ -274,6 +274,78 @@ int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t st
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
+// ------------------------------------------------------------------ decode-step glue
+
+int i4b_add_rmsnorm(void* h, const void* delta, const void* weight, void* out, int64_t rows, int64_t H, float eps,
+                    void* stream) {
+  if (rows < 0 || H <= 0 || H % 8 != 0 || rows > INT32_MAX || H > INT32_MAX) return I4B_ERR_SHAPE;
+  if (rows == 0) return I4B_OK;
+  if (!h || !weight || !out) return I4B_ERR_INVALID_ARG;
+  if (!aligned16(h) || (delta && !aligned16(delta)) || !aligned16(weight) || !aligned16(out)) return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const cudaError_t e = launch_add_rmsnorm(static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
+                                           static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out),
+                                           int(rows), int(H), eps, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_rope_kv_cache(const void* qkv, const void* cos_table, const void* sin_table, const int64_t* pos, void* q_out,
+                      void* k_cache, void* v_cache, int64_t B, int64_t nq, int64_t nkv, int64_t head_dim,
+                      int64_t max_seq, void* stream) {
+  if (head_dim != 64) return I4B_ERR_SHAPE;
+  if (B < 0 || nq <= 0 || nkv <= 0 || max_seq <= 0 || B * (nq + 2 * nkv) > INT32_MAX || max_seq > INT32_MAX)
+    return I4B_ERR_SHAPE;
+  if (B == 0) return I4B_OK;
+  if (!qkv || !cos_table || !sin_table || !pos || !q_out || !k_cache || !v_cache) return I4B_ERR_INVALID_ARG;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const cudaError_t e = launch_rope_kv(
+      static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(cos_table),
+      static_cast<const uint16_t*>(sin_table), pos, static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),
+      static_cast<uint16_t*>(v_cache), int(B), int(nq), int(nkv), int(max_seq), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                         int64_t B, int64_t nq, int64_t nkv, int64_t head_dim, int64_t max_seq, float scale,
+                         void* stream) {
+  if (head_dim != 64 || B < 0 || nq <= 0 || nkv <= 0 || nq % nkv != 0 || max_seq <= 0) return I4B_ERR_SHAPE;
+  if (max_seq > 48 * 1024 || B > 65535 || nq > INT32_MAX) return I4B_ERR_SHAPE;  // scores live in shared memory
+  if (B == 0) return I4B_OK;
+  if (!q || !k_cache || !v_cache || !pos || !out) return I4B_ERR_INVALID_ARG;
+  if (!aligned16(k_cache) || !aligned16(v_cache)) return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const cudaError_t e = launch_decode_attn(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
+                                           static_cast<const uint16_t*>(v_cache), pos, static_cast<uint16_t*>(out),
+                                           int(B), int(nq), int(nkv), int(max_seq), scale,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_silu_mul(const void* gate_up, void* y, int64_t B, int64_t I, void* stream) {
+  if (B < 0 || I <= 0 || I % 8 != 0 || B * I > INT32_MAX) return I4B_ERR_SHAPE;
+  if (B == 0) return I4B_OK;
+  if (!gate_up || !y) return I4B_ERR_INVALID_ARG;
+  if (!aligned16(gate_up) || !aligned16(y)) return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const cudaError_t e = launch_silu_mul(static_cast<const uint16_t*>(gate_up), static_cast<uint16_t*>(y), int(B),
+                                        int(I), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_argmax_rows(const void* x, int64_t rows, int64_t n, int64_t* out, void* stream) {
+  if (rows < 0 || n <= 0 || rows > INT32_MAX) return I4B_ERR_SHAPE;
+  if (rows == 0) return I4B_OK;
+  if (!x || !out) return I4B_ERR_INVALID_ARG;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const cudaError_t e = launch_argmax(static_cast<const uint16_t*>(x), rows, n, out, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
 int i4b_device_error_flags(int device, int clear) {
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess) return -1;

@@ -68,4 +68,15 @@ cudaError_t launch_repack(const void* in, int esize, int64_t rows, int64_t cols_
                           int64_t cols_out, cudaStream_t stream);
 unsigned int read_tc_error(bool clear);
 
+// decode_ops.cu (decode-step glue of a Llama layer)
+cudaError_t launch_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, uint16_t* out, int rows, int H,
+                               float eps, cudaStream_t s);
+cudaError_t launch_rope_kv(const uint16_t* qkv, const uint16_t* cosT, const uint16_t* sinT, const int64_t* pos,
+                           uint16_t* q_out, uint16_t* kc, uint16_t* vc, int B, int nq, int nkv, int max_seq,
+                           cudaStream_t s);
+cudaError_t launch_decode_attn(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
+                               uint16_t* out, int B, int nq, int nkv, int max_seq, float scale, cudaStream_t s);
+cudaError_t launch_silu_mul(const uint16_t* gu, uint16_t* y, int B, int I, cudaStream_t s);
+cudaError_t launch_argmax(const uint16_t* x, int64_t rows, int64_t n, int64_t* out, cudaStream_t s);
+
 }  // namespace i4b

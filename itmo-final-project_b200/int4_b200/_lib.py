@@ -34,6 +34,13 @@ _SIGNATURES = {
     "i4b_w16a16_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "i4b_w16a16_matmul": (_c_int, [_c_vp, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64,
                                    _c_vp, _c_i64, _c_vp, _c_size, _c_vp]),
+    "i4b_add_rmsnorm": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_float, _c_vp]),
+    "i4b_rope_kv_cache": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64,
+                                   _c_i64, _c_vp]),
+    "i4b_decode_attention": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                      ctypes.c_float, _c_vp]),
+    "i4b_silu_mul": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
+    "i4b_argmax_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp]),
     "i4b_set_pdl": (None, [_c_int]),
     "i4b_set_skinny_override": (None, [_c_int, _c_int, _c_int]),
     "i4b_device_error_flags": (_c_int, [_c_int, _c_int]),

@@ -28,6 +28,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
+from . import _lib
 from .gemm import w4a16_matmul
 from .quantize import quantize_int4
 
@@ -85,6 +86,55 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return weight * h.to(x.dtype)
 
 
+# ---------------------------------------------------------------------- fused decode-step kernels (C ABI)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return _lib.stream_handle(t.device)
+
+
+def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, out: torch.Tensor,
+                eps: float) -> None:
+    """h = bf16(h + delta) in place (delta may be None); out = rms_norm(h, weight, eps).  h, out: [rows, H]."""
+    rows, H = h.shape
+    st = _lib.lib().i4b_add_rmsnorm(h.data_ptr(), None if delta is None else delta.data_ptr(), weight.data_ptr(),
+                                    out.data_ptr(), rows, H, eps, _stream(h))
+    _lib.check(st, "add_rmsnorm")
+
+
+def rope_kv_cache(qkv, cos, sin, pos, q_out, k_cache, v_cache, nq: int, nkv: int) -> None:
+    """Rotary embedding of q and k of one token per sequence; k and v written to the caches at ``pos``."""
+    B = qkv.shape[0]
+    st = _lib.lib().i4b_rope_kv_cache(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), q_out.data_ptr(),
+                                      k_cache.data_ptr(), v_cache.data_ptr(), B, nq, nkv, 64, k_cache.shape[2],
+                                      _stream(qkv))
+    _lib.check(st, "rope_kv_cache")
+
+
+def decode_attention(q, k_cache, v_cache, pos, out, nq: int, nkv: int, scale: float) -> None:
+    """out[B, nq*64] = grouped-query attention of q[B, nq, 64] over cache positions 0..pos."""
+    B = q.shape[0]
+    st = _lib.lib().i4b_decode_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), pos.data_ptr(),
+                                         out.data_ptr(), B, nq, nkv, 64, k_cache.shape[2], scale, _stream(q))
+    _lib.check(st, "decode_attention")
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor) -> None:
+    """out[B, I] = bf16(bf16(silu(g)) * u) for gate_up[B, 2I] = (g | u)."""
+    B, I2 = gate_up.shape
+    st = _lib.lib().i4b_silu_mul(gate_up.data_ptr(), out.data_ptr(), B, I2 // 2, _stream(gate_up))
+    _lib.check(st, "silu_mul")
+
+
+def argmax_last(x: torch.Tensor) -> torch.Tensor:
+    """Index of the first maximum along the last dim of a bf16 tensor (torch.argmax(-1, keepdim=True))."""
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    out = torch.empty(x2.shape[0], dtype=torch.long, device=x.device)
+    st = _lib.lib().i4b_argmax_rows(x2.data_ptr(), x2.shape[0], x2.shape[1], out.data_ptr(), _stream(x2))
+    _lib.check(st, "argmax_rows")
+    return out.view(*x.shape[:-1], 1)
+
+
 def _rotate_half(x: torch.Tensor) -> torch.Tensor:
     x1, x2 = x.chunk(2, dim=-1)
     return torch.cat((-x2, x1), dim=-1)
@@ -95,12 +145,16 @@ class LlamaTP:
 
     ``group`` is the ``torch.distributed`` process group of the ranks (None when
     ``world == 1``).  ``max_seq`` and ``max_batch`` size the static KV cache.
+    ``fused`` runs a decode step's norms, rotary embedding, attention and SwiGLU
+    as the library's fused kernels (9 launches per layer); ``fused=False`` runs
+    them as the torch ops transformers uses.
     """
 
     def __init__(self, hf_model, *, w4: bool = True, group_size: int = 128, quantize_lm_head: bool = False,
                  rank: int = 0, world: int = 1, group=None, max_seq: int = 2048, max_batch: int = 1,
-                 device: torch.device | None = None):
+                 device: torch.device | None = None, fused: bool = True):
         cfg = hf_model.config
+        self.fused = fused
         self.cfg = cfg
         self.rank, self.world, self.group = rank, world, group
         self.device = device or torch.device("cuda", torch.cuda.current_device())
@@ -114,6 +168,9 @@ class LlamaTP:
             assert (nh // world * hd) % group_size == 0 and (inter // world) % group_size == 0, \
                 "row-parallel shards must hold whole quantization groups"
         self.hd, self.nh_l, self.nkv_l = hd, nh // world, nkv // world
+        self.hidden, self.inter_l = H, inter // world
+        if fused:
+            assert hd == 64, "the fused decode kernels are written for head_dim 64"
         self.eps = cfg.rms_norm_eps
         self.max_seq, self.max_batch = max_seq, max_batch
         self.w4 = w4
@@ -226,7 +283,9 @@ class LlamaTP:
 
     @torch.no_grad()
     def decode_step(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
-        """One token per sequence: ids[B, 1] at position ``pos`` (a one-element device tensor); logits [B, 1, V]."""
+        """One token per sequence: ids[B, 1] at position ``pos`` (a one-element int64 device tensor); logits [B, 1, V]."""
+        if self.fused:
+            return self._decode_step_fused(ids, pos)
         B = ids.shape[0]
         h = F.embedding(ids, self.embed)
         cos = self.cos.index_select(0, pos)
@@ -235,3 +294,24 @@ class LlamaTP:
         for i in range(len(self.layers)):
             h = self._layer(i, h, cos, sin, pos, mask)
         return self._head(h)
+
+    def _decode_step_fused(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        B = ids.shape[0]
+        nq, nkv, hd = self.nh_l, self.nkv_l, self.hd
+        h = F.embedding(ids.view(B), self.embed)  # [B, H], the residual stream
+        x = torch.empty_like(h)
+        q = torch.empty(B, nq, hd, device=h.device, dtype=torch.bfloat16)
+        att = torch.empty(B, nq * hd, device=h.device, dtype=torch.bfloat16)
+        act = torch.empty(B, self.inter_l, device=h.device, dtype=torch.bfloat16)
+        delta = None
+        for i, L in enumerate(self.layers):
+            add_rmsnorm(h, delta, L["ln1"], x, self.eps)
+            qkv = L["qkv"](x)
+            kc, vc = self.k_cache[i, :B], self.v_cache[i, :B]
+            rope_kv_cache(qkv, self.cos, self.sin, pos, q, kc, vc, nq, nkv)
+            decode_attention(q, kc, vc, pos, att, nq, nkv, hd ** -0.5)
+            add_rmsnorm(h, self._all_reduce(L["o"](att)), L["ln2"], x, self.eps)
+            silu_mul(L["gu"](x), act)
+            delta = self._all_reduce(L["down"](act))
+        add_rmsnorm(h, delta, self.norm, x, self.eps)
+        return self._gather_vocab(self.lm_head(x)).view(B, 1, -1)

@@ -150,3 +150,22 @@ def test_two_rank_tensor_parallel_matches_one_rank():
            "--master-addr=127.0.0.1", f"--master-port={port}", os.path.join(HERE, "tp_decode_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+@torch.no_grad()
+def test_fused_decode_kernels_match_the_torch_ops(models):
+    """The 9-launch fused decode step against the same step run as transformers' torch ops."""
+    from int4_b200.decode import LlamaTP
+
+    hf, _ = models
+    fused = LlamaTP(hf, w4=True, max_seq=128, max_batch=2, fused=True)
+    plain = LlamaTP(hf, w4=True, max_seq=128, max_batch=2, fused=False)
+    ids = _ids(2, 20, 9)
+    tok = fused.prefill(ids)[:, -1].argmax(-1, keepdim=True)
+    plain.prefill(ids)
+    for step in range(5):
+        pos = torch.tensor([20 + step], device="cuda")
+        a, b = fused.decode_step(tok, pos), plain.decode_step(tok, pos)
+        err = (a.float() - b.float()).abs().max().item()
+        assert err <= LOGIT_TOL, (step, err)
+        tok = b[:, -1].argmax(-1, keepdim=True)
