@@ -76,8 +76,9 @@ size_t tc_w16_workspace(int64_t M, int64_t N, int64_t K) {
   return b;
 }
 
-// Up to this M the register-dequant kernel runs (the reference switches paths at
-// SMALL_M = 64, gemm.py:17; here tokens 17..64 already fill tcgen05 tiles well).
+// Up to these M the register-dequant kernels run (the reference switches paths at
+// SMALL_M = 64, gemm.py:17; measured on B200 the tcgen05 GEMM wins from 33 tokens on):
+// INT4 kW4MaxM = 32, W16 kSkinnyMaxM = 16.
 constexpr int64_t kSmallM = kSkinnyMaxM;
 
 }  // namespace
@@ -146,7 +147,7 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
   if (M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || group_size % 32 != 0 || K % group_size != 0) return 0;
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
-  if (M <= kSmallM) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
+  if (M <= kW4MaxM) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
   return tc_w4_workspace(M, N, K, group_size);
 }
 
@@ -168,7 +169,7 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool f16 = x_dtype == I4B_F16;
 
-  if (M <= kSmallM) {
+  if (M <= kW4MaxM) {
     const W4Plan p = plan_w4(M, N, K, G, d.sms);
     if (p.mode == 3) return I4B_ERR_SHAPE;
     if (w4_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;

@@ -1,30 +1,29 @@
-// Large-M (M > 64) W4A16 / W16A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Large-M (M > 16) W4A16 / W16A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
 // Replaces the reference's large-M Triton path _matmul_kernel (int4_triton/gemm.py:74-157,
 // launched at gemm.py:270-296).  y[M, N] = x[M, K] @ W_hat[N, K]^T.
 //
-// One CTA computes a 128 x BN output tile (BN = 128 or 256) with 6 warps:
-//   warp 0      TMA producer: per 64-wide k-block loads the activation tile
-//               (128 x 64 bf16, 128-byte swizzle), and either the packed
-//               weight tile (8 k8-rows x BN int32) plus two rows of scales and
-//               zeros (INT4), or the bf16 weight tile BN x 64 (W16);
-//   warp 1      allocates BN TMEM columns and, from one thread, issues four
-//               tcgen05.mma.kind::f16 (K = 16 each) per k-block into the fp32
-//               TMEM accumulator, then tcgen05.commit to free the stage;
-//   warps 2..5  INT4 only: dequantize the packed tile into the K-major,
-//               128-byte-swizzled B operand in shared memory,
-//                 W_hat = bf16_rn((q - z) * s)   (exactly the reference's
-//                 dequantize-then-round, int4_triton/gemm.py:137-140),
-//               using bf16x2 arithmetic: (128+q) - (128+z) is exact, the fp16
-//               scale is split into s_hi (top 8 significant bits, a bf16) and
-//               s_lo (the remaining 3 bits, also an exact bf16), q*s_lo is
-//               exact and fma(qz, s_hi, qz*s_lo) rounds once;
-//               then all four read the accumulator back with tcgen05.ld and
-//               store bf16 / fp16 rows of y.
-// Stages are handed over with mbarriers (TMA transaction bytes, dequant
-// arrivals, tcgen05.commit).  Every wait is bounded; on expiry the kernel
-// records I4B_DEVERR_WAIT_TIMEOUT, drains its own TMA copies, frees TMEM and
-// returns.
+// One CTA computes a 256 x 128 output tile as two 128 x 128 tcgen05 MMAs per k16 step that share
+// one B (weight) tile, so every dequantized weight feeds 256 rows (a 128 x 128 tile with one MMA when
+// 256-row tiles would leave most SMs idle).  18 warps:
+//   warp 0      TMA producer: per 64-wide k-block the activation tile (256 x 64 bf16, 128-byte
+//               swizzle) and either the packed weight tile (8 k8-rows x 128 int32) plus two rows
+//               of scales and zeros (INT4), or the bf16 weight tile 128 x 64 (W16);
+//   warp 1      allocates 256 TMEM columns (two fp32 accumulators) and, from one thread, issues
+//               eight tcgen05.mma.kind::f16 (two row halves x four K = 16 steps) per k-block,
+//               then tcgen05.commit to free the stage;
+//   warps 2..17 INT4 only: dequantize the packed tile into the K-major, 128-byte-swizzled B
+//               operand in shared memory (thread = one weight row x two packed words),
+//                 W_hat = bf16_rn((q - z) * s)   (exactly the reference's dequantize-then-round,
+//                 int4_triton/gemm.py:137-140),
+//               using bf16x2 arithmetic: (128+q) - (128+z) is exact, the fp16 scale is split
+//               into s_hi (top 8 significant bits, a bf16) and s_lo (the remaining 3 bits, also
+//               an exact bf16), q*s_lo is exact and fma(qz, s_hi, qz*s_lo) rounds once;
+//               then all sixteen read the accumulators back with tcgen05.ld and store bf16 /
+//               fp16 rows of y.
+// Stages are handed over with mbarriers (TMA transaction bytes, dequant arrivals,
+// tcgen05.commit).  Every wait is bounded; on expiry the kernel records
+// I4B_DEVERR_WAIT_TIMEOUT, drains its own TMA copies, frees TMEM and returns.
 #include <algorithm>
 
 #include "common.cuh"
@@ -34,18 +33,21 @@ namespace i4b {
 
 static __device__ unsigned int g_tc_err = 0;
 
-template <bool INT4, int BN>
+template <bool INT4, int BN, int BMT>
 struct TcCfg {
-  static constexpr int BM = 128, BK = 64;
-  static constexpr int A_BYTES = BM * BK * 2;              // 16 KB
-  static constexpr int B_BYTES = BN * BK * 2;              // BN rows of 128 B
-  static constexpr int P_BYTES = INT4 ? 8 * BN * 4 : 0;    // packed words of one k-block
+  static constexpr int BM = 128 * BMT, BK = 64;  // BMT row halves of 128 share each B tile
+  static constexpr int DQ_WARPS = 16;
+  static constexpr int THREADS = 64 + 32 * DQ_WARPS;
+  static constexpr int A_BYTES = BM * BK * 2;                 // 32 KB
+  static constexpr int B_BYTES = BN * BK * 2;                 // BN rows of 128 B
+  static constexpr int P_BYTES = INT4 ? 8 * BN * 4 : 0;       // packed words of one k-block
   static constexpr int SZ_BYTES = INT4 ? 2 * 2 * BN * 2 : 0;  // scales + zeros, two group rows
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES + SZ_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (216 * 1024) / STAGE_BYTES > 8 ? 8 : (216 * 1024) / STAGE_BYTES;
   static constexpr int TX_BYTES = INT4 ? (A_BYTES + P_BYTES + SZ_BYTES) : (A_BYTES + B_BYTES);
   static constexpr int BAR_BYTES = (3 * STAGES + 1) * 8 + 8;
   static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + BAR_BYTES;
+  static constexpr int TMEM_COLS = BMT * BN;
 };
 
 struct DqParams {
@@ -99,12 +101,12 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, const DqParams& p) {
                     __byte_perm(r[0], r[1], 0x7632), __byte_perm(r[2], r[3], 0x7632));
 }
 
-template <bool INT4, bool F16, int BN>
-__global__ void __launch_bounds__(192, 1)
+template <bool INT4, bool F16, int BN, int BMT>
+__global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z, int M, int N,
                    int K, int G, uint16_t* __restrict__ y, int64_t sym) {
-  using C = TcCfg<INT4, BN>;
+  using C = TcCfg<INT4, BN, BMT>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bready[s], 4);
+      mbar_init(&bready[s], C::DQ_WARPS);
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -152,11 +154,34 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
+      for (int kp = S; kp < 2 * S && kp < KB; ++kp) {  // the first S k-blocks are loaded right away
+        tma_prefetch_l2_2d(&tm_x, kp * C::BK, m0);
+        if constexpr (INT4) {
+          tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
+          tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
+          tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
+        } else {
+          tma_prefetch_l2_2d(&tm_w, kp * C::BK, n0);
+        }
+      }
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % S, u = kb / S;
         if (kb >= S && !mbar_wait(&empty[s], (u - 1) & 1)) { ok = false; break; }
         mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
         tma_load_2d(sA + s * C::A_BYTES, &tm_x, &full[s], kb * C::BK, m0);
+        // Pull the tiles of k-block kb + 2S into L2 now, so that their TMA loads, issued S k-blocks
+        // from now, do not wait for HBM.
+        const int kp = kb + 2 * S;
+        if (kp < KB) {
+          tma_prefetch_l2_2d(&tm_x, kp * C::BK, m0);
+          if constexpr (INT4) {
+            tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
+            tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
+            tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
+          } else {
+            tma_prefetch_l2_2d(&tm_w, kp * C::BK, n0);
+          }
+        }
         if constexpr (INT4) {
           const int g_lo = (kb * C::BK) / G;
           tma_load_2d(sP + s * C::P_BYTES, &tm_w, &full[s], n0, kb * 8);
@@ -182,53 +207,83 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
         if (INT4 && !mbar_wait(&bready[s], u & 1)) { ok = false; break; }
         tc_fence_after();
-        const uint64_t adesc = umma_desc_sw128(smem_u32(sA + s * C::A_BYTES));
+        const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA + s * C::A_BYTES));
+        const uint64_t adesc1 = umma_desc_sw128(smem_u32(sA + s * C::A_BYTES + C::A_BYTES / 2));
         const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * C::B_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < C::BK / 16; ++kk)
-          umma_f16_ss(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+        for (int kk = 0; kk < C::BK / 16; ++kk) {
+          const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+          umma_f16_ss(tmem, adesc0 + 2 * kk, bdesc + 2 * kk, idesc, acc);
+          if constexpr (BMT == 2) umma_f16_ss(tmem + uint32_t(BN), adesc1 + 2 * kk, bdesc + 2 * kk, idesc, acc);
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(tfull);  // also on the error path: completes once issued MMAs are done
     }
   } else {
     if constexpr (INT4) {
-      const int dt = threadIdx.x - 64;  // 0..127
+      // thread dt: weight row nl = dt % BN, packed words WPT*h .. WPT*h + WPT - 1 of the k-block (h = dt / BN)
+      constexpr int WPT = 8 * BN / (32 * C::DQ_WARPS);
+      const int dt = threadIdx.x - 64;
+      const int nl = dt % BN, h = dt / BN;
+      // Group bookkeeping without divisions: k-block kb covers k in [64 kb, 64 kb + 64); g_lo is the group
+      // of its first k and g_end the first k of the next group.  The scale / zero parameters of a group
+      // are computed once and kept while the group lasts (G >= 32, so a k-block touches at most 2 groups).
+      int g_lo = 0, g_end = G;
+      int g_cached = -1;
+      DqParams pc{};
       for (int kb = 0; kb < KB && ok; ++kb) {
         const int s = kb % S, u = kb / S;
-        if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
+        const int k_begin = kb * C::BK;
+        while (k_begin >= g_end) {
+          ++g_lo;
+          g_end += G;
+        }
+        if (!mbar_wait_sleep(&full[s], u & 1)) { ok = false; break; }
         const uint32_t* P = reinterpret_cast<const uint32_t*>(sP + s * C::P_BYTES);
         const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ + s * C::SZ_BYTES);
         const uint16_t* Zs = Ss + 2 * BN;
-        const int g_lo = (kb * C::BK) / G;
         uint8_t* Bs = sB + s * C::B_BYTES;
+        if (g_cached != g_lo) {
+          pc = dq_params<F16>(Ss[nl], Zs[nl]);
+          g_cached = g_lo;
+        }
+        const DqParams p0 = pc;
+        const int jsplit = (g_end - k_begin) >> 3;  // words of this k-block inside group g_lo (>= 1)
+        DqParams p1 = p0;
+        if (jsplit < 8) {
+          p1 = dq_params<F16>(Ss[BN + nl], Zs[BN + nl]);
+          pc = p1;
+          g_cached = g_lo + 1;
+        }
 #pragma unroll
-        for (int rr = 0; rr < BN / 128; ++rr) {
-          const int nl = dt + 128 * rr;
-          const DqParams p0 = dq_params<F16>(Ss[nl], Zs[nl]);
-          const DqParams p1 = dq_params<F16>(Ss[BN + nl], Zs[BN + nl]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int sel = (kb * C::BK + 8 * j) / G - g_lo;
-            const uint4 v = dequant_word<F16>(P[j * BN + nl], sel ? p1 : p0);
-            *reinterpret_cast<uint4*>(Bs + nl * 128 + ((j ^ (nl & 7)) << 4)) = v;
-          }
+        for (int jj = 0; jj < WPT; ++jj) {
+          const int j = WPT * h + jj;
+          const uint4 v = dequant_word<F16>(P[j * BN + nl], j >= jsplit ? p1 : p0);
+          *reinterpret_cast<uint4*>(Bs + nl * 128 + ((j ^ (nl & 7)) << 4)) = v;
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bready[s]);
       }
     }
-    // ---- epilogue: TMEM -> registers -> y
-    if (!mbar_wait(tfull, 0)) ok = false;
+    // ---- epilogue: TMEM -> registers -> y.  The dequant warps form DQ_WARPS / 4 sets of four (one per
+    // TMEM lane quarter); with two row halves set j reads accumulator j % 2, and the sets split the
+    // columns of their accumulator evenly.
+    if (!mbar_wait_sleep(tfull, 0)) ok = false;
     tc_fence_after();
-    const int q = warp & 3;
-    const int m = m0 + 32 * q + lane;
+    constexpr int SETS = C::DQ_WARPS / 4;
+    constexpr int CSPLIT = BMT == 2 ? SETS / 2 : SETS;  // column slices per accumulator
+    const int q = warp & 3, set = (warp - 2) >> 2;
+    const int half = BMT == 2 ? (set & 1) : 0, cs = BMT == 2 ? (set >> 1) : set;
+    const int m = m0 + 128 * half + 32 * q + lane;
+    const int cbeg = cs * (BN / CSPLIT), cend = cbeg + BN / CSPLIT;
+    const uint32_t acc_col = uint32_t(half * BN);
     const bool vec = (sym % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
+    for (int c0 = cbeg; c0 < cend; c0 += 16) {
       uint32_t v[16];
-      tmem_ld_32x32b_x16(tmem + (uint32_t(32 * q) << 16) + uint32_t(c0), v);
+      tmem_ld_32x32b_x16(tmem + (uint32_t(32 * q) << 16) + acc_col + uint32_t(c0), v);
       tmem_ld_wait();
       if (m < M) {
         uint32_t pk[8];
@@ -236,11 +291,11 @@ __global__ void __launch_bounds__(192, 1)
         for (int i = 0; i < 8; ++i) {
           const float a = __uint_as_float(v[2 * i]), b = __uint_as_float(v[2 * i + 1]);
           if constexpr (F16) {
-            const __half2 h = __floats2half2_rn(a, b);
-            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+            const __half2 hh = __floats2half2_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&hh);
           } else {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+            const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&hh);
           }
         }
         const int n = n0 + c0;
@@ -261,7 +316,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
@@ -325,13 +380,13 @@ static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
 
 
 
-template <bool INT4, bool F16, int BN>
+template <bool INT4, bool F16, int BN, int BMT>
 static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                                   int64_t sym, cudaStream_t stream) {
-  using C = TcCfg<INT4, BN>;
+  using C = TcCfg<INT4, BN, BMT>;
   const CUtensorMapDataType act = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap mx{}, mw{}, ms{}, mz{};
-  bool ok = make_map(&mx, act, o.x, uint64_t(K), uint64_t(M), uint64_t(o.sxm) * 2, 64, 128,
+  bool ok = make_map(&mx, act, o.x, uint64_t(K), uint64_t(M), uint64_t(o.sxm) * 2, 64, C::BM,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if constexpr (INT4) {
     ok = ok && make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, o.w, uint64_t(N), uint64_t(K / 8), uint64_t(o.sw) * 4, BN,
@@ -347,31 +402,30 @@ static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int
     mz = mw;
   }
   if (!ok) return cudaErrorInvalidValue;
-  auto kern = tc_gemm_kernel<INT4, F16, BN>;
+  auto kern = tc_gemm_kernel<INT4, F16, BN, BMT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM));
   if (e != cudaSuccess) return e;
-  dim3 grid(unsigned(cdiv(N, BN)), unsigned(cdiv(M, 128)));
-  kern<<<grid, 192, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym);
+  dim3 grid(unsigned(cdiv(N, BN)), unsigned(cdiv(M, C::BM)));
+  kern<<<grid, C::THREADS, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym);
   return cudaGetLastError();
 }
 
-int tc_pick_bn(int64_t M, int64_t N, int num_sms) {
-  // 256-wide tiles halve the activation re-reads but only pay off with enough tiles.
-  const int64_t tiles256 = cdiv(M, 128) * cdiv(N, 256);
-  return tiles256 >= num_sms ? 256 : 128;
-}
+// Rows per CTA: 256 (two accumulators share each dequantized weight tile) when that still fills half a
+// wave of the GPU, else 128 (twice the CTAs).
+int tc_pick_bn(int64_t M, int64_t N, int num_sms) { return 2 * cdiv(M, 256) * cdiv(N, 128) >= num_sms ? 2 : 1; }
 
 cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                       int64_t sym, int bn, cudaStream_t stream) {
-#define I4B_TC(I, F, B) return launch_tc_impl<I, F, B>(o, M, N, K, G, y, sym, stream)
+  // bn: row halves per CTA from tc_pick_bn (1 -> 128 x 128 tiles, 2 -> 256 x 128 tiles)
+#define I4B_TC(I, F) \
+  return bn == 2 ? launch_tc_impl<I, F, 128, 2>(o, M, N, K, G, y, sym, stream) \
+                 : launch_tc_impl<I, F, 128, 1>(o, M, N, K, G, y, sym, stream)
   if (int4) {
-    if (f16) { if (bn == 256) I4B_TC(true, true, 256); I4B_TC(true, true, 128); }
-    if (bn == 256) I4B_TC(true, false, 256);
-    I4B_TC(true, false, 128);
+    if (f16) I4B_TC(true, true);
+    I4B_TC(true, false);
   }
-  if (f16) { if (bn == 256) I4B_TC(false, true, 256); I4B_TC(false, true, 128); }
-  if (bn == 256) I4B_TC(false, false, 256);
-  I4B_TC(false, false, 128);
+  if (f16) I4B_TC(false, true);
+  I4B_TC(false, false);
 #undef I4B_TC
 }
 

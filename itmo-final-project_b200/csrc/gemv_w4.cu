@@ -1,4 +1,4 @@
-// Small-M (M <= 16) W4A16 kernel: the M == 1 decode GEMV and the small-batch split-K path.
+// Small-M (M <= 32) W4A16 kernel: the M == 1 decode GEMV and the small-batch split-K path.
 //
 // Replaces the reference's _gemv_kernel (int4_triton/gemm.py:185-220) and its
 // small-M split-K pair _matmul_kernel + _reduce_split_k (gemm.py:74-182,
@@ -42,7 +42,7 @@ namespace i4b {
 namespace {
 
 constexpr int kBN = 128;      // output columns per CTA (4 warps x 32)
-constexpr int kMaxKC = 1024;  // k per CTA
+constexpr int kMaxKCAll = 1024;  // k per CTA, at most
 constexpr int kStageSteps = 4;
 
 struct W4SArgs {
@@ -400,8 +400,17 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     const int tok = idx / kBN;
     const int64_t n = n0 + idx % kBN;
     if (n >= a.N) continue;
-    float v = __ldcg(a.partials + int64_t(tok) * a.N + n);
-    for (int s = 1; s < a.S; ++s) v += __ldcg(a.partials + (int64_t(s) * M + tok) * a.N + n);
+    const float* src = a.partials + int64_t(tok) * a.N + n;
+    const int64_t sstride = int64_t(M) * a.N;
+    float v = 0.0f;
+    for (int s0 = 0; s0 < a.S; s0 += 8) {  // eight partials in flight, added in split order
+      float t[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = s0 + j < a.S ? __ldcg(src + (s0 + j) * sstride) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < a.S) v = (s0 + j == 0) ? t[j] : v + t[j];
+    }
     y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
   }
   if (tid == 0) atomicExch(a.tickets + blockIdx.x, 0u);
@@ -426,14 +435,16 @@ static int gcd_i(int a, int b) {
 // a CTA owns KC = K / S consecutive k, a whole number of units, at most kMaxKC.
 W4Plan plan_w4(int64_t M, int64_t N, int64_t K, int G, int num_sms) {
   W4Plan p{};
-  p.MT = M <= 8 ? 1 : 2;
+  p.MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
   p.SPS = gcd_i(G / 32, 8);
   p.ntiles = cdiv(N, kBN);
   const int64_t L = 32 * p.SPS;
   const int64_t units = K / L;
+  // k per CTA is capped so that the staged activations (M rows) leave room for several CTAs per SM
+  const int64_t kMaxKC = p.MT <= 2 ? int64_t(1024) : int64_t(512);
   // Split count S (a divisor of the units): within one cluster (S <= 8) the smallest S giving two CTAs
-  // per SM with at most kMaxKC / 2 k each (more CTAs resident per SM), else the largest S that keeps >= 128 k per CTA, else the smallest that fits; only
-  // K > 8 * kMaxKC needs S > 8 (workspace partials).
+  // per SM with at most kMaxKC / 2 k each (more CTAs resident per SM), else the largest S that keeps
+  // >= 128 k per CTA, else the smallest that fits; only K > 8 * kMaxKC needs S > 8 (workspace partials).
   int64_t S = 0;
   const int64_t smax = std::min<int64_t>(8, units);
   auto fits = [&](int64_t s) { return units % s == 0 && K / s <= kMaxKC; };
@@ -551,8 +562,11 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   a.off_part = int(off);
   off += size_t(M) * kBN * 4;
   const size_t smem = off;
-  if (p.MT == 1) return f16 ? launch_w4_sps<1, true>(a, p, smem, stream) : launch_w4_sps<1, false>(a, p, smem, stream);
-  return f16 ? launch_w4_sps<2, true>(a, p, smem, stream) : launch_w4_sps<2, false>(a, p, smem, stream);
+  switch (p.MT) {
+    case 1: return f16 ? launch_w4_sps<1, true>(a, p, smem, stream) : launch_w4_sps<1, false>(a, p, smem, stream);
+    case 2: return f16 ? launch_w4_sps<2, true>(a, p, smem, stream) : launch_w4_sps<2, false>(a, p, smem, stream);
+    default: return f16 ? launch_w4_sps<4, true>(a, p, smem, stream) : launch_w4_sps<4, false>(a, p, smem, stream);
+  }
 }
 
 }  // namespace i4b

@@ -37,7 +37,8 @@ cudaError_t launch_skinny(bool int4, bool f16, const void* x, int64_t M, int64_t
 // Tuning override of the automatic decomposition (0 = automatic).
 void set_skinny_override(int wn, int wk, int splits);
 
-// gemv_w4.cu (INT4, M <= kSkinnyMaxM)
+// gemv_w4.cu (INT4, M <= kW4MaxM: 8, 16 or 32 tokens per CTA)
+constexpr int64_t kW4MaxM = 32;
 struct W4Plan {
   int MT, SPS, S, KC;
   int mode;  // 0: one CTA per column tile; 1: cluster along K; 2: workspace split-K; 3: unsupported
