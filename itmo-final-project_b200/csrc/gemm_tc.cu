@@ -109,7 +109,9 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
   using C = TcCfg<INT4, BN, BMT>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment for the 128-byte swizzle atoms, by offsetting the shared array itself (a round trip
+  // through an integer would turn every shared access below into a generic one).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = sA + S * C::A_BYTES;
   uint8_t* sP = sB + S * C::B_BYTES;
