@@ -157,7 +157,8 @@ int i4b_rope_kv_cache(const void* qkv, const void* cos_table, const void* sin_ta
                       int64_t max_seq, void* stream);
 
 /* out[B, nq * 64] = softmax(q . K^T * scale) . V over cache positions 0..*pos, query head h reading kv head
- * h / (nq / nkv) (grouped-query attention); fp32 softmax.  max_seq <= 49152. */
+ * h / (nq / nkv) (grouped-query attention); fp32 softmax.  max_seq <= 49152.  The positions of a head
+ * are split over a cluster of up to 8 CTAs whose partial softmax sums combine in a fixed order. */
 int i4b_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
                          int64_t B, int64_t nq, int64_t nkv, int64_t head_dim, int64_t max_seq, float scale,
                          void* stream);

@@ -312,7 +312,7 @@ int i4b_decode_attention(const void* q, const void* k_cache, const void* v_cache
                          int64_t B, int64_t nq, int64_t nkv, int64_t head_dim, int64_t max_seq, float scale,
                          void* stream) {
   if (head_dim != 64 || B < 0 || nq <= 0 || nkv <= 0 || nq % nkv != 0 || max_seq <= 0) return I4B_ERR_SHAPE;
-  if (max_seq > 48 * 1024 || B > 65535 || nq > INT32_MAX) return I4B_ERR_SHAPE;  // scores live in shared memory
+  if (max_seq > 8 * 6144 || B > 65535 || nq * 8 > INT32_MAX) return I4B_ERR_SHAPE;  // scores live in shared memory
   if (B == 0) return I4B_OK;
   if (!q || !k_cache || !v_cache || !pos || !out) return I4B_ERR_INVALID_ARG;
   if (!aligned16(k_cache) || !aligned16(v_cache)) return I4B_ERR_LAYOUT;

@@ -131,66 +131,85 @@ __global__ void __launch_bounds__(128) rope_kv_kernel(const uint16_t* __restrict
   dst[lane + 32] = y1;
 }
 
-// One CTA per (query head, token): scores over cache positions 0..pos in shared memory, fp32 softmax,
-// then the probability-weighted sum of V: thread t owns dims 8*(t%8)..+7 of positions t/8, t/8 + 32, ...
-// (16-byte loads, four positions in flight), and the 32 position phases are added in a fixed order.
-__global__ void __launch_bounds__(256) decode_attn_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
-                                                          const uint16_t* __restrict__ vc, const int64_t* __restrict__ pos,
-                                                          uint16_t* __restrict__ out, int nq, int nkv, int max_seq,
-                                                          float scale) {
+// Split-sequence decode attention: the cached positions 0..pos of one (query head, token) are cut into NS
+// consecutive chunks, one per CTA of a (NS, 1, 1) cluster.  Each CTA computes its chunk's scores
+// (four threads per position, 16 dims each), its local max m_r, sum l_r = sum exp(s - m_r) and the
+// unnormalised o_r = sum exp(s - m_r) v; rank 0 then combines the NS partials in rank order through
+// distributed shared memory:  out = sum_r o_r e^(m_r - m) / sum_r l_r e^(m_r - m),  m = max_r m_r.
+constexpr int kAttnThreads = 128;
+constexpr int kAttnMaxChunk = 6144;  // positions per CTA held as scores in shared memory
+
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const uint16_t* __restrict__ q,
+                                                                   const uint16_t* __restrict__ kc,
+                                                                   const uint16_t* __restrict__ vc,
+                                                                   const int64_t* __restrict__ pos,
+                                                                   uint16_t* __restrict__ out, int nq, int nkv,
+                                                                   int max_seq, float scale) {
   constexpr int HD = 64;
-  extern __shared__ float sc[];  // [max_seq] scores, then [32][64] partial sums
+  extern __shared__ float sc[];  // [chunk] scores, then [16][64] partial sums of V
   __shared__ float red[32];
   __shared__ float qs[HD];
-  const int head = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  __shared__ float part_o[HD];   // this CTA's unnormalised output, read by rank 0
+  __shared__ float part_ml[2];   // this CTA's (m_r, l_r)
+  const int NS = int(gridDim.x) / nq;
+  const int rank = int(cluster_ctarank());
+  const int head = int(blockIdx.x) / NS, b = blockIdx.y, tid = threadIdx.x;
   const int kvh = head / (nq / nkv);
   const int64_t p = *pos;
   const int L = p < 0 ? 0 : (p >= max_seq ? max_seq : int(p) + 1);  // never reads past the cache
+  const int chunk = (L + NS - 1) / NS;
+  const int i0 = rank * chunk, i1 = min(L, i0 + chunk);
+  const int n = i1 > i0 ? i1 - i0 : 0;
   if (tid < HD) qs[tid] = bf(q[(int64_t(b) * nq + head) * HD + tid]);
   __syncthreads();
-  const uint16_t* K = kc + (int64_t(b) * nkv + kvh) * max_seq * HD;
-  const uint16_t* V = vc + (int64_t(b) * nkv + kvh) * max_seq * HD;
+  const uint16_t* K = kc + ((int64_t(b) * nkv + kvh) * max_seq + i0) * HD;
+  const uint16_t* V = vc + ((int64_t(b) * nkv + kvh) * max_seq + i0) * HD;
+
+  // scores: thread (position i = t / 4, quarter qd = t % 4) dots 16 dims; quarters meet by shuffle
   float mx = -INFINITY;
-  for (int i = tid; i < L; i += blockDim.x) {
-    const uint4* kr = reinterpret_cast<const uint4*>(K + int64_t(i) * HD);
-    uint4 kv[HD / 8];
-#pragma unroll
-    for (int j = 0; j < HD / 8; ++j) kv[j] = __ldg(kr + j);
+  const int qd = tid & 3;
+  for (int i = tid >> 2; i < ((n + 31) & ~31); i += kAttnThreads / 4) {  // whole warps stay in the loop
     float d = 0.0f;
+    if (i < n) {
+      const uint4* kr = reinterpret_cast<const uint4*>(K + int64_t(i) * HD + 16 * qd);
+      const uint4 k0 = __ldg(kr), k1 = __ldg(kr + 1);
+      const uint32_t u[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
-      const uint32_t u[4] = {kv[j].x, kv[j].y, kv[j].z, kv[j].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        d = fmaf(qs[8 * j + 2 * e], bf(uint16_t(u[e])), d);
-        d = fmaf(qs[8 * j + 2 * e + 1], bf(uint16_t(u[e] >> 16)), d);
+      for (int e = 0; e < 8; ++e) {
+        d = fmaf(qs[16 * qd + 2 * e], bf(uint16_t(u[e])), d);
+        d = fmaf(qs[16 * qd + 2 * e + 1], bf(uint16_t(u[e] >> 16)), d);
       }
     }
-    d *= scale;
-    sc[i] = d;
-    mx = fmaxf(mx, d);
+    d += __shfl_xor_sync(0xFFFFFFFFu, d, 1);
+    d += __shfl_xor_sync(0xFFFFFFFFu, d, 2);
+    if (i < n && qd == 0) {
+      d *= scale;
+      sc[i] = d;
+      mx = fmaxf(mx, d);
+    }
   }
   mx = block_max(mx, red);
   float sum = 0.0f;
-  for (int i = tid; i < L; i += blockDim.x) {
+  for (int i = tid; i < n; i += kAttnThreads) {
     const float e = expf(sc[i] - mx);
     sc[i] = e;
     sum += e;
   }
   sum = block_sum(sum, red);  // (synchronises: all probabilities written)
-  const int dg = tid & 7, ph = tid >> 3;  // 8 dim groups x 32 position phases
+  // o_r: thread t owns dims 8*(t%8)..+7 of positions t/8, t/8 + 16, ... (16 position phases)
+  const int dg = tid & 7, ph = tid >> 3;
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
   const uint16_t* vp = V + 8 * dg;
   int i = ph;
-  for (; i + 96 < L; i += 128) {  // four positions in flight
+  for (; i + 48 < n; i += 64) {  // four positions in flight
     uint4 v4[4];
     float pr[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      v4[u] = __ldg(reinterpret_cast<const uint4*>(vp + int64_t(i + 32 * u) * HD));
-      pr[u] = sc[i + 32 * u];
+      v4[u] = __ldg(reinterpret_cast<const uint4*>(vp + int64_t(i + 16 * u) * HD));
+      pr[u] = sc[i + 16 * u];
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -202,7 +221,7 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const uint16_t* __rest
       }
     }
   }
-  for (; i < L; i += 32) {
+  for (; i < n; i += 16) {
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(vp + int64_t(i) * HD));
     const float pr = sc[i];
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -212,15 +231,34 @@ __global__ void __launch_bounds__(256) decode_attn_kernel(const uint16_t* __rest
       acc[2 * e + 1] = fmaf(pr, bf(uint16_t(w[e] >> 16)), acc[2 * e + 1]);
     }
   }
-  float* part = sc + max_seq;
+  float* part = sc + kAttnMaxChunk;
 #pragma unroll
   for (int e = 0; e < 8; ++e) part[ph * HD + 8 * dg + e] = acc[e];
   __syncthreads();
   if (tid < HD) {
     float v = 0.0f;
-    for (int k = 0; k < 32; ++k) v += part[k * HD + tid];
-    out[(int64_t(b) * nq + head) * HD + tid] = L > 0 ? to_bf(v / sum) : uint16_t(0);
+    for (int k = 0; k < 16; ++k) v += part[k * HD + tid];
+    part_o[tid] = v;
   }
+  if (tid == 0) {
+    part_ml[0] = n > 0 ? mx : -INFINITY;
+    part_ml[1] = n > 0 ? sum : 0.0f;
+  }
+  cluster_sync();
+  if (rank == 0 && tid < HD) {
+    float m = -INFINITY;
+    for (int r = 0; r < NS; ++r) m = fmaxf(m, ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[0]), uint32_t(r))));
+    float num = 0.0f, den = 0.0f;
+    for (int r = 0; r < NS; ++r) {
+      const float mr = ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[0]), uint32_t(r)));
+      const float lr = ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[1]), uint32_t(r)));
+      const float w = lr > 0.0f ? expf(mr - m) : 0.0f;
+      num = fmaf(ld_shared_cluster_f32(mapa_shared(smem_u32(&part_o[tid]), uint32_t(r))), w, num);
+      den = fmaf(lr, w, den);
+    }
+    out[(int64_t(b) * nq + head) * HD + tid] = L > 0 ? to_bf(num / den) : uint16_t(0);
+  }
+  cluster_sync();  // no CTA leaves while rank 0 may still read its shared memory
 }
 
 // Row-wise argmax of bf16 values (first index of the maximum, as torch.argmax): one CTA per row.
@@ -315,16 +353,30 @@ cudaError_t launch_rope_kv(const uint16_t* qkv, const uint16_t* cosT, const uint
 
 cudaError_t launch_decode_attn(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos,
                                uint16_t* out, int B, int nq, int nkv, int max_seq, float scale, cudaStream_t s) {
-  const size_t smem = (size_t(max_seq) + 32 * 64) * sizeof(float);
-  static size_t configured = 48 * 1024;
-  if (smem > configured) {
+  // sequence splits: one CTA per 64 cache positions, at most a portable cluster of 8
+  int ns = (max_seq + 63) / 64;
+  ns = ns < 1 ? 1 : (ns > 8 ? 8 : ns);
+  const size_t smem = (size_t(kAttnMaxChunk) + 16 * 64) * sizeof(float);
+  static bool configured = false;
+  if (!configured) {
     const cudaError_t e =
         cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    configured = smem;
+    configured = true;
   }
-  decode_attn_kernel<<<dim3(nq, B), 256, smem, s>>>(q, kc, vc, pos, out, nq, nkv, max_seq, scale);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(nq * ns), unsigned(B));
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(ns);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_attn_kernel, q, kc, vc, pos, out, nq, nkv, max_seq, scale);
 }
 
 cudaError_t launch_argmax(const uint16_t* x, int64_t rows, int64_t n, int64_t* out, cudaStream_t s) {
