@@ -93,6 +93,22 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
                      const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* i4b_w4a16_matmul for 1 <= M <= 32 bf16 tokens whose activations are produced inside the kernel from
+ * the previous step's tensors, saving the separate launch transformers' Llama runs for them:
+ *   I4B_PROLOGUE_RMSNORM: x = bf16(w * bf16(h' * rsqrt(mean(h'^2) + eps))), h' = bf16(src + delta)
+ *       (delta may be NULL).  When resid_out is not NULL, h' is also written there (rows of stride_src);
+ *       resid_out must not overlap src or delta.  norm_weight: bf16 [K].  (input / post-attention
+ *       LlamaRMSNorm after the residual add)
+ *   I4B_PROLOGUE_SWIGLU: x = bf16(bf16(silu(g)) * u), g = src[m, 0:K], u = src[m, K:2K]  (LlamaMLP)
+ * src rows are contiguous with stride_src % 8 == 0; all pointers 16-byte aligned.  Workspace as for
+ * i4b_w4a16_matmul (i4b_w4a16_workspace_size).  No counterpart in the reference. */
+enum { I4B_PROLOGUE_RMSNORM = 1, I4B_PROLOGUE_SWIGLU = 2 };
+int i4b_w4a16_matmul_prologue(int prologue, const void* src, const void* delta, const void* norm_weight, float eps,
+                              void* resid_out, int64_t M, int64_t K, int64_t stride_src, const int32_t* qweight,
+                              int64_t N, int64_t stride_qk, const uint16_t* scales, const uint16_t* zeros,
+                              int64_t stride_sg, int group_size, void* y, int64_t stride_ym, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* Workspace bytes for i4b_w16a16_matmul (same zero-fill rule as above). */
 size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K);
 

@@ -214,6 +214,36 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
+int i4b_w4a16_matmul_prologue(int prologue, const void* src, const void* delta, const void* norm_weight, float eps,
+                              void* resid_out, int64_t M, int64_t K, int64_t stride_src, const int32_t* qweight,
+                              int64_t N, int64_t stride_qk, const uint16_t* scales, const uint16_t* zeros,
+                              int64_t stride_sg, int group_size, void* y, int64_t stride_ym, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (prologue != I4B_PROLOGUE_RMSNORM && prologue != I4B_PROLOGUE_SWIGLU) return I4B_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return I4B_ERR_INVALID_ARG;
+  if (M > kW4MaxM || K % 8 != 0) return I4B_ERR_SHAPE;
+  const int G = group_size;
+  if (G <= 0 || G % 32 != 0 || K % G != 0) return I4B_ERR_GROUP;
+  if (M == 0 || N == 0) return I4B_OK;
+  if (!src || !qweight || !scales || !zeros || !y) return I4B_ERR_INVALID_ARG;
+  if (prologue == I4B_PROLOGUE_RMSNORM && !norm_weight) return I4B_ERR_INVALID_ARG;
+  if (N > INT32_MAX || K > INT32_MAX) return I4B_ERR_SHAPE;
+  if (stride_qk < N || stride_sg < N || stride_ym < N) return I4B_ERR_LAYOUT;
+  const int64_t row = prologue == I4B_PROLOGUE_SWIGLU ? 2 * K : K;
+  if (stride_src < row || stride_src % 8 != 0 || !aligned16(src) || (delta && !aligned16(delta)) ||
+      (norm_weight && !aligned16(norm_weight)) || (resid_out && !aligned16(resid_out)))
+    return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const W4Plan p = plan_w4(M, N, K, G, d.sms);
+  if (p.mode == 3) return I4B_ERR_SHAPE;
+  if (w4_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;
+  const W4Prologue pro{prologue, delta, norm_weight, resid_out, eps};
+  cudaError_t e = launch_w4(false, src, M, K, stride_src, 1, qweight, N, stride_qk, scales, zeros, stride_sg, G, y,
+                            stride_ym, workspace, p, g_pdl, static_cast<cudaStream_t>(stream), &pro);
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
 size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   DevInfo d;

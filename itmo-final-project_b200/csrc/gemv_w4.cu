@@ -65,7 +65,18 @@ struct W4SArgs {
   int vec_w, vec_s, vec_x, pdl;
   int xpitch;
   int off_sz, off_x, off_xs, off_part;
+  int pro;
+  // activation prologue (bf16 only): 1 = x := rmsnorm(x + delta) * norm_w, 2 = x := silu(g) * u with g | u = x
+  const uint16_t* delta;
+  const uint16_t* norm_w;
+  uint16_t* resid_out;
+  float eps;
 };
+
+enum { kProPlain = 0, kProRmsNorm = 1, kProSwiGlu = 2 };
+
+__device__ __forceinline__ float bfv(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+__device__ __forceinline__ uint32_t bfr(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
 
 __device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i, uint32_t magic) {
   return and_or(w >> (4 * i), 0x000F000Fu, magic);
@@ -113,7 +124,7 @@ __device__ __forceinline__ void cp_async_wait_upto(int pending) {
 // activations [token][k/8] x 16 B (pre-permuted) | segment sums of x [segment][8*MT] fp32 |
 // partial sums [token][128] fp32.  The K range of a CTA is
 // padded to whole stages with zero weights, zero activations and zero scales, which add nothing.
-template <int MT, bool F16, int SPS>
+template <int MT, bool F16, int SPS, int PRO>
 __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
   constexpr int SPST = SPS > 4 ? SPS : 4;  // 32-k steps per stage (one cp.async group); whole segments
   constexpr int SEGST = SPST / SPS;        // segments per stage
@@ -214,6 +225,43 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     const int nreal = a.KC / 8;
     const int total = M * nch;
     float* sXS = reinterpret_cast<float*>(smem + a.off_xs);
+    __shared__ float s_inv[32];
+    if constexpr (PRO == kProRmsNorm) {
+      // Full-row statistics of h' = bf16(h + delta) for every token (warp t % 4 owns token t); CTA (0, 0)
+      // also writes h' to resid_out.  Rows are contiguous with K % 8 == 0 and 16-byte alignment.
+      const bool writer = a.resid_out && blockIdx.x == 0 && blockIdx.y == 0;
+      for (int t = warp; t < M; t += 4) {
+        const uint16_t* hr = a.x + int64_t(t) * a.sxm;
+        const uint16_t* dr = a.delta ? a.delta + int64_t(t) * a.sxm : nullptr;
+        float ss = 0.0f;
+        for (int c = lane * 8; c < a.K; c += 256) {
+          uint4 hv = __ldg(reinterpret_cast<const uint4*>(hr + c));
+          if (dr) {
+            const uint4 dv = __ldg(reinterpret_cast<const uint4*>(dr + c));
+            const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
+            const uint32_t* da = reinterpret_cast<const uint32_t*>(&dv);
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              o[i] = bfr(bfv(ha[i] & 0xFFFFu) + bfv(da[i] & 0xFFFFu)) |
+                     (bfr(bfv(ha[i] >> 16) + bfv(da[i] >> 16)) << 16);
+            hv = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+          if (writer) *reinterpret_cast<uint4*>(a.resid_out + int64_t(t) * a.sxm + c) = hv;
+          const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float lo = bfv(ha[i] & 0xFFFFu), hi = bfv(ha[i] >> 16);
+            ss = fmaf(lo, lo, ss);
+            ss = fmaf(hi, hi, ss);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        if (lane == 0) s_inv[t] = rsqrtf(ss / float(a.K) + a.eps);
+      }
+      __syncthreads();
+    }
     for (int base = 0; base < total; base += XB * 128) {
       uint4 v[XB];
 #pragma unroll
@@ -223,7 +271,43 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
         v[j] = make_uint4(0u, 0u, 0u, 0u);
         if (idx < total && ch < nreal) {
           const uint16_t* p = a.x + int64_t(t) * a.sxm + int64_t(k0 + 8 * ch) * a.sxk;
-          if (a.vec_x) {
+          if constexpr (PRO == kProRmsNorm) {
+            // x = bf16(w * bf16(h' * inv)),  h' = bf16(h + delta)        (LlamaRMSNorm after the residual add)
+            const uint4 hv = __ldg(reinterpret_cast<const uint4*>(p));
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0 + 8 * ch));
+            uint4 dv = make_uint4(0u, 0u, 0u, 0u);
+            if (a.delta) dv = __ldg(reinterpret_cast<const uint4*>(a.delta + int64_t(t) * a.sxm + k0 + 8 * ch));
+            const float inv = s_inv[t];
+            const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
+            const uint32_t* da = reinterpret_cast<const uint32_t*>(&dv);
+            const uint32_t* wa = reinterpret_cast<const uint32_t*>(&wv);
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t lo = ha[i] & 0xFFFFu, hi = ha[i] >> 16;
+              if (a.delta) {
+                lo = bfr(bfv(lo) + bfv(da[i] & 0xFFFFu));
+                hi = bfr(bfv(hi) + bfv(da[i] >> 16));
+              }
+              o[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(lo) * inv))) |
+                     (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(hi) * inv))) << 16);
+            }
+            v[j] = make_uint4(o[0], o[1], o[2], o[3]);
+          } else if constexpr (PRO == kProSwiGlu) {
+            // x = bf16(bf16(silu(g)) * u),  g = row[k], u = row[K + k]                       (LlamaMLP)
+            const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p));
+            const uint4 uv = __ldg(reinterpret_cast<const uint4*>(p + a.K));
+            const uint32_t* ga = reinterpret_cast<const uint32_t*>(&gv);
+            const uint32_t* ua = reinterpret_cast<const uint32_t*>(&uv);
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float g0 = bfv(ga[i] & 0xFFFFu), g1 = bfv(ga[i] >> 16);
+              const float s0 = bfv(bfr(g0 / (1.0f + expf(-g0)))), s1 = bfv(bfr(g1 / (1.0f + expf(-g1))));
+              o[i] = bfr(s0 * bfv(ua[i] & 0xFFFFu)) | (bfr(s1 * bfv(ua[i] >> 16)) << 16);
+            }
+            v[j] = make_uint4(o[0], o[1], o[2], o[3]);
+          } else if (a.vec_x) {
             v[j] = __ldg(reinterpret_cast<const uint4*>(p));
           } else {
             uint16_t e[8];
@@ -467,9 +551,9 @@ W4Plan plan_w4(int64_t M, int64_t N, int64_t K, int G, int num_sms) {
 
 size_t w4_workspace_bytes(const W4Plan& p) { return p.mode == 2 ? kTicketBytes + p.partial_bytes : 0; }
 
-template <int MT, bool F16, int SPS>
+template <int MT, bool F16, int SPS, int PRO>
 static cudaError_t launch_w4_impl(const W4SArgs& a, const W4Plan& p, size_t smem, cudaStream_t stream) {
-  auto kern = w4_skinny_kernel<MT, F16, SPS>;
+  auto kern = w4_skinny_kernel<MT, F16, SPS, PRO>;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(std::max<size_t>(smem, 48 * 1024)));
@@ -502,21 +586,37 @@ static cudaError_t launch_w4_impl(const W4SArgs& a, const W4Plan& p, size_t smem
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+template <int MT, bool F16, int PRO>
+static cudaError_t launch_w4_pro(const W4SArgs& a, const W4Plan& p, size_t smem, cudaStream_t stream) {
+  switch (p.SPS) {
+    case 1: return launch_w4_impl<MT, F16, 1, PRO>(a, p, smem, stream);
+    case 2: return launch_w4_impl<MT, F16, 2, PRO>(a, p, smem, stream);
+    case 4: return launch_w4_impl<MT, F16, 4, PRO>(a, p, smem, stream);
+    default: return launch_w4_impl<MT, F16, 8, PRO>(a, p, smem, stream);
+  }
+}
+
 template <int MT, bool F16>
 static cudaError_t launch_w4_sps(const W4SArgs& a, const W4Plan& p, size_t smem, cudaStream_t stream) {
-  switch (p.SPS) {
-    case 1: return launch_w4_impl<MT, F16, 1>(a, p, smem, stream);
-    case 2: return launch_w4_impl<MT, F16, 2>(a, p, smem, stream);
-    case 4: return launch_w4_impl<MT, F16, 4>(a, p, smem, stream);
-    default: return launch_w4_impl<MT, F16, 8>(a, p, smem, stream);
+  if constexpr (!F16) {
+    if (a.pro == kProRmsNorm) return launch_w4_pro<MT, false, kProRmsNorm>(a, p, smem, stream);
+    if (a.pro == kProSwiGlu) return launch_w4_pro<MT, false, kProSwiGlu>(a, p, smem, stream);
   }
+  return launch_w4_pro<MT, F16, kProPlain>(a, p, smem, stream);
 }
 
 cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
                       int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
-                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream) {
+                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream, const W4Prologue* pro) {
   if (p.mode == 3) return cudaErrorInvalidConfiguration;
   W4SArgs a{};
+  if (pro) {
+    a.pro = pro->kind;
+    a.delta = static_cast<const uint16_t*>(pro->delta);
+    a.norm_w = static_cast<const uint16_t*>(pro->norm_weight);
+    a.resid_out = static_cast<uint16_t*>(pro->resid_out);
+    a.eps = pro->eps;
+  }
   a.x = static_cast<const uint16_t*>(x);
   a.sxm = sxm;
   a.sxk = sxk;

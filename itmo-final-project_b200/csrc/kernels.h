@@ -47,9 +47,19 @@ struct W4Plan {
 };
 W4Plan plan_w4(int64_t M, int64_t N, int64_t K, int G, int num_sms);
 size_t w4_workspace_bytes(const W4Plan& p);
+// Optional activation prologue of the small-M kernel (bf16): kind 1 = rmsnorm(x + delta) * norm_weight
+// (resid_out, when set, receives x + delta), kind 2 = silu(g) * u with g | u = the two halves of an x row.
+struct W4Prologue {
+  int kind;
+  const void* delta;
+  const void* norm_weight;
+  void* resid_out;
+  float eps;
+};
 cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
                       int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
-                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream);
+                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream,
+                      const W4Prologue* pro = nullptr);
 void set_w4_split_override(int splits);
 
 // gemm_tc.cu (M > 64)

@@ -126,6 +126,34 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor) -> None:
     _lib.check(st, "silu_mul")
 
 
+PROLOGUE_RMSNORM, PROLOGUE_SWIGLU = 1, 2
+
+
+def w4a16_matmul_prologue(kind: int, src: torch.Tensor, qweight, scales, zeros, *, delta=None, norm_weight=None,
+                          eps: float = 1e-5, resid_out=None) -> torch.Tensor:
+    """W4A16 matmul of M <= 32 bf16 rows whose activations the kernel derives from ``src``.
+
+    kind PROLOGUE_RMSNORM: x = rms_norm(src + delta, norm_weight, eps); ``resid_out`` receives src + delta.
+    kind PROLOGUE_SWIGLU:  x = silu(g) * u for src = (g | u).
+    """
+    M = src.shape[0]
+    K = qweight.shape[0] * 8
+    N = qweight.shape[1]
+    G = K // scales.shape[0]
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=src.device)
+    L = _lib.lib()
+    stream = _stream(src)
+    need = L.i4b_w4a16_workspace_size(M, N, K, G)
+    ws_ptr, ws_size = _lib.workspace(src.device, stream, need)
+    st = L.i4b_w4a16_matmul_prologue(kind, src.data_ptr(), None if delta is None else delta.data_ptr(),
+                                     None if norm_weight is None else norm_weight.data_ptr(), eps,
+                                     None if resid_out is None else resid_out.data_ptr(), M, K, src.stride(0),
+                                     qweight.data_ptr(), N, qweight.stride(0), scales.data_ptr(), zeros.data_ptr(),
+                                     scales.stride(0), G, y.data_ptr(), y.stride(0), ws_ptr, ws_size, stream)
+    _lib.check(st, "w4a16_matmul_prologue")
+    return y
+
+
 def argmax_last(x: torch.Tensor) -> torch.Tensor:
     """Index of the first maximum along the last dim of a bf16 tensor (torch.argmax(-1, keepdim=True))."""
     x2 = x.reshape(-1, x.shape[-1]).contiguous()
@@ -298,20 +326,37 @@ class LlamaTP:
     def _decode_step_fused(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         B = ids.shape[0]
         nq, nkv, hd = self.nh_l, self.nkv_l, self.hd
-        h = F.embedding(ids.view(B), self.embed)  # [B, H], the residual stream
-        x = torch.empty_like(h)
-        q = torch.empty(B, nq, hd, device=h.device, dtype=torch.bfloat16)
-        att = torch.empty(B, nq * hd, device=h.device, dtype=torch.bfloat16)
-        act = torch.empty(B, self.inter_l, device=h.device, dtype=torch.bfloat16)
+        cur = F.embedding(ids.view(B), self.embed)  # [B, H], the residual stream (ping-pongs with `other`)
+        other = torch.empty_like(cur)
+        x = torch.empty_like(cur)
+        q = torch.empty(B, nq, hd, device=cur.device, dtype=torch.bfloat16)
+        att = torch.empty(B, nq * hd, device=cur.device, dtype=torch.bfloat16)
+        act = torch.empty(B, self.inter_l, device=cur.device, dtype=torch.bfloat16)
+        fold = self.w4 and B <= 32  # norms and SwiGLU run inside the W4 kernels' activation staging
         delta = None
         for i, L in enumerate(self.layers):
-            add_rmsnorm(h, delta, L["ln1"], x, self.eps)
-            qkv = L["qkv"](x)
             kc, vc = self.k_cache[i, :B], self.v_cache[i, :B]
+            if fold:
+                if delta is None:
+                    qkv = w4a16_matmul_prologue(PROLOGUE_RMSNORM, cur, *L["qkv"].q, norm_weight=L["ln1"], eps=self.eps)
+                else:
+                    qkv = w4a16_matmul_prologue(PROLOGUE_RMSNORM, cur, *L["qkv"].q, delta=delta, norm_weight=L["ln1"],
+                                                eps=self.eps, resid_out=other)
+                    cur, other = other, cur
+            else:
+                add_rmsnorm(cur, delta, L["ln1"], x, self.eps)
+                qkv = L["qkv"](x)
             rope_kv_cache(qkv, self.cos, self.sin, pos, q, kc, vc, nq, nkv)
             decode_attention(q, kc, vc, pos, att, nq, nkv, hd ** -0.5)
-            add_rmsnorm(h, self._all_reduce(L["o"](att)), L["ln2"], x, self.eps)
-            silu_mul(L["gu"](x), act)
-            delta = self._all_reduce(L["down"](act))
-        add_rmsnorm(h, delta, self.norm, x, self.eps)
+            o = self._all_reduce(L["o"](att))
+            if fold:
+                gu = w4a16_matmul_prologue(PROLOGUE_RMSNORM, cur, *L["gu"].q, delta=o, norm_weight=L["ln2"],
+                                           eps=self.eps, resid_out=other)
+                cur, other = other, cur
+                delta = self._all_reduce(w4a16_matmul_prologue(PROLOGUE_SWIGLU, gu, *L["down"].q))
+            else:
+                add_rmsnorm(cur, o, L["ln2"], x, self.eps)
+                silu_mul(L["gu"](x), act)
+                delta = self._all_reduce(L["down"](act))
+        add_rmsnorm(cur, delta, self.norm, x, self.eps)
         return self._gather_vocab(self.lm_head(x)).view(B, 1, -1)

@@ -112,3 +112,47 @@ def test_argmax_matches_torch_including_ties(cuda_device, rows, n):
     assert torch.equal(argmax_last(x), x.argmax(-1, keepdim=True))
     y = torch.randn(rows, n, device="cuda", generator=g).to(torch.bfloat16)
     assert torch.equal(argmax_last(y), y.argmax(-1, keepdim=True))
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 32])
+def test_matmul_with_rmsnorm_prologue_matches_norm_then_matmul(cuda_device, M):
+    import int4_b200
+    from int4_b200.decode import PROLOGUE_RMSNORM, add_rmsnorm, w4a16_matmul_prologue
+
+    N, K = 3072, 2048
+    g = torch.Generator(device="cuda").manual_seed(M)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    q = int4_b200.quantize_int4(w, 128)
+    h = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    d = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(K, device="cuda", generator=g)).to(torch.bfloat16)
+    resid = torch.empty_like(h)
+    y = w4a16_matmul_prologue(PROLOGUE_RMSNORM, h, *q, delta=d, norm_weight=nw, eps=1e-5, resid_out=resid)
+    hh, x = h.clone(), torch.empty_like(h)
+    add_rmsnorm(hh, d, nw, x, 1e-5)
+    ref = int4_b200.w4a16_matmul(x, *q)
+    assert torch.equal(resid, hh)
+    err = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
+    assert err < 1e-3, err
+    # without a delta and without a residual output
+    y0 = w4a16_matmul_prologue(PROLOGUE_RMSNORM, h, *q, norm_weight=nw, eps=1e-5)
+    x0 = torch.empty_like(h)
+    add_rmsnorm(h.clone(), None, nw, x0, 1e-5)
+    ref0 = int4_b200.w4a16_matmul(x0, *q)
+    assert ((y0.float() - ref0.float()).norm() / ref0.float().norm()).item() < 1e-3
+
+
+@pytest.mark.parametrize("M", [1, 5, 32])
+def test_matmul_with_swiglu_prologue_matches_silu_mul_then_matmul(cuda_device, M):
+    import int4_b200
+    from int4_b200.decode import PROLOGUE_SWIGLU, silu_mul, w4a16_matmul_prologue
+
+    N, K = 2048, 8192
+    g = torch.Generator(device="cuda").manual_seed(100 + M)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    q = int4_b200.quantize_int4(w, 128)
+    gu = (torch.randn(M, 2 * K, device="cuda", generator=g) * 2).to(torch.bfloat16)
+    y = w4a16_matmul_prologue(PROLOGUE_SWIGLU, gu, *q)
+    act = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+    silu_mul(gu, act)
+    assert torch.equal(y, int4_b200.w4a16_matmul(act, *q))  # same activations, same kernel: same bits
