@@ -500,6 +500,224 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
   if (tid == 0) atomicExch(a.tickets + blockIdx.x, 0u);
 }
 
+// ------------------------------------------------------------------ streaming variant (very wide N)
+
+#ifndef I4B_STREAM_RING
+#define I4B_STREAM_RING 3
+#endif
+#ifndef I4B_STREAM_STEPS
+#define I4B_STREAM_STEPS 4
+#endif
+constexpr int kStreamRing = I4B_STREAM_RING;    // stages in flight per warp
+constexpr int kStreamSteps = I4B_STREAM_STEPS;  // 32-k steps per stage (at least SPS)
+
+// For matrices with many more 32-column slabs than warps (an lm_head: N = 128256), a persistent grid of
+// warps streams slabs of 32 columns x the whole K: warp g takes slabs g, g + W, g + 2W, ... (W warps in
+// the grid), keeping kStreamRing stages of 4 (or SPS) 32-k steps in flight through its own cp.async ring, so
+// the weight stream never stops between slabs.  The activations (M <= 8 rows x K) and their segment sums
+// are staged once per CTA.  No K split, hence no cross-CTA reduction; the dequant / MMA / segment
+// arithmetic is that of w4_skinny_kernel.
+template <bool F16, int SPS, bool ONE>
+__global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
+  constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;  // 32-k steps per ring stage
+  constexpr int SEGST = SPST / SPS;
+  constexpr int RING = kStreamRing;
+  constexpr int WSTAGE = SPST * 512;       // weight bytes of a stage (32 lanes x 16 B per step)
+  constexpr int SZSTAGE = SEGST * 128;     // scale / zero bytes of a stage (8 records of 16 B per segment)
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = lane >> 2, c = lane & 3;
+  const int M = a.M;
+  const int K = a.K;
+  const int stages_slab = K / (32 * SPST);
+  const int nslabs = (a.N + 31) / 32;
+  const int W = int(gridDim.x) * 4;
+  const int gw = int(blockIdx.x) * 4 + warp;
+  const int my_slabs = gw < nslabs ? (nslabs - gw + W - 1) / W : 0;
+  const int total = my_slabs * stages_slab;
+
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t s_x = s_base;                                   // [M][xpitch]
+  float* sXS = reinterpret_cast<float*>(smem + a.off_xs);        // [K / L][8]
+  const uint32_t s_w = s_base + a.off_sz + warp * RING * (WSTAGE + SZSTAGE);  // this warp's ring
+
+  // Issue cursor: the next stage of this warp's stream (slab, stage in the slab, ring slot), kept as
+  // running pointers so that no division is needed per stage.
+  const int64_t row4 = 4 * a.sqk;  // words between the k8 rows of consecutive 32-k steps
+  int is_left = total, is_st = 0, is_slot = 0;
+  int64_t is_n = int64_t(gw) * 32 + 4 * r;
+  const uint32_t* is_w = a.qw + int64_t(c) * a.sqk + is_n;
+  const uint16_t* const sz0 = (c < 2 ? a.sc : a.zr) + 2 * (c & 1);
+  const uint16_t* is_sz = sz0 + is_n;
+  int is_gcnt = 0;  // segments issued in the current group
+  auto issue_next = [&]() {
+    if (is_left > 0) {
+      const bool n_in = is_n < a.N;
+      const uint32_t dst = s_w + is_slot * (WSTAGE + SZSTAGE);
+      if (n_in) {
+        const uint32_t* src = is_w;
+#pragma unroll
+        for (int i = 0; i < SPST; ++i) {
+          cp16(dst + i * 512 + lane * 16, src, 16u);
+          src += row4;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < SPST; ++i) cp16(dst + i * 512 + lane * 16, a.qw, 0u);  // columns past N: zeros
+      }
+#pragma unroll
+      for (int j = 0; j < SEGST; ++j) {
+        cp4(dst + WSTAGE + j * 128 + r * 16 + 4 * c, n_in ? is_sz : a.sc, n_in ? 4u : 0u);
+        if (++is_gcnt == a.gpl) {
+          is_gcnt = 0;
+          is_sz += a.ssg;
+        }
+      }
+      --is_left;
+      is_slot = is_slot == RING - 1 ? 0 : is_slot + 1;
+      if (++is_st == stages_slab) {  // next slab of this warp
+        is_st = 0;
+        is_n += int64_t(W) * 32;
+        is_w = a.qw + int64_t(c) * a.sqk + is_n;
+        is_sz = sz0 + is_n;
+        is_gcnt = 0;
+      } else {
+        is_w += SPST * row4;
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll 1
+  for (int g = 0; g < RING; ++g) issue_next();
+
+  if (a.pdl) {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+  {
+    constexpr int C = 4 * SPS;
+    const int nch = K / 8;
+    const int ntot = M * nch;
+    for (int base = 0; base < ntot; base += 128) {
+      const int idx = base + tid;
+      const int t = idx / nch, ch = idx - t * nch;
+      uint32_t u[4] = {0u, 0u, 0u, 0u};
+      if (idx < ntot) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.x + int64_t(t) * a.sxm + 8 * ch));
+        u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+      }
+      float sum = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float lo = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] & 0xFFFFu))) : __uint_as_float(u[q] << 16);
+        const float hi = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] >> 16))) : __uint_as_float(u[q] & 0xFFFF0000u);
+        sum += lo + hi;
+      }
+#pragma unroll
+      for (int o = 1; o < C; o <<= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+      if (idx < ntot) {
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
+                     "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
+                     "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
+                     : "memory");
+        if (ch % C == 0) sXS[(ch / C) * 8 + t] = sum;
+      }
+    }
+  }
+  __syncthreads();
+
+  const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
+  const float bias = F16 ? 1024.0f : 128.0f;
+  const uint32_t xl0 = s_x + min(r, M - 1) * a.xpitch + 16 * c;
+  const uint32_t xsl0 = s_base + a.off_xs + 2 * c * 4;
+  float acc[2][4], dacc[2][4];
+  int st = 0, slot = 0;
+  int64_t n_base = int64_t(gw) * 32 + 4 * r;
+  uint32_t xl = xl0, xsl = xsl0;
+#pragma unroll 1
+  for (int g = 0; g < total; ++g) {
+    if (st == 0) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+    }
+    cp_async_wait<RING - 1>();
+    __syncwarp();
+    const uint32_t sl = s_w + slot * (WSTAGE + SZSTAGE);
+#pragma unroll
+    for (int i = 0; i < SPST; ++i) {
+      const uint4 w4 = lds128(sl + i * 512 + lane * 16);
+      const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
+      uint32_t af[2][2][4];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          af[t][q][0] = nib_pair(wd[2 * t], 2 * q, magic);
+          af[t][q][1] = nib_pair(wd[2 * t + 1], 2 * q, magic);
+          af[t][q][2] = nib_pair(wd[2 * t], 2 * q + 1, magic);
+          af[t][q][3] = nib_pair(wd[2 * t + 1], 2 * q + 1, magic);
+        }
+      const uint4 b = lds128(xl + i * 64);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (i % SPS == 0) mma_16816_first<F16>(dacc[t], af[t][0], b.x, b.y);
+        else mma_16816<F16>(dacc[t], af[t][0], b.x, b.y);
+        mma_16816<F16>(dacc[t], af[t][1], b.z, b.w);
+      }
+      if (i % SPS == SPS - 1) {  // segment complete: acc += s * (D - (bias + z) * X)
+        const uint4 sz = lds128(sl + WSTAGE + (i / SPS) * 128 + r * 16);
+        float X0, X1 = 0.0f;
+        if constexpr (ONE) {
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(X0) : "r"(xsl + (i / SPS) * 8 * 4));
+        } else {
+          asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(X0), "=f"(X1) : "r"(xsl + (i / SPS) * 8 * 4));
+        }
+        float sv[4], zv[4];
+        sv[0] = __half2float(__ushort_as_half(uint16_t(sz.x & 0xFFFFu)));
+        sv[1] = __half2float(__ushort_as_half(uint16_t(sz.x >> 16)));
+        sv[2] = __half2float(__ushort_as_half(uint16_t(sz.y & 0xFFFFu)));
+        sv[3] = __half2float(__ushort_as_half(uint16_t(sz.y >> 16)));
+        zv[0] = bias + __half2float(__ushort_as_half(uint16_t(sz.z & 0xFFFFu)));
+        zv[1] = bias + __half2float(__ushort_as_half(uint16_t(sz.z >> 16)));
+        zv[2] = bias + __half2float(__ushort_as_half(uint16_t(sz.w & 0xFFFFu)));
+        zv[3] = bias + __half2float(__ushort_as_half(uint16_t(sz.w >> 16)));
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          acc[t][0] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X0, dacc[t][0]), acc[t][0]);
+          acc[t][2] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X0, dacc[t][2]), acc[t][2]);
+          if constexpr (!ONE) {  // the odd tokens 2c + 1 (none when M == 1)
+            acc[t][1] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X1, dacc[t][1]), acc[t][1]);
+            acc[t][3] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X1, dacc[t][3]), acc[t][3]);
+          }
+        }
+      }
+    }
+    __syncwarp();  // every lane is done with the slot before it is refilled
+    issue_next();
+    slot = slot == RING - 1 ? 0 : slot + 1;
+    xl += SPST * 64;
+    xsl += SEGST * 8 * 4;
+    if (++st == stages_slab) {  // slab complete: acc[t][e] is (token 2c + (e & 1), column 4r + 2t + (e >> 1))
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (ONE && (e & 1)) continue;
+          const int tok = 2 * c + (e & 1);
+          const int64_t n = n_base + 2 * t + (e >> 1);
+          if (tok < M && n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(acc[t][e]);
+        }
+      st = 0;
+      n_base += int64_t(W) * 32;
+      xl = xl0;
+      xsl = xsl0;
+    }
+  }
+  cp_async_wait<0>();
+}
+
 // ------------------------------------------------------------------ planning
 
 static int g_w4_ovr_s = 0;
@@ -605,6 +823,69 @@ static cudaError_t launch_w4_sps(const W4SArgs& a, const W4Plan& p, size_t smem,
   return launch_w4_pro<MT, F16, kProPlain>(a, p, smem, stream);
 }
 
+// Streaming variant: M <= 8, plain activations (contiguous, 16-byte aligned rows), K a whole number of
+// stages, the staged activations small, and far more 32-column slabs than the warps of a wave.
+static bool stream_eligible(const W4SArgs& a, const W4Plan& p, int num_sms) {
+  const int spst = p.SPS > kStreamSteps ? p.SPS : kStreamSteps;
+  const int64_t slabs = (int64_t(a.N) + 31) / 32;
+  return a.M <= 8 && a.pro == kProPlain && a.vec_x && a.vec_w && a.vec_s && a.K % (32 * spst) == 0 &&
+         int64_t(a.M) * (2 * int64_t(a.K) + 64) <= 48 * 1024 && slabs >= int64_t(num_sms) * 12 * 2;
+}
+
+template <bool F16, int SPS, bool ONE>
+static cudaError_t launch_stream_impl(W4SArgs a, int num_sms, cudaStream_t stream) {
+  auto kern = w4_stream_kernel<F16, SPS, ONE>;
+  constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;
+  constexpr int SEGST = SPST / SPS;
+  a.xpitch = (a.K / 8) % 8 == 0 ? a.K * 2 + 64 : a.K * 2;
+  a.off_xs = int((size_t(a.M) * a.xpitch + 15) / 16 * 16);
+  a.off_sz = int((size_t(a.off_xs) + size_t(a.K / (32 * SPS)) * 8 * 4 + 127) / 128 * 128);  // start of the rings
+  const size_t smem = size_t(a.off_sz) + 4 * kStreamRing * (SPST * 512 + SEGST * 128);
+  static size_t configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  int per_sm = int((227 * 1024) / (smem + 1024));
+  per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(num_sms * per_sm));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (a.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+static cudaError_t launch_stream(bool f16, const W4SArgs& a, int sps, int num_sms, cudaStream_t stream) {
+#define I4B_ST(F, O) \
+  switch (sps) { \
+    case 1: return launch_stream_impl<F, 1, O>(a, num_sms, stream); \
+    case 2: return launch_stream_impl<F, 2, O>(a, num_sms, stream); \
+    case 4: return launch_stream_impl<F, 4, O>(a, num_sms, stream); \
+    default: return launch_stream_impl<F, 8, O>(a, num_sms, stream); \
+  }
+  const bool one = a.M == 1;
+  if (f16) {
+    if (one) I4B_ST(true, true);
+    I4B_ST(true, false);
+  }
+  if (one) I4B_ST(false, true);
+  I4B_ST(false, false);
+#undef I4B_ST
+}
+
 cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
                       int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
                       int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream, const W4Prologue* pro) {
@@ -643,12 +924,15 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   a.vec_w = addr(qw) % 16 == 0 && sqk % 4 == 0 && N % 4 == 0;
   a.vec_s = addr(sc) % 4 == 0 && addr(zr) % 4 == 0 && ssg % 2 == 0 && N % 4 == 0;
   a.vec_x = addr(x) % 16 == 0 && sxk == 1 && (sxm % 8 == 0 || M == 1);
-  const int spst = p.SPS > 4 ? p.SPS : 4;  // steps per stage, as in the kernel
-  const int nsteps = p.KC / 32;
-  a.nstages = (nsteps + spst - 1) / spst;
   const int L = 32 * p.SPS;
   a.gpl = G / L;  // L divides G
   a.gpl_shift = (a.gpl & (a.gpl - 1)) == 0 ? __builtin_ctz(unsigned(a.gpl)) : -1;
+  int sms = 0, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms > 0 && stream_eligible(a, p, sms)) return launch_stream(f16, a, p.SPS, sms, stream);
+  const int spst = p.SPS > 4 ? p.SPS : 4;  // steps per stage, as in the kernel
+  const int nsteps = p.KC / 32;
+  a.nstages = (nsteps + spst - 1) / spst;
   // token rows of x in shared memory: 4 mod 8 16-byte units apart (conflict-free fragment reads)
   const int kcp = a.nstages * spst * 32;  // padded k per CTA
   a.xpitch = (kcp / 8) % 8 == 0 ? kcp * 2 + 64 : kcp * 2;
