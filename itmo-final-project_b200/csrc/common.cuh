@@ -279,6 +279,8 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
   return d;
 }
+// Volatile: stays after the cluster barrier that publishes the data.  Independent loads written one after
+// another are still in flight together; callers issue all of them before using any result.
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");

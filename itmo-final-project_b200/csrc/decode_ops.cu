@@ -246,15 +246,22 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const uint16_
   }
   cluster_sync();
   if (rank == 0 && tid < HD) {
+    float mr[8], lr[8], orr[8];  // all remote loads in flight first, then combined in rank order
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      mr[r] = r < NS ? ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[0]), uint32_t(r))) : -INFINITY;
+      lr[r] = r < NS ? ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[1]), uint32_t(r))) : 0.0f;
+      orr[r] = r < NS ? ld_shared_cluster_f32(mapa_shared(smem_u32(&part_o[tid]), uint32_t(r))) : 0.0f;
+    }
     float m = -INFINITY;
-    for (int r = 0; r < NS; ++r) m = fmaxf(m, ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[0]), uint32_t(r))));
+#pragma unroll
+    for (int r = 0; r < 8; ++r) m = fmaxf(m, mr[r]);
     float num = 0.0f, den = 0.0f;
-    for (int r = 0; r < NS; ++r) {
-      const float mr = ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[0]), uint32_t(r)));
-      const float lr = ld_shared_cluster_f32(mapa_shared(smem_u32(&part_ml[1]), uint32_t(r)));
-      const float w = lr > 0.0f ? expf(mr - m) : 0.0f;
-      num = fmaf(ld_shared_cluster_f32(mapa_shared(smem_u32(&part_o[tid]), uint32_t(r))), w, num);
-      den = fmaf(lr, w, den);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float w = lr[r] > 0.0f ? expf(mr[r] - m) : 0.0f;
+      num = fmaf(orr[r], w, num);
+      den = fmaf(lr[r], w, den);
     }
     out[(int64_t(b) * nq + head) * HD + tid] = L > 0 ? to_bf(num / den) : uint16_t(0);
   }

@@ -455,8 +455,13 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     const uint32_t rank = cluster_ctarank();
     for (int idx = int(rank) * kBN + tid; idx < M * kBN; idx += a.S * kBN) {
       const uint32_t addr = smem_u32(sP + idx);
-      float v = ld_shared_cluster_f32(mapa_shared(addr, 0));
-      for (int q = 1; q < a.S; ++q) v += ld_shared_cluster_f32(mapa_shared(addr, uint32_t(q)));
+      float t[8];  // all S (<= 8) remote loads in flight, then added in rank order
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t[q] = q < a.S ? ld_shared_cluster_f32(mapa_shared(addr, uint32_t(q))) : 0.0f;
+      float v = t[0];
+#pragma unroll
+      for (int q = 1; q < 8; ++q)
+        if (q < a.S) v += t[q];
       const int tok = idx / kBN;
       const int64_t n = n0 + idx % kBN;
       if (n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);

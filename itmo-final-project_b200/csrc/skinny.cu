@@ -1,4 +1,6 @@
-// Small-M (M <= 16) W4A16 / W16A16 kernel: the decode GEMV (M == 1) and the small-batch split-K path.
+// Small-M (M <= 16) W16A16 kernel (full-precision weights): the w16a16_matmul decode GEMV and small-batch
+// split-K path.  Only its W16 instantiations are built; INT4 weights are served by gemv_w4.cu, and the
+// INT4 branches below are what that kernel grew out of.
 //
 // Replaces the reference's _gemv_kernel (int4_triton/gemm.py:185-220) and its
 // small-M split-K _matmul_kernel + _reduce_split_k pair (gemm.py:74-182,
@@ -406,8 +408,13 @@ __global__ void __launch_bounds__(INT4 ? 512 : 256) skinny_kernel(const SkinnyAr
     const uint32_t rank = cluster_ctarank();
     for (int idx = int(rank) * blockDim.x + tid; idx < M_eff * BN; idx += a.S * blockDim.x) {
       const uint32_t addr = smem_u32(part + idx);
-      float v = ld_shared_cluster_f32(mapa_shared(addr, 0));
-      for (int q = 1; q < a.S; ++q) v += ld_shared_cluster_f32(mapa_shared(addr, uint32_t(q)));
+      float t[8];  // all S (<= 8) remote loads in flight, then added in rank order
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t[q] = q < a.S ? ld_shared_cluster_f32(mapa_shared(addr, uint32_t(q))) : 0.0f;
+      float v = t[0];
+#pragma unroll
+      for (int q = 1; q < 8; ++q)
+        if (q < a.S) v += t[q];
       const int tok = idx / BN;
       const int64_t n = n_cta + idx % BN;
       if (n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
@@ -596,7 +603,7 @@ cudaError_t launch_skinny(bool int4, bool f16, const void* x, int64_t M, int64_t
     a.vec_w = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (sw1 == 1) && (sw0 % 8 == 0);
   }
   a.vec_x = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (sxk == 1) && (sxm % 8 == 0 || M == 1);
-  if (int4) return f16 ? launch_mt<true, true>(a, p, stream) : launch_mt<true, false>(a, p, stream);
+  if (int4) return cudaErrorInvalidValue;  // INT4 weights go through launch_w4 (gemv_w4.cu)
   return f16 ? launch_mt<false, true>(a, p, stream) : launch_mt<false, false>(a, p, stream);
 }
 
