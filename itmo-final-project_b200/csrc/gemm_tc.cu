@@ -38,16 +38,22 @@ struct TcCfg {
   static constexpr int BM = 128 * BMT, BK = 64;  // BMT row halves of 128 share each B tile
   static constexpr int DQ_WARPS = 16;
   static constexpr int THREADS = 64 + 32 * DQ_WARPS;
-  static constexpr int A_BYTES = BM * BK * 2;                 // 32 KB
-  static constexpr int B_BYTES = BN * BK * 2;                 // BN rows of 128 B
+  static constexpr int A_BYTES = BM * BK * 2;                 // activation tile, 128-byte rows
+  static constexpr int B_BYTES = BN * BK * 2;                 // weight tile (bf16 / fp16), BN rows of 128 B
   static constexpr int P_BYTES = INT4 ? 8 * BN * 4 : 0;       // packed words of one k-block
   static constexpr int SZ_BYTES = INT4 ? 2 * 2 * BN * 2 : 0;  // scales + zeros, two group rows
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES + SZ_BYTES;
-  static constexpr int STAGES = (216 * 1024) / STAGE_BYTES > 8 ? 8 : (216 * 1024) / STAGE_BYTES;
-  static constexpr int TX_BYTES = INT4 ? (A_BYTES + P_BYTES + SZ_BYTES) : (A_BYTES + B_BYTES);
-  static constexpr int BAR_BYTES = (3 * STAGES + 1) * 8 + 8;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + BAR_BYTES;
+  // TMA stages carry A (+ packed weights, scales, zeros for INT4, or the B tile for W16).  INT4 B tiles
+  // are written by the dequant warps into their own NB-deep ring, decoupled from the TMA stages.
+  static constexpr int NB = INT4 ? 2 : 0;
+  static constexpr int STAGE_BYTES = INT4 ? (A_BYTES + P_BYTES + SZ_BYTES) : (A_BYTES + B_BYTES);
+  static constexpr int BUDGET = 216 * 1024 - NB * B_BYTES;
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
+  static constexpr int TX_BYTES = STAGE_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 2 * NB + 1) * 8 + 8;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + size_t(NB) * B_BYTES + BAR_BYTES;
   static constexpr int TMEM_COLS = BMT * BN;
+  static_assert(STAGES >= 2, "at least two pipeline stages");
+  static_assert(TMEM_COLS <= 512, "accumulators exceed TMEM");
 };
 
 struct DqParams {
@@ -108,19 +114,27 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
                    int K, int G, uint16_t* __restrict__ y, int64_t sym) {
   using C = TcCfg<INT4, BN, BMT>;
   constexpr int S = C::STAGES;
+  constexpr int NB = C::NB;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms, by offsetting the shared array itself (a round trip
   // through an integer would turn every shared access below into a generic one).
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* sA = smem;
-  uint8_t* sB = sA + S * C::A_BYTES;
-  uint8_t* sP = sB + S * C::B_BYTES;
-  uint8_t* sSZ = sP + S * C::P_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSZ + S * C::SZ_BYTES);
-  uint64_t* bready = full + S;
-  uint64_t* empty = bready + S;
-  uint64_t* tfull = empty + S;
+  // [S stages: A | (P | SZ) or B] [NB dequantized B tiles] [barriers]
+  uint8_t* stage0 = smem;
+  uint8_t* bring = stage0 + S * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bring + NB * C::B_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* bready = empty + S;  // INT4: B tile b dequantized
+  uint64_t* bfree = bready + NB; // INT4: B tile b no longer read by the MMAs
+  uint64_t* tfull = bfree + NB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  auto sA = [&](int s) { return stage0 + s * C::STAGE_BYTES; };
+  auto sP = [&](int s) { return stage0 + s * C::STAGE_BYTES + C::A_BYTES; };             // INT4
+  auto sSZ = [&](int s) { return stage0 + s * C::STAGE_BYTES + C::A_BYTES + C::P_BYTES; };  // INT4
+  auto sB = [&](int kb) {
+    if constexpr (INT4) return bring + (kb % NB) * C::B_BYTES;
+    else return stage0 + (kb % S) * C::STAGE_BYTES + C::A_BYTES;
+  };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * C::BM;
@@ -129,8 +143,11 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bready[s], C::DQ_WARPS);
       mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(&bready[b], C::DQ_WARPS);
+      mbar_init(&bfree[b], 1);
     }
     mbar_init(tfull, 1);
     fence_mbar_init();
@@ -169,8 +186,6 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % S, u = kb / S;
         if (kb >= S && !mbar_wait(&empty[s], (u - 1) & 1)) { ok = false; break; }
-        mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
-        tma_load_2d(sA + s * C::A_BYTES, &tm_x, &full[s], kb * C::BK, m0);
         // Pull the tiles of k-block kb + 2S into L2 now, so that their TMA loads, issued S k-blocks
         // from now, do not wait for HBM.
         const int kp = kb + 2 * S;
@@ -184,13 +199,15 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
             tma_prefetch_l2_2d(&tm_w, kp * C::BK, n0);
           }
         }
+        mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+        tma_load_2d(sA(s), &tm_x, &full[s], kb * C::BK, m0);
         if constexpr (INT4) {
           const int g_lo = (kb * C::BK) / G;
-          tma_load_2d(sP + s * C::P_BYTES, &tm_w, &full[s], n0, kb * 8);
-          tma_load_2d(sSZ + s * C::SZ_BYTES, &tm_s, &full[s], n0, g_lo);
-          tma_load_2d(sSZ + s * C::SZ_BYTES + 2 * BN * 2, &tm_z, &full[s], n0, g_lo);
+          tma_load_2d(sP(s), &tm_w, &full[s], n0, kb * 8);
+          tma_load_2d(sSZ(s), &tm_s, &full[s], n0, g_lo);
+          tma_load_2d(sSZ(s) + 2 * BN * 2, &tm_z, &full[s], n0, g_lo);
         } else {
-          tma_load_2d(sB + s * C::B_BYTES, &tm_w, &full[s], kb * C::BK, n0);
+          tma_load_2d(sB(kb), &tm_w, &full[s], kb * C::BK, n0);
         }
         ++issued;
       }
@@ -205,13 +222,15 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
       constexpr uint32_t idesc = umma_idesc_f16(F16 ? 0 : 1, 128, BN);
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % S, u = kb / S;
-        // INT4: the activation tile arrives on full[s], the dequantized weights on bready[s].
+        // The activation tile arrives on full[s]; INT4 weights come dequantized on bready[kb % NB].
         if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
-        if (INT4 && !mbar_wait(&bready[s], u & 1)) { ok = false; break; }
+        if constexpr (INT4) {
+          if (!mbar_wait(&bready[kb % NB], (kb / NB) & 1)) { ok = false; break; }
+        }
         tc_fence_after();
-        const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA + s * C::A_BYTES));
-        const uint64_t adesc1 = umma_desc_sw128(smem_u32(sA + s * C::A_BYTES + C::A_BYTES / 2));
-        const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * C::B_BYTES));
+        const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA(s)));
+        const uint64_t adesc1 = umma_desc_sw128(smem_u32(sA(s) + C::A_BYTES / 2));
+        const uint64_t bdesc = umma_desc_sw128(smem_u32(sB(kb)));
 #pragma unroll
         for (int kk = 0; kk < C::BK / 16; ++kk) {
           const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
@@ -219,6 +238,7 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
           if constexpr (BMT == 2) umma_f16_ss(tmem + uint32_t(BN), adesc1 + 2 * kk, bdesc + 2 * kk, idesc, acc);
         }
         umma_commit(&empty[s]);
+        if constexpr (INT4) umma_commit(&bfree[kb % NB]);
       }
       umma_commit(tfull);  // also on the error path: completes once issued MMAs are done
     }
@@ -242,10 +262,11 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
           g_end += G;
         }
         if (!mbar_wait_sleep(&full[s], u & 1)) { ok = false; break; }
-        const uint32_t* P = reinterpret_cast<const uint32_t*>(sP + s * C::P_BYTES);
-        const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ + s * C::SZ_BYTES);
+        if (kb >= NB && !mbar_wait_sleep(&bfree[kb % NB], ((kb / NB) - 1) & 1)) { ok = false; break; }
+        const uint32_t* P = reinterpret_cast<const uint32_t*>(sP(s));
+        const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ(s));
         const uint16_t* Zs = Ss + 2 * BN;
-        uint8_t* Bs = sB + s * C::B_BYTES;
+        uint8_t* Bs = sB(kb);
         if (g_cached != g_lo) {
           pc = dq_params<F16>(Ss[nl], Zs[nl]);
           g_cached = g_lo;
@@ -266,7 +287,7 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bready[s]);
+        if (lane == 0) mbar_arrive(&bready[kb % NB]);
       }
     }
     // ---- epilogue: TMEM -> registers -> y.  The dequant warps form DQ_WARPS / 4 sets of four (one per
@@ -414,14 +435,26 @@ static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int
 
 // Rows per CTA: 256 (two accumulators share each dequantized weight tile) when that still fills half a
 // wave of the GPU, else 128 (twice the CTAs).
-int tc_pick_bn(int64_t M, int64_t N, int num_sms) { return 2 * cdiv(M, 256) * cdiv(N, 128) >= num_sms ? 2 : 1; }
+#ifndef I4B_TC_FORCE
+#define I4B_TC_FORCE 0
+#endif
+// Tile code: 1 -> 128 x 128, 2 -> 256 x 128 (two MMAs share a B tile), 3 -> 128 x 256, 4 -> 256 x 256.
+// The largest tile that still gives at least half a wave of CTAs: bigger tiles read fewer activation and
+// weight bytes per flop from L2.
+int tc_pick_bn(int64_t M, int64_t N, int num_sms) {
+  if (I4B_TC_FORCE) return I4B_TC_FORCE;
+  if (2 * cdiv(M, 256) * cdiv(N, 256) >= num_sms) return 4;
+  return 2 * cdiv(M, 256) * cdiv(N, 128) >= num_sms ? 2 : 1;
+}
 
 cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                       int64_t sym, int bn, cudaStream_t stream) {
-  // bn: row halves per CTA from tc_pick_bn (1 -> 128 x 128 tiles, 2 -> 256 x 128 tiles)
+  // bn: tile code from tc_pick_bn
 #define I4B_TC(I, F) \
-  return bn == 2 ? launch_tc_impl<I, F, 128, 2>(o, M, N, K, G, y, sym, stream) \
-                 : launch_tc_impl<I, F, 128, 1>(o, M, N, K, G, y, sym, stream)
+  return bn == 4   ? launch_tc_impl<I, F, 256, 2>(o, M, N, K, G, y, sym, stream) \
+         : bn == 2 ? launch_tc_impl<I, F, 128, 2>(o, M, N, K, G, y, sym, stream) \
+         : bn == 3 ? launch_tc_impl<I, F, 256, 1>(o, M, N, K, G, y, sym, stream) \
+                   : launch_tc_impl<I, F, 128, 1>(o, M, N, K, G, y, sym, stream)
   if (int4) {
     if (f16) I4B_TC(true, true);
     I4B_TC(true, false);
