@@ -185,6 +185,72 @@ int i4b_silu_mul(const void* gate_up, void* y, int64_t B, int64_t I, void* strea
 /* out[r] = index of the first maximum of bf16 row x[r, 0..n) (greedy decoding, as torch.argmax). */
 int i4b_argmax_rows(const void* x, int64_t rows, int64_t n, int64_t* out, void* stream);
 
+/* ---- Persistent decode of all decoder layers (one launch per token step) ----
+ *
+ * Replaces, for batch <= 8 single-token steps of a Llama-shaped W4A16 model on
+ * one GPU, the reference's per-layer sequence inside transformers' Llama with
+ * Int4Linear projections (int4_triton/qlinear.py:8-43 -> gemm.py:185-220 per
+ * projection, benchmarks/eval_llama.py:121-183): RMSNorm, q/k/v, rotary
+ * embedding, KV-cache write, attention, o_proj + residual, RMSNorm, gate/up,
+ * SiLU * up, down_proj + residual, for every layer, in ONE cooperative kernel.
+ * Weights are the quantize_int4 triples re-laid by i4b_tile_w4; the gate/up
+ * projection has its rows interleaved (row 2j = gate row j, row 2j + 1 = up
+ * row j).  Numerics follow transformers' bf16 rounding points; attention is
+ * fp32 inside. */
+typedef struct i4b_decode_model {
+  int32_t layers, hidden, heads, kv_heads, head_dim, intermediate, vocab;
+  int32_t group_size; /* 32, 64 or 128 */
+  int32_t batch;      /* tokens this step, 1..8 (one per sequence, all at position *pos) */
+  int32_t max_seq;    /* positions of the caches and the rotary tables */
+  int32_t cache_batch; /* sequences the caches hold (>= batch) */
+  float eps;          /* RMSNorm epsilon */
+  float attn_scale;   /* softmax scale, normally head_dim^-0.5 */
+  const int64_t* tokens; /* device [batch] token ids */
+  const int64_t* pos;    /* device [1] position of this step */
+  const void* embed;     /* bf16 [vocab, hidden] */
+  const void* w_qkv;     /* tiled [layers] x i4b_tile_w4_bytes((heads + 2 kv_heads) * 64, hidden) */
+  const void* w_o;       /* tiled [layers] x i4b_tile_w4_bytes(hidden, heads * 64) */
+  const void* w_gu;      /* tiled [layers] x i4b_tile_w4_bytes(2 * intermediate, hidden), rows interleaved */
+  const void* w_down;    /* tiled [layers] x i4b_tile_w4_bytes(hidden, intermediate) */
+  const void* ln1;       /* bf16 [layers, hidden] input_layernorm weights */
+  const void* ln2;       /* bf16 [layers, hidden] post_attention_layernorm weights */
+  const void* cos_table; /* bf16 [max_seq, 64] */
+  const void* sin_table; /* bf16 [max_seq, 64] */
+  void* k_cache;         /* bf16 [layers, cache_batch, kv_heads, max_seq, 64] */
+  void* v_cache;         /* bf16 [layers, cache_batch, kv_heads, max_seq, 64] */
+  void* h_out;           /* bf16 [batch, hidden]: the residual stream after the last layer */
+} i4b_decode_model;
+
+/* Bytes of the tiled form of a quantize_int4 triple; 0 when N % 32, K % 512 or G is unsupported. */
+size_t i4b_tile_w4_bytes(int64_t N, int64_t K, int group_size);
+
+/* Re-lay qweight[K/8, N] (+ scales / zeros [K/G, N]) into 32-column x 512-k pieces of packed words followed
+ * by their scales and zeros, the order in which the persistent decode streams them. */
+int i4b_tile_w4(const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales, const uint16_t* zeros,
+                int64_t stride_sg, int64_t K, int group_size, void* out, void* stream);
+
+/* Workspace of i4b_decode_layers.  It must be zero before its first use; every call leaves it zero again.
+ * Calls that share a workspace must not overlap in time. */
+int i4b_decode_workspace_size(const i4b_decode_model* model, size_t* bytes);
+
+/* One decode step through every layer: h_out = residual stream after the last layer (the final norm and
+ * the lm_head are separate calls).  Writes k and v of position *pos into the caches. */
+int i4b_decode_layers(const i4b_decode_model* model, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Diagnostic hook: when buffer is not null (device memory of at least SMs x layers x 5 x 16 x 8 bytes),
+ * later i4b_decode_layers launches record uint64 stamps per (CTA, layer, stage) as [CTA][layer][stage][16]:
+ * slots 0-6 are SM clock cycles, slot 7 the %globaltimer (ns) at stage entry, slots 8-11 warp 0's
+ * cycles waiting for weights, cycles in the piece MMAs, piece count, and the producer's lead in pieces.  Stages: qkv, attention,
+ * o_proj, gate/up, down_proj.  Projection stages: entry, dependency met, activations staged, pieces done,
+ * epilogue done, fence done, published.  Attention: entry, dependency met, queries ready, partial written,
+ * fence done, ticket taken, combined and published.  Process-wide; null turns it off. */
+void i4b_set_decode_trace(void* buffer, size_t bytes);
+
+/* Tuning hook for the M > 32 tcgen05 GEMM: tile (1: 128x128, 2: 256x128, 3: 128x256, 4: 256x256) and
+ * K splits (1..4); 0 keeps the automatic choice.  Process-wide.  Changes the workspace size a later
+ * i4b_w4a16_workspace_size / i4b_w16a16_workspace_size reports.  No counterpart in the reference. */
+void i4b_set_gemm_override(int tile, int splits);
+
 /* Device-side error flags raised by kernels of this library on `device`
  * (a bounded wait that expired sets bit 0).  Synchronises that device;
  * clear != 0 resets the flags.  Returns -1 if the flags cannot be read. */

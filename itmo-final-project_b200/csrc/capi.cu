@@ -30,6 +30,7 @@ int fail_cuda(cudaError_t e) {
 struct DevInfo {
   int sms = 0;
   int major = 0, minor = 0;
+  int smem_optin = 0;  // shared memory per block with the opt-in attribute
 };
 
 // Per-device properties, read once (the device of the calling thread).
@@ -47,6 +48,8 @@ int current_device_info(DevInfo* out) {
       return fail_cuda(e);
     if ((e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
       return fail_cuda(e);
+    if ((e = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+      return fail_cuda(e);
     cache[dev] = d;
     filled[dev] = true;
   }
@@ -59,21 +62,22 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
-// Workspace of the large-M INT4 path for the worst case the size query can see.
-size_t tc_w4_workspace(int64_t M, int64_t N, int64_t K, int G) {
+// Workspace of the large-M INT4 path for the worst case the size query can see:
+// [tickets][x copy][qweight / scales / zeros copies when N % 8 != 0][split-K fp32 partials].
+size_t tc_w4_workspace(int64_t M, int64_t N, int64_t K, int G, int sms) {
   size_t b = kTicketBytes + align256(size_t(M) * size_t(K) * 2);
   if (N % 8 != 0) {
     const int64_t Np = round_up(N, 8);
     b += align256(size_t(K / 8) * Np * 4) + 2 * align256(size_t(K / G) * Np * 2);
   }
-  return b;
+  return b + align256(tc_partial_bytes(tc_plan(M, N, K, sms), M, N));
 }
 
-size_t tc_w16_workspace(int64_t M, int64_t N, int64_t K) {
+size_t tc_w16_workspace(int64_t M, int64_t N, int64_t K, int sms) {
   const int64_t Kp = round_up(K, 8);
   size_t b = kTicketBytes + align256(size_t(M) * size_t(Kp) * 2);
   if (K % 8 != 0) b += align256(size_t(N) * size_t(Kp) * 2);
-  return b;
+  return b + align256(tc_partial_bytes(tc_plan(M, N, Kp, sms), M, N));
 }
 
 // Up to these M the register-dequant kernels run (the reference switches paths at
@@ -110,6 +114,8 @@ void i4b_set_skinny_override(int wn, int wk, int splits) {
 }
 
 void i4b_set_pdl(int enable) { g_pdl = enable != 0; }
+
+void i4b_set_gemm_override(int tile, int splits) { set_tc_override(tile, splits); }
 
 int i4b_quantize_int4(const void* w, int w_dtype, int64_t N, int64_t K, int64_t stride_wn, int64_t stride_wk,
                       int group_size, int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream) {
@@ -148,7 +154,7 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
   if (M <= kW4MaxM) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
-  return tc_w4_workspace(M, N, K, group_size);
+  return tc_w4_workspace(M, N, K, group_size, d.sms);
 }
 
 int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
@@ -183,7 +189,7 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
   const bool w_ok = aligned16(qweight) && (stride_qk * 4) % 16 == 0 && aligned16(scales) && aligned16(zeros) &&
                     (stride_sg * 2) % 16 == 0;
   if (!w_ok && N % 8 == 0) return I4B_ERR_LAYOUT;  // no workspace reserved for this case
-  if (tc_w4_workspace(M, N, K, G) > workspace_bytes || !workspace) return I4B_ERR_WORKSPACE;
+  if (tc_w4_workspace(M, N, K, G, d.sms) > workspace_bytes || !workspace) return I4B_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace) + kTicketBytes;
   TcOperands o{x, stride_xm, qweight, stride_qk, scales, zeros, stride_sg};
   cudaError_t e = cudaSuccess;
@@ -210,7 +216,11 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
     o.zr = reinterpret_cast<const uint16_t*>(zc);
     o.ssg = Np;
   }
-  e = launch_tc(true, f16, o, M, N, K, G, static_cast<uint16_t*>(y), stride_ym, tc_pick_bn(M, N, d.sms), s);
+  const TcPlan plan = tc_plan(M, N, K, d.sms);
+  uint8_t* part = static_cast<uint8_t*>(workspace) + tc_w4_workspace(M, N, K, G, d.sms) -
+                  align256(tc_partial_bytes(plan, M, N));
+  e = launch_tc(true, f16, o, M, N, K, G, static_cast<uint16_t*>(y), stride_ym, plan, reinterpret_cast<float*>(part),
+                static_cast<unsigned int*>(workspace), s);
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
@@ -249,7 +259,7 @@ size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K) {
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
   if (M <= kSmallM) return skinny_workspace_bytes(plan_skinny(M, N, K, 32, false, d.sms));
-  return tc_w16_workspace(M, N, K);
+  return tc_w16_workspace(M, N, K, d.sms);
 }
 
 int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
@@ -285,7 +295,7 @@ int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t st
   const bool x_ok = K % 8 == 0 && aligned16(x) && stride_xk == 1 && (stride_xm * 2) % 16 == 0;
   const bool w_ok = K % 8 == 0 && aligned16(w) && stride_wk == 1 && (stride_wn * 2) % 16 == 0;
   if (!w_ok && K % 8 == 0) return I4B_ERR_LAYOUT;
-  if (tc_w16_workspace(M, N, K) > workspace_bytes || !workspace) return I4B_ERR_WORKSPACE;
+  if (tc_w16_workspace(M, N, K, d.sms) > workspace_bytes || !workspace) return I4B_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace) + kTicketBytes;
   TcOperands o{x, stride_xm, w, stride_wn, nullptr, nullptr, 0};
   cudaError_t e = cudaSuccess;
@@ -301,7 +311,11 @@ int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t st
     o.w = ws;
     o.sw = Kp;
   }
-  e = launch_tc(false, f16, o, M, N, Kp, 0, static_cast<uint16_t*>(y), stride_ym, tc_pick_bn(M, N, d.sms), s);
+  const TcPlan plan = tc_plan(M, N, Kp, d.sms);
+  uint8_t* part = static_cast<uint8_t*>(workspace) + tc_w16_workspace(M, N, K, d.sms) -
+                  align256(tc_partial_bytes(plan, M, N));
+  e = launch_tc(false, f16, o, M, N, Kp, 0, static_cast<uint16_t*>(y), stride_ym, plan,
+                reinterpret_cast<float*>(part), static_cast<unsigned int*>(workspace), s);
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
@@ -377,13 +391,55 @@ int i4b_argmax_rows(const void* x, int64_t rows, int64_t n, int64_t* out, void* 
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
+size_t i4b_tile_w4_bytes(int64_t N, int64_t K, int group_size) { return tile_w4_bytes(N, K, group_size); }
+
+int i4b_tile_w4(const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales, const uint16_t* zeros,
+                int64_t stride_sg, int64_t K, int group_size, void* out, void* stream) {
+  if (group_size != 32 && group_size != 64 && group_size != 128) return I4B_ERR_GROUP;
+  if (tile_w4_bytes(N, K, group_size) == 0) return I4B_ERR_SHAPE;
+  if (!qweight || !scales || !zeros || !out) return I4B_ERR_INVALID_ARG;
+  if (stride_qk < N || stride_sg < N) return I4B_ERR_LAYOUT;
+  if (!aligned16(out)) return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const cudaError_t e =
+      launch_tile_w4(qweight, stride_qk, scales, zeros, stride_sg, N, K, group_size, out, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_decode_workspace_size(const i4b_decode_model* model, size_t* bytes) {
+  if (!model || !bytes) return I4B_ERR_INVALID_ARG;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  return decode_layers_workspace(*model, d.sms, bytes);
+}
+
+int i4b_decode_layers(const i4b_decode_model* model, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!model || !workspace) return I4B_ERR_INVALID_ARG;
+  const i4b_decode_model& m = *model;
+  if (!m.tokens || !m.pos || !m.embed || !m.w_qkv || !m.w_o || !m.w_gu || !m.w_down || !m.ln1 || !m.ln2 ||
+      !m.cos_table || !m.sin_table || !m.k_cache || !m.v_cache || !m.h_out)
+    return I4B_ERR_INVALID_ARG;
+  const void* vec[] = {m.embed, m.w_qkv, m.w_o, m.w_gu, m.w_down, m.ln1, m.ln2, m.k_cache, m.v_cache, m.h_out, workspace};
+  for (const void* p : vec)
+    if (!aligned16(p)) return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  cudaError_t e = cudaSuccess;
+  const int st = launch_decode_layers(m, d.sms, d.smem_optin, workspace, workspace_bytes,
+                                      static_cast<cudaStream_t>(stream), &e);
+  return st == I4B_ERR_CUDA ? fail_cuda(e) : st;
+}
+
+void i4b_set_decode_trace(void* buffer, size_t bytes) { set_decode_trace(buffer, bytes); }
+
 int i4b_device_error_flags(int device, int clear) {
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess) return -1;
   if (cudaSetDevice(device) != cudaSuccess) return -1;
   int flags = -1;
   if (cudaDeviceSynchronize() == cudaSuccess) {
-    flags = int(read_quant_error(clear != 0) | read_tc_error(clear != 0));
+    flags = int(read_quant_error(clear != 0) | read_tc_error(clear != 0) | read_dk_error(clear != 0));
   }
   cudaSetDevice(prev);
   return flags;

@@ -1,0 +1,1152 @@
+// Persistent decode step: every decoder layer of a Llama-shaped W4A16 model for one token per sequence
+// (batch <= 8), in ONE cooperative launch with one CTA per SM.
+//
+// The reference decodes through transformers' Llama with Int4Linear projections
+// (int4_triton/qlinear.py:8-43, benchmarks/eval_llama.py:121-183): per layer four
+// W4A16 GEMV launches (gemm.py:185-220) plus some forty torch kernels, each a
+// dependent launch whose fixed cost (launch, ramp-up, drain) is several times the
+// ~0.3-1.4 us it takes to stream one projection's packed weights from HBM.  Here
+// the whole stack of layers is one kernel, organised around the fact that the
+// weights do not depend on the data:
+//
+// * Weight stream.  Each CTA owns a fixed list of 32-column slabs of the four
+//   projections of every layer (the same list in every layer).  A producer warp
+//   streams those slabs, as 8 KB pieces of packed words plus their scales and
+//   zeros, from HBM into a ring of shared-memory slots with bulk copies
+//   (cp.async.bulk, completion on an mbarrier per slot), in the order the CTA
+//   will use them, running ahead across stage and layer boundaries as far as the
+//   ring allows.  The packed weights are pre-tiled once (i4b_tile_w4) so that
+//   each piece is one contiguous copy.
+// * Stages.  Per layer: (1) qkv GEMV with the RMSNorm prologue, (2) attention
+//   with the rotary embedding and the KV-cache write, (3) o_proj GEMV with the
+//   residual add, (4) gate/up GEMV (rows interleaved gate/up) with the RMSNorm
+//   prologue and the SiLU*up epilogue, (5) down_proj GEMV with the residual add.
+//   A stage needs every output of the previous one, so each stage ends with one
+//   atomic increment per CTA of a counter in the workspace, and the next stage's
+//   CTAs wait (thread 0, acquire loads, bounded) until it reaches its total.
+//   While compute warps wait, the producer keeps streaming: the critical path of
+//   a layer is five such hand-offs plus compute on weights already on chip.
+// * GEMV arithmetic is the decode GEMV's (gemv_w4.cu): one lop3 turns a nibble
+//   pair into the bf16 pair (128 + q_i, 128 + q_{i+4}), the A fragment of an
+//   mma.m16n8k16 with output columns as rows and tokens as the 8 columns; zero and
+//   scale are applied once per group, sum_k x (q - z) s = s (D - (128 + z) X),
+//   with X the group sums of the activations.  The 8 compute warps split a
+//   stage's pieces; fp32 partials of one slab are added in a fixed order.
+// * Attention: items (token, kv head, sequence split), one per CTA; the last
+//   split of a (token, kv head) to finish (atomic ticket) combines the fp32
+//   partial softmax sums in split order.
+//
+// Every wait is bounded (I4B_WAIT_LIMIT_NS) and checks an abort word, so an error
+// in one CTA ends all of them; the last CTA to leave resets the counters.  All
+// sums are in a fixed order: results are identical from run to run.
+#include <math.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace i4b {
+
+namespace {
+
+constexpr int kCW = 8;               // compute warps
+constexpr int kCT = kCW * 32;        // compute threads
+constexpr int kThreads = kCT + 32;   // + the producer warp
+constexpr int kPieceK = 512;         // k of one weight piece
+constexpr int kPieceW = 8192;        // packed-word bytes of one piece (32 columns x 512 k x 4 bit)
+constexpr int kMaxSlots = 32;
+constexpr int kMaxCtas = 160;
+constexpr int kMaxItems = 16;        // slabs per CTA per layer
+constexpr int kMaxTok = 8;
+constexpr int kHD = 64;
+constexpr int kPartRow = 68;  // floats per attention partial: o[64], m, l, padding to 16 bytes
+
+enum { G_QKV = 0, G_O = 1, G_GU = 2, G_DOWN = 3 };                       // GEMV stages
+enum { C_QKV = 0, C_ATTN = 1, C_O = 2, C_GU = 3, C_DOWN = 4, C_LAYER = 5 };  // counters of a layer
+
+// Scalars and pointers of one launch; the kernel copies them to shared memory once.
+struct DkHot {
+  i4b_decode_model m;
+  int nslab[4], npiece[4];  // 32-column slabs and 512-k pieces per slab of qkv, o, gate/up, down
+  int64_t layer_bytes[4];   // tiled bytes of one layer's projection
+  int piece_bytes, nslot, nsplit, gqa, qkv_n, q_n;
+  int xpitch, off_x, off_xs, off_part;
+  unsigned int* ctr;  // [layers][5] stage counters | [B * kv_heads] attention tickets | done | abort
+  int n_ctr, i_ticket, i_done, i_abort;
+  float* apart;       // attention partials [B * kv_heads * nsplit][gqa][kPartRow]
+  uint16_t* qkv;      // [B][qkv_n]
+  uint16_t* att;      // [B][q_n]
+  uint16_t* act;      // [B][intermediate]
+  unsigned long long* trace;  // optional: [grid][layers][5 stages][8] %globaltimer stamps, or null
+};
+
+struct DkParams {
+  DkHot h;
+  uint8_t nitems[kMaxCtas];
+  uint16_t items[kMaxCtas][kMaxItems];  // (stage << 14) | slab, in stage order
+};
+
+// Trace stamps per (CTA, layer, stage), 8 slots of SM clock cycles (clock64): 0 entry, 1 dependency met,
+// 2 activations staged, 3 pieces done, 4 epilogue done, 5 fence done, 6 published; slot 7 holds
+// %globaltimer at entry, the time base shared by all SMs.
+// Slots 8..15: warp 0's cycles waiting for weight pieces, its cycles in the piece MMAs, its piece count,
+// and the producer's issued-piece count relative to this stage's first piece, at stage entry.
+constexpr int kTraceSlots = 16;
+__device__ __forceinline__ void stamp(const DkHot& P, int l, int st, int k) {
+  if (P.trace && threadIdx.x == 0) {
+    unsigned long long* t = P.trace + ((int64_t(blockIdx.x) * P.m.layers + l) * 5 + st) * kTraceSlots;
+    t[k] = clock64();
+    if (k == 0) t[7] = globaltimer_ns();
+  }
+}
+__device__ __forceinline__ void trace_put(const DkHot& P, int l, int st, int k, long long v) {
+  if (P.trace) P.trace[((int64_t(blockIdx.x) * P.m.layers + l) * 5 + st) * kTraceSlots + k] = (unsigned long long)v;
+}
+
+__device__ unsigned int g_dk_err = 0;
+
+__device__ __forceinline__ float bfv(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+__device__ __forceinline__ uint32_t bfr(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory"); }
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned int ld_relaxed_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint16_t ldcg16(const uint16_t* p) {
+  return __ldcg(reinterpret_cast<const unsigned short*>(p));
+}
+__device__ __forceinline__ uint4 ldcg128(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Wait until *c >= target (acquire).  False on the abort word or after I4B_WAIT_LIMIT_NS.
+__device__ bool wait_counter(const unsigned int* c, unsigned int target, const unsigned int* abort_word) {
+  if (ld_acquire_u32(c) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_u32(c) >= target) return true;
+    if ((i & 31u) == 0) {
+      if (ld_relaxed_u32(abort_word)) return false;
+      if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
+    }
+  }
+}
+
+// mbarrier phase wait, bounded, giving up early when another CTA aborted.
+__device__ bool wait_slot(uint64_t* bar, uint32_t parity, const unsigned int* abort_word) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (ld_relaxed_u32(abort_word)) return false;
+      if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i) { return and_or(w >> (4 * i), 0x000F000Fu, 0x43004300u); }
+
+// mma.m16n8k16 bf16 -> fp32 without `volatile`: a pure function of its operands, so the compiler may
+// schedule the shared-memory loads of later steps ahead of it.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_bf16_first(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// One 512-k piece of a 32-column slab, by one warp: acc[t][e] += the piece's contribution to columns
+// 4r + 2t (e = 0, 1) and 4r + 2t + 1 (e = 2, 3) for tokens 2c + (e & 1), r = lane / 4, c = lane % 4.
+// wb: the piece in shared memory; xb: this lane's activations at the piece's first k;
+// xsb: this lane's group sums X[group of the piece's first k][2c].  The two k16 halves of a step
+// accumulate in separate registers (four independent MMA chains per warp), added once per group.
+template <int SPS>
+__device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, const float* xsb, int lane,
+                                          float (&acc)[2][4]) {
+  const int r = lane >> 2;
+  float d0[2][4], d1[2][4];
+  // four blocks of four 32-k steps: the loads of a block are scheduled together, the block loop is not
+  // unrolled (register budget of 288 threads per SM); SPS divides 4, so group boundaries fall inside blocks
+#pragma unroll 1
+  for (int j0 = 0; j0 < 16; j0 += 4)
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const int j = j0 + jj;
+    const uint4 w4 = *reinterpret_cast<const uint4*>(wb + (j * 32 + lane) * 16);
+    const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
+    uint32_t af[2][2][4];
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        af[t][s][0] = nib_pair(wd[2 * t], 2 * s);
+        af[t][s][1] = nib_pair(wd[2 * t + 1], 2 * s);
+        af[t][s][2] = nib_pair(wd[2 * t], 2 * s + 1);
+        af[t][s][3] = nib_pair(wd[2 * t + 1], 2 * s + 1);
+      }
+    const uint4 b = *reinterpret_cast<const uint4*>(xb + j * 64);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (jj % SPS == 0) {
+        mma_bf16_first(d0[t], af[t][0], b.x, b.y);
+        mma_bf16_first(d1[t], af[t][1], b.z, b.w);
+      } else {
+        mma_bf16(d0[t], af[t][0], b.x, b.y);
+        mma_bf16(d1[t], af[t][1], b.z, b.w);
+      }
+    }
+    if (jj % SPS == SPS - 1) {  // group complete: acc += s * (D - (128 + z) * X)
+      const int gi = j / SPS;
+      const uint4 sz = *reinterpret_cast<const uint4*>(wb + kPieceW + (gi * 8 + r) * 16);
+      float sv[4], zv[4];
+      sv[0] = __half2float(__ushort_as_half(uint16_t(sz.x & 0xFFFFu)));
+      sv[1] = __half2float(__ushort_as_half(uint16_t(sz.x >> 16)));
+      sv[2] = __half2float(__ushort_as_half(uint16_t(sz.y & 0xFFFFu)));
+      sv[3] = __half2float(__ushort_as_half(uint16_t(sz.y >> 16)));
+      zv[0] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.z & 0xFFFFu)));
+      zv[1] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.z >> 16)));
+      zv[2] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.w & 0xFFFFu)));
+      zv[3] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.w >> 16)));
+      const float2 X = *reinterpret_cast<const float2*>(xsb + gi * 8);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        acc[t][0] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X.x, d0[t][0] + d1[t][0]), acc[t][0]);
+        acc[t][1] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X.y, d0[t][1] + d1[t][1]), acc[t][1]);
+        acc[t][2] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X.x, d0[t][2] + d1[t][2]), acc[t][2]);
+        acc[t][3] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X.y, d0[t][3] + d1[t][3]), acc[t][3]);
+      }
+    }
+  }
+}
+
+struct Smem {
+  uint64_t full[kMaxSlots];
+  uint64_t empty[kMaxSlots];
+  float inv[kMaxTok];
+  float wss[kCW * kMaxTok];  // per-warp sums of squares of the RMSNorm rows
+  uint16_t slab[kMaxItems];
+  uint8_t stage[kMaxItems];
+  uint16_t poff[kMaxItems];  // piece offset of each item inside the CTA's layer sequence
+  int nit, ppl;
+  int flag;
+  volatile int prod_seq;  // pieces issued by the producer so far (diagnostics)
+};
+
+constexpr int kXR = 8;  // 16-byte activation chunks per thread in flight
+constexpr int kResPerThread = 4;  // residual values per thread: o / down slabs x tokens x 32 <= kCT * 4
+
+// Stage the activations of GEMV stage g into shared memory: x permuted to the nibble-pair order of the
+// A fragments, [token][k / 8] x 16 bytes with row pitch xpitch, and the group sums X[group][token] (fp32).
+// Each thread puts kXR chunk loads in flight before using any.  RMSNorm stages (the whole [B, K] block is
+// one round, B * K <= 8 * kCT * kXR, checked on the host) compute x = bf16(w * bf16(h * rsqrt(mean(h^2) +
+// eps))) (LlamaRMSNorm) from the registers once the block-wide sums of squares are known.
+__device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int g, int l, int K) {
+  const i4b_decode_model& m = P.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int B = m.batch, H = m.hidden;
+  const bool norm = g == G_QKV || g == G_GU;
+  const uint16_t* nw = static_cast<const uint16_t*>(g == G_QKV ? m.ln1 : m.ln2) + int64_t(l) * H;
+  const uint16_t* hbuf = static_cast<const uint16_t*>(m.h_out);
+  const uint16_t* emb = static_cast<const uint16_t*>(m.embed);
+  // row of token t: the embedding row in layer 0 (qkv), else h / att / act
+  auto row = [&](int t) -> const uint16_t* {
+    if (g == G_QKV) {
+      if (l == 0) {
+        int64_t id = m.tokens[t];
+        if (id < 0 || id >= m.vocab) id = 0;
+        return emb + id * H;
+      }
+      return hbuf + int64_t(t) * H;
+    }
+    if (g == G_GU) return hbuf + int64_t(t) * H;
+    if (g == G_O) return P.att + int64_t(t) * P.q_n;
+    return P.act + int64_t(t) * m.intermediate;
+  };
+  uint8_t* sx = smem + P.off_x;
+  float* sXS = reinterpret_cast<float*>(smem + P.off_xs);
+  const int st_id = g == G_QKV ? C_QKV : g == G_O ? C_O : g == G_GU ? C_GU : C_DOWN;
+  if (tid == 0) trace_put(P, l, st_id, 12, clock64());
+  const int nch = K / 8, total = B * nch;  // nch is a multiple of 64: a warp's 32 chunks share one token
+  const int cpg = m.group_size / 8;        // chunks per group (4, 8 or 16 consecutive lanes)
+  for (int base = 0; base < total; base += kCT * kXR) {
+    uint4 v[kXR];
+#pragma unroll
+    for (int r = 0; r < kXR; ++r) {
+      const int idx = base + r * kCT + tid;
+      if (idx < total) {
+        const int t = idx / nch, ch = idx - t * nch;
+        v[r] = ldcg128(row(t) + 8 * ch);
+        if (norm) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + 8 * ch));  // read after the statistics
+      }
+    }
+    if (tid == 0 && base == 0) trace_put(P, l, st_id, 13, clock64());
+    if (norm) {
+      float ssum[kMaxTok];
+#pragma unroll
+      for (int t = 0; t < kMaxTok; ++t) ssum[t] = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kXR; ++r) {
+        const int idx = base + r * kCT + tid;
+        if (idx < total) {  // warp-uniform
+          const uint32_t u[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+          float ss = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float lo = bfv(u[i] & 0xFFFFu), hi = bfv(u[i] >> 16);
+            ss = fmaf(lo, lo, ss);
+            ss = fmaf(hi, hi, ss);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+          const int t = idx / nch;
+#pragma unroll
+          for (int tt = 0; tt < kMaxTok; ++tt)
+            if (tt == t) ssum[tt] += ss;
+        }
+      }
+      if (lane == 0)
+        for (int t = 0; t < B; ++t) S.wss[warp * kMaxTok + t] = ssum[t];
+      cbar();
+      if (tid < B) {
+        float sum = 0.0f;
+        for (int w = 0; w < kCW; ++w) sum += S.wss[w * kMaxTok + tid];
+        S.inv[tid] = rsqrtf(sum / float(K) + m.eps);
+      }
+      cbar();
+    }
+    if (tid == 0 && base == 0) trace_put(P, l, st_id, 14, clock64());
+#pragma unroll
+    for (int r = 0; r < kXR; ++r) {
+      const int idx = base + r * kCT + tid;
+      if (idx >= total) continue;  // warp-uniform
+      const int t = idx / nch, ch = idx - t * nch;
+      uint32_t u[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+      if (norm) {
+        const float inv = S.inv[t];
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(nw + 8 * ch));
+        const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          u[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(u[i] & 0xFFFFu) * inv))) |
+                 (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(u[i] >> 16) * inv))) << 16);
+      }
+      float sum = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sum += bfv(u[q] & 0xFFFFu) + __uint_as_float(u[q] & 0xFFFF0000u);
+      for (int o = 1; o < cpg; o <<= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+      // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
+      *reinterpret_cast<uint4*>(sx + t * P.xpitch + ch * 16) =
+          make_uint4(__byte_perm(u[0], u[2], 0x5410), __byte_perm(u[0], u[2], 0x7632),
+                     __byte_perm(u[1], u[3], 0x5410), __byte_perm(u[1], u[3], 0x7632));
+      if (ch % cpg == 0) sXS[(ch / cpg) * 8 + t] = sum;
+    }
+  }
+  if (tid == 0) trace_put(P, l, st_id, 15, clock64());
+}
+
+// One GEMV stage of layer l for this CTA's slabs of it.  False on a failed wait.
+template <int SPS>
+__device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, int g, int l) {
+  const i4b_decode_model& m = P.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int ib = 0, n = 0;
+  for (int i = 0; i < S.nit; ++i) {
+    if (S.stage[i] < g) ++ib;
+    else if (S.stage[i] == g) ++n;
+  }
+  if (n == 0) return true;
+  const int st_id = g == G_QKV ? C_QKV : g == G_O ? C_O : g == G_GU ? C_GU : C_DOWN;
+  stamp(P, l, st_id, 0);
+  const unsigned int* abort_word = P.ctr + P.i_abort;
+  // ---- dependency: every output of the previous stage
+  if (tid == 0) {
+    const unsigned int* c = nullptr;
+    unsigned int target = 0;
+    if (g == G_QKV) {
+      if (l > 0) c = P.ctr + (l - 1) * C_LAYER + C_DOWN, target = unsigned(P.nslab[G_DOWN]);
+    } else if (g == G_O) {
+      c = P.ctr + l * C_LAYER + C_ATTN, target = unsigned(m.batch * m.kv_heads);
+    } else if (g == G_GU) {
+      c = P.ctr + l * C_LAYER + C_O, target = unsigned(P.nslab[G_O]);
+    } else {
+      c = P.ctr + l * C_LAYER + C_GU, target = unsigned(P.nslab[G_GU]);
+    }
+    S.flag = (c == nullptr || wait_counter(c, target, abort_word)) ? 1 : 0;
+  }
+  cbar();
+  if (!S.flag) return false;
+  stamp(P, l, st_id, 1);
+  const int K = g == G_DOWN ? m.intermediate : (g == G_O ? P.q_n : m.hidden);
+  stage_x(P, S, smem, g, l, K);
+  cbar();
+  stamp(P, l, st_id, 2);
+  // residual inputs of the o_proj / down_proj epilogue: loaded here, consumed after the pieces
+  uint16_t* h = static_cast<uint16_t*>(m.h_out);
+  const int H = m.hidden;
+  const int B = m.batch;
+  constexpr int kRes = kResPerThread;
+  uint16_t res[kRes];
+  if (g == G_O || g == G_DOWN) {
+#pragma unroll
+    for (int k = 0; k < kRes; ++k) {
+      const int idx = tid + k * kCT;
+      if (idx < n * B * 32) {
+        const int i = idx / (B * 32), rem = idx - i * B * 32, b = rem / 32, col = rem % 32;
+        const int64_t nn = int64_t(S.slab[ib + i]) * 32 + col;
+        if (g == G_O && l == 0) {
+          int64_t id = m.tokens[b];
+          if (id < 0 || id >= m.vocab) id = 0;
+          res[k] = __ldg(static_cast<const uint16_t*>(m.embed) + id * H + nn);
+        } else {
+          res[k] = ldcg16(h + int64_t(b) * H + nn);
+        }
+      }
+    }
+  }
+
+  // ---- pieces: piece q = i * Pc + p of this stage goes to warp q % 8
+  const int Pc = P.npiece[g], J = Pc < 8 ? Pc : 8;
+  float* part = reinterpret_cast<float*>(smem + P.off_part);
+  const int r = lane >> 2, c = lane & 3;
+  const uint8_t* xl = smem + P.off_x + min(r, B - 1) * P.xpitch + 16 * c;
+  const float* xsl = reinterpret_cast<const float*>(smem + P.off_xs) + 2 * c;
+  const int gpp = kPieceK / m.group_size;  // groups per piece
+  bool ok = true;
+  float acc[2][4];
+  int cur = -1, cur_j = 0;
+  auto flush = [&](int i, int j) {
+    float* pp = part + (i * J + j) * (B * 32);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 4 * r + 2 * t + (e >> 1), tok = 2 * c + (e & 1);
+        if (tok < B) pp[tok * 32 + col] = acc[t][e];
+      }
+  };
+  const int total = n * Pc;
+  const int seq0 = l * S.ppl;
+  if (tid == 0) trace_put(P, l, st_id, 11, S.prod_seq - (seq0 + S.poff[ib]));
+  long long t_wait = 0, t_mma = 0;
+  int npc = 0;
+  for (int q = warp; q < total; q += kCW) {
+    const int i = q / Pc, p = q - i * Pc;
+    if (i != cur) {
+      if (cur >= 0) flush(cur, cur_j);
+      cur = i;
+      cur_j = p & 7;
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+    }
+    const int seq = seq0 + S.poff[ib + i] + p;
+    const int slot = seq % P.nslot;
+    const long long c0 = clock64();
+    if (!wait_slot(&S.full[slot], uint32_t(seq / P.nslot) & 1u, abort_word)) {
+      ok = false;
+      break;
+    }
+    const long long c1 = clock64();
+    piece_mma<SPS>(smem + slot * P.piece_bytes, xl + p * (kPieceK / 32) * 64, xsl + p * gpp * 8, lane, acc);
+    t_wait += c1 - c0;
+    t_mma += clock64() - c1;
+    ++npc;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.empty[slot]);
+  }
+  if (ok && cur >= 0) flush(cur, cur_j);
+  if (tid == 0) {
+    trace_put(P, l, st_id, 8, t_wait);
+    trace_put(P, l, st_id, 9, t_mma);
+    trace_put(P, l, st_id, 10, npc);
+  }
+  if (!ok && lane == 0) S.flag = 0;
+  cbar();
+  if (!S.flag) return false;
+  stamp(P, l, st_id, 3);
+
+  // ---- epilogue: fixed-order sum of the partials of each slab, then the stage's output operation
+  if (g == G_GU) {
+    for (int idx = tid; idx < n * B * 16; idx += kCT) {
+      const int i = idx / (B * 16), rem = idx - i * B * 16, b = rem / 16, pr = rem % 16;
+      float gs = 0.0f, us = 0.0f;
+      for (int j = 0; j < J; ++j) {
+        const float* pp = part + (i * J + j) * (B * 32) + b * 32;
+        gs += pp[2 * pr];
+        us += pp[2 * pr + 1];
+      }
+      const float gt = bfv(bfr(gs)), up = bfv(bfr(us));
+      const float sl = bfv(bfr(gt / (1.0f + expf(-gt))));
+      P.act[int64_t(b) * m.intermediate + int64_t(S.slab[ib + i]) * 16 + pr] = uint16_t(bfr(sl * up));
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kRes; ++k) {
+      const int idx = tid + k * kCT;
+      if (idx >= n * B * 32) break;
+      const int i = idx / (B * 32), rem = idx - i * B * 32, b = rem / 32, col = rem % 32;
+      float s = 0.0f;
+      for (int j = 0; j < J; ++j) s += part[(i * J + j) * (B * 32) + b * 32 + col];
+      const int64_t nn = int64_t(S.slab[ib + i]) * 32 + col;
+      if (g == G_QKV) P.qkv[int64_t(b) * P.qkv_n + nn] = uint16_t(bfr(s));
+      else h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(s))));
+    }
+  }
+  cbar();
+  stamp(P, l, st_id, 4);
+  if (tid == 0) {
+    __threadfence();
+    stamp(P, l, st_id, 5);
+    atomicAdd(P.ctr + l * C_LAYER + st_id, unsigned(n));
+  }
+  stamp(P, l, st_id, 6);
+  return true;
+}
+
+// Attention item a = (token b, kv head, split j) of layer l: GS query heads over cache positions of split j.
+template <int GS>
+__device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* smem, int l, int a) {
+  const i4b_decode_model& m = P.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nkv = m.kv_heads, ns = P.nsplit, nq = m.heads;
+  const int b = a / (nkv * ns), kvh = (a / ns) % nkv, j = a % ns;
+  const unsigned int* abort_word = P.ctr + P.i_abort;
+  stamp(P, l, C_ATTN, 0);
+  if (tid == 0) S.flag = wait_counter(P.ctr + l * C_LAYER + C_QKV, unsigned(P.nslab[G_QKV]), abort_word) ? 1 : 0;
+  cbar();
+  if (!S.flag) return false;
+  stamp(P, l, C_ATTN, 1);
+  float* qs = reinterpret_cast<float*>(smem + P.off_x);  // [GS][64] rotated queries
+  float* sc = qs + GS * kHD;                              // [GS][64] scores, then probabilities
+  float* sm = sc + GS * kHD;                              // [GS] running max, [GS] running sum, [GS] rescale
+  float* sl = sm + GS;
+  float* scr = sl + GS;
+  const int64_t pos = *m.pos;
+  const bool pvalid = pos >= 0 && pos < m.max_seq;
+  const int Lp = pvalid ? int(pos) + 1 : 0;
+  const int chunk = (Lp + ns - 1) / ns;
+  const int i0 = j * chunk, i1 = min(Lp, i0 + chunk);
+  const uint16_t* qrow = P.qkv + int64_t(b) * P.qkv_n;
+  const uint16_t* cosT = static_cast<const uint16_t*>(m.cos_table);
+  const uint16_t* sinT = static_cast<const uint16_t*>(m.sin_table);
+  const int64_t head_stride = int64_t(m.max_seq) * kHD;
+  const int64_t cache_off = ((int64_t(l) * m.cache_batch + b) * nkv + kvh) * head_stride;
+  uint16_t* kc = static_cast<uint16_t*>(m.k_cache) + cache_off;
+  uint16_t* vc = static_cast<uint16_t*>(m.v_cache) + cache_off;
+  // rotary embedding, apply_rotary_pos_emb's rounding: bf16(bf16(t * cos) + bf16(rotate_half(t) * sin))
+  float c0 = 0.f, c1 = 0.f, s0 = 0.f, s1 = 0.f;
+  if (pvalid) {
+    c0 = bfv(__ldg(cosT + pos * kHD + lane));
+    c1 = bfv(__ldg(cosT + pos * kHD + lane + 32));
+    s0 = bfv(__ldg(sinT + pos * kHD + lane));
+    s1 = bfv(__ldg(sinT + pos * kHD + lane + 32));
+  }
+  for (int hh = warp; hh < GS; hh += kCW) {
+    const uint16_t* src = qrow + (kvh * GS + hh) * kHD;
+    const float x0 = bfv(ldcg16(src + lane)), x1 = bfv(ldcg16(src + lane + 32));
+    qs[hh * kHD + lane] = bfv(bfr(bfv(bfr(x0 * c0)) + bfv(bfr(-x1 * s0))));
+    qs[hh * kHD + lane + 32] = bfv(bfr(bfv(bfr(x1 * c1)) + bfv(bfr(x0 * s1))));
+  }
+  if (pvalid && pos >= i0 && pos < i1) {  // this split holds the new position: write k and v to the caches
+    if (warp == kCW - 1) {
+      const uint16_t* src = qrow + (nq + kvh) * kHD;
+      const float x0 = bfv(ldcg16(src + lane)), x1 = bfv(ldcg16(src + lane + 32));
+      kc[pos * kHD + lane] = uint16_t(bfr(bfv(bfr(x0 * c0)) + bfv(bfr(-x1 * s0))));
+      kc[pos * kHD + lane + 32] = uint16_t(bfr(bfv(bfr(x1 * c1)) + bfv(bfr(x0 * s1))));
+    } else if (warp == kCW - 2) {
+      const uint16_t* src = qrow + (nq + nkv + kvh) * kHD;
+      vc[pos * kHD + lane] = ldcg16(src + lane);
+      vc[pos * kHD + lane + 32] = ldcg16(src + lane + 32);
+    }
+  }
+  if (tid < GS) {
+    sm[tid] = -INFINITY;
+    sl[tid] = 0.0f;
+  }
+  cbar();  // rotated queries ready, the new cache row visible to this CTA
+  stamp(P, l, C_ATTN, 2);
+
+  float acc[GS][8];
+#pragma unroll
+  for (int hh = 0; hh < GS; ++hh)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[hh][e] = 0.0f;
+  const float scale = m.attn_scale;
+  for (int blk = i0; blk < i1; blk += 64) {
+    // this block's keys (thread: position tid / 4, 16 dims) and values (warp w: dims 8w..8w+7 of positions
+    // lane and lane + 32) are all put in flight first
+    const int i = tid >> 2, qd = tid & 3, pi = blk + i;
+    uint4 k0 = make_uint4(0u, 0u, 0u, 0u), k1 = k0, vv[2] = {k0, k0};
+    if (pi < i1) {
+      k0 = ldcg128(kc + int64_t(pi) * kHD + 16 * qd);
+      k1 = ldcg128(kc + int64_t(pi) * kHD + 16 * qd + 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      if (blk + lane + 32 * u < i1) vv[u] = ldcg128(vc + int64_t(blk + lane + 32 * u) * kHD + 8 * warp);
+    {  // scores
+      float d[GS];
+#pragma unroll
+      for (int hh = 0; hh < GS; ++hh) d[hh] = 0.0f;
+      if (pi < i1) {
+        const uint32_t u[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float klo = bfv(u[e] & 0xFFFFu), khi = bfv(u[e] >> 16);
+#pragma unroll
+          for (int hh = 0; hh < GS; ++hh) {
+            d[hh] = fmaf(qs[hh * kHD + 16 * qd + 2 * e], klo, d[hh]);
+            d[hh] = fmaf(qs[hh * kHD + 16 * qd + 2 * e + 1], khi, d[hh]);
+          }
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < GS; ++hh) {
+        d[hh] += __shfl_xor_sync(0xFFFFFFFFu, d[hh], 1);
+        d[hh] += __shfl_xor_sync(0xFFFFFFFFu, d[hh], 2);
+      }
+      if (qd == 0) {
+#pragma unroll
+        for (int hh = 0; hh < GS; ++hh) sc[hh * kHD + i] = pi < i1 ? d[hh] * scale : -INFINITY;
+      }
+    }
+    cbar();
+    for (int hh = warp; hh < GS; hh += kCW) {  // online softmax of head hh over this block
+      const float x0 = sc[hh * kHD + lane], x1 = sc[hh * kHD + lane + 32];
+      float mb = fmaxf(x0, x1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, o));
+      const float mo = sm[hh], mn = fmaxf(mo, mb);
+      const float p0 = expf(x0 - mn), p1 = expf(x1 - mn);
+      float su = p0 + p1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) su += __shfl_xor_sync(0xFFFFFFFFu, su, o);
+      sc[hh * kHD + lane] = p0;
+      sc[hh * kHD + lane + 32] = p1;
+      __syncwarp();
+      if (lane == 0) {
+        const float corr = expf(mo - mn);  // 0 for the first block (mo = -inf)
+        scr[hh] = corr;
+        sl[hh] = sl[hh] * corr + su;
+        sm[hh] = mn;
+      }
+    }
+    cbar();
+    {  // o += p . V: warp w owns dims 8w..8w+7, lane the positions lane and lane + 32 of the block
+#pragma unroll
+      for (int hh = 0; hh < GS; ++hh) {
+        const float corr = scr[hh];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[hh][e] *= corr;
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (blk + lane + 32 * u < i1) {
+          const uint32_t w[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+          for (int hh = 0; hh < GS; ++hh) {
+            const float pr = sc[hh * kHD + lane + 32 * u];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              acc[hh][2 * e] = fmaf(pr, bfv(w[e] & 0xFFFFu), acc[hh][2 * e]);
+              acc[hh][2 * e + 1] = fmaf(pr, bfv(w[e] >> 16), acc[hh][2 * e + 1]);
+            }
+          }
+        }
+      }
+    }
+    cbar();  // the block's probabilities are read before the next block's scores overwrite them
+  }
+#pragma unroll
+  for (int hh = 0; hh < GS; ++hh)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float v = acc[hh][e];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+      acc[hh][e] = v;
+    }
+  float* mine = P.apart + int64_t(a) * GS * kPartRow;
+  if (lane == 0) {
+#pragma unroll
+    for (int hh = 0; hh < GS; ++hh)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mine[hh * kPartRow + 8 * warp + e] = acc[hh][e];
+  }
+  if (tid < GS) {
+    const bool any = i1 > i0;
+    mine[tid * kPartRow + 64] = any ? sm[tid] : -INFINITY;
+    mine[tid * kPartRow + 65] = any ? sl[tid] : 0.0f;
+  }
+  cbar();
+  stamp(P, l, C_ATTN, 3);
+  unsigned int* ticket = P.ctr + P.i_ticket + b * nkv + kvh;
+  if (tid == 0) {
+    __threadfence();
+    stamp(P, l, C_ATTN, 4);
+    S.flag = atomicAdd(ticket, 1u) == unsigned(ns - 1) ? 2 : 1;
+  }
+  cbar();
+  stamp(P, l, C_ATTN, 5);
+  if (S.flag != 2) return true;
+  // last split of (b, kvh): out = sum_j o_j e^(m_j - M) / sum_j l_j e^(m_j - M), splits in order.  All
+  // partials are copied to shared memory first, every load in flight at once.
+  __threadfence();
+  const float4* base = reinterpret_cast<const float4*>(P.apart + int64_t(a - j) * GS * kPartRow);
+  // [ns][GS][kPartRow] partials, 16-byte aligned after the rescale factors
+  float4* cm = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(scr + GS) + 15) & ~uintptr_t(15));
+  const int n4 = ns * GS * kPartRow / 4;
+  for (int q0 = tid; q0 < n4; q0 += 4 * kCT) {
+    float4 t4[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (q0 + u * kCT < n4) t4[u] = __ldcg(base + q0 + u * kCT);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (q0 + u * kCT < n4) cm[q0 + u * kCT] = t4[u];
+  }
+  cbar();
+  const float* cf = reinterpret_cast<const float*>(cm);
+  for (int idx = tid; idx < GS * kHD; idx += kCT) {
+    const int hh = idx / kHD, d = idx % kHD;
+    float M = -INFINITY;
+    for (int jj = 0; jj < ns; ++jj) M = fmaxf(M, cf[(jj * GS + hh) * kPartRow + 64]);
+    float num = 0.0f, den = 0.0f;
+    for (int jj = 0; jj < ns; ++jj) {
+      const float* pj = cf + (jj * GS + hh) * kPartRow;
+      const float lj = pj[65];
+      const float w = lj > 0.0f ? expf(pj[64] - M) : 0.0f;
+      num = fmaf(pj[d], w, num);
+      den = fmaf(lj, w, den);
+    }
+    P.att[int64_t(b) * P.q_n + (kvh * GS + hh) * kHD + d] = Lp > 0 ? uint16_t(bfr(num / den)) : uint16_t(0);
+  }
+  cbar();
+  if (tid == 0) {
+    *ticket = 0u;
+    __threadfence();
+    atomicAdd(P.ctr + l * C_LAYER + C_ATTN, 1u);
+  }
+  stamp(P, l, C_ATTN, 6);
+  return true;
+}
+
+template <int SPS, int GS>
+__global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid_constant__ DkParams Pg) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Smem S;
+  __shared__ DkHot P_s;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  static_assert(sizeof(DkHot) % 4 == 0, "word copy");
+  for (int i = tid; i < int(sizeof(DkHot) / 4); i += kThreads)
+    reinterpret_cast<uint32_t*>(&P_s)[i] = reinterpret_cast<const uint32_t*>(&Pg.h)[i];
+  __syncthreads();
+  const DkHot& P = P_s;
+  const i4b_decode_model& m = P.m;
+  const unsigned int* abort_word = P.ctr + P.i_abort;
+  if (tid == 0) {
+    const int cta = blockIdx.x;
+    const int nit = Pg.nitems[cta];
+    int off = 0;
+    for (int i = 0; i < nit; ++i) {
+      const uint16_t it = Pg.items[cta][i];
+      S.stage[i] = uint8_t(it >> 14);
+      S.slab[i] = uint16_t(it & 0x3FFFu);
+      S.poff[i] = uint16_t(off);
+      off += P.npiece[it >> 14];
+    }
+    S.nit = nit;
+    S.ppl = off;
+    S.flag = 1;
+    S.prod_seq = 0;
+    for (int s = 0; s < P.nslot; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  bool ok = true;
+  if (warp == kCW) {
+    // ---- producer: stream this CTA's pieces, layer after layer, into the ring
+    if (lane == 0) {
+      uint64_t policy;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      const uint32_t ring = smem_u32(smem);
+      const uint8_t* wsrc[4] = {static_cast<const uint8_t*>(m.w_qkv), static_cast<const uint8_t*>(m.w_o),
+                                static_cast<const uint8_t*>(m.w_gu), static_cast<const uint8_t*>(m.w_down)};
+      int seq = 0;
+      for (int l = 0; l < m.layers && ok; ++l) {
+        for (int i = 0; i < S.nit && ok; ++i) {
+          const int g = S.stage[i], Pc = P.npiece[g];
+          const uint8_t* src = wsrc[g] + int64_t(l) * P.layer_bytes[g] + int64_t(S.slab[i]) * Pc * P.piece_bytes;
+          for (int p = 0; p < Pc; ++p, ++seq) {
+            const int slot = seq % P.nslot;
+            if (seq >= P.nslot && !wait_slot(&S.empty[slot], uint32_t(seq / P.nslot - 1) & 1u, abort_word)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&S.full[slot], uint32_t(P.piece_bytes));
+            bulk_g2s(ring + slot * P.piece_bytes, src + int64_t(p) * P.piece_bytes, uint32_t(P.piece_bytes),
+                     &S.full[slot], policy);
+            S.prod_seq = seq + 1;
+          }
+        }
+      }
+      // every copy issued has landed before the CTA may exit (normally all were consumed already)
+      for (int s = max(0, seq - P.nslot); s < seq; ++s)
+        if (!mbar_wait(&S.full[s % P.nslot], uint32_t(s / P.nslot) & 1u)) ok = false;
+      if (!ok) {
+        atomicOr(&g_dk_err, I4B_DEVERR_WAIT_TIMEOUT);
+        atomicExch(P.ctr + P.i_abort, 1u);
+      }
+    }
+  } else {
+    // ---- compute warps: the stages of every layer in order
+    const int nattn = m.batch * m.kv_heads * P.nsplit;
+    for (int l = 0; l < m.layers && ok; ++l) {
+      ok = gemv_stage<SPS>(P, S, smem, G_QKV, l);
+      if (ok && int(blockIdx.x) < nattn) ok = attention_item<GS>(P, S, smem, l, blockIdx.x);
+      ok = ok && gemv_stage<SPS>(P, S, smem, G_O, l);
+      ok = ok && gemv_stage<SPS>(P, S, smem, G_GU, l);
+      ok = ok && gemv_stage<SPS>(P, S, smem, G_DOWN, l);
+    }
+    if (!ok && tid == 0) {
+      atomicOr(&g_dk_err, I4B_DEVERR_WAIT_TIMEOUT);
+      atomicExch(P.ctr + P.i_abort, 1u);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // token ids outside the vocabulary were read as row 0: reported, not silently used
+    if (blockIdx.x == 0)
+      for (int b = 0; b < m.batch; ++b)
+        if (m.tokens[b] < 0 || m.tokens[b] >= m.vocab) atomicOr(&g_dk_err, 2u);
+    __threadfence();
+    if (atomicAdd(P.ctr + P.i_done, 1u) == gridDim.x - 1) {  // the last CTA out resets the workspace counters
+      for (int i = 0; i < P.n_ctr; ++i) P.ctr[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+// Re-lay a quantize_int4 tensor triple into pieces: for slab s (columns 32s..32s+31) and piece p (k in
+// [512p, 512p + 512)), 16 steps x 32 lanes x 4 words -- lane (r, c) of step j holds qweight rows
+// 64p + 4j + c at columns 32s + 4r .. +3 -- then 512 / G records of 8 x 16 bytes (s0..s3, z0..z3 of
+// columns 32s + 4r .. +3).  One thread per 16-byte unit.
+__global__ void tile_w4_kernel(const int32_t* __restrict__ qw, int64_t sqk, const uint16_t* __restrict__ sc,
+                               const uint16_t* __restrict__ zr, int64_t ssg, int64_t N, int64_t K, int G,
+                               uint8_t* __restrict__ out, int piece_bytes) {
+  const int units_per_piece = piece_bytes / 16;
+  const int64_t npieces = (N / 32) * (K / kPieceK);
+  const int64_t total = npieces * units_per_piece;
+  for (int64_t u = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; u < total; u += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t piece = u / units_per_piece;
+    const int w = int(u - piece * units_per_piece);
+    const int64_t pk = K / kPieceK;
+    const int64_t s = piece / pk, p = piece - s * pk;
+    uint4 v;
+    if (w < 512) {
+      const int j = w / 32, lane = w % 32, r = lane >> 2, c = lane & 3;
+      const int32_t* src = qw + (64 * p + 4 * j + c) * sqk + 32 * s + 4 * r;
+      v = make_uint4(uint32_t(src[0]), uint32_t(src[1]), uint32_t(src[2]), uint32_t(src[3]));
+    } else {
+      const int rec = w - 512, gi = rec / 8, r = rec % 8;
+      const int64_t g = p * (kPieceK / G) + gi;
+      const uint16_t* s4 = sc + g * ssg + 32 * s + 4 * r;
+      const uint16_t* z4 = zr + g * ssg + 32 * s + 4 * r;
+      v = make_uint4(uint32_t(s4[0]) | (uint32_t(s4[1]) << 16), uint32_t(s4[2]) | (uint32_t(s4[3]) << 16),
+                     uint32_t(z4[0]) | (uint32_t(z4[1]) << 16), uint32_t(z4[2]) | (uint32_t(z4[3]) << 16));
+    }
+    reinterpret_cast<uint4*>(out)[u] = v;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+int piece_bytes_for(int G) { return kPieceW + (kPieceK / G) * 128; }
+
+struct Sched {
+  int max_part = 0;
+  int max_res = 0;  // most o_proj or down_proj slabs of one CTA
+  bool ok = false;
+  std::vector<uint8_t> nitems;
+  std::vector<uint16_t> items;  // [grid][kMaxItems]
+};
+
+// Longest-processing-time assignment of one layer's slabs to the CTAs: slabs by decreasing piece count
+// (then stage, then slab), each to the least-loaded CTA (lowest index on ties); each CTA's list is then
+// put in stage order.  The same lists serve every layer.
+Sched build_sched(int grid, const int nslab[4], const int npiece[4]) {
+  Sched sc;
+  sc.nitems.assign(grid, 0);
+  sc.items.assign(size_t(grid) * kMaxItems, 0);
+  std::vector<std::tuple<int, int, int>> all;  // (-pieces, stage, slab)
+  for (int g = 0; g < 4; ++g)
+    for (int s = 0; s < nslab[g]; ++s) all.emplace_back(-npiece[g], g, s);
+  std::sort(all.begin(), all.end());
+  std::vector<int64_t> load(grid, 0);
+  std::vector<std::vector<std::pair<int, int>>> lists(grid);
+  for (const auto& [neg, g, s] : all) {
+    int best = 0;
+    for (int c = 1; c < grid; ++c)
+      if (load[c] < load[best]) best = c;
+    load[best] += -neg;
+    lists[best].emplace_back(g, s);
+  }
+  for (int c = 0; c < grid; ++c) {
+    auto& L = lists[c];
+    if (L.size() > size_t(kMaxItems)) return sc;
+    std::sort(L.begin(), L.end());
+    sc.nitems[c] = uint8_t(L.size());
+    int cnt[4] = {0, 0, 0, 0};
+    for (size_t i = 0; i < L.size(); ++i) {
+      sc.items[size_t(c) * kMaxItems + i] = uint16_t((L[i].first << 14) | L[i].second);
+      ++cnt[L[i].first];
+    }
+    for (int g = 0; g < 4; ++g) sc.max_part = std::max(sc.max_part, cnt[g] * std::min(npiece[g], 8));
+    sc.max_res = std::max(sc.max_res, std::max(cnt[G_O], cnt[G_DOWN]));
+  }
+  sc.ok = true;
+  return sc;
+}
+
+struct Layout {
+  int nslab[4], npiece[4];
+  int64_t layer_bytes[4];
+  int piece_bytes, gqa, nsplit, qkv_n, q_n;
+  int n_ctr, i_ticket, i_done, i_abort;
+  size_t off_apart, off_qkv, off_att, off_act, total;
+};
+
+int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
+  if (m.layers <= 0 || m.hidden <= 0 || m.heads <= 0 || m.kv_heads <= 0 || m.intermediate <= 0 || m.vocab <= 0 ||
+      m.max_seq <= 0)
+    return I4B_ERR_SHAPE;
+  if (m.head_dim != kHD) return I4B_ERR_SHAPE;
+  if (m.batch < 1 || m.batch > kMaxTok || m.cache_batch < m.batch) return I4B_ERR_SHAPE;
+  if (m.group_size != 32 && m.group_size != 64 && m.group_size != 128) return I4B_ERR_GROUP;
+  if (m.heads % m.kv_heads != 0) return I4B_ERR_SHAPE;
+  const int gqa = m.heads / m.kv_heads;
+  if (gqa != 1 && gqa != 2 && gqa != 4 && gqa != 8) return I4B_ERR_SHAPE;
+  const int q_n = m.heads * kHD, qkv_n = (m.heads + 2 * m.kv_heads) * kHD;
+  if (m.hidden % kPieceK || m.intermediate % kPieceK || q_n % kPieceK) return I4B_ERR_SHAPE;
+  if (int64_t(m.batch) * m.hidden > int64_t(8) * kCT * kXR) return I4B_ERR_SHAPE;  // RMSNorm rows in one round
+  L->gqa = gqa;
+  L->q_n = q_n;
+  L->qkv_n = qkv_n;
+  L->piece_bytes = piece_bytes_for(m.group_size);
+  const int64_t N[4] = {qkv_n, m.hidden, 2 * int64_t(m.intermediate), m.hidden};
+  const int64_t K[4] = {m.hidden, q_n, m.hidden, m.intermediate};
+  for (int g = 0; g < 4; ++g) {
+    if (N[g] / 32 >= (1 << 14)) return I4B_ERR_SHAPE;
+    L->nslab[g] = int(N[g] / 32);
+    L->npiece[g] = int(K[g] / kPieceK);
+    L->layer_bytes[g] = int64_t(L->nslab[g]) * L->npiece[g] * L->piece_bytes;
+  }
+  const int items = m.batch * m.kv_heads;
+  L->nsplit = std::max(1, std::min(16, grid / items));
+  if (items > grid) return I4B_ERR_SHAPE;
+  // the counter region (zero between calls) has the same size for every batch, so one workspace serves all
+  L->i_ticket = m.layers * C_LAYER;
+  L->i_done = L->i_ticket + kMaxTok * m.kv_heads;
+  L->i_abort = L->i_done + 1;
+  L->n_ctr = L->i_abort + 1;
+  auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+  size_t off = al(size_t(L->n_ctr) * 4);
+  L->off_apart = off;
+  off = al(off + size_t(items) * L->nsplit * gqa * kPartRow * 4);
+  L->off_qkv = off;
+  off = al(off + size_t(m.batch) * qkv_n * 2);
+  L->off_att = off;
+  off = al(off + size_t(m.batch) * q_n * 2);
+  L->off_act = off;
+  off = al(off + size_t(m.batch) * m.intermediate * 2);
+  L->total = off;
+  return I4B_OK;
+}
+
+template <int SPS, int GS>
+cudaError_t launch_dk_t(const DkParams& p, int grid, size_t smem, cudaStream_t stream) {
+  auto kern = decode_layers_kernel<SPS, GS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int SPS>
+cudaError_t launch_dk_s(const DkParams& p, int grid, size_t smem, cudaStream_t stream) {
+  switch (p.h.gqa) {
+    case 1: return launch_dk_t<SPS, 1>(p, grid, smem, stream);
+    case 2: return launch_dk_t<SPS, 2>(p, grid, smem, stream);
+    case 4: return launch_dk_t<SPS, 4>(p, grid, smem, stream);
+    default: return launch_dk_t<SPS, 8>(p, grid, smem, stream);
+  }
+}
+
+}  // namespace
+
+size_t tile_w4_bytes(int64_t N, int64_t K, int G) {
+  if (N <= 0 || K <= 0 || N % 32 || K % kPieceK || (G != 32 && G != 64 && G != 128)) return 0;
+  return size_t(N / 32) * size_t(K / kPieceK) * size_t(piece_bytes_for(G));
+}
+
+cudaError_t launch_tile_w4(const int32_t* qw, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg,
+                           int64_t N, int64_t K, int G, void* out, cudaStream_t stream) {
+  const int64_t units = int64_t(tile_w4_bytes(N, K, G) / 16);
+  const int blocks = int(std::min<int64_t>((units + 255) / 256, 148 * 16));
+  tile_w4_kernel<<<blocks, 256, 0, stream>>>(qw, sqk, sc, zr, ssg, N, K, G, static_cast<uint8_t*>(out),
+                                             piece_bytes_for(G));
+  return cudaGetLastError();
+}
+
+int decode_layers_workspace(const i4b_decode_model& m, int num_sms, size_t* bytes) {
+  Layout L;
+  if (int st = make_layout(m, std::min(num_sms, kMaxCtas), &L)) return st;
+  *bytes = L.total;
+  return I4B_OK;
+}
+
+static unsigned long long* g_dk_trace = nullptr;
+static size_t g_dk_trace_bytes = 0;
+
+void set_decode_trace(void* buf, size_t bytes) {
+  g_dk_trace = static_cast<unsigned long long*>(buf);
+  g_dk_trace_bytes = bytes;
+}
+
+int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin, void* ws, size_t ws_bytes,
+                         cudaStream_t stream, cudaError_t* err) {
+  *err = cudaSuccess;
+  const int grid = std::min(num_sms, kMaxCtas);
+  Layout L;
+  if (int st = make_layout(m, grid, &L)) return st;
+  if (ws_bytes < L.total) return I4B_ERR_WORKSPACE;
+  // the schedule depends on the grid and the projection shapes only: built once per shape
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int, int, int, int>, Sched> cache;
+  const Sched* sc;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto key = std::make_tuple(grid, L.nslab[0], L.nslab[1], L.nslab[2], L.nslab[3], L.npiece[0], L.npiece[1],
+                               L.npiece[2], L.npiece[3]);
+    auto it = cache.find(key);
+    if (it == cache.end()) it = cache.emplace(key, build_sched(grid, L.nslab, L.npiece)).first;
+    sc = &it->second;
+  }
+  if (!sc->ok) return I4B_ERR_SHAPE;
+  if (sc->max_res * m.batch * 32 > kCT * kResPerThread) return I4B_ERR_SHAPE;
+
+  DkParams p;
+  memset(&p, 0, sizeof(p));
+  p.h.m = m;
+  for (int g = 0; g < 4; ++g) {
+    p.h.nslab[g] = L.nslab[g];
+    p.h.npiece[g] = L.npiece[g];
+    p.h.layer_bytes[g] = L.layer_bytes[g];
+  }
+  p.h.piece_bytes = L.piece_bytes;
+  p.h.nsplit = L.nsplit;
+  p.h.gqa = L.gqa;
+  p.h.qkv_n = L.qkv_n;
+  p.h.q_n = L.q_n;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  p.h.ctr = reinterpret_cast<unsigned int*>(w);
+  p.h.n_ctr = L.n_ctr;
+  p.h.i_ticket = L.i_ticket;
+  p.h.i_done = L.i_done;
+  p.h.i_abort = L.i_abort;
+  p.h.apart = reinterpret_cast<float*>(w + L.off_apart);
+  p.h.qkv = reinterpret_cast<uint16_t*>(w + L.off_qkv);
+  p.h.att = reinterpret_cast<uint16_t*>(w + L.off_att);
+  p.h.act = reinterpret_cast<uint16_t*>(w + L.off_act);
+  if (g_dk_trace && g_dk_trace_bytes >= size_t(grid) * m.layers * 5 * kTraceSlots * 8) p.h.trace = g_dk_trace;
+  for (int c = 0; c < grid; ++c) {
+    p.nitems[c] = sc->nitems[c];
+    for (int i = 0; i < kMaxItems; ++i) p.items[c][i] = sc->items[size_t(c) * kMaxItems + i];
+  }
+  // dynamic shared memory: ring | activations | group sums | partials; the attention scratch reuses the
+  // activation region
+  const int kmax = std::max(std::max(m.hidden, m.intermediate), L.q_n);
+  p.h.xpitch = 2 * kmax + 16;
+  auto al = [](int v) { return (v + 127) & ~127; };
+  // attention: queries, scores, running max / sum / rescale, then the partials of all splits when combining
+  const int attn_bytes = (2 * L.gqa * kHD + 3 * L.gqa + 4) * 4 + L.nsplit * L.gqa * kPartRow * 4;
+  const int x_bytes = al(std::max(m.batch * p.h.xpitch, attn_bytes));
+  const int xs_bytes = al((kmax / m.group_size) * 8 * 4);
+  const int part_bytes = al(sc->max_part * m.batch * 32 * 4);
+  const int fixed = x_bytes + xs_bytes + part_bytes;
+  const int avail = smem_optin - int(sizeof(Smem)) - 1024;
+  const int nslot = std::min(kMaxSlots, (avail - fixed) / p.h.piece_bytes);
+  if (nslot < 2) return I4B_ERR_SHAPE;
+  p.h.nslot = nslot;
+  p.h.off_x = nslot * p.h.piece_bytes;
+  p.h.off_xs = p.h.off_x + x_bytes;
+  p.h.off_part = p.h.off_xs + xs_bytes;
+  const size_t smem = size_t(p.h.off_part + part_bytes);
+  cudaError_t e;
+  switch (m.group_size) {
+    case 32: e = launch_dk_s<1>(p, grid, smem, stream); break;
+    case 64: e = launch_dk_s<2>(p, grid, smem, stream); break;
+    default: e = launch_dk_s<4>(p, grid, smem, stream); break;
+  }
+  if (e != cudaSuccess) {
+    *err = e;
+    return I4B_ERR_CUDA;
+  }
+  return I4B_OK;
+}
+
+unsigned int read_dk_error(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_dk_err, sizeof(v));
+  if (clear && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_dk_err, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace i4b

@@ -44,7 +44,8 @@ struct TcCfg {
   static constexpr int SZ_BYTES = INT4 ? 2 * 2 * BN * 2 : 0;  // scales + zeros, two group rows
   // TMA stages carry A (+ packed weights, scales, zeros for INT4, or the B tile for W16).  INT4 B tiles
   // are written by the dequant warps into their own NB-deep ring, decoupled from the TMA stages.
-  static constexpr int NB = INT4 ? 2 : 0;
+  // Four slots for 128-column tiles (a k-block's dequant, MMA and slot hand-back overlap); two for 256.
+  static constexpr int NB = INT4 ? (BN == 128 ? 4 : 2) : 0;
   static constexpr int STAGE_BYTES = INT4 ? (A_BYTES + P_BYTES + SZ_BYTES) : (A_BYTES + B_BYTES);
   static constexpr int BUDGET = 216 * 1024 - NB * B_BYTES;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
@@ -111,7 +112,8 @@ template <bool INT4, bool F16, int BN, int BMT>
 __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z, int M, int N,
-                   int K, int G, uint16_t* __restrict__ y, int64_t sym) {
+                   int K, int G, uint16_t* __restrict__ y, int64_t sym, int ksplit, float* __restrict__ partials,
+                   unsigned int* __restrict__ tickets) {
   using C = TcCfg<INT4, BN, BMT>;
   constexpr int S = C::STAGES;
   constexpr int NB = C::NB;
@@ -138,7 +140,11 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * C::BM;
-  const int KB = (K + C::BK - 1) / C::BK;
+  // split-K: this CTA owns k-blocks [kb0, kb1); kbl = kb - kb0 indexes the pipeline stages
+  const int KBT = (K + C::BK - 1) / C::BK;
+  const int kb0 = int((int64_t(blockIdx.z) * KBT) / ksplit), kb1 = int((int64_t(blockIdx.z + 1) * KBT) / ksplit);
+  const int KB = kb1 - kb0;
+  __shared__ int s_last;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -173,7 +179,7 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
-      for (int kp = S; kp < 2 * S && kp < KB; ++kp) {  // the first S k-blocks are loaded right away
+      for (int kp = kb0 + S; kp < kb0 + 2 * S && kp < kb1; ++kp) {  // the first S k-blocks are loaded right away
         tma_prefetch_l2_2d(&tm_x, kp * C::BK, m0);
         if constexpr (INT4) {
           tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
@@ -183,13 +189,14 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
           tma_prefetch_l2_2d(&tm_w, kp * C::BK, n0);
         }
       }
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % S, u = kb / S;
-        if (kb >= S && !mbar_wait(&empty[s], (u - 1) & 1)) { ok = false; break; }
+      for (int kbl = 0; kbl < KB; ++kbl) {
+        const int kb = kb0 + kbl;
+        const int s = kbl % S, u = kbl / S;
+        if (kbl >= S && !mbar_wait(&empty[s], (u - 1) & 1)) { ok = false; break; }
         // Pull the tiles of k-block kb + 2S into L2 now, so that their TMA loads, issued S k-blocks
         // from now, do not wait for HBM.
         const int kp = kb + 2 * S;
-        if (kp < KB) {
+        if (kp < kb1) {
           tma_prefetch_l2_2d(&tm_x, kp * C::BK, m0);
           if constexpr (INT4) {
             tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
@@ -207,7 +214,7 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
           tma_load_2d(sSZ(s), &tm_s, &full[s], n0, g_lo);
           tma_load_2d(sSZ(s) + 2 * BN * 2, &tm_z, &full[s], n0, g_lo);
         } else {
-          tma_load_2d(sB(kb), &tm_w, &full[s], kb * C::BK, n0);
+          tma_load_2d(sB(kbl), &tm_w, &full[s], kb * C::BK, n0);
         }
         ++issued;
       }
@@ -220,25 +227,25 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(F16 ? 0 : 1, 128, BN);
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % S, u = kb / S;
-        // The activation tile arrives on full[s]; INT4 weights come dequantized on bready[kb % NB].
+      for (int kbl = 0; kbl < KB; ++kbl) {
+        const int s = kbl % S, u = kbl / S;
+        // The activation tile arrives on full[s]; INT4 weights come dequantized on bready[kbl % NB].
         if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
         if constexpr (INT4) {
-          if (!mbar_wait(&bready[kb % NB], (kb / NB) & 1)) { ok = false; break; }
+          if (!mbar_wait(&bready[kbl % NB], (kbl / NB) & 1)) { ok = false; break; }
         }
         tc_fence_after();
         const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA(s)));
         const uint64_t adesc1 = umma_desc_sw128(smem_u32(sA(s) + C::A_BYTES / 2));
-        const uint64_t bdesc = umma_desc_sw128(smem_u32(sB(kb)));
+        const uint64_t bdesc = umma_desc_sw128(smem_u32(sB(kbl)));
 #pragma unroll
         for (int kk = 0; kk < C::BK / 16; ++kk) {
-          const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+          const uint32_t acc = (kbl | kk) != 0 ? 1u : 0u;
           umma_f16_ss(tmem, adesc0 + 2 * kk, bdesc + 2 * kk, idesc, acc);
           if constexpr (BMT == 2) umma_f16_ss(tmem + uint32_t(BN), adesc1 + 2 * kk, bdesc + 2 * kk, idesc, acc);
         }
         umma_commit(&empty[s]);
-        if constexpr (INT4) umma_commit(&bfree[kb % NB]);
+        if constexpr (INT4) umma_commit(&bfree[kbl % NB]);
       }
       umma_commit(tfull);  // also on the error path: completes once issued MMAs are done
     }
@@ -251,22 +258,22 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
       // Group bookkeeping without divisions: k-block kb covers k in [64 kb, 64 kb + 64); g_lo is the group
       // of its first k and g_end the first k of the next group.  The scale / zero parameters of a group
       // are computed once and kept while the group lasts (G >= 32, so a k-block touches at most 2 groups).
-      int g_lo = 0, g_end = G;
+      int g_lo = (kb0 * C::BK) / G, g_end = (g_lo + 1) * G;
       int g_cached = -1;
       DqParams pc{};
-      for (int kb = 0; kb < KB && ok; ++kb) {
-        const int s = kb % S, u = kb / S;
-        const int k_begin = kb * C::BK;
+      for (int kbl = 0; kbl < KB && ok; ++kbl) {
+        const int s = kbl % S, u = kbl / S;
+        const int k_begin = (kb0 + kbl) * C::BK;
         while (k_begin >= g_end) {
           ++g_lo;
           g_end += G;
         }
         if (!mbar_wait_sleep(&full[s], u & 1)) { ok = false; break; }
-        if (kb >= NB && !mbar_wait_sleep(&bfree[kb % NB], ((kb / NB) - 1) & 1)) { ok = false; break; }
+        if (kbl >= NB && !mbar_wait_sleep(&bfree[kbl % NB], ((kbl / NB) - 1) & 1)) { ok = false; break; }
         const uint32_t* P = reinterpret_cast<const uint32_t*>(sP(s));
         const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ(s));
         const uint16_t* Zs = Ss + 2 * BN;
-        uint8_t* Bs = sB(kb);
+        uint8_t* Bs = sB(kbl);
         if (g_cached != g_lo) {
           pc = dq_params<F16>(Ss[nl], Zs[nl]);
           g_cached = g_lo;
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bready[kb % NB]);
+        if (lane == 0) mbar_arrive(&bready[kbl % NB]);
       }
     }
     // ---- epilogue: TMEM -> registers -> y.  The dequant warps form DQ_WARPS / 4 sets of four (one per
@@ -308,6 +315,22 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
       uint32_t v[16];
       tmem_ld_32x32b_x16(tmem + (uint32_t(32 * q) << 16) + acc_col + uint32_t(c0), v);
       tmem_ld_wait();
+      if (ksplit > 1) {  // fp32 partial of this K split; the tile's last CTA adds the splits below
+        const int n = n0 + c0;
+        if (m < M) {
+          float* dst = partials + (int64_t(blockIdx.z) * M + m) * N + n;
+          if ((N % 4) == 0 && n + 16 <= N) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<uint4*>(dst)[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (n + i < N) dst[i] = __uint_as_float(v[i]);
+          }
+        }
+        continue;
+      }
       if (m < M) {
         uint32_t pk[8];
 #pragma unroll
@@ -340,6 +363,83 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (ksplit > 1) {
+    // The last CTA of this output tile (atomic ticket, no spinning) adds the ksplit fp32 partials in split
+    // order and writes y; then it resets the ticket for the next call.
+    const unsigned int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(tickets + tile, 1u) == unsigned(ksplit - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int64_t stride_z = int64_t(M) * N;
+    if (N % 4 == 0) {
+      // items of 4 consecutive columns; each thread keeps 4 items x ksplit (<= 4) float4 loads in flight
+      constexpr int NQ = BN / 4;
+      constexpr int ITEMS = C::BM * NQ;
+      for (int base = threadIdx.x; base < ITEMS; base += 4 * blockDim.x) {
+        float4 t[4][4];
+        int64_t off[4];
+        bool valid[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int idx = base + u * blockDim.x;
+          const int m = m0 + idx / NQ, n = n0 + 4 * (idx % NQ);
+          valid[u] = idx < ITEMS && m < M && n < N;
+          off[u] = valid[u] ? int64_t(m) * N + n : 0;
+        }
+#pragma unroll
+        for (int z = 0; z < 4; ++z)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            t[z][u] = (z < ksplit && valid[u]) ? __ldcg(reinterpret_cast<const float4*>(partials + off[u] + z * stride_z))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (!valid[u]) continue;
+          float4 a = t[0][u];
+#pragma unroll
+          for (int z = 1; z < 4; ++z)
+            if (z < ksplit) {  // split order
+              a.x += t[z][u].x;
+              a.y += t[z][u].y;
+              a.z += t[z][u].z;
+              a.w += t[z][u].w;
+            }
+          const int64_t m = off[u] / N, n = off[u] % N;
+          uint16_t* dst = y + m * sym + n;
+          if constexpr (F16) {
+            dst[0] = __half_as_ushort(__float2half_rn(a.x));
+            dst[1] = __half_as_ushort(__float2half_rn(a.y));
+            dst[2] = __half_as_ushort(__float2half_rn(a.z));
+            dst[3] = __half_as_ushort(__float2half_rn(a.w));
+          } else {
+            dst[0] = __bfloat16_as_ushort(__float2bfloat16_rn(a.x));
+            dst[1] = __bfloat16_as_ushort(__float2bfloat16_rn(a.y));
+            dst[2] = __bfloat16_as_ushort(__float2bfloat16_rn(a.z));
+            dst[3] = __bfloat16_as_ushort(__float2bfloat16_rn(a.w));
+          }
+        }
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < C::BM * BN; idx += blockDim.x) {
+        const int m = m0 + idx / BN, n = n0 + idx % BN;
+        if (m >= M || n >= N) continue;
+        const float* src = partials + int64_t(m) * N + n;
+        float t[4];
+#pragma unroll
+        for (int z = 0; z < 4; ++z) t[z] = z < ksplit ? __ldcg(src + z * stride_z) : 0.0f;
+        float acc = t[0];
+#pragma unroll
+        for (int z = 1; z < 4; ++z)
+          if (z < ksplit) acc += t[z];
+        if constexpr (F16) y[int64_t(m) * sym + n] = __half_as_ushort(__float2half_rn(acc));
+        else y[int64_t(m) * sym + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
+      }
+    }
+    if (threadIdx.x == 0) atomicExch(tickets + tile, 0u);
   }
 }
 
@@ -405,7 +505,8 @@ static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
 
 template <bool INT4, bool F16, int BN, int BMT>
 static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
-                                  int64_t sym, cudaStream_t stream) {
+                                  int64_t sym, int ksplit, float* partials, unsigned int* tickets,
+                                  cudaStream_t stream) {
   using C = TcCfg<INT4, BN, BMT>;
   const CUtensorMapDataType act = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap mx{}, mw{}, ms{}, mz{};
@@ -428,8 +529,9 @@ static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int
   auto kern = tc_gemm_kernel<INT4, F16, BN, BMT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM));
   if (e != cudaSuccess) return e;
-  dim3 grid(unsigned(cdiv(N, BN)), unsigned(cdiv(M, C::BM)));
-  kern<<<grid, C::THREADS, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym);
+  dim3 grid(unsigned(cdiv(N, BN)), unsigned(cdiv(M, C::BM)), unsigned(ksplit));
+  kern<<<grid, C::THREADS, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym, ksplit, partials,
+                                               tickets);
   return cudaGetLastError();
 }
 
@@ -439,22 +541,73 @@ static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int
 #define I4B_TC_FORCE 0
 #endif
 // Tile code: 1 -> 128 x 128, 2 -> 256 x 128 (two MMAs share a B tile), 3 -> 128 x 256, 4 -> 256 x 256.
-// The largest tile that still gives at least half a wave of CTAs: bigger tiles read fewer activation and
-// weight bytes per flop from L2.
-int tc_pick_bn(int64_t M, int64_t N, int num_sms) {
-  if (I4B_TC_FORCE) return I4B_TC_FORCE;
-  if (2 * cdiv(M, 256) * cdiv(N, 256) >= num_sms) return 4;
-  return 2 * cdiv(M, 256) * cdiv(N, 128) >= num_sms ? 2 : 1;
+// The plan minimises a cost model fitted to B200 measurements of this kernel (INT4, G = 128, 148 SMs):
+// a wave of CTAs costs F + c * (k-blocks per CTA) microseconds, with (F, c) = (4.0, 0.72) for 128 x 128,
+// (6.4, 0.74) for 256 x 128 and (7.5, 0.90) for 256 x 256 -- the small tiles are bound by per-CTA
+// latency, the large one by the tensor pipe -- and a K split adds 5 us + 17 us per MiB of fp32 partials
+// that the last CTA of a tile reads back.  Bigger tiles read fewer activation and weight bytes per flop;
+// splits fill the machine when there are few output tiles.
+static int g_tc_ovr_tile = 0, g_tc_ovr_splits = 0;
+
+void set_tc_override(int tile, int splits) {
+  g_tc_ovr_tile = tile >= 1 && tile <= 4 ? tile : 0;
+  g_tc_ovr_splits = splits >= 1 && splits <= 4 ? splits : 0;
+}
+
+static int64_t tc_tiles(int tile, int64_t M, int64_t N) {
+  const int64_t bm = (tile == 2 || tile == 4) ? 256 : 128, bn = (tile == 3 || tile == 4) ? 256 : 128;
+  return cdiv(M, bm) * cdiv(N, bn);
+}
+
+static double tc_cost(int tile, int splits, int64_t M, int64_t N, int64_t kb, int num_sms) {
+  const double F = tile == 4 ? 7.5 : tile == 2 ? 6.4 : 4.0;
+  const double c = tile == 4 ? 0.90 : tile == 2 ? 0.74 : 0.72;
+  const int64_t tiles = tc_tiles(tile, M, N);
+  const int64_t waves = cdiv(tiles * splits, int64_t(num_sms));
+  double t = double(waves) * (F + c * double(cdiv(kb, int64_t(splits))));
+  if (splits > 1) {
+    const double bm = (tile == 2 || tile == 4) ? 256 : 128, bn = (tile == 3 || tile == 4) ? 256 : 128;
+    t += 5.0 + 17.0 * double(splits) * bm * bn * 4.0 / double(1 << 20);
+  }
+  return t;
+}
+
+TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
+  const int64_t kb = cdiv(K, 64);
+  TcPlan best{1, 1};
+  double best_t = 1e30;
+  for (int tile : {4, 2, 1}) {
+    if (I4B_TC_FORCE && tile != I4B_TC_FORCE) continue;
+    if (g_tc_ovr_tile && tile != g_tc_ovr_tile) continue;
+    if (tile != 1 && M <= 128) continue;  // a 256-row tile would be half empty
+    for (int splits : {1, 2, 4}) {
+      if (g_tc_ovr_splits && splits != g_tc_ovr_splits) continue;
+      if (splits > 1 && (tc_tiles(tile, M, N) > kMaxTickets || kb < 4 * splits)) continue;
+      const double t = tc_cost(tile, splits, M, N, kb, num_sms);
+      if (t < best_t) {
+        best_t = t;
+        best = TcPlan{tile, splits};
+      }
+    }
+  }
+  if (I4B_TC_FORCE && best_t >= 1e30) best = TcPlan{I4B_TC_FORCE, 1};
+  if (g_tc_ovr_tile && best_t >= 1e30) best = TcPlan{g_tc_ovr_tile, 1};
+  return best;
+}
+
+size_t tc_partial_bytes(const TcPlan& p, int64_t M, int64_t N) {
+  return p.splits > 1 ? size_t(p.splits) * size_t(M) * size_t(N) * 4 : 0;
 }
 
 cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
-                      int64_t sym, int bn, cudaStream_t stream) {
-  // bn: tile code from tc_pick_bn
+                      int64_t sym, const TcPlan& plan, float* partials, unsigned int* tickets, cudaStream_t stream) {
+  const int bn = plan.tile, ks = plan.splits;
+  // bn: tile code, ks: K splits (from tc_plan)
 #define I4B_TC(I, F) \
-  return bn == 4   ? launch_tc_impl<I, F, 256, 2>(o, M, N, K, G, y, sym, stream) \
-         : bn == 2 ? launch_tc_impl<I, F, 128, 2>(o, M, N, K, G, y, sym, stream) \
-         : bn == 3 ? launch_tc_impl<I, F, 256, 1>(o, M, N, K, G, y, sym, stream) \
-                   : launch_tc_impl<I, F, 128, 1>(o, M, N, K, G, y, sym, stream)
+  return bn == 4   ? launch_tc_impl<I, F, 256, 2>(o, M, N, K, G, y, sym, ks, partials, tickets, stream) \
+         : bn == 2 ? launch_tc_impl<I, F, 128, 2>(o, M, N, K, G, y, sym, ks, partials, tickets, stream) \
+         : bn == 3 ? launch_tc_impl<I, F, 256, 1>(o, M, N, K, G, y, sym, ks, partials, tickets, stream) \
+                   : launch_tc_impl<I, F, 128, 1>(o, M, N, K, G, y, sym, ks, partials, tickets, stream)
   if (int4) {
     if (f16) I4B_TC(true, true);
     I4B_TC(true, false);

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "../../include/int4_b200.h"
+
 namespace i4b {
 
 // quantize.cu
@@ -72,9 +74,15 @@ struct TcOperands {
   const uint16_t* zr;
   int64_t ssg;
 };
-int tc_pick_bn(int64_t M, int64_t N, int num_sms);
+struct TcPlan {
+  int tile;    // 1: 128 x 128, 2: 256 x 128, 3: 128 x 256, 4: 256 x 256
+  int splits;  // K splits (fp32 partials in the workspace when > 1)
+};
+TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int num_sms);
+void set_tc_override(int tile, int splits);  // tuning: 0 keeps the automatic choice
+size_t tc_partial_bytes(const TcPlan& p, int64_t M, int64_t N);
 cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
-                      int64_t sym, int bn, cudaStream_t stream);
+                      int64_t sym, const TcPlan& plan, float* partials, unsigned int* tickets, cudaStream_t stream);
 cudaError_t launch_repack(const void* in, int esize, int64_t rows, int64_t cols_in, int64_t sr, int64_t sc, void* out,
                           int64_t cols_out, cudaStream_t stream);
 unsigned int read_tc_error(bool clear);
@@ -89,5 +97,15 @@ cudaError_t launch_decode_attn(const uint16_t* q, const uint16_t* kc, const uint
                                uint16_t* out, int B, int nq, int nkv, int max_seq, float scale, cudaStream_t s);
 cudaError_t launch_silu_mul(const uint16_t* gu, uint16_t* y, int B, int I, cudaStream_t s);
 cudaError_t launch_argmax(const uint16_t* x, int64_t rows, int64_t n, int64_t* out, cudaStream_t s);
+
+// decode_persistent.cu (all decoder layers of a decode step in one cooperative launch)
+size_t tile_w4_bytes(int64_t N, int64_t K, int G);
+cudaError_t launch_tile_w4(const int32_t* qw, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg,
+                           int64_t N, int64_t K, int G, void* out, cudaStream_t stream);
+int decode_layers_workspace(const i4b_decode_model& m, int num_sms, size_t* bytes);
+int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin, void* ws, size_t ws_bytes,
+                         cudaStream_t stream, cudaError_t* err);
+unsigned int read_dk_error(bool clear);
+void set_decode_trace(void* buf, size_t bytes);
 
 }  // namespace i4b

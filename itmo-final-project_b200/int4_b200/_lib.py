@@ -46,8 +46,24 @@ _SIGNATURES = {
     "i4b_argmax_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp]),
     "i4b_set_pdl": (None, [_c_int]),
     "i4b_set_skinny_override": (None, [_c_int, _c_int, _c_int]),
+    "i4b_set_gemm_override": (None, [_c_int, _c_int]),
     "i4b_device_error_flags": (_c_int, [_c_int, _c_int]),
+    "i4b_tile_w4_bytes": (_c_size, [_c_i64, _c_i64, _c_int]),
+    "i4b_tile_w4": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
+    "i4b_decode_workspace_size": (_c_int, [_c_vp, ctypes.POINTER(_c_size)]),
+    "i4b_decode_layers": (_c_int, [_c_vp, _c_vp, _c_size, _c_vp]),
+    "i4b_set_decode_trace": (None, [_c_vp, _c_size]),
 }
+
+
+class DecodeModel(ctypes.Structure):
+    """``i4b_decode_model`` of include/int4_b200.h."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in ("layers", "hidden", "heads", "kv_heads", "head_dim", "intermediate",
+                                              "vocab", "group_size", "batch", "max_seq", "cache_batch")] + \
+               [("eps", ctypes.c_float), ("attn_scale", ctypes.c_float)] + \
+               [(n, ctypes.c_void_p) for n in ("tokens", "pos", "embed", "w_qkv", "w_o", "w_gu", "w_down", "ln1",
+                                               "ln2", "cos_table", "sin_table", "k_cache", "v_cache", "h_out")]
 
 
 class Int4B200Error(RuntimeError):

@@ -25,6 +25,8 @@ step can be captured in a CUDA graph.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.nn.functional as F
 
@@ -163,6 +165,94 @@ def argmax_last(x: torch.Tensor) -> torch.Tensor:
     return out.view(*x.shape[:-1], 1)
 
 
+def tile_w4(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """The quantize_int4 triple re-laid into the 32-column x 512-k pieces the persistent decode streams.
+
+    ``out`` (uint8, 16-byte aligned, at least ``tile_w4_bytes`` long) receives the pieces when given.
+    """
+    K, N = qweight.shape[0] * 8, qweight.shape[1]
+    G = K // scales.shape[0]
+    L = _lib.lib()
+    nbytes = L.i4b_tile_w4_bytes(N, K, G)
+    if nbytes == 0:
+        raise ValueError(f"tile_w4: N={N} must be a multiple of 32, K={K} of 512, group size {G} in (32, 64, 128)")
+    if out is None:
+        out = torch.empty(nbytes, dtype=torch.uint8, device=qweight.device)
+    assert out.dtype == torch.uint8 and out.numel() >= nbytes and out.is_contiguous()
+    st = L.i4b_tile_w4(qweight.data_ptr(), N, qweight.stride(0), scales.data_ptr(), zeros.data_ptr(), scales.stride(0),
+                       K, G, out.data_ptr(), _stream(qweight))
+    _lib.check(st, "tile_w4")
+    return out
+
+
+def interleave_gate_up(q: tuple[torch.Tensor, torch.Tensor, torch.Tensor], inter: int):
+    """Columns of a stacked (gate | up) quantize_int4 triple reordered to gate 0, up 0, gate 1, up 1, ...
+
+    Quantization is per output column, so this is the same bits as quantizing the interleaved weight.
+    """
+    j = torch.arange(inter, device=q[0].device)
+    perm = torch.stack([j, j + inter], dim=1).reshape(-1)
+    return tuple(t[:, perm].contiguous() for t in q)
+
+
+class PersistentDecoder:
+    """Every decoder layer of a single-token decode step in one launch (``i4b_decode_layers``).
+
+    Holds the tiled weights of all layers (one buffer per projection kind), the stacked norm weights,
+    the residual-stream buffer and the workspace (zeroed once; every launch leaves it zero).
+    """
+
+    def __init__(self, model: "LlamaTP", layer_q: list, group_size: int):
+        dev = model.device
+        H, I = model.hidden, model.inter_l
+        nq, nkv = model.nh_l, model.nkv_l
+        Lc = len(layer_q)
+        L = _lib.lib()
+        shapes = {"qkv": ((nq + 2 * nkv) * 64, H), "o": (H, nq * 64), "gu": (2 * I, H), "down": (H, I)}
+        self.tiles = {}
+        for kind, (N, K) in shapes.items():
+            per = L.i4b_tile_w4_bytes(N, K, group_size)
+            buf = torch.empty(Lc * per, dtype=torch.uint8, device=dev)
+            for li, qd in enumerate(layer_q):
+                q = qd[kind]
+                if kind == "gu":
+                    q = interleave_gate_up(q, I)
+                tile_w4(*q, out=buf[li * per:(li + 1) * per])
+            self.tiles[kind] = buf
+        self.ln1 = torch.stack([ly["ln1"] for ly in model.layers]).contiguous()
+        self.ln2 = torch.stack([ly["ln2"] for ly in model.layers]).contiguous()
+        self.h = torch.empty(model.max_batch, H, device=dev, dtype=torch.bfloat16)
+        m = _lib.DecodeModel()
+        m.layers, m.hidden, m.heads, m.kv_heads, m.head_dim = Lc, H, nq, nkv, 64
+        m.intermediate, m.vocab, m.group_size = I, model.embed.shape[0], group_size
+        m.batch, m.max_seq, m.cache_batch = model.max_batch, model.max_seq, model.max_batch
+        m.eps, m.attn_scale = model.eps, 64 ** -0.5
+        m.embed = model.embed.data_ptr()
+        m.w_qkv, m.w_o = self.tiles["qkv"].data_ptr(), self.tiles["o"].data_ptr()
+        m.w_gu, m.w_down = self.tiles["gu"].data_ptr(), self.tiles["down"].data_ptr()
+        m.ln1, m.ln2 = self.ln1.data_ptr(), self.ln2.data_ptr()
+        m.cos_table, m.sin_table = model.cos.data_ptr(), model.sin.data_ptr()
+        m.k_cache, m.v_cache = model.k_cache.data_ptr(), model.v_cache.data_ptr()
+        m.h_out = self.h.data_ptr()
+        self.m = m
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(L.i4b_decode_workspace_size(ctypes.byref(m), ctypes.byref(nbytes)), "decode_workspace_size")
+        self.ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=dev)
+
+    def run(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """Residual stream [B, H] after the last layer for token ids[B, 1] at position pos (device int64)."""
+        B = ids.shape[0]
+        ids = ids.reshape(B)
+        assert ids.dtype == torch.int64 and ids.is_contiguous() and pos.dtype == torch.int64
+        self.m.batch = B
+        self.m.tokens = ids.data_ptr()
+        self.m.pos = pos.data_ptr()
+        st = _lib.lib().i4b_decode_layers(ctypes.byref(self.m), self.ws.data_ptr(), self.ws.numel(), _stream(ids))
+        _lib.check(st, "decode_layers")
+        return self.h[:B]
+
+
 def _rotate_half(x: torch.Tensor) -> torch.Tensor:
     x1, x2 = x.chunk(2, dim=-1)
     return torch.cat((-x2, x1), dim=-1)
@@ -174,13 +264,15 @@ class LlamaTP:
     ``group`` is the ``torch.distributed`` process group of the ranks (None when
     ``world == 1``).  ``max_seq`` and ``max_batch`` size the static KV cache.
     ``fused`` runs a decode step's norms, rotary embedding, attention and SwiGLU
-    as the library's fused kernels (9 launches per layer); ``fused=False`` runs
-    them as the torch ops transformers uses.
+    as the library's fused kernels; ``fused=False`` runs them as the torch ops
+    transformers uses.  ``persistent`` (default: whenever the model qualifies --
+    W4, one rank, fused, batch <= 8, widths multiples of 512) runs all decoder
+    layers of a decode step as one launch of ``i4b_decode_layers``.
     """
 
     def __init__(self, hf_model, *, w4: bool = True, group_size: int = 128, quantize_lm_head: bool = False,
                  rank: int = 0, world: int = 1, group=None, max_seq: int = 2048, max_batch: int = 1,
-                 device: torch.device | None = None, fused: bool = True):
+                 device: torch.device | None = None, fused: bool = True, persistent: bool | None = None):
         cfg = hf_model.config
         self.fused = fused
         self.cfg = cfg
@@ -245,6 +337,17 @@ class LlamaTP:
         self.k_cache = torch.zeros(n_layers, max_batch, self.nkv_l, max_seq, hd, device=dev, dtype=torch.bfloat16)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.positions = torch.arange(max_seq, device=dev)
+
+        qualifies = (w4 and world == 1 and fused and hd == 64 and max_batch <= 8 and group_size in (32, 64, 128)
+                     and H % 512 == 0 and self.inter_l % 512 == 0 and (self.nh_l * hd) % 512 == 0
+                     and self.nh_l // self.nkv_l in (1, 2, 4, 8) and self.nh_l % self.nkv_l == 0)
+        if persistent and not qualifies:
+            raise ValueError("persistent decode needs W4 (G 32/64/128), one rank, fused kernels, head_dim 64, "
+                             "batch <= 8 and hidden / intermediate / q widths that are multiples of 512")
+        self.persistent = None
+        if qualifies and persistent is not False:
+            self.persistent = PersistentDecoder(
+                self, [{k: L[k].q for k in ("qkv", "o", "gu", "down")} for L in self.layers], group_size)
 
     # ------------------------------------------------------------------ collectives
 
@@ -312,6 +415,12 @@ class LlamaTP:
     @torch.no_grad()
     def decode_step(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """One token per sequence: ids[B, 1] at position ``pos`` (a one-element int64 device tensor); logits [B, 1, V]."""
+        if self.persistent is not None and ids.shape[0] <= self.max_batch:
+            B = ids.shape[0]
+            h = self.persistent.run(ids, pos)
+            x = torch.empty_like(h)
+            add_rmsnorm(h, None, self.norm, x, self.eps)
+            return self._gather_vocab(self.lm_head(x)).view(B, 1, -1)
         if self.fused:
             return self._decode_step_fused(ids, pos)
         B = ids.shape[0]

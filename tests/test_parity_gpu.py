@@ -182,6 +182,23 @@ def test_w4a16_matmul(M, NK, dtype, cuda_device):
     _assert_matches(out, _oracle_mm(x, qw, s, z))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K,G", [(1, 114688, 256, 128), (5, 114692, 512, 64), (8, 118784, 256, 32),
+                                     (1, 128256, 2048, 128)])
+def test_wide_gemv_streaming_variant(M, N, K, G, dtype, cuda_device):
+    """Very wide matrices (an lm_head) take the persistent streaming variant of the small-M kernel."""
+    from int4_b200 import quantize_int4, w4a16_matmul
+
+    torch.manual_seed(N + K)
+    x = torch.randn(M, K, dtype=dtype, device=cuda_device)
+    w = torch.randn(N, K, dtype=torch.bfloat16, device=cuda_device) * 0.02
+    qw, s, z = quantize_int4(w, G)
+    out = w4a16_matmul(x, qw, s, z)
+    assert out.shape == (M, N)
+    _assert_matches(out, _oracle_mm(x, qw, s, z))
+    torch.testing.assert_close(w4a16_matmul(x, qw, s, z), out, rtol=0, atol=0)  # run to run identical
+
+
 @pytest.mark.parametrize("name", list(cases.GEMM_CASES))
 def test_w4a16_matmul_vs_golden(name, golden_arrays, cuda_device):
     from int4_b200 import quantize_int4_ref, w4a16_matmul

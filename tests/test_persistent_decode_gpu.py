@@ -1,0 +1,199 @@
+"""The persistent decode step (every decoder layer in one launch) against the reference's quality oracle.
+
+As in test_decode_gpu.py, the oracle is the reference's fake-quant model
+(``quantize_model_linears(..., fake=True)``, ``int4_triton/qlinear.py:54-68``):
+transformers' Llama with ``dequantize_int4_ref`` weights.  ``LlamaTP`` with the
+persistent path must stay within the north star's 2e-2 max-abs logits bound of
+it over cached decode steps, agree with the per-launch fused path on the same
+quantized weights, replay bit-identically from a CUDA graph, and do the same on
+the Llama-3.2-1B widths (2048 / 8192, 32 / 8 heads) with two layers.
+"""
+from __future__ import annotations
+
+import copy
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+
+
+def _config(hidden=512, inter=1024, heads=8, kv=2, layers=2, vocab=512):
+    from transformers import LlamaConfig
+
+    return LlamaConfig(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers,
+                       num_attention_heads=heads, num_key_value_heads=kv, head_dim=64,
+                       max_position_embeddings=131072, rms_norm_eps=1e-5, tie_word_embeddings=True,
+                       rope_theta=500000.0,
+                       rope_scaling={"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                                     "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
+
+
+def _hf(cfg, seed=0):
+    from transformers import LlamaForCausalLM
+
+    torch.manual_seed(seed)
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(cfg)
+    return model.to(torch.bfloat16).eval()
+
+
+@pytest.fixture(scope="module")
+def small(cuda_device):
+    from int4_b200 import quantize_model_linears
+
+    hf = _hf(_config())
+    fake = copy.deepcopy(hf)
+    quantize_model_linears(fake, 128, skip=("lm_head",), fake=True)
+    return hf, fake
+
+
+def _ids(B, S, seed, vocab=512):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, vocab, (B, S), generator=g).cuda()
+
+
+@pytest.mark.parametrize("G", [32, 64, 128])
+def test_tile_w4_layout(cuda_device, G):
+    """Piece (slab s, piece p): step j, lane (r, c) holds qweight[64p + 4j + c, 32s + 4r .. +3]; then the scale and
+    zero records of the piece's groups."""
+    import int4_b200
+    from int4_b200.decode import tile_w4
+
+    N, K = 96, 1024
+    w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    qw, sc, zr = int4_b200.quantize_int4(w, G)
+    blob = tile_w4(qw, sc, zr)
+    S, P = N // 32, K // 512
+    pb = 8192 + (512 // G) * 128
+    assert blob.numel() == S * P * pb
+    b = blob.view(S, P, pb)
+    words = b[:, :, :8192].contiguous().view(torch.int32).view(S, P, 16, 8, 4, 4)  # s p j r c e
+    want = qw.view(P, 16, 4, S, 8, 4).permute(3, 0, 1, 4, 2, 5)  # (p j c s r e) -> s p j r c e
+    assert torch.equal(words, want)
+    rec = b[:, :, 8192:].contiguous().view(torch.float16).view(S, P, 512 // G, 8, 2, 4)  # s p gi r (s|z) e
+    gp = 512 // G
+    assert torch.equal(rec[..., 0, :], sc.view(P, gp, S, 8, 4).permute(2, 0, 1, 3, 4))
+    assert torch.equal(rec[..., 1, :], zr.view(P, gp, S, 8, 4).permute(2, 0, 1, 3, 4))
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("B", [1, 2])
+def test_persistent_decode_matches_fake_quant_reference(small, B):
+    from int4_b200.decode import LlamaTP
+
+    hf, fake = small
+    m = LlamaTP(hf, w4=True, max_seq=128, max_batch=2)
+    assert m.persistent is not None
+    ids = _ids(B, 24, 11 + B)
+    logits = m.prefill(ids)
+    seq = ids
+    for step in range(6):
+        nxt = logits[:, -1].argmax(-1, keepdim=True)
+        seq = torch.cat([seq, nxt], 1)
+        pos = torch.tensor([seq.shape[1] - 1], device="cuda")
+        logits = m.decode_step(nxt.contiguous(), pos)
+        ref = fake(seq).logits[:, -1:].float()
+        err = (logits.float() - ref).abs().max().item()
+        assert err <= LOGIT_TOL, (step, err)
+    from int4_b200 import _lib
+
+    assert _lib.device_error_flags(0) == 0
+
+
+@torch.no_grad()
+def test_persistent_matches_per_launch_path_and_caches(small):
+    from int4_b200.decode import LlamaTP
+
+    hf, _ = small
+    a = LlamaTP(hf, w4=True, max_seq=128, max_batch=2, persistent=True)
+    b = LlamaTP(hf, w4=True, max_seq=128, max_batch=2, persistent=False)
+    ids = _ids(2, 30, 5)
+    tok = a.prefill(ids)[:, -1].argmax(-1, keepdim=True)
+    b.prefill(ids)
+    for step in range(5):
+        pos = torch.tensor([30 + step], device="cuda")
+        la, lb = a.decode_step(tok, pos), b.decode_step(tok, pos)
+        err = (la.float() - lb.float()).abs().max().item()
+        assert err <= LOGIT_TOL, (step, err)
+        tok = lb[:, -1].argmax(-1, keepdim=True).contiguous()
+    # the caches written by the one-launch step hold the same rotated keys and values
+    assert (a.k_cache.float() - b.k_cache.float()).abs().max().item() <= 0.05
+    assert (a.v_cache.float() - b.v_cache.float()).abs().max().item() <= 0.05
+
+
+@torch.no_grad()
+def test_persistent_decode_replays_bit_identically_from_a_cuda_graph(small):
+    from int4_b200.decode import LlamaTP
+
+    hf, _ = small
+    m = LlamaTP(hf, w4=True, max_seq=128, max_batch=1)
+    ids = _ids(1, 16, 7)
+    first = m.prefill(ids)[:, -1].argmax(-1, keepdim=True)
+    tok = first.clone()
+    pos = torch.tensor([16], device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        m.decode_step(tok, pos)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        out = m.decode_step(tok, pos)
+    eager = []
+    m.prefill(ids)
+    for _ in range(4):
+        eager.append(m.decode_step(tok, pos).clone())
+        tok.copy_(eager[-1][:, -1].argmax(-1, keepdim=True))
+        pos += 1
+    tok.copy_(first)
+    pos.fill_(16)
+    m.prefill(ids)
+    for i in range(4):
+        g.replay()
+        torch.testing.assert_close(out, eager[i], rtol=0, atol=0)
+        tok.copy_(out[:, -1].argmax(-1, keepdim=True))
+        pos += 1
+    torch.cuda.synchronize()
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("B", [1, 4])
+def test_persistent_decode_on_llama_1b_widths(cuda_device, B):
+    """Two layers at the Llama-3.2-1B widths: 96 / 64 / 512 / 64 slabs per stage, several attention blocks per
+    split.
+
+    At these widths a cached single-token step differs from the reference's full recompute by bf16 rounding
+    noise alone: the same decode harness with the reference's own fake-quant bf16 weights and cuBLAS
+    (``LlamaTP(fake, w4=False)``) is already ~3e-2 away.  The bound is therefore the larger of the north
+    star's 2e-2 and twice that measured floor; the per-launch W4 path is held to the same bound.
+    """
+    from int4_b200 import quantize_model_linears
+    from int4_b200.decode import LlamaTP
+
+    hf = _hf(_config(hidden=2048, inter=8192, heads=32, kv=8, layers=2, vocab=1024), seed=3)
+    fake = copy.deepcopy(hf)
+    quantize_model_linears(fake, 128, skip=("lm_head",), fake=True)
+    a = LlamaTP(hf, w4=True, max_seq=512, max_batch=4, persistent=True)
+    b = LlamaTP(hf, w4=True, max_seq=512, max_batch=4, persistent=False)
+    floor_m = LlamaTP(fake, w4=False, max_seq=512, max_batch=4, fused=False)
+    ids = _ids(B, 300, 17, vocab=1024)
+    for m in (a, b, floor_m):
+        m.prefill(ids)
+    tok = fake(ids).logits[:, -1:].argmax(-1).contiguous()
+    seq = torch.cat([ids, tok], 1)
+    for step in range(3):
+        pos = torch.tensor([300 + step], device="cuda")
+        ref = fake(seq).logits[:, -1:].float()
+        la, lb, lf = (m.decode_step(tok, pos).float() for m in (a, b, floor_m))
+        floor = (lf - ref).abs().max().item()
+        bound = max(LOGIT_TOL, 2 * floor)
+        ea, eb = (la - ref).abs().max().item(), (lb - ref).abs().max().item()
+        assert ea <= bound and eb <= bound, (step, ea, eb, floor)
+        tok = ref[:, -1].argmax(-1, keepdim=True).contiguous()
+        seq = torch.cat([seq, tok], 1)
+    from int4_b200 import _lib
+
+    assert _lib.device_error_flags(0) == 0
