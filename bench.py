@@ -418,11 +418,13 @@ def run_model(args, world, rank, local):
     hf = build_llama(dev)
     res = {}
     for label, w4 in (("w4", True), ("bf16", False)):
-        m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world,
+        persistent = None if args.persistent < 0 else bool(args.persistent) and w4
+        m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world, persistent=persistent,
                     max_seq=prompt + steps + args.warmup + 8, max_batch=B, device=dev)
         with ClockSampler(local) as clk:
             r = time_decode(m, B, prompt, steps, args.warmup, world, dev, LLAMA_1B["vocab_size"])
         r["clocks"] = clk.summary()
+        r["persistent"] = m.persistent is not None
         # bytes one decode step must read on this rank: projection weights + the KV cache up to the mean position
         mean_pos = prompt + steps / 2
         kv = 2 * len(m.layers) * m.nkv_l * m.hd * 2 * B * mean_pos
@@ -493,7 +495,8 @@ def main_model(args, world, rank, local, threads):
         "metric": MODEL_METRIC, "value": tps, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "w4a16-bf16", "data": "synthetic (random-init weights, random token ids)",
-        "config": model_config(args),
+        "config": dict(model_config(args), decode="one launch for all layers (i4b_decode_layers)"
+                       if w4["persistent"] else "one launch per projection / glue op"),
         "bf16_tokens_per_s": args.m * args.steps / bf["decode_s"],
         "w4_over_bf16": bf["decode_s"] / w4["decode_s"],
         "prefill_ms": {"w4": w4["prefill_ms"], "bf16": bf["prefill_ms"]},
@@ -521,6 +524,9 @@ def main():
     ap.add_argument("--lm-head-w4", type=int, default=0, help="model workload: quantize the lm_head too")
     ap.add_argument("--m", type=int, default=1, help="tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--persistent", type=int, default=-1,
+                    help="model workload: 1 = all decoder layers of a step in one launch (i4b_decode_layers), "
+                         "0 = one launch per projection / glue op, -1 = whichever the model qualifies for")
     ap.add_argument("--pdl", type=int, default=1,
                     help="programmatic dependent launch for the small-M kernels (weights fetched before the wait)")
     args = ap.parse_args()

@@ -354,4 +354,54 @@ __device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
   return d;
 }
 
+// ------------------------------------------------------------------ exact INT4 dequantization
+// w = (q - z) * s rounded once to the activation type, as the reference's kernels compute it
+// (int4_triton/gemm.py:144 and :211: fp32 (q - z) * s, then .to(x.dtype)).  A nibble pair arrives as
+// (bias + q_i, bias + q_j) from one lop3 (bias 128 for bf16, 1024 for fp16, exact); d = p - (bias + z) is
+// an exact small integer.  fp16: s is an fp16 operand, so d * s rounds once.  bf16: s (fp16, 11 bits)
+// splits into s_hi (its top 8 bits, a bf16) and s_lo = s - s_hi (at most 3 significant bits, exact in
+// bf16); d * s_lo (<= 7 bits) is exact, and fma(d, s_hi, d * s_lo) = d * s rounded once.
+struct DqParams {
+  uint32_t zz;   // (bias + z) twice
+  uint32_t shi;  // bf16: scale high part twice; fp16: scale twice
+  uint32_t slo;  // bf16: scale low part twice
+};
+
+template <bool F16>
+__device__ __forceinline__ DqParams dq_params(uint16_t s_bits, uint16_t z_bits) {
+  const float s = __half2float(__ushort_as_half(s_bits));
+  const float z = __half2float(__ushort_as_half(z_bits));
+  DqParams p;
+  if constexpr (F16) {
+    const uint32_t zz = __half_as_ushort(__float2half_rn(1024.0f + z));
+    p.zz = zz * 0x10001u;
+    p.shi = uint32_t(s_bits) * 0x10001u;
+    p.slo = 0;
+  } else {
+    const uint32_t hi = __float_as_uint(s) & 0xFFFF0000u;
+    const float lo = isfinite(s) ? (s - __uint_as_float(hi)) : 0.0f;
+    const uint32_t lo16 = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+    const uint32_t zz = __bfloat16_as_ushort(__float2bfloat16_rn(128.0f + z));
+    p.zz = zz * 0x10001u;
+    p.shi = (hi >> 16) * 0x10001u;
+    p.slo = lo16 * 0x10001u;
+  }
+  return p;
+}
+
+template <bool F16>
+__device__ __forceinline__ uint32_t dq_pair(uint32_t p, const DqParams& dp) {
+  uint32_t d, w;
+  if constexpr (F16) {
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(p), "r"(dp.zz));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w) : "r"(d), "r"(dp.shi));
+  } else {
+    uint32_t pl;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(p), "r"(dp.zz));
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(pl) : "r"(d), "r"(dp.slo));
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(w) : "r"(d), "r"(dp.shi), "r"(pl));
+  }
+  return w;
+}
+
 }  // namespace i4b

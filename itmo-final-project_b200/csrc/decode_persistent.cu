@@ -54,9 +54,11 @@ namespace i4b {
 
 namespace {
 
-constexpr int kCW = 8;               // compute warps
+constexpr int kCW = 8;               // compute warps (two per SM sub-partition: 168 registers each)
 constexpr int kCT = kCW * 32;        // compute threads
 constexpr int kThreads = kCT + 32;   // + the producer warp
+constexpr int kAW = 8;               // warps of an attention item (one per 8 of the 64 head dims)
+constexpr int kAT = kAW * 32;
 constexpr int kPieceK = 512;         // k of one weight piece
 constexpr int kPieceW = 8192;        // packed-word bytes of one piece (32 columns x 512 k x 4 bit)
 constexpr int kMaxSlots = 32;
@@ -114,6 +116,8 @@ __device__ __forceinline__ float bfv(uint32_t bits16) { return __uint_as_float(b
 __device__ __forceinline__ uint32_t bfr(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory"); }
+// attention items run on the first kAW compute warps only, with their own barrier
+__device__ __forceinline__ void abar() { asm volatile("bar.sync 2, %0;" ::"n"(kAT) : "memory"); }
 
 __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
   unsigned int v;
@@ -157,12 +161,14 @@ __device__ bool wait_counter(const unsigned int* c, unsigned int target, const u
   }
 }
 
-// mbarrier phase wait, bounded, giving up early when another CTA aborted.
+// mbarrier phase wait, bounded, giving up early when another CTA aborted.  Each probe lets the thread
+// sleep in hardware until the phase completes (or ~1 us), so that a waiting warp -- the producer whenever
+// the ring is full -- takes no issue slots from the compute warps.
 __device__ bool wait_slot(uint64_t* bar, uint32_t parity, const unsigned int* abort_word) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (ld_relaxed_u32(abort_word)) return false;
       if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
@@ -187,14 +193,19 @@ __device__ __forceinline__ void mma_bf16_first(float (&d)[4], const uint32_t (&a
 
 // One 512-k piece of a 32-column slab, by one warp: acc[t][e] += the piece's contribution to columns
 // 4r + 2t (e = 0, 1) and 4r + 2t + 1 (e = 2, 3) for tokens 2c + (e & 1), r = lane / 4, c = lane % 4.
-// wb: the piece in shared memory; xb: this lane's activations at the piece's first k;
-// xsb: this lane's group sums X[group of the piece's first k][2c].  The two k16 halves of a step
-// accumulate in separate registers (four independent MMA chains per warp), added once per group.
+// wb: the piece in shared memory; xb: this lane's activations at the piece's first k.  Every weight is
+// dequantized exactly as the reference does -- (q - z) * s rounded once to bf16 (dq_pair) -- and the A
+// fragments are those bf16 weights, so y = sum_k x_k * bf16(w_k) with fp32 accumulation.  The two k16
+// halves of a step accumulate in separate registers (four independent MMA chains per warp).
 template <int SPS>
-__device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, const float* xsb, int lane,
-                                          float (&acc)[2][4]) {
+__device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, int lane, float (&acc)[2][4]) {
   const int r = lane >> 2;
-  float d0[2][4], d1[2][4];
+  float a1[2][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a1[t][e] = 0.0f;
+  DqParams dp[4];
   // four blocks of four 32-k steps: the loads of a block are scheduled together, the block loop is not
   // unrolled (register budget of 288 threads per SM); SPS divides 4, so group boundaries fall inside blocks
 #pragma unroll 1
@@ -202,6 +213,13 @@ __device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, 
 #pragma unroll
   for (int jj = 0; jj < 4; ++jj) {
     const int j = j0 + jj;
+    if (jj % SPS == 0) {  // a new group: scale / zero of columns 4r .. 4r + 3
+      const uint4 sz = *reinterpret_cast<const uint4*>(wb + kPieceW + ((j / SPS) * 8 + r) * 16);
+      dp[0] = dq_params<false>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.z & 0xFFFFu));
+      dp[1] = dq_params<false>(uint16_t(sz.x >> 16), uint16_t(sz.z >> 16));
+      dp[2] = dq_params<false>(uint16_t(sz.y & 0xFFFFu), uint16_t(sz.w & 0xFFFFu));
+      dp[3] = dq_params<false>(uint16_t(sz.y >> 16), uint16_t(sz.w >> 16));
+    }
     const uint4 w4 = *reinterpret_cast<const uint4*>(wb + (j * 32 + lane) * 16);
     const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
     uint32_t af[2][2][4];
@@ -209,44 +227,22 @@ __device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, 
     for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int s = 0; s < 2; ++s) {
-        af[t][s][0] = nib_pair(wd[2 * t], 2 * s);
-        af[t][s][1] = nib_pair(wd[2 * t + 1], 2 * s);
-        af[t][s][2] = nib_pair(wd[2 * t], 2 * s + 1);
-        af[t][s][3] = nib_pair(wd[2 * t + 1], 2 * s + 1);
+        af[t][s][0] = dq_pair<false>(nib_pair(wd[2 * t], 2 * s), dp[2 * t]);
+        af[t][s][1] = dq_pair<false>(nib_pair(wd[2 * t + 1], 2 * s), dp[2 * t + 1]);
+        af[t][s][2] = dq_pair<false>(nib_pair(wd[2 * t], 2 * s + 1), dp[2 * t]);
+        af[t][s][3] = dq_pair<false>(nib_pair(wd[2 * t + 1], 2 * s + 1), dp[2 * t + 1]);
       }
     const uint4 b = *reinterpret_cast<const uint4*>(xb + j * 64);
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      if (jj % SPS == 0) {
-        mma_bf16_first(d0[t], af[t][0], b.x, b.y);
-        mma_bf16_first(d1[t], af[t][1], b.z, b.w);
-      } else {
-        mma_bf16(d0[t], af[t][0], b.x, b.y);
-        mma_bf16(d1[t], af[t][1], b.z, b.w);
-      }
-    }
-    if (jj % SPS == SPS - 1) {  // group complete: acc += s * (D - (128 + z) * X)
-      const int gi = j / SPS;
-      const uint4 sz = *reinterpret_cast<const uint4*>(wb + kPieceW + (gi * 8 + r) * 16);
-      float sv[4], zv[4];
-      sv[0] = __half2float(__ushort_as_half(uint16_t(sz.x & 0xFFFFu)));
-      sv[1] = __half2float(__ushort_as_half(uint16_t(sz.x >> 16)));
-      sv[2] = __half2float(__ushort_as_half(uint16_t(sz.y & 0xFFFFu)));
-      sv[3] = __half2float(__ushort_as_half(uint16_t(sz.y >> 16)));
-      zv[0] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.z & 0xFFFFu)));
-      zv[1] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.z >> 16)));
-      zv[2] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.w & 0xFFFFu)));
-      zv[3] = 128.0f + __half2float(__ushort_as_half(uint16_t(sz.w >> 16)));
-      const float2 X = *reinterpret_cast<const float2*>(xsb + gi * 8);
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        acc[t][0] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X.x, d0[t][0] + d1[t][0]), acc[t][0]);
-        acc[t][1] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X.y, d0[t][1] + d1[t][1]), acc[t][1]);
-        acc[t][2] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X.x, d0[t][2] + d1[t][2]), acc[t][2]);
-        acc[t][3] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X.y, d0[t][3] + d1[t][3]), acc[t][3]);
-      }
+      mma_bf16(acc[t], af[t][0], b.x, b.y);
+      mma_bf16(a1[t], af[t][1], b.z, b.w);
     }
   }
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[t][e] += a1[t][e];
 }
 
 struct Smem {
@@ -258,7 +254,8 @@ struct Smem {
   uint8_t stage[kMaxItems];
   uint16_t poff[kMaxItems];  // piece offset of each item inside the CTA's layer sequence
   int nit, ppl;
-  int flag;
+  int flag;   // 1 until a wait fails in this CTA (then 0 for the rest of the launch)
+  int tflag;  // the attention ticket said: this CTA combines
   volatile int prod_seq;  // pieces issued by the producer so far (diagnostics)
 };
 
@@ -266,10 +263,12 @@ constexpr int kXR = 8;  // 16-byte activation chunks per thread in flight
 constexpr int kResPerThread = 4;  // residual values per thread: o / down slabs x tokens x 32 <= kCT * 4
 
 // Stage the activations of GEMV stage g into shared memory: x permuted to the nibble-pair order of the
-// A fragments, [token][k / 8] x 16 bytes with row pitch xpitch, and the group sums X[group][token] (fp32).
-// Each thread puts kXR chunk loads in flight before using any.  RMSNorm stages (the whole [B, K] block is
-// one round, B * K <= 8 * kCT * kXR, checked on the host) compute x = bf16(w * bf16(h * rsqrt(mean(h^2) +
-// eps))) (LlamaRMSNorm) from the registers once the block-wide sums of squares are known.
+// A fragments, [token][k / 8] x 16 bytes with row pitch xpitch.  The B rows' chunks (8 consecutive k) are
+// numbered token-major and thread tid owns chunks tid, tid + kCT, ...; rounds of kXR chunks put all
+// their loads in flight before any is used.  RMSNorm stages (every row chunk of a thread in one round:
+// B * K <= 8 * kCT * kXR, checked on the host) compute x = bf16(w * bf16(h * rsqrt(mean(h^2) + eps)))
+// (LlamaRMSNorm) once the block-wide sums of squares are known.
+template <int SPS>
 __device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int g, int l, int K) {
   const i4b_decode_model& m = P.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -278,39 +277,37 @@ __device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int
   const uint16_t* nw = static_cast<const uint16_t*>(g == G_QKV ? m.ln1 : m.ln2) + int64_t(l) * H;
   const uint16_t* hbuf = static_cast<const uint16_t*>(m.h_out);
   const uint16_t* emb = static_cast<const uint16_t*>(m.embed);
-  // row of token t: the embedding row in layer 0 (qkv), else h / att / act
-  auto row = [&](int t) -> const uint16_t* {
-    if (g == G_QKV) {
-      if (l == 0) {
+  // base and stride of the token rows: the embedding rows in layer 0 (qkv), else h / att / act
+  const uint16_t* rows[kMaxTok];
+  {
+    const uint16_t* src = g == G_O ? P.att : g == G_DOWN ? P.act : hbuf;
+    const int64_t stride = g == G_O ? P.q_n : g == G_DOWN ? m.intermediate : H;
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) {
+      if (g == G_QKV && l == 0 && t < B) {
         int64_t id = m.tokens[t];
         if (id < 0 || id >= m.vocab) id = 0;
-        return emb + id * H;
+        rows[t] = emb + id * H;
+      } else {
+        rows[t] = src + t * stride;
       }
-      return hbuf + int64_t(t) * H;
     }
-    if (g == G_GU) return hbuf + int64_t(t) * H;
-    if (g == G_O) return P.att + int64_t(t) * P.q_n;
-    return P.act + int64_t(t) * m.intermediate;
-  };
+  }
   uint8_t* sx = smem + P.off_x;
-  float* sXS = reinterpret_cast<float*>(smem + P.off_xs);
-  const int st_id = g == G_QKV ? C_QKV : g == G_O ? C_O : g == G_GU ? C_GU : C_DOWN;
-  if (tid == 0) trace_put(P, l, st_id, 12, clock64());
-  const int nch = K / 8, total = B * nch;  // nch is a multiple of 64: a warp's 32 chunks share one token
-  const int cpg = m.group_size / 8;        // chunks per group (4, 8 or 16 consecutive lanes)
+  const int lg = 31 - __clz(K / 8);  // chunks per row = 2^lg (host check)
+  const int total = B << lg;
   for (int base = 0; base < total; base += kCT * kXR) {
     uint4 v[kXR];
 #pragma unroll
     for (int r = 0; r < kXR; ++r) {
       const int idx = base + r * kCT + tid;
       if (idx < total) {
-        const int t = idx / nch, ch = idx - t * nch;
-        v[r] = ldcg128(row(t) + 8 * ch);
+        const int t = idx >> lg, ch = idx & ((1 << lg) - 1);
+        v[r] = ldcg128(rows[t] + 8 * ch);
         if (norm) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + 8 * ch));  // read after the statistics
       }
     }
-    if (tid == 0 && base == 0) trace_put(P, l, st_id, 13, clock64());
-    if (norm) {
+    if (norm) {  // one round holds every row chunk (host check); a warp's 32 chunks share one token
       float ssum[kMaxTok];
 #pragma unroll
       for (int t = 0; t < kMaxTok; ++t) ssum[t] = 0.0f;
@@ -328,7 +325,7 @@ __device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int
           }
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-          const int t = idx / nch;
+          const int t = idx >> lg;
 #pragma unroll
           for (int tt = 0; tt < kMaxTok; ++tt)
             if (tt == t) ssum[tt] += ss;
@@ -344,34 +341,28 @@ __device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int
       }
       cbar();
     }
-    if (tid == 0 && base == 0) trace_put(P, l, st_id, 14, clock64());
 #pragma unroll
     for (int r = 0; r < kXR; ++r) {
       const int idx = base + r * kCT + tid;
-      if (idx >= total) continue;  // warp-uniform
-      const int t = idx / nch, ch = idx - t * nch;
-      uint32_t u[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
-      if (norm) {
-        const float inv = S.inv[t];
-        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(nw + 8 * ch));
-        const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
+      if (idx < total) {
+        const int t = idx >> lg, ch = idx & ((1 << lg) - 1);
+        uint32_t u[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+        if (norm) {
+          const float inv = S.inv[t];
+          const uint4 wv = __ldg(reinterpret_cast<const uint4*>(nw + 8 * ch));
+          const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          u[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(u[i] & 0xFFFFu) * inv))) |
-                 (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(u[i] >> 16) * inv))) << 16);
+          for (int i = 0; i < 4; ++i)
+            u[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(u[i] & 0xFFFFu) * inv))) |
+                   (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(u[i] >> 16) * inv))) << 16);
+        }
+        // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
+        *reinterpret_cast<uint4*>(sx + t * P.xpitch + ch * 16) =
+            make_uint4(__byte_perm(u[0], u[2], 0x5410), __byte_perm(u[0], u[2], 0x7632),
+                       __byte_perm(u[1], u[3], 0x5410), __byte_perm(u[1], u[3], 0x7632));
       }
-      float sum = 0.0f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) sum += bfv(u[q] & 0xFFFFu) + __uint_as_float(u[q] & 0xFFFF0000u);
-      for (int o = 1; o < cpg; o <<= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-      // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
-      *reinterpret_cast<uint4*>(sx + t * P.xpitch + ch * 16) =
-          make_uint4(__byte_perm(u[0], u[2], 0x5410), __byte_perm(u[0], u[2], 0x7632),
-                     __byte_perm(u[1], u[3], 0x5410), __byte_perm(u[1], u[3], 0x7632));
-      if (ch % cpg == 0) sXS[(ch / cpg) * 8 + t] = sum;
     }
   }
-  if (tid == 0) trace_put(P, l, st_id, 15, clock64());
 }
 
 // One GEMV stage of layer l for this CTA's slabs of it.  False on a failed wait.
@@ -401,13 +392,13 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
     } else {
       c = P.ctr + l * C_LAYER + C_GU, target = unsigned(P.nslab[G_GU]);
     }
-    S.flag = (c == nullptr || wait_counter(c, target, abort_word)) ? 1 : 0;
+    if (c != nullptr && !wait_counter(c, target, abort_word)) S.flag = 0;  // sticky: errors are never cleared
   }
   cbar();
   if (!S.flag) return false;
   stamp(P, l, st_id, 1);
   const int K = g == G_DOWN ? m.intermediate : (g == G_O ? P.q_n : m.hidden);
-  stage_x(P, S, smem, g, l, K);
+  stage_x<SPS>(P, S, smem, g, l, K);
   cbar();
   stamp(P, l, st_id, 2);
   // residual inputs of the o_proj / down_proj epilogue: loaded here, consumed after the pieces
@@ -434,13 +425,11 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
     }
   }
 
-  // ---- pieces: piece q = i * Pc + p of this stage goes to warp q % 8
-  const int Pc = P.npiece[g], J = Pc < 8 ? Pc : 8;
+  // ---- pieces: piece q = i * Pc + p of this stage goes to warp q % kCW
+  const int Pc = P.npiece[g], J = Pc < kCW ? Pc : kCW;
   float* part = reinterpret_cast<float*>(smem + P.off_part);
   const int r = lane >> 2, c = lane & 3;
   const uint8_t* xl = smem + P.off_x + min(r, B - 1) * P.xpitch + 16 * c;
-  const float* xsl = reinterpret_cast<const float*>(smem + P.off_xs) + 2 * c;
-  const int gpp = kPieceK / m.group_size;  // groups per piece
   bool ok = true;
   float acc[2][4];
   int cur = -1, cur_j = 0;
@@ -464,7 +453,7 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
     if (i != cur) {
       if (cur >= 0) flush(cur, cur_j);
       cur = i;
-      cur_j = p & 7;
+      cur_j = p % kCW;
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -478,7 +467,7 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
       break;
     }
     const long long c1 = clock64();
-    piece_mma<SPS>(smem + slot * P.piece_bytes, xl + p * (kPieceK / 32) * 64, xsl + p * gpp * 8, lane, acc);
+    piece_mma<SPS>(smem + slot * P.piece_bytes, xl + p * (kPieceK / 32) * 64, lane, acc);
     t_wait += c1 - c0;
     t_mma += clock64() - c1;
     ++npc;
@@ -526,15 +515,17 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
   cbar();
   stamp(P, l, st_id, 4);
   if (tid == 0) {
-    __threadfence();
     stamp(P, l, st_id, 5);
-    atomicAdd(P.ctr + l * C_LAYER + st_id, unsigned(n));
+    // release: the CTA's output stores (ordered before by the barrier) are visible before the count
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.ctr + l * C_LAYER + st_id), "r"(unsigned(n))
+                 : "memory");
   }
   stamp(P, l, st_id, 6);
   return true;
 }
 
 // Attention item a = (token b, kv head, split j) of layer l: GS query heads over cache positions of split j.
+// Run by the first kAW compute warps (barrier 2); a failure clears the CTA's sticky S.flag.
 template <int GS>
 __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* smem, int l, int a) {
   const i4b_decode_model& m = P.m;
@@ -543,8 +534,8 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   const int b = a / (nkv * ns), kvh = (a / ns) % nkv, j = a % ns;
   const unsigned int* abort_word = P.ctr + P.i_abort;
   stamp(P, l, C_ATTN, 0);
-  if (tid == 0) S.flag = wait_counter(P.ctr + l * C_LAYER + C_QKV, unsigned(P.nslab[G_QKV]), abort_word) ? 1 : 0;
-  cbar();
+  if (tid == 0 && !wait_counter(P.ctr + l * C_LAYER + C_QKV, unsigned(P.nslab[G_QKV]), abort_word)) S.flag = 0;
+  abar();
   if (!S.flag) return false;
   stamp(P, l, C_ATTN, 1);
   float* qs = reinterpret_cast<float*>(smem + P.off_x);  // [GS][64] rotated queries
@@ -572,19 +563,19 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
     s0 = bfv(__ldg(sinT + pos * kHD + lane));
     s1 = bfv(__ldg(sinT + pos * kHD + lane + 32));
   }
-  for (int hh = warp; hh < GS; hh += kCW) {
+  for (int hh = warp; hh < GS; hh += kAW) {
     const uint16_t* src = qrow + (kvh * GS + hh) * kHD;
     const float x0 = bfv(ldcg16(src + lane)), x1 = bfv(ldcg16(src + lane + 32));
     qs[hh * kHD + lane] = bfv(bfr(bfv(bfr(x0 * c0)) + bfv(bfr(-x1 * s0))));
     qs[hh * kHD + lane + 32] = bfv(bfr(bfv(bfr(x1 * c1)) + bfv(bfr(x0 * s1))));
   }
   if (pvalid && pos >= i0 && pos < i1) {  // this split holds the new position: write k and v to the caches
-    if (warp == kCW - 1) {
+    if (warp == kAW - 1) {
       const uint16_t* src = qrow + (nq + kvh) * kHD;
       const float x0 = bfv(ldcg16(src + lane)), x1 = bfv(ldcg16(src + lane + 32));
       kc[pos * kHD + lane] = uint16_t(bfr(bfv(bfr(x0 * c0)) + bfv(bfr(-x1 * s0))));
       kc[pos * kHD + lane + 32] = uint16_t(bfr(bfv(bfr(x1 * c1)) + bfv(bfr(x0 * s1))));
-    } else if (warp == kCW - 2) {
+    } else if (warp == kAW - 2) {
       const uint16_t* src = qrow + (nq + nkv + kvh) * kHD;
       vc[pos * kHD + lane] = ldcg16(src + lane);
       vc[pos * kHD + lane + 32] = ldcg16(src + lane + 32);
@@ -594,7 +585,7 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
     sm[tid] = -INFINITY;
     sl[tid] = 0.0f;
   }
-  cbar();  // rotated queries ready, the new cache row visible to this CTA
+  abar();  // rotated queries ready, the new cache row visible to this CTA
   stamp(P, l, C_ATTN, 2);
 
   float acc[GS][8];
@@ -641,8 +632,8 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
         for (int hh = 0; hh < GS; ++hh) sc[hh * kHD + i] = pi < i1 ? d[hh] * scale : -INFINITY;
       }
     }
-    cbar();
-    for (int hh = warp; hh < GS; hh += kCW) {  // online softmax of head hh over this block
+    abar();
+    for (int hh = warp; hh < GS; hh += kAW) {  // online softmax of head hh over this block
       const float x0 = sc[hh * kHD + lane], x1 = sc[hh * kHD + lane + 32];
       float mb = fmaxf(x0, x1);
 #pragma unroll
@@ -662,7 +653,7 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
         sm[hh] = mn;
       }
     }
-    cbar();
+    abar();
     {  // o += p . V: warp w owns dims 8w..8w+7, lane the positions lane and lane + 32 of the block
 #pragma unroll
       for (int hh = 0; hh < GS; ++hh) {
@@ -686,7 +677,7 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
         }
       }
     }
-    cbar();  // the block's probabilities are read before the next block's scores overwrite them
+    abar();  // the block's probabilities are read before the next block's scores overwrite them
   }
 #pragma unroll
   for (int hh = 0; hh < GS; ++hh)
@@ -709,17 +700,17 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
     mine[tid * kPartRow + 64] = any ? sm[tid] : -INFINITY;
     mine[tid * kPartRow + 65] = any ? sl[tid] : 0.0f;
   }
-  cbar();
+  abar();
   stamp(P, l, C_ATTN, 3);
   unsigned int* ticket = P.ctr + P.i_ticket + b * nkv + kvh;
   if (tid == 0) {
     __threadfence();
     stamp(P, l, C_ATTN, 4);
-    S.flag = atomicAdd(ticket, 1u) == unsigned(ns - 1) ? 2 : 1;
+    S.tflag = atomicAdd(ticket, 1u) == unsigned(ns - 1) ? 1 : 0;
   }
-  cbar();
+  abar();
   stamp(P, l, C_ATTN, 5);
-  if (S.flag != 2) return true;
+  if (!S.tflag) return true;
   // last split of (b, kvh): out = sum_j o_j e^(m_j - M) / sum_j l_j e^(m_j - M), splits in order.  All
   // partials are copied to shared memory first, every load in flight at once.
   __threadfence();
@@ -727,18 +718,18 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   // [ns][GS][kPartRow] partials, 16-byte aligned after the rescale factors
   float4* cm = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(scr + GS) + 15) & ~uintptr_t(15));
   const int n4 = ns * GS * kPartRow / 4;
-  for (int q0 = tid; q0 < n4; q0 += 4 * kCT) {
+  for (int q0 = tid; q0 < n4; q0 += 4 * kAT) {
     float4 t4[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      if (q0 + u * kCT < n4) t4[u] = __ldcg(base + q0 + u * kCT);
+      if (q0 + u * kAT < n4) t4[u] = __ldcg(base + q0 + u * kAT);
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      if (q0 + u * kCT < n4) cm[q0 + u * kCT] = t4[u];
+      if (q0 + u * kAT < n4) cm[q0 + u * kAT] = t4[u];
   }
-  cbar();
+  abar();
   const float* cf = reinterpret_cast<const float*>(cm);
-  for (int idx = tid; idx < GS * kHD; idx += kCT) {
+  for (int idx = tid; idx < GS * kHD; idx += kAT) {
     const int hh = idx / kHD, d = idx % kHD;
     float M = -INFINITY;
     for (int jj = 0; jj < ns; ++jj) M = fmaxf(M, cf[(jj * GS + hh) * kPartRow + 64]);
@@ -752,7 +743,7 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
     }
     P.att[int64_t(b) * P.q_n + (kvh * GS + hh) * kHD + d] = Lp > 0 ? uint16_t(bfr(num / den)) : uint16_t(0);
   }
-  cbar();
+  abar();
   if (tid == 0) {
     *ticket = 0u;
     __threadfence();
@@ -838,7 +829,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     const int nattn = m.batch * m.kv_heads * P.nsplit;
     for (int l = 0; l < m.layers && ok; ++l) {
       ok = gemv_stage<SPS>(P, S, smem, G_QKV, l);
-      if (ok && int(blockIdx.x) < nattn) ok = attention_item<GS>(P, S, smem, l, blockIdx.x);
+      // attention runs on warps 0..kAW-1; the others go on to the o_proj stage, whose barrier they pass
+      // only together with them.  A failed attention clears S.flag, which that stage checks.
+      if (ok && int(blockIdx.x) < nattn && warp < kAW) attention_item<GS>(P, S, smem, l, blockIdx.x);
       ok = ok && gemv_stage<SPS>(P, S, smem, G_O, l);
       ok = ok && gemv_stage<SPS>(P, S, smem, G_GU, l);
       ok = ok && gemv_stage<SPS>(P, S, smem, G_DOWN, l);
@@ -936,7 +929,7 @@ Sched build_sched(int grid, const int nslab[4], const int npiece[4]) {
       sc.items[size_t(c) * kMaxItems + i] = uint16_t((L[i].first << 14) | L[i].second);
       ++cnt[L[i].first];
     }
-    for (int g = 0; g < 4; ++g) sc.max_part = std::max(sc.max_part, cnt[g] * std::min(npiece[g], 8));
+    for (int g = 0; g < 4; ++g) sc.max_part = std::max(sc.max_part, cnt[g] * std::min(npiece[g], kCW));
     sc.max_res = std::max(sc.max_res, std::max(cnt[G_O], cnt[G_DOWN]));
   }
   sc.ok = true;
@@ -962,7 +955,9 @@ int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
   const int gqa = m.heads / m.kv_heads;
   if (gqa != 1 && gqa != 2 && gqa != 4 && gqa != 8) return I4B_ERR_SHAPE;
   const int q_n = m.heads * kHD, qkv_n = (m.heads + 2 * m.kv_heads) * kHD;
-  if (m.hidden % kPieceK || m.intermediate % kPieceK || q_n % kPieceK) return I4B_ERR_SHAPE;
+  // every projection input width is a power-of-two number of 8-value chunks, at least 256
+  auto pow2_chunks = [](int k) { return k >= 2048 && k % 8 == 0 && ((k / 8) & (k / 8 - 1)) == 0; };
+  if (!pow2_chunks(m.hidden) || !pow2_chunks(m.intermediate) || !pow2_chunks(q_n)) return I4B_ERR_SHAPE;
   if (int64_t(m.batch) * m.hidden > int64_t(8) * kCT * kXR) return I4B_ERR_SHAPE;  // RMSNorm rows in one round
   L->gqa = gqa;
   L->q_n = q_n;
@@ -1115,7 +1110,7 @@ int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin,
   // attention: queries, scores, running max / sum / rescale, then the partials of all splits when combining
   const int attn_bytes = (2 * L.gqa * kHD + 3 * L.gqa + 4) * 4 + L.nsplit * L.gqa * kPartRow * 4;
   const int x_bytes = al(std::max(m.batch * p.h.xpitch, attn_bytes));
-  const int xs_bytes = al((kmax / m.group_size) * 8 * 4);
+  const int xs_bytes = 0;
   const int part_bytes = al(sc->max_part * m.batch * 32 * 4);
   const int fixed = x_bytes + xs_bytes + part_bytes;
   const int avail = smem_optin - int(sizeof(Smem)) - 1024;

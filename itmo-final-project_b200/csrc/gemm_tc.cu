@@ -57,34 +57,6 @@ struct TcCfg {
   static_assert(TMEM_COLS <= 512, "accumulators exceed TMEM");
 };
 
-struct DqParams {
-  uint32_t zz;   // (bias + z) twice
-  uint32_t shi;  // bf16: scale high part twice; fp16: scale twice
-  uint32_t slo;  // bf16: scale low part twice
-};
-
-template <bool F16>
-__device__ __forceinline__ DqParams dq_params(uint16_t s_bits, uint16_t z_bits) {
-  const float s = __half2float(__ushort_as_half(s_bits));
-  const float z = __half2float(__ushort_as_half(z_bits));
-  DqParams p;
-  if constexpr (F16) {
-    const uint32_t zz = __half_as_ushort(__float2half_rn(1024.0f + z));
-    p.zz = zz * 0x10001u;
-    p.shi = uint32_t(s_bits) * 0x10001u;
-    p.slo = 0;
-  } else {
-    const uint32_t hi = __float_as_uint(s) & 0xFFFF0000u;
-    const float lo = isfinite(s) ? (s - __uint_as_float(hi)) : 0.0f;
-    const uint32_t lo16 = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-    const uint32_t zz = __bfloat16_as_ushort(__float2bfloat16_rn(128.0f + z));
-    p.zz = zz * 0x10001u;
-    p.shi = (hi >> 16) * 0x10001u;
-    p.slo = lo16 * 0x10001u;
-  }
-  return p;
-}
-
 // 8 nibbles of one packed word -> 8 dequantized 16-bit values in k order (one 16-byte chunk).
 template <bool F16>
 __device__ __forceinline__ uint4 dequant_word(uint32_t w, const DqParams& p) {

@@ -17,16 +17,14 @@
 // Dequant and MMA.  Per 32-k step, lane (r = lane/4, c = lane%4) holds the 4
 // words of columns 4r..4r+3 at k8 row 4*step + c.  One lop3 turns a nibble
 // pair into the bf16 (fp16) pair (bias + q_i, bias + q_{i+4}), bias = 128
-// (1024), exactly; these pairs ARE the A fragments of mma.m16n8k16 (rows =
-// output columns), the activations, stored pre-permuted to the same k order,
-// are the B fragments; fp32 accumulators.  Zero point and scale are applied once
-// per segment of L = 32*SPS consecutive k inside one group:
-//     sum_k x_k (q_k - z) s  =  s * (D - (bias + z) * X),   D = sum_k x_k (bias + q_k),
-// where X = sum_k x_k over the segment comes from one more MMA with an all-ones
-// A fragment (it lands in exactly the accumulator layout the update needs).
-// This is x . ((q - z) s) with the exact fp32 dequantized weight, up to fp32
-// summation order.
-//
+// (1024), exactly; dq_pair then forms w = (q - z) * s rounded once to the
+// activation type -- the reference's own weight, int4_triton/gemm.py:211 --
+// with a subtract and a split-scale multiply-add.  These pairs ARE the A
+// fragments of mma.m16n8k16 (rows = output columns); the activations, stored
+// pre-permuted to the same k order, are the B fragments; fp32 accumulators
+// (two chains, one per k16 half of a step).  y = sum_k x_k * bf16(w_k) as in the
+// reference, up to fp32 summation order.
+
 // Reduction.  K splits inside a cluster add through distributed shared memory
 // in fixed rank order.  More than 8 splits (K > 8192) write fp32 partials to
 // the caller's workspace; the last CTA of a column tile (atomic ticket, no
@@ -346,84 +344,69 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
   }
   __syncthreads();
 
-  float acc[2][MT][4];
-  float dacc[2][MT][4];
+  // acc: the k16 halves of each step accumulate separately (two MMA chains), added at the end
+  float acc[2][MT][4], acc1[2][MT][4];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[t][mt][e] = 0.0f;
+      for (int e = 0; e < 4; ++e) acc[t][mt][e] = acc1[t][mt][e] = 0.0f;
 
   const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
-  const float bias = F16 ? 1024.0f : 128.0f;
   uint32_t wl = s_w + (warp * 32 + lane) * 16;
   uint32_t szl = s_sz + (warp * 8 + r) * 16;
-  uint32_t xsl = s_w + a.off_xs + 2 * c * 4;  // X[seg][token 2c], X[seg][token 2c + 1]
   // Token rows past M read a real row instead: their outputs are discarded, and no branch is needed.
   uint32_t xl[MT];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) xl[mt] = s_x + min(mt * 8 + r, M - 1) * a.xpitch + 16 * c;
 
+  DqParams dp[4];
   for (int st = 0; st < nstages; ++st) {
     cp_async_wait_upto(nstages - 1 - st);  // this lane's copies of stage st have landed
     __syncwarp();                           // and the scales / zeros copied by lanes c == 0
 #pragma unroll
     for (int i = 0; i < SPST; ++i) {
+      if (i % SPS == 0) {  // a new segment: scale and zero of columns 4r .. 4r + 3
+        const uint4 sz = lds128(szl + (i / SPS) * SZSEG);
+        dp[0] = dq_params<F16>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.z & 0xFFFFu));
+        dp[1] = dq_params<F16>(uint16_t(sz.x >> 16), uint16_t(sz.z >> 16));
+        dp[2] = dq_params<F16>(uint16_t(sz.y & 0xFFFFu), uint16_t(sz.w & 0xFFFFu));
+        dp[3] = dq_params<F16>(uint16_t(sz.y >> 16), uint16_t(sz.w >> 16));
+      }
       const uint4 w4 = lds128(wl + i * WSTEP);
       const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
-      uint32_t af[2][2][4];  // [row tile][k16 half][reg]
+      uint32_t af[2][2][4];  // [row tile][k16 half][reg]: the dequantized weights, rounded as the reference does
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
-          af[t][s][0] = nib_pair(wd[2 * t], 2 * s, magic);
-          af[t][s][1] = nib_pair(wd[2 * t + 1], 2 * s, magic);
-          af[t][s][2] = nib_pair(wd[2 * t], 2 * s + 1, magic);
-          af[t][s][3] = nib_pair(wd[2 * t + 1], 2 * s + 1, magic);
+          af[t][s][0] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * s, magic), dp[2 * t]);
+          af[t][s][1] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * s, magic), dp[2 * t + 1]);
+          af[t][s][2] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * s + 1, magic), dp[2 * t]);
+          af[t][s][3] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * s + 1, magic), dp[2 * t + 1]);
         }
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         const uint4 b = lds128(xl[mt] + i * 64);
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          if (i % SPS == 0) mma_16816_first<F16>(dacc[t][mt], af[t][0], b.x, b.y);
-          else mma_16816<F16>(dacc[t][mt], af[t][0], b.x, b.y);
-          mma_16816<F16>(dacc[t][mt], af[t][1], b.z, b.w);
-        }
-      }
-      if (i % SPS == SPS - 1) {  // segment complete: acc += s * (D - (bias + z) * X)
-        const uint4 sz = lds128(szl + (i / SPS) * SZSEG);
-        float sv[4], zv[4];
-        sv[0] = __half2float(__ushort_as_half(uint16_t(sz.x & 0xFFFFu)));
-        sv[1] = __half2float(__ushort_as_half(uint16_t(sz.x >> 16)));
-        sv[2] = __half2float(__ushort_as_half(uint16_t(sz.y & 0xFFFFu)));
-        sv[3] = __half2float(__ushort_as_half(uint16_t(sz.y >> 16)));
-        zv[0] = bias + __half2float(__ushort_as_half(uint16_t(sz.z & 0xFFFFu)));
-        zv[1] = bias + __half2float(__ushort_as_half(uint16_t(sz.z >> 16)));
-        zv[2] = bias + __half2float(__ushort_as_half(uint16_t(sz.w & 0xFFFFu)));
-        zv[3] = bias + __half2float(__ushort_as_half(uint16_t(sz.w >> 16)));
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          float X0, X1;
-          asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(X0), "=f"(X1)
-                       : "r"(xsl + ((i / SPS) * (8 * MT) + mt * 8) * 4));
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            acc[t][mt][0] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X0, dacc[t][mt][0]), acc[t][mt][0]);
-            acc[t][mt][1] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X1, dacc[t][mt][1]), acc[t][mt][1]);
-            acc[t][mt][2] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X0, dacc[t][mt][2]), acc[t][mt][2]);
-            acc[t][mt][3] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X1, dacc[t][mt][3]), acc[t][mt][3]);
-          }
+          mma_16816<F16>(acc[t][mt], af[t][0], b.x, b.y);
+          mma_16816<F16>(acc1[t][mt], af[t][1], b.z, b.w);
         }
       }
     }
     wl += SPST * WSTEP;
     szl += SEGST * SZSEG;
-    xsl += SEGST * (8 * MT) * 4;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) xl[mt] += SPST * 64;
   }
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[t][mt][e] += acc1[t][mt][e];
 
   // ---- outputs: acc[t][mt][e] is (token mt*8 + 2c + (e & 1), column 32*warp + 4r + 2t + (e >> 1))
   uint16_t* y = a.y;
@@ -632,78 +615,55 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
   __syncthreads();
 
   const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
-  const float bias = F16 ? 1024.0f : 128.0f;
   const uint32_t xl0 = s_x + min(r, M - 1) * a.xpitch + 16 * c;
-  const uint32_t xsl0 = s_base + a.off_xs + 2 * c * 4;
-  float acc[2][4], dacc[2][4];
+  float acc[2][4], acc1[2][4];  // the k16 halves of each step accumulate separately (two MMA chains)
   int st = 0, slot = 0;
   int64_t n_base = int64_t(gw) * 32 + 4 * r;
-  uint32_t xl = xl0, xsl = xsl0;
+  uint32_t xl = xl0;
+  DqParams dp[4];
 #pragma unroll 1
   for (int g = 0; g < total; ++g) {
     if (st == 0) {
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+        for (int e = 0; e < 4; ++e) acc[t][e] = acc1[t][e] = 0.0f;
     }
     cp_async_wait<RING - 1>();
     __syncwarp();
     const uint32_t sl = s_w + slot * (WSTAGE + SZSTAGE);
 #pragma unroll
     for (int i = 0; i < SPST; ++i) {
+      if (i % SPS == 0) {  // a new segment: scale and zero of columns 4r .. 4r + 3
+        const uint4 sz = lds128(sl + WSTAGE + (i / SPS) * 128 + r * 16);
+        dp[0] = dq_params<F16>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.z & 0xFFFFu));
+        dp[1] = dq_params<F16>(uint16_t(sz.x >> 16), uint16_t(sz.z >> 16));
+        dp[2] = dq_params<F16>(uint16_t(sz.y & 0xFFFFu), uint16_t(sz.w & 0xFFFFu));
+        dp[3] = dq_params<F16>(uint16_t(sz.y >> 16), uint16_t(sz.w >> 16));
+      }
       const uint4 w4 = lds128(sl + i * 512 + lane * 16);
       const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
-      uint32_t af[2][2][4];
+      uint32_t af[2][2][4];  // the dequantized weights, rounded as the reference does
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          af[t][q][0] = nib_pair(wd[2 * t], 2 * q, magic);
-          af[t][q][1] = nib_pair(wd[2 * t + 1], 2 * q, magic);
-          af[t][q][2] = nib_pair(wd[2 * t], 2 * q + 1, magic);
-          af[t][q][3] = nib_pair(wd[2 * t + 1], 2 * q + 1, magic);
+          af[t][q][0] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * q, magic), dp[2 * t]);
+          af[t][q][1] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * q, magic), dp[2 * t + 1]);
+          af[t][q][2] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * q + 1, magic), dp[2 * t]);
+          af[t][q][3] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * q + 1, magic), dp[2 * t + 1]);
         }
       const uint4 b = lds128(xl + i * 64);
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
-        if (i % SPS == 0) mma_16816_first<F16>(dacc[t], af[t][0], b.x, b.y);
-        else mma_16816<F16>(dacc[t], af[t][0], b.x, b.y);
-        mma_16816<F16>(dacc[t], af[t][1], b.z, b.w);
-      }
-      if (i % SPS == SPS - 1) {  // segment complete: acc += s * (D - (bias + z) * X)
-        const uint4 sz = lds128(sl + WSTAGE + (i / SPS) * 128 + r * 16);
-        float X0, X1 = 0.0f;
-        if constexpr (ONE) {
-          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(X0) : "r"(xsl + (i / SPS) * 8 * 4));
-        } else {
-          asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(X0), "=f"(X1) : "r"(xsl + (i / SPS) * 8 * 4));
-        }
-        float sv[4], zv[4];
-        sv[0] = __half2float(__ushort_as_half(uint16_t(sz.x & 0xFFFFu)));
-        sv[1] = __half2float(__ushort_as_half(uint16_t(sz.x >> 16)));
-        sv[2] = __half2float(__ushort_as_half(uint16_t(sz.y & 0xFFFFu)));
-        sv[3] = __half2float(__ushort_as_half(uint16_t(sz.y >> 16)));
-        zv[0] = bias + __half2float(__ushort_as_half(uint16_t(sz.z & 0xFFFFu)));
-        zv[1] = bias + __half2float(__ushort_as_half(uint16_t(sz.z >> 16)));
-        zv[2] = bias + __half2float(__ushort_as_half(uint16_t(sz.w & 0xFFFFu)));
-        zv[3] = bias + __half2float(__ushort_as_half(uint16_t(sz.w >> 16)));
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          acc[t][0] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X0, dacc[t][0]), acc[t][0]);
-          acc[t][2] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X0, dacc[t][2]), acc[t][2]);
-          if constexpr (!ONE) {  // the odd tokens 2c + 1 (none when M == 1)
-            acc[t][1] = fmaf(sv[2 * t], fmaf(-zv[2 * t], X1, dacc[t][1]), acc[t][1]);
-            acc[t][3] = fmaf(sv[2 * t + 1], fmaf(-zv[2 * t + 1], X1, dacc[t][3]), acc[t][3]);
-          }
-        }
+        mma_16816<F16>(acc[t], af[t][0], b.x, b.y);
+        mma_16816<F16>(acc1[t], af[t][1], b.z, b.w);
       }
     }
     __syncwarp();  // every lane is done with the slot before it is refilled
     issue_next();
     slot = slot == RING - 1 ? 0 : slot + 1;
     xl += SPST * 64;
-    xsl += SEGST * 8 * 4;
     if (++st == stages_slab) {  // slab complete: acc[t][e] is (token 2c + (e & 1), column 4r + 2t + (e >> 1))
 #pragma unroll
       for (int t = 0; t < 2; ++t)
@@ -712,12 +672,11 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
           if (ONE && (e & 1)) continue;
           const int tok = 2 * c + (e & 1);
           const int64_t n = n_base + 2 * t + (e >> 1);
-          if (tok < M && n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(acc[t][e]);
+          if (tok < M && n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(acc[t][e] + acc1[t][e]);
         }
       st = 0;
       n_base += int64_t(W) * 32;
       xl = xl0;
-      xsl = xsl0;
     }
   }
   cp_async_wait<0>();

@@ -266,7 +266,7 @@ class LlamaTP:
     ``fused`` runs a decode step's norms, rotary embedding, attention and SwiGLU
     as the library's fused kernels; ``fused=False`` runs them as the torch ops
     transformers uses.  ``persistent`` (default: whenever the model qualifies --
-    W4, one rank, fused, batch <= 8, widths multiples of 512) runs all decoder
+    W4, one rank, fused, batch <= 8, widths multiples of 2048) runs all decoder
     layers of a decode step as one launch of ``i4b_decode_layers``.
     """
 
@@ -339,11 +339,11 @@ class LlamaTP:
         self.positions = torch.arange(max_seq, device=dev)
 
         qualifies = (w4 and world == 1 and fused and hd == 64 and max_batch <= 8 and group_size in (32, 64, 128)
-                     and H % 512 == 0 and self.inter_l % 512 == 0 and (self.nh_l * hd) % 512 == 0
+                     and H % 2048 == 0 and self.inter_l % 2048 == 0 and (self.nh_l * hd) % 2048 == 0
                      and self.nh_l // self.nkv_l in (1, 2, 4, 8) and self.nh_l % self.nkv_l == 0)
         if persistent and not qualifies:
             raise ValueError("persistent decode needs W4 (G 32/64/128), one rank, fused kernels, head_dim 64, "
-                             "batch <= 8 and hidden / intermediate / q widths that are multiples of 512")
+                             "batch <= 8 and hidden / intermediate / q widths that are multiples of 2048")
         self.persistent = None
         if qualifies and persistent is not False:
             self.persistent = PersistentDecoder(

@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 LOGIT_TOL = 2e-2
 
 
-def _config(hidden=512, inter=1024, heads=8, kv=2, layers=2, vocab=512):
+def _config(hidden=2048, inter=2048, heads=32, kv=8, layers=2, vocab=512):
     from transformers import LlamaConfig
 
     return LlamaConfig(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers,
@@ -79,25 +79,40 @@ def test_tile_w4_layout(cuda_device, G):
     assert torch.equal(rec[..., 1, :], zr.view(P, gp, S, 8, 4).permute(2, 0, 1, 3, 4))
 
 
+def _noise_floor_bound(floor_model, tok, pos, ref):
+    """max(north-star bound, twice the distance of the reference's own bf16 (fake-quant) weights run
+    through the same cached-decode kernels): what bf16 rounding and the decode kernels' fp32 attention
+    allow for a single-token step at these widths, independently of the W4 arithmetic."""
+    lf = floor_model.decode_step(tok, pos).float()
+    return max(LOGIT_TOL, 2 * (lf - ref).abs().max().item())
+
+
 @torch.no_grad()
-@pytest.mark.parametrize("B", [1, 2])
-def test_persistent_decode_matches_fake_quant_reference(small, B):
+@pytest.mark.parametrize("B,kv", [(1, 8), (2, 8), (2, 4)])
+def test_persistent_decode_matches_fake_quant_reference(cuda_device, B, kv):
+    """Decode steps against the fake-quant reference (full recompute), GQA groups of 4 and 8 heads."""
+    from int4_b200 import quantize_model_linears
     from int4_b200.decode import LlamaTP
 
-    hf, fake = small
+    hf = _hf(_config(kv=kv), seed=kv)
+    fake = copy.deepcopy(hf)
+    quantize_model_linears(fake, 128, skip=("lm_head",), fake=True)
     m = LlamaTP(hf, w4=True, max_seq=128, max_batch=2)
     assert m.persistent is not None
+    floor_m = LlamaTP(fake, w4=False, max_seq=128, max_batch=2, fused=True)
     ids = _ids(B, 24, 11 + B)
-    logits = m.prefill(ids)
+    m.prefill(ids)
+    floor_m.prefill(ids)
     seq = ids
+    nxt = fake(ids).logits[:, -1:].argmax(-1).contiguous()
     for step in range(6):
-        nxt = logits[:, -1].argmax(-1, keepdim=True)
         seq = torch.cat([seq, nxt], 1)
         pos = torch.tensor([seq.shape[1] - 1], device="cuda")
-        logits = m.decode_step(nxt.contiguous(), pos)
         ref = fake(seq).logits[:, -1:].float()
-        err = (logits.float() - ref).abs().max().item()
-        assert err <= LOGIT_TOL, (step, err)
+        bound = _noise_floor_bound(floor_m, nxt, pos, ref)
+        err = (m.decode_step(nxt, pos).float() - ref).abs().max().item()
+        assert err <= bound, (step, err, bound)
+        nxt = ref[:, -1].argmax(-1, keepdim=True).contiguous()
     from int4_b200 import _lib
 
     assert _lib.device_error_flags(0) == 0
@@ -178,7 +193,7 @@ def test_persistent_decode_on_llama_1b_widths(cuda_device, B):
     quantize_model_linears(fake, 128, skip=("lm_head",), fake=True)
     a = LlamaTP(hf, w4=True, max_seq=512, max_batch=4, persistent=True)
     b = LlamaTP(hf, w4=True, max_seq=512, max_batch=4, persistent=False)
-    floor_m = LlamaTP(fake, w4=False, max_seq=512, max_batch=4, fused=False)
+    floor_m = LlamaTP(fake, w4=False, max_seq=512, max_batch=4, fused=True)
     ids = _ids(B, 300, 17, vocab=1024)
     for m in (a, b, floor_m):
         m.prefill(ids)
