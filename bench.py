@@ -337,7 +337,7 @@ def build_llama(dev, seed: int = 0):
     return model.to(torch.bfloat16).eval()
 
 
-def time_decode(m, B: int, prompt: int, steps: int, warmup: int, world: int, dev, vocab: int):
+def time_decode(m, B: int, prompt: int, steps: int, warmup: int, world: int, dev, vocab: int, trace: bool = False):
     """Prefill ``prompt`` random tokens, then time ``steps`` greedy decode steps replayed from a CUDA graph."""
     g = torch.Generator().manual_seed(7)
     ids = torch.randint(0, vocab, (B, prompt), generator=g).to(dev)
@@ -407,7 +407,11 @@ def time_decode(m, B: int, prompt: int, steps: int, warmup: int, world: int, dev
     wall = time.perf_counter() - t0
     e2e_s = max_over_ranks(max(wall, e0.elapsed_time(e1) * 1e-3), world)
     del graph
-    return {"prefill_ms": prefill_ms, "decode_s": dev_s, "e2e_s": e2e_s, "h2d": B * 8, "d2h": B * 8}
+    res = {"prefill_ms": prefill_ms, "decode_s": dev_s, "e2e_s": e2e_s, "h2d": B * 8, "d2h": B * 8}
+    if trace and getattr(m, "persistent", None) is not None:
+        reset()
+        res["trace"] = m.persistent.trace(tok, pos)
+    return res
 
 
 def run_model(args, world, rank, local):
@@ -422,7 +426,8 @@ def run_model(args, world, rank, local):
         m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world, persistent=persistent,
                     max_seq=prompt + steps + args.warmup + 8, max_batch=B, device=dev)
         with ClockSampler(local) as clk:
-            r = time_decode(m, B, prompt, steps, args.warmup, world, dev, LLAMA_1B["vocab_size"])
+            r = time_decode(m, B, prompt, steps, args.warmup, world, dev, LLAMA_1B["vocab_size"],
+                            trace=bool(args.trace) and w4)
         r["clocks"] = clk.summary()
         r["persistent"] = m.persistent is not None
         # bytes one decode step must read on this rank: projection weights + the KV cache up to the mean position
@@ -484,6 +489,8 @@ def main_model(args, world, rank, local, threads):
         return
     pk = peaks()
     w4, bf = res["w4"], res["bf16"]
+    if "trace" in w4:
+        print(json.dumps({"persistent_decode_trace": w4["trace"]}), file=sys.stderr, flush=True)
     tps = args.m * args.steps / w4["decode_s"]
     step_s = w4["decode_s"] / args.steps
     achieved = w4["bytes_per_step_rank"] / step_s / 1e9
@@ -524,6 +531,9 @@ def main():
     ap.add_argument("--lm-head-w4", type=int, default=0, help="model workload: quantize the lm_head too")
     ap.add_argument("--m", type=int, default=1, help="tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", type=int, default=0,
+                    help="model workload: after timing, trace one persistent step and print its per-stage "
+                         "breakdown as a second JSON line on stderr")
     ap.add_argument("--persistent", type=int, default=-1,
                     help="model workload: 1 = all decoder layers of a step in one launch (i4b_decode_layers), "
                          "0 = one launch per projection / glue op, -1 = whichever the model qualifies for")

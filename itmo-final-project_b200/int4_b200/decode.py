@@ -240,6 +240,57 @@ class PersistentDecoder:
         _lib.check(L.i4b_decode_workspace_size(ctypes.byref(m), ctypes.byref(nbytes)), "decode_workspace_size")
         self.ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=dev)
 
+    STAGES = ("qkv", "attention", "o_proj", "gate_up", "down_proj")
+
+    def trace(self, ids: torch.Tensor, pos: torch.Tensor) -> dict:
+        """Run one step with the kernel's trace hook on; per-stage medians over CTAs and inner layers (µs).
+
+        Projection stages: ``wait`` (entry to dependency met), ``stage_x`` (inputs staged), ``pieces``,
+        ``epilogue``, ``publish``; warp 0's ``weight_wait`` / ``mma`` per piece; ``producer_lead`` (pieces
+        the producer had issued ahead of the stage).  Attention: ``wait``, ``queries``, ``blocks``,
+        ``fence``, ``ticket``.  ``layer_us``: median CTA's time from one qkv entry to the next.
+        """
+        import numpy as np
+
+        L = self.m.layers
+        grid = torch.cuda.get_device_properties(self.h.device).multi_processor_count
+        buf = torch.zeros(grid * L * 5 * 16, dtype=torch.int64, device=self.h.device)
+        lib = _lib.lib()
+        lib.i4b_set_decode_trace(buf.data_ptr(), buf.numel() * 8)
+        try:
+            self.run(ids, pos)
+            torch.cuda.synchronize()
+        finally:
+            lib.i4b_set_decode_trace(None, 0)
+        t = buf.view(grid, L, 5, 16).cpu().numpy().astype(np.float64)
+        valid = t[..., 7] > 0
+        # SM clock from the trace itself: clock64 cycles per %globaltimer ns between stage entries of one CTA
+        cta = int(np.argmax(valid[:, :, 0].sum(1)))
+        ent = [(t[cta, l, 0, 0], t[cta, l, 0, 7]) for l in range(L) if valid[cta, l, 0]]
+        mhz = (ent[-1][0] - ent[0][0]) / max(ent[-1][1] - ent[0][1], 1) * 1e3 if len(ent) > 1 else 1965.0
+        inner = range(1, L - 1) if L > 2 else range(L)
+        out = {"sm_mhz": round(mhz, 1), "stages": {}}
+        names = [("wait", 0, 1), ("stage_x", 1, 2), ("pieces", 2, 3), ("epilogue", 3, 4), ("publish", 4, 6)]
+        anames = [("wait", 0, 1), ("queries", 1, 2), ("blocks", 2, 3), ("fence", 3, 4), ("ticket", 4, 5)]
+        for si, sname in enumerate(self.STAGES):
+            rows = np.concatenate([t[valid[:, l, si], l, si] for l in inner]) if any(
+                valid[:, l, si].any() for l in inner) else None
+            if rows is None or len(rows) == 0:
+                continue
+            d = {"ctas": int(valid[:, inner[0], si].sum())}
+            for nm, a, b in (anames if si == 1 else names):
+                d[nm] = round(float(np.median(rows[:, b] - rows[:, a])) / mhz, 2)
+            if si != 1:
+                npc = np.maximum(rows[:, 10], 1)
+                d["weight_wait_per_piece"] = round(float(np.median(rows[:, 8] / npc)) / mhz, 3)
+                d["mma_per_piece"] = round(float(np.median(rows[:, 9] / npc)) / mhz, 3)
+                d["pieces_warp0"] = float(np.median(rows[:, 10]))
+                d["producer_lead"] = float(np.median(rows[:, 11]))
+            out["stages"][sname] = d
+        g0 = [np.median(t[valid[:, l, 0], l, 0, 7]) for l in range(L) if valid[:, l, 0].any()]
+        out["layer_us"] = round(float(np.median(np.diff(g0))) / 1e3, 2) if len(g0) > 1 else None
+        return out
+
     def run(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """Residual stream [B, H] after the last layer for token ids[B, 1] at position pos (device int64)."""
         B = ids.shape[0]
