@@ -3,11 +3,12 @@
 Workload ``block``: the seven linears of one
 Llama-3.2-1B-shaped decoder block (q/k/v/o 2048-wide, gate/up 8192, down
 K=8192), weights N(0, 0.02) with 0.1% of entries x10, INT4 G=128, bf16
-activations.  A step runs them as the tensor-parallel dataflow of the block:
+activations.  A step runs them as the tensor-parallel dataflow of the block,
+the linears that share an input stacked into one projection (four launches):
 
-    q, k, v = x @ Wq/k/v^T          (column shards, N / world)
+    q|k|v = x @ [Wq;Wk;Wv]^T        (column shards, N / world)
     o = q @ Wo^T ; all-reduce(o)    (row shard, K / world; NCCL when world > 1)
-    g, u = o @ Wgate/up^T           (column shards)
+    g|u = o @ [Wgate;Wup]^T         (column shards)
     d = g @ Wdown^T ; all-reduce(d) (row shard)
 
 At M = 1 this is one decoder block's decode-step GEMV work (32.4 MB of packed
@@ -181,27 +182,31 @@ def block_weights(rank: int, world: int, copies: int, dev):
         for _ in range(copies - 1):
             qs.append(tuple(t.clone() for t in qs[0]))
         layers.append((name, w.shape[0], w.shape[1], qs))
-    return layers
+    # q|k|v and gate|up share their input: each group runs as one stacked projection (quantization is per
+    # output column, so stacking the quantized tensors is the same bits as quantizing the stacked weight)
+    def stack(ids):
+        n = sum(layers[i][1] for i in ids)
+        qs = [tuple(torch.cat([layers[i][3][c][t] for i in ids], dim=1) for t in range(3)) for c in range(copies)]
+        return ("|".join(layers[i][0] for i in ids), n, layers[ids[0]][2], qs, [layers[i][1] for i in ids])
+    return [stack([0, 1, 2]), layers[3] + ([layers[3][1]],), stack([4, 5]), layers[6] + ([layers[6][1]],)]
 
 
 def block_step(x, layers, copy: int, world: int):
+    """The block's dataflow as four launches: q|k|v, o_proj, gate|up, down_proj (+ all-reduces under TP)."""
     import int4_b200 as ib
 
     def mm(i, inp):
         qw, s, z = layers[i][3][copy]
         return ib.w4a16_matmul(inp, qw, s, z)
 
-    q = mm(0, x)
-    mm(1, x)
-    mm(2, x)
-    o = mm(3, q)
+    qkv = mm(0, x)
+    o = mm(1, qkv[:, :layers[0][4][0]])
     if world > 1:
         import torch.distributed as dist
 
         dist.all_reduce(o)
-    g = mm(4, o)
-    mm(5, o)
-    d = mm(6, g)
+    gu = mm(2, o)
+    d = mm(3, gu[:, :layers[2][4][0]])
     if world > 1:
         import torch.distributed as dist
 
@@ -283,13 +288,15 @@ def run_block(args, world, rank, local):
     e2e_us = max_over_ranks(max(t_dev, wall), world) * 1e6 / args.steps
 
     flags = _lib.device_error_flags(local)
-    total_bytes = sum(alg_bytes(M, l[1], l[2]) for l in layers)
-    total_flops = sum(2 * M * l[1] * l[2] for l in layers)
+    # algorithmic bytes / flops of the seven linears (shard shapes), as the metric defines them
+    shards = [((N // world if c else N), (K if c else K // world)) for (_, N, K, c) in BLOCK]
+    total_bytes = sum(alg_bytes(M, n, k) for (n, k) in shards)
+    total_flops = sum(2 * M * n * k for (n, k) in shards)
     del graph, graph_hot, graph_e2e
     return {
         "us_per_step": us_per_step, "hot_us": hot_us, "e2e_us": e2e_us, "clocks": clk.summary(),
         "bytes_per_step_rank": total_bytes, "flops_per_step_rank": total_flops, "copies": copies,
-        "launches_per_step": len(BLOCK), "device_error_flags": flags,
+        "launches_per_step": len(layers), "device_error_flags": flags,
         "h2d": M * 2048 * 2, "d2h": M * 2048 * 2,
     }
 
@@ -621,7 +628,7 @@ def main():
             "block_gbs_per_gpu": achieved, "block_us_l2_hot": r["hot_us"],
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": prof_traffic,
-                         "kernel": "w4_skinny_kernel (decode GEMV), all 7 launches of a step",
+                         "kernel": "w4_skinny_kernel (decode GEMV), the 4 launches of a step (q|k|v, o, gate|up, down)",
                          "peak_source": pk["source"]},
             "cpu_baseline": cpu,
             "e2e": {"value": r["e2e_us"], "unit": "us", "h2d_bytes_per_step": r["h2d"],

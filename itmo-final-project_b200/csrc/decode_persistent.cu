@@ -67,6 +67,7 @@ constexpr int kMaxItems = 16;        // slabs per CTA per layer
 constexpr int kMaxTok = 8;
 constexpr int kHD = 64;
 constexpr int kPartRow = 68;  // floats per attention partial: o[64], m, l, padding to 16 bytes
+constexpr int kAttnMinSplit = 32;  // cached positions per attention split, at least (short contexts use fewer)
 
 enum { G_QKV = 0, G_O = 1, G_GU = 2, G_DOWN = 3 };                       // GEMV stages
 enum { C_QKV = 0, C_ATTN = 1, C_O = 2, C_GU = 3, C_DOWN = 4, C_LAYER = 5 };  // counters of a layer
@@ -259,109 +260,86 @@ struct Smem {
   volatile int prod_seq;  // pieces issued by the producer so far (diagnostics)
 };
 
-constexpr int kXR = 8;  // 16-byte activation chunks per thread in flight
 constexpr int kResPerThread = 4;  // residual values per thread: o / down slabs x tokens x 32 <= kCT * 4
 
 // Stage the activations of GEMV stage g into shared memory: x permuted to the nibble-pair order of the
-// A fragments, [token][k / 8] x 16 bytes with row pitch xpitch.  The B rows' chunks (8 consecutive k) are
-// numbered token-major and thread tid owns chunks tid, tid + kCT, ...; rounds of kXR chunks put all
-// their loads in flight before any is used.  RMSNorm stages (every row chunk of a thread in one round:
-// B * K <= 8 * kCT * kXR, checked on the host) compute x = bf16(w * bf16(h * rsqrt(mean(h^2) + eps)))
-// (LlamaRMSNorm) once the block-wide sums of squares are known.
-template <int SPS>
+// A fragments, [token][k / 8] x 16 bytes with row pitch xpitch.  Written as plain (not unrolled) loops:
+// this code runs once per stage and must stay small in the instruction cache.  (1) every 16-byte chunk
+// of every token row is put in flight with cp.async straight into its staging slot; (2) RMSNorm stages
+// take per-token sums of squares over the staged rows (fixed order: lanes, then warps); (3) each thread
+// rewrites its chunks in place: x = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) (LlamaRMSNorm) where
+// needed, then the permutation.
 __device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int g, int l, int K) {
   const i4b_decode_model& m = P.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = m.batch, H = m.hidden;
   const bool norm = g == G_QKV || g == G_GU;
+  const bool emb = g == G_QKV && l == 0;
   const uint16_t* nw = static_cast<const uint16_t*>(g == G_QKV ? m.ln1 : m.ln2) + int64_t(l) * H;
-  const uint16_t* hbuf = static_cast<const uint16_t*>(m.h_out);
-  const uint16_t* emb = static_cast<const uint16_t*>(m.embed);
-  // base and stride of the token rows: the embedding rows in layer 0 (qkv), else h / att / act
-  const uint16_t* rows[kMaxTok];
-  {
-    const uint16_t* src = g == G_O ? P.att : g == G_DOWN ? P.act : hbuf;
-    const int64_t stride = g == G_O ? P.q_n : g == G_DOWN ? m.intermediate : H;
-#pragma unroll
-    for (int t = 0; t < kMaxTok; ++t) {
-      if (g == G_QKV && l == 0 && t < B) {
-        int64_t id = m.tokens[t];
-        if (id < 0 || id >= m.vocab) id = 0;
-        rows[t] = emb + id * H;
-      } else {
-        rows[t] = src + t * stride;
-      }
-    }
-  }
+  const uint16_t* src = g == G_O ? P.att : g == G_DOWN ? P.act : static_cast<const uint16_t*>(m.h_out);
+  const int64_t stride = g == G_O ? P.q_n : g == G_DOWN ? m.intermediate : H;
   uint8_t* sx = smem + P.off_x;
-  const int lg = 31 - __clz(K / 8);  // chunks per row = 2^lg (host check)
-  const int total = B << lg;
-  for (int base = 0; base < total; base += kCT * kXR) {
-    uint4 v[kXR];
-#pragma unroll
-    for (int r = 0; r < kXR; ++r) {
-      const int idx = base + r * kCT + tid;
-      if (idx < total) {
-        const int t = idx >> lg, ch = idx & ((1 << lg) - 1);
-        v[r] = ldcg128(rows[t] + 8 * ch);
-        if (norm) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + 8 * ch));  // read after the statistics
-      }
+  const int nch = K / 8, lg = 31 - __clz(nch), total = B << lg;  // chunks per row: a power of two
+#pragma unroll 1
+  for (int idx = tid; idx < total; idx += kCT) {
+    const int t = idx >> lg, ch = idx & (nch - 1);
+    const uint16_t* row = src + t * stride;
+    if (emb) {
+      int64_t id = m.tokens[t];
+      if (id < 0 || id >= m.vocab) id = 0;
+      row = static_cast<const uint16_t*>(m.embed) + id * H;
     }
-    if (norm) {  // one round holds every row chunk (host check); a warp's 32 chunks share one token
-      float ssum[kMaxTok];
+    cp_async_16(sx + t * P.xpitch + ch * 16, row + 8 * ch, 16);
+    if (norm) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + 8 * ch));  // read in step (3)
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  cbar();
+  if (norm) {
+#pragma unroll 1
+    for (int t = 0; t < B; ++t) {
+      float ss = 0.0f;
+#pragma unroll 1
+      for (int ch = tid; ch < nch; ch += kCT) {
+        const uint4 v = *reinterpret_cast<const uint4*>(sx + t * P.xpitch + ch * 16);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int t = 0; t < kMaxTok; ++t) ssum[t] = 0.0f;
-#pragma unroll
-      for (int r = 0; r < kXR; ++r) {
-        const int idx = base + r * kCT + tid;
-        if (idx < total) {  // warp-uniform
-          const uint32_t u[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
-          float ss = 0.0f;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float lo = bfv(u[i] & 0xFFFFu), hi = bfv(u[i] >> 16);
-            ss = fmaf(lo, lo, ss);
-            ss = fmaf(hi, hi, ss);
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-          const int t = idx >> lg;
-#pragma unroll
-          for (int tt = 0; tt < kMaxTok; ++tt)
-            if (tt == t) ssum[tt] += ss;
+        for (int i = 0; i < 4; ++i) {
+          const float lo = bfv(u[i] & 0xFFFFu), hi = bfv(u[i] >> 16);
+          ss = fmaf(lo, lo, ss);
+          ss = fmaf(hi, hi, ss);
         }
       }
-      if (lane == 0)
-        for (int t = 0; t < B; ++t) S.wss[warp * kMaxTok + t] = ssum[t];
-      cbar();
-      if (tid < B) {
-        float sum = 0.0f;
-        for (int w = 0; w < kCW; ++w) sum += S.wss[w * kMaxTok + tid];
-        S.inv[tid] = rsqrtf(sum / float(K) + m.eps);
-      }
-      cbar();
-    }
 #pragma unroll
-    for (int r = 0; r < kXR; ++r) {
-      const int idx = base + r * kCT + tid;
-      if (idx < total) {
-        const int t = idx >> lg, ch = idx & ((1 << lg) - 1);
-        uint32_t u[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
-        if (norm) {
-          const float inv = S.inv[t];
-          const uint4 wv = __ldg(reinterpret_cast<const uint4*>(nw + 8 * ch));
-          const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            u[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(u[i] & 0xFFFFu) * inv))) |
-                   (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(u[i] >> 16) * inv))) << 16);
-        }
-        // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
-        *reinterpret_cast<uint4*>(sx + t * P.xpitch + ch * 16) =
-            make_uint4(__byte_perm(u[0], u[2], 0x5410), __byte_perm(u[0], u[2], 0x7632),
-                       __byte_perm(u[1], u[3], 0x5410), __byte_perm(u[1], u[3], 0x7632));
-      }
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+      if (lane == 0) S.wss[warp * kMaxTok + t] = ss;
     }
+    cbar();
+    if (tid < B) {
+      float sum = 0.0f;
+      for (int w = 0; w < kCW; ++w) sum += S.wss[w * kMaxTok + tid];
+      S.inv[tid] = rsqrtf(sum / float(K) + m.eps);
+    }
+    cbar();
+  }
+#pragma unroll 1
+  for (int idx = tid; idx < total; idx += kCT) {
+    const int t = idx >> lg, ch = idx & (nch - 1);
+    uint4* pchunk = reinterpret_cast<uint4*>(sx + t * P.xpitch + ch * 16);
+    const uint4 v = *pchunk;
+    uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    if (norm) {
+      const float inv = S.inv[t];
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(nw + 8 * ch));
+      const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        u[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(u[i] & 0xFFFFu) * inv))) |
+               (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(u[i] >> 16) * inv))) << 16);
+    }
+    // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
+    *pchunk = make_uint4(__byte_perm(u[0], u[2], 0x5410), __byte_perm(u[0], u[2], 0x7632),
+                         __byte_perm(u[1], u[3], 0x5410), __byte_perm(u[1], u[3], 0x7632));
   }
 }
 
@@ -398,7 +376,7 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
   if (!S.flag) return false;
   stamp(P, l, st_id, 1);
   const int K = g == G_DOWN ? m.intermediate : (g == G_O ? P.q_n : m.hidden);
-  stage_x<SPS>(P, S, smem, g, l, K);
+  stage_x(P, S, smem, g, l, K);
   cbar();
   stamp(P, l, st_id, 2);
   // residual inputs of the o_proj / down_proj epilogue: loaded here, consumed after the pieces
@@ -425,8 +403,8 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
     }
   }
 
-  // ---- pieces: piece q = i * Pc + p of this stage goes to warp q % kCW
-  const int Pc = P.npiece[g], J = Pc < kCW ? Pc : kCW;
+  // ---- pieces: piece q = i * ppi + p of this stage goes to warp q % kCW
+  const int ppi = P.npiece[g], J = ppi < kCW ? ppi : kCW;
   float* part = reinterpret_cast<float*>(smem + P.off_part);
   const int r = lane >> 2, c = lane & 3;
   const uint8_t* xl = smem + P.off_x + min(r, B - 1) * P.xpitch + 16 * c;
@@ -443,23 +421,24 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
         if (tok < B) pp[tok * 32 + col] = acc[t][e];
       }
   };
-  const int total = n * Pc;
+  const int total = n * ppi;
   const int seq0 = l * S.ppl;
   if (tid == 0) trace_put(P, l, st_id, 11, S.prod_seq - (seq0 + S.poff[ib]));
   long long t_wait = 0, t_mma = 0;
   int npc = 0;
+#pragma unroll 1
   for (int q = warp; q < total; q += kCW) {
-    const int i = q / Pc, p = q - i * Pc;
+    const int i = q / ppi, pl = q - i * ppi, p = pl;
     if (i != cur) {
       if (cur >= 0) flush(cur, cur_j);
       cur = i;
-      cur_j = p % kCW;
+      cur_j = pl % kCW;
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
     }
-    const int seq = seq0 + S.poff[ib + i] + p;
+    const int seq = seq0 + S.poff[ib + i] + pl;
     const int slot = seq % P.nslot;
     const long long c0 = clock64();
     if (!wait_slot(&S.full[slot], uint32_t(seq / P.nslot) & 1u, abort_word)) {
@@ -487,6 +466,7 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
 
   // ---- epilogue: fixed-order sum of the partials of each slab, then the stage's output operation
   if (g == G_GU) {
+#pragma unroll 1
     for (int idx = tid; idx < n * B * 16; idx += kCT) {
       const int i = idx / (B * 16), rem = idx - i * B * 16, b = rem / 16, pr = rem % 16;
       float gs = 0.0f, us = 0.0f;
@@ -505,11 +485,11 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
       const int idx = tid + k * kCT;
       if (idx >= n * B * 32) break;
       const int i = idx / (B * 32), rem = idx - i * B * 32, b = rem / 32, col = rem % 32;
-      float s = 0.0f;
-      for (int j = 0; j < J; ++j) s += part[(i * J + j) * (B * 32) + b * 32 + col];
+      float sum = 0.0f;
+      for (int j = 0; j < J; ++j) sum += part[(i * J + j) * (B * 32) + b * 32 + col];
       const int64_t nn = int64_t(S.slab[ib + i]) * 32 + col;
-      if (g == G_QKV) P.qkv[int64_t(b) * P.qkv_n + nn] = uint16_t(bfr(s));
-      else h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(s))));
+      if (g == G_QKV) P.qkv[int64_t(b) * P.qkv_n + nn] = uint16_t(bfr(sum));
+      else h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(sum))));
     }
   }
   cbar();
@@ -530,9 +510,15 @@ template <int GS>
 __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* smem, int l, int a) {
   const i4b_decode_model& m = P.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nkv = m.kv_heads, ns = P.nsplit, nq = m.heads;
-  const int b = a / (nkv * ns), kvh = (a / ns) % nkv, j = a % ns;
+  const int nkv = m.kv_heads, nsplit = P.nsplit, nq = m.heads;
+  const int b = a / (nkv * nsplit), kvh = (a / nsplit) % nkv, j = a % nsplit;
   const unsigned int* abort_word = P.ctr + P.i_abort;
+  const int64_t pos = *m.pos;
+  const bool pvalid = pos >= 0 && pos < m.max_seq;
+  const int Lp = pvalid ? int(pos) + 1 : 0;
+  // splits in use: at least kAttnMinSplit positions each, so that short contexts combine fewer partials
+  const int ns = max(1, min(nsplit, (Lp + kAttnMinSplit - 1) / kAttnMinSplit));
+  if (j >= ns) return true;
   stamp(P, l, C_ATTN, 0);
   if (tid == 0 && !wait_counter(P.ctr + l * C_LAYER + C_QKV, unsigned(P.nslab[G_QKV]), abort_word)) S.flag = 0;
   abar();
@@ -543,9 +529,6 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   float* sm = sc + GS * kHD;                              // [GS] running max, [GS] running sum, [GS] rescale
   float* sl = sm + GS;
   float* scr = sl + GS;
-  const int64_t pos = *m.pos;
-  const bool pvalid = pos >= 0 && pos < m.max_seq;
-  const int Lp = pvalid ? int(pos) + 1 : 0;
   const int chunk = (Lp + ns - 1) / ns;
   const int i0 = j * chunk, i1 = min(Lp, i0 + chunk);
   const uint16_t* qrow = P.qkv + int64_t(b) * P.qkv_n;
@@ -594,6 +577,7 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[hh][e] = 0.0f;
   const float scale = m.attn_scale;
+#pragma unroll 1
   for (int blk = i0; blk < i1; blk += 64) {
     // this block's keys (thread: position tid / 4, 16 dims) and values (warp w: dims 8w..8w+7 of positions
     // lane and lane + 32) are all put in flight first
@@ -714,10 +698,11 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   // last split of (b, kvh): out = sum_j o_j e^(m_j - M) / sum_j l_j e^(m_j - M), splits in order.  All
   // partials are copied to shared memory first, every load in flight at once.
   __threadfence();
-  const float4* base = reinterpret_cast<const float4*>(P.apart + int64_t(a - j) * GS * kPartRow);
+  const float4* base = reinterpret_cast<const float4*>(P.apart + int64_t(a - j) * GS * kPartRow);  // split 0
   // [ns][GS][kPartRow] partials, 16-byte aligned after the rescale factors
   float4* cm = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(scr + GS) + 15) & ~uintptr_t(15));
   const int n4 = ns * GS * kPartRow / 4;
+#pragma unroll 1
   for (int q0 = tid; q0 < n4; q0 += 4 * kAT) {
     float4 t4[4];
 #pragma unroll
@@ -729,6 +714,7 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   }
   abar();
   const float* cf = reinterpret_cast<const float*>(cm);
+#pragma unroll 1
   for (int idx = tid; idx < GS * kHD; idx += kAT) {
     const int hh = idx / kHD, d = idx % kHD;
     float M = -INFINITY;
@@ -801,9 +787,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
       int seq = 0;
       for (int l = 0; l < m.layers && ok; ++l) {
         for (int i = 0; i < S.nit && ok; ++i) {
-          const int g = S.stage[i], Pc = P.npiece[g];
-          const uint8_t* src = wsrc[g] + int64_t(l) * P.layer_bytes[g] + int64_t(S.slab[i]) * Pc * P.piece_bytes;
-          for (int p = 0; p < Pc; ++p, ++seq) {
+          const int g = S.stage[i], ppi = P.npiece[g];
+          const uint8_t* src = wsrc[g] + int64_t(l) * P.layer_bytes[g] + int64_t(S.slab[i]) * ppi * P.piece_bytes;
+          for (int p = 0; p < ppi; ++p, ++seq) {
             const int slot = seq % P.nslot;
             if (seq >= P.nslot && !wait_slot(&S.empty[slot], uint32_t(seq / P.nslot - 1) & 1u, abort_word)) {
               ok = false;
@@ -958,7 +944,6 @@ int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
   // every projection input width is a power-of-two number of 8-value chunks, at least 256
   auto pow2_chunks = [](int k) { return k >= 2048 && k % 8 == 0 && ((k / 8) & (k / 8 - 1)) == 0; };
   if (!pow2_chunks(m.hidden) || !pow2_chunks(m.intermediate) || !pow2_chunks(q_n)) return I4B_ERR_SHAPE;
-  if (int64_t(m.batch) * m.hidden > int64_t(8) * kCT * kXR) return I4B_ERR_SHAPE;  // RMSNorm rows in one round
   L->gqa = gqa;
   L->q_n = q_n;
   L->qkv_n = qkv_n;
