@@ -524,11 +524,16 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   abar();
   if (!S.flag) return false;
   stamp(P, l, C_ATTN, 1);
-  float* qs = reinterpret_cast<float*>(smem + P.off_x);  // [GS][64] rotated queries
-  float* sc = qs + GS * kHD;                              // [GS][64] scores, then probabilities
-  float* sm = sc + GS * kHD;                              // [GS] running max, [GS] running sum, [GS] rescale
-  float* sl = sm + GS;
-  float* scr = sl + GS;
+  // scratch (the activation staging area): rotated queries, this block's keys and values, probabilities,
+  // running max / sum / rescale per head
+  constexpr int KP = 33;  // words per staged key row: 32 bf16 pairs + 1, so that 32 positions hit 32 banks
+  float* qs = reinterpret_cast<float*>(smem + P.off_x);   // [GS][64]
+  uint32_t* ks = reinterpret_cast<uint32_t*>(qs + GS * kHD);  // [64][KP] bf16 pairs
+  uint16_t* vs = reinterpret_cast<uint16_t*>(ks + 64 * KP);   // [64][64]
+  float* pr = reinterpret_cast<float*>(vs + 64 * kHD);        // [GS][64]
+  float* sm = pr + GS * kHD;                                  // [GS] running max
+  float* sl = sm + GS;                                        // [GS] running sum
+  float* scr = sl + GS;                                       // [GS] rescale of this block
   const int chunk = (Lp + ns - 1) / ns;
   const int i0 = j * chunk, i1 = min(Lp, i0 + chunk);
   const uint16_t* qrow = P.qkv + int64_t(b) * P.qkv_n;
@@ -546,6 +551,7 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
     s0 = bfv(__ldg(sinT + pos * kHD + lane));
     s1 = bfv(__ldg(sinT + pos * kHD + lane + 32));
   }
+#pragma unroll 1
   for (int hh = warp; hh < GS; hh += kAW) {
     const uint16_t* src = qrow + (kvh * GS + hh) * kHD;
     const float x0 = bfv(ldcg16(src + lane)), x1 = bfv(ldcg16(src + lane + 32));
@@ -571,54 +577,49 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   abar();  // rotated queries ready, the new cache row visible to this CTA
   stamp(P, l, C_ATTN, 2);
 
-  float acc[GS][8];
+  // thread (head hh = tid / 64 + 4 pass, index x = tid % 64): position x of the block for the scores,
+  // dimension x for the output, whose sum over positions it owns outright
+  const int x = tid & 63, hq = tid >> 6;
+  float acc[(GS + 3) / 4];
 #pragma unroll
-  for (int hh = 0; hh < GS; ++hh)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[hh][e] = 0.0f;
+  for (int u = 0; u < (GS + 3) / 4; ++u) acc[u] = 0.0f;
   const float scale = m.attn_scale;
 #pragma unroll 1
   for (int blk = i0; blk < i1; blk += 64) {
-    // this block's keys (thread: position tid / 4, 16 dims) and values (warp w: dims 8w..8w+7 of positions
-    // lane and lane + 32) are all put in flight first
-    const int i = tid >> 2, qd = tid & 3, pi = blk + i;
-    uint4 k0 = make_uint4(0u, 0u, 0u, 0u), k1 = k0, vv[2] = {k0, k0};
-    if (pi < i1) {
-      k0 = ldcg128(kc + int64_t(pi) * kHD + 16 * qd);
-      k1 = ldcg128(kc + int64_t(pi) * kHD + 16 * qd + 8);
-    }
+    const int nb = min(64, i1 - blk);
+    // keys (4-byte copies into conflict-free rows) and values (16-byte copies), all in flight at once
+#pragma unroll 1
+    for (int c = tid; c < nb * 32; c += kAT)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ks + (c >> 5) * KP + (c & 31))),
+                   "l"(kc + int64_t(blk) * kHD + 2 * c)
+                   : "memory");
+#pragma unroll 1
+    for (int c = tid; c < nb * 8; c += kAT) cp_async_16(vs + c * 8, vc + int64_t(blk) * kHD + c * 8, 16);
+    cp_async_commit();
+    cp_async_wait<0>();
+    abar();
+    // scores s[hh][x] = q[hh] . k[x] * scale
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
-      if (blk + lane + 32 * u < i1) vv[u] = ldcg128(vc + int64_t(blk + lane + 32 * u) * kHD + 8 * warp);
-    {  // scores
-      float d[GS];
-#pragma unroll
-      for (int hh = 0; hh < GS; ++hh) d[hh] = 0.0f;
-      if (pi < i1) {
-        const uint32_t u[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float klo = bfv(u[e] & 0xFFFFu), khi = bfv(u[e] >> 16);
-#pragma unroll
-          for (int hh = 0; hh < GS; ++hh) {
-            d[hh] = fmaf(qs[hh * kHD + 16 * qd + 2 * e], klo, d[hh]);
-            d[hh] = fmaf(qs[hh * kHD + 16 * qd + 2 * e + 1], khi, d[hh]);
-          }
+    for (int u = 0; u < (GS + 3) / 4; ++u) {
+      const int hh = hq + 4 * u;
+      if (hh < GS) {
+        float d = 0.0f;
+        const uint32_t* kr = ks + x * KP;
+        const float* q = qs + hh * kHD;
+#pragma unroll 8
+        for (int w = 0; w < 32; ++w) {
+          const uint32_t kw = kr[w];
+          d = fmaf(q[2 * w], bfv(kw & 0xFFFFu), d);
+          d = fmaf(q[2 * w + 1], bfv(kw >> 16), d);
         }
-      }
-#pragma unroll
-      for (int hh = 0; hh < GS; ++hh) {
-        d[hh] += __shfl_xor_sync(0xFFFFFFFFu, d[hh], 1);
-        d[hh] += __shfl_xor_sync(0xFFFFFFFFu, d[hh], 2);
-      }
-      if (qd == 0) {
-#pragma unroll
-        for (int hh = 0; hh < GS; ++hh) sc[hh * kHD + i] = pi < i1 ? d[hh] * scale : -INFINITY;
+        pr[hh * kHD + x] = x < nb ? d * scale : -INFINITY;
       }
     }
     abar();
-    for (int hh = warp; hh < GS; hh += kAW) {  // online softmax of head hh over this block
-      const float x0 = sc[hh * kHD + lane], x1 = sc[hh * kHD + lane + 32];
+    // online softmax per head (warp hh)
+#pragma unroll 1
+    for (int hh = warp; hh < GS; hh += kAW) {
+      const float x0 = pr[hh * kHD + lane], x1 = pr[hh * kHD + lane + 32];
       float mb = fmaxf(x0, x1);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, o));
@@ -627,8 +628,8 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
       float su = p0 + p1;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) su += __shfl_xor_sync(0xFFFFFFFFu, su, o);
-      sc[hh * kHD + lane] = p0;
-      sc[hh * kHD + lane + 32] = p1;
+      pr[hh * kHD + lane] = p0;
+      pr[hh * kHD + lane + 32] = p1;
       __syncwarp();
       if (lane == 0) {
         const float corr = expf(mo - mn);  // 0 for the first block (mo = -inf)
@@ -638,46 +639,25 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
       }
     }
     abar();
-    {  // o += p . V: warp w owns dims 8w..8w+7, lane the positions lane and lane + 32 of the block
+    // o[hh][x] = o[hh][x] * rescale + sum over the block's positions of p * v[., x]
 #pragma unroll
-      for (int hh = 0; hh < GS; ++hh) {
-        const float corr = scr[hh];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[hh][e] *= corr;
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (blk + lane + 32 * u < i1) {
-          const uint32_t w[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
-#pragma unroll
-          for (int hh = 0; hh < GS; ++hh) {
-            const float pr = sc[hh * kHD + lane + 32 * u];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              acc[hh][2 * e] = fmaf(pr, bfv(w[e] & 0xFFFFu), acc[hh][2 * e]);
-              acc[hh][2 * e + 1] = fmaf(pr, bfv(w[e] >> 16), acc[hh][2 * e + 1]);
-            }
-          }
-        }
+    for (int u = 0; u < (GS + 3) / 4; ++u) {
+      const int hh = hq + 4 * u;
+      if (hh < GS) {
+        float o = acc[u] * scr[hh];
+        const float* ph = pr + hh * kHD;
+#pragma unroll 4
+        for (int t = 0; t < nb; ++t) o = fmaf(ph[t], bfv(vs[t * kHD + x]), o);
+        acc[u] = o;
       }
     }
-    abar();  // the block's probabilities are read before the next block's scores overwrite them
+    abar();  // the block's keys, values and probabilities are read before the next block overwrites them
   }
-#pragma unroll
-  for (int hh = 0; hh < GS; ++hh)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float v = acc[hh][e];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-      acc[hh][e] = v;
-    }
   float* mine = P.apart + int64_t(a) * GS * kPartRow;
-  if (lane == 0) {
 #pragma unroll
-    for (int hh = 0; hh < GS; ++hh)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mine[hh * kPartRow + 8 * warp + e] = acc[hh][e];
+  for (int u = 0; u < (GS + 3) / 4; ++u) {
+    const int hh = hq + 4 * u;
+    if (hh < GS) mine[hh * kPartRow + x] = acc[u];
   }
   if (tid < GS) {
     const bool any = i1 > i0;
@@ -699,8 +679,8 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
   // partials are copied to shared memory first, every load in flight at once.
   __threadfence();
   const float4* base = reinterpret_cast<const float4*>(P.apart + int64_t(a - j) * GS * kPartRow);  // split 0
-  // [ns][GS][kPartRow] partials, 16-byte aligned after the rescale factors
-  float4* cm = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(scr + GS) + 15) & ~uintptr_t(15));
+  // [ns][GS][kPartRow] partials, over the (now dead) key / value staging rows
+  float4* cm = reinterpret_cast<float4*>(ks);
   const int n4 = ns * GS * kPartRow / 4;
 #pragma unroll 1
   for (int q0 = tid; q0 < n4; q0 += 4 * kAT) {
@@ -1093,7 +1073,8 @@ int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin,
   p.h.xpitch = 2 * kmax + 16;
   auto al = [](int v) { return (v + 127) & ~127; };
   // attention: queries, scores, running max / sum / rescale, then the partials of all splits when combining
-  const int attn_bytes = (2 * L.gqa * kHD + 3 * L.gqa + 4) * 4 + L.nsplit * L.gqa * kPartRow * 4;
+  const int attn_block = (2 * L.gqa * kHD + 3 * L.gqa) * 4 + 64 * 33 * 4 + 64 * kHD * 2;
+  const int attn_bytes = std::max(attn_block, L.gqa * kHD * 4 + L.nsplit * L.gqa * kPartRow * 4);
   const int x_bytes = al(std::max(m.batch * p.h.xpitch, attn_bytes));
   const int xs_bytes = 0;
   const int part_bytes = al(sc->max_part * m.batch * 32 * 4);
