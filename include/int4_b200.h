@@ -221,11 +221,12 @@ typedef struct i4b_decode_model {
   void* h_out;           /* bf16 [batch, hidden]: the residual stream after the last layer */
 } i4b_decode_model;
 
-/* Bytes of the tiled form of a quantize_int4 triple; 0 when N % 32, K % 512 or G is unsupported. */
+/* Bytes of the tiled form of a quantize_int4 triple; 0 when N % 16, K % 512 or G is unsupported. */
 size_t i4b_tile_w4_bytes(int64_t N, int64_t K, int group_size);
 
-/* Re-lay qweight[K/8, N] (+ scales / zeros [K/G, N]) into 32-column x 512-k pieces of packed words followed
- * by their scales and zeros, the order in which the persistent decode streams them. */
+/* Re-lay qweight[K/8, N] (+ scales / zeros [K/G, N]) into 16-column x 512-k pieces of packed words (4 KB)
+ * followed by their scales and zeros (64 bytes per group), slab by slab, the order in which the persistent
+ * decode streams them. */
 int i4b_tile_w4(const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales, const uint16_t* zeros,
                 int64_t stride_sg, int64_t K, int group_size, void* out, void* stream);
 

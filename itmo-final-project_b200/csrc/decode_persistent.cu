@@ -9,10 +9,11 @@
 // the whole stack of layers is one kernel, organised around the fact that the
 // weights do not depend on the data:
 //
-// * Weight stream.  Each CTA owns a fixed list of 32-column slabs of the four
-//   projections of every layer (the same list in every layer).  A producer warp
-//   streams those slabs, as 8 KB pieces of packed words plus their scales and
-//   zeros, from HBM into a ring of shared-memory slots with bulk copies
+// * Weight stream.  Each CTA owns a fixed list of 16-column slabs of the four
+//   projections of every layer (the same list in every layer; every stage's
+//   slabs spread evenly over all CTAs).  A producer warp streams those slabs, as
+//   4 KB pieces of packed words plus their scales and zeros, from HBM into a
+//   ring of shared-memory slots with bulk copies
 //   (cp.async.bulk, completion on an mbarrier per slot), in the order the CTA
 //   will use them, running ahead across stage and layer boundaries as far as the
 //   ring allows.  The packed weights are pre-tiled once (i4b_tile_w4) so that
@@ -27,11 +28,11 @@
 //   While compute warps wait, the producer keeps streaming: the critical path of
 //   a layer is five such hand-offs plus compute on weights already on chip.
 // * GEMV arithmetic is the decode GEMV's (gemv_w4.cu): one lop3 turns a nibble
-//   pair into the bf16 pair (128 + q_i, 128 + q_{i+4}), the A fragment of an
-//   mma.m16n8k16 with output columns as rows and tokens as the 8 columns; zero and
-//   scale are applied once per group, sum_k x (q - z) s = s (D - (128 + z) X),
-//   with X the group sums of the activations.  The 8 compute warps split a
-//   stage's pieces; fp32 partials of one slab are added in a fixed order.
+//   pair into the bf16 pair (128 + q_i, 128 + q_{i+4}), three bf16x2 operations
+//   turn it into the reference's weights (q - z) * s rounded once to bf16
+//   (dq_pair), which are the A fragment of an mma.m16n8k16 with a slab's 16
+//   output columns as rows and tokens as the 8 columns.  The 8 compute warps
+//   split a stage's pieces; fp32 partials of one slab are added in a fixed order.
 // * Attention: items (token, kv head, sequence split), one per CTA; the last
 //   split of a (token, kv head) to finish (atomic ticket) combines the fp32
 //   partial softmax sums in split order.
@@ -59,11 +60,13 @@ constexpr int kCT = kCW * 32;        // compute threads
 constexpr int kThreads = kCT + 32;   // + the producer warp
 constexpr int kAW = 8;               // warps of an attention item (one per 8 of the 64 head dims)
 constexpr int kAT = kAW * 32;
+constexpr int kSlabW = 16;           // output columns of one slab (the rows of one m16n8k16 tile)
 constexpr int kPieceK = 512;         // k of one weight piece
-constexpr int kPieceW = 8192;        // packed-word bytes of one piece (32 columns x 512 k x 4 bit)
-constexpr int kMaxSlots = 32;
+constexpr int kPieceW = 4096;        // packed-word bytes of one piece (16 columns x 512 k x 4 bit)
+constexpr int kRecB = 64;            // bytes of one group's scale / zero records in a piece (16 columns x 2 x fp16)
+constexpr int kMaxSlots = 48;
 constexpr int kMaxCtas = 160;
-constexpr int kMaxItems = 16;        // slabs per CTA per layer
+constexpr int kMaxItems = 24;        // slabs per CTA per layer
 constexpr int kMaxTok = 8;
 constexpr int kHD = 64;
 constexpr int kPartRow = 68;  // floats per attention partial: o[64], m, l, padding to 16 bytes
@@ -75,7 +78,7 @@ enum { C_QKV = 0, C_ATTN = 1, C_O = 2, C_GU = 3, C_DOWN = 4, C_LAYER = 5 };  // 
 // Scalars and pointers of one launch; the kernel copies them to shared memory once.
 struct DkHot {
   i4b_decode_model m;
-  int nslab[4], npiece[4];  // 32-column slabs and 512-k pieces per slab of qkv, o, gate/up, down
+  int nslab[4], npiece[4];  // 16-column slabs and 512-k pieces per slab of qkv, o, gate/up, down
   int64_t layer_bytes[4];   // tiled bytes of one layer's projection
   int piece_bytes, nslot, nsplit, gqa, qkv_n, q_n;
   int xpitch, off_x, off_xs, off_part;
@@ -98,7 +101,8 @@ struct DkParams {
 // 2 activations staged, 3 pieces done, 4 epilogue done, 5 fence done, 6 published; slot 7 holds
 // %globaltimer at entry, the time base shared by all SMs.
 // Slots 8..15: warp 0's cycles waiting for weight pieces, its cycles in the piece MMAs, its piece count,
-// and the producer's issued-piece count relative to this stage's first piece, at stage entry.
+// the producer's issued-piece count relative to this stage's first piece, at stage entry; the clocks at
+// which the first and the last compute warp ended their pieces, and the last warp's index.
 constexpr int kTraceSlots = 16;
 __device__ __forceinline__ void stamp(const DkHot& P, int l, int st, int k) {
   if (P.trace && threadIdx.x == 0) {
@@ -192,58 +196,45 @@ __device__ __forceinline__ void mma_bf16_first(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
-// One 512-k piece of a 32-column slab, by one warp: acc[t][e] += the piece's contribution to columns
-// 4r + 2t (e = 0, 1) and 4r + 2t + 1 (e = 2, 3) for tokens 2c + (e & 1), r = lane / 4, c = lane % 4.
-// wb: the piece in shared memory; xb: this lane's activations at the piece's first k.  Every weight is
-// dequantized exactly as the reference does -- (q - z) * s rounded once to bf16 (dq_pair) -- and the A
-// fragments are those bf16 weights, so y = sum_k x_k * bf16(w_k) with fp32 accumulation.  The two k16
-// halves of a step accumulate in separate registers (four independent MMA chains per warp).
+// One 512-k piece of a 16-column slab, by one warp: acc[e] += the piece's contribution to slab column
+// r (e = 0, 1) and r + 8 (e = 2, 3) for tokens 2c + (e & 1), r = lane / 4, c = lane % 4.  Step j (32 k)
+// gives lane (r, c) the packed words of k-row 4j + c at columns r and r + 8: the rows r and r + 8 of the
+// A fragment.  wb: the piece in shared memory; xb: this lane's activations at the piece's first k.
+// Every weight is dequantized exactly as the reference does -- (q - z) * s rounded once to bf16
+// (dq_pair) -- so y = sum_k x_k * bf16(w_k) with fp32 accumulation.  The two k16 halves of a step
+// accumulate in separate registers (two independent MMA chains).
 template <int SPS>
-__device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, int lane, float (&acc)[2][4]) {
+__device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, int lane, float (&acc)[4]) {
   const int r = lane >> 2;
-  float a1[2][4];
-#pragma unroll
-  for (int t = 0; t < 2; ++t)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) a1[t][e] = 0.0f;
-  DqParams dp[4];
+  float a1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  DqParams dp[2];
   // four blocks of four 32-k steps: the loads of a block are scheduled together, the block loop is not
-  // unrolled (register budget of 288 threads per SM); SPS divides 4, so group boundaries fall inside blocks
+  // unrolled (instruction cache); SPS divides 4, so group boundaries fall inside blocks
 #pragma unroll 1
   for (int j0 = 0; j0 < 16; j0 += 4)
 #pragma unroll
   for (int jj = 0; jj < 4; ++jj) {
     const int j = j0 + jj;
-    if (jj % SPS == 0) {  // a new group: scale / zero of columns 4r .. 4r + 3
-      const uint4 sz = *reinterpret_cast<const uint4*>(wb + kPieceW + ((j / SPS) * 8 + r) * 16);
-      dp[0] = dq_params<false>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.z & 0xFFFFu));
-      dp[1] = dq_params<false>(uint16_t(sz.x >> 16), uint16_t(sz.z >> 16));
-      dp[2] = dq_params<false>(uint16_t(sz.y & 0xFFFFu), uint16_t(sz.w & 0xFFFFu));
-      dp[3] = dq_params<false>(uint16_t(sz.y >> 16), uint16_t(sz.w >> 16));
+    if (jj % SPS == 0) {  // a new group: scale / zero of columns r and r + 8
+      const uint2 sz = *reinterpret_cast<const uint2*>(wb + kPieceW + ((j / SPS) * 8 + r) * 8);
+      dp[0] = dq_params<false>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.y & 0xFFFFu));
+      dp[1] = dq_params<false>(uint16_t(sz.x >> 16), uint16_t(sz.y >> 16));
     }
-    const uint4 w4 = *reinterpret_cast<const uint4*>(wb + (j * 32 + lane) * 16);
-    const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
-    uint32_t af[2][2][4];
+    const uint2 w2 = *reinterpret_cast<const uint2*>(wb + (j * 32 + lane) * 8);
+    uint32_t af[2][4];
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        af[t][s][0] = dq_pair<false>(nib_pair(wd[2 * t], 2 * s), dp[2 * t]);
-        af[t][s][1] = dq_pair<false>(nib_pair(wd[2 * t + 1], 2 * s), dp[2 * t + 1]);
-        af[t][s][2] = dq_pair<false>(nib_pair(wd[2 * t], 2 * s + 1), dp[2 * t]);
-        af[t][s][3] = dq_pair<false>(nib_pair(wd[2 * t + 1], 2 * s + 1), dp[2 * t + 1]);
-      }
+    for (int s = 0; s < 2; ++s) {
+      af[s][0] = dq_pair<false>(nib_pair(w2.x, 2 * s), dp[0]);
+      af[s][1] = dq_pair<false>(nib_pair(w2.y, 2 * s), dp[1]);
+      af[s][2] = dq_pair<false>(nib_pair(w2.x, 2 * s + 1), dp[0]);
+      af[s][3] = dq_pair<false>(nib_pair(w2.y, 2 * s + 1), dp[1]);
+    }
     const uint4 b = *reinterpret_cast<const uint4*>(xb + j * 64);
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      mma_bf16(acc[t], af[t][0], b.x, b.y);
-      mma_bf16(a1[t], af[t][1], b.z, b.w);
-    }
+    mma_bf16(acc, af[0], b.x, b.y);
+    mma_bf16(a1, af[1], b.z, b.w);
   }
 #pragma unroll
-  for (int t = 0; t < 2; ++t)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[t][e] += a1[t][e];
+  for (int e = 0; e < 4; ++e) acc[e] += a1[e];
 }
 
 struct Smem {
@@ -258,9 +249,17 @@ struct Smem {
   int flag;   // 1 until a wait fails in this CTA (then 0 for the rest of the launch)
   int tflag;  // the attention ticket said: this CTA combines
   volatile int prod_seq;  // pieces issued by the producer so far (diagnostics)
+  long long wexit[kCW];   // each compute warp's clock at the end of its pieces (diagnostics)
 };
 
-constexpr int kResPerThread = 4;  // residual values per thread: o / down slabs x tokens x 32 <= kCT * 4
+// The launch's shared memory as file-scope symbols: device functions that name them directly (rather than
+// through a pointer or reference parameter) compile every access to a shared-memory instruction instead of
+// a generic one.
+__shared__ Smem dk_S;
+__shared__ DkHot dk_P;
+extern __shared__ __align__(128) uint8_t dk_smem[];  // ring | activations / attention scratch | partials
+
+constexpr int kResPerThread = 4;  // residual values per thread: o / down slabs x tokens x 16 <= kCT * 4
 
 // Stage the activations of GEMV stage g into shared memory: x permuted to the nibble-pair order of the
 // A fragments, [token][k / 8] x 16 bytes with row pitch xpitch.  Written as plain (not unrolled) loops:
@@ -269,7 +268,10 @@ constexpr int kResPerThread = 4;  // residual values per thread: o / down slabs 
 // take per-token sums of squares over the staged rows (fixed order: lanes, then warps); (3) each thread
 // rewrites its chunks in place: x = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) (LlamaRMSNorm) where
 // needed, then the permutation.
-__device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int g, int l, int K) {
+__device__ __noinline__ void stage_x(int g, int l, int K) {
+  const DkHot& P = dk_P;
+  Smem& S = dk_S;
+  uint8_t* const smem = dk_smem;
   const i4b_decode_model& m = P.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = m.batch, H = m.hidden;
@@ -345,7 +347,10 @@ __device__ __noinline__ void stage_x(const DkHot& P, Smem& S, uint8_t* smem, int
 
 // One GEMV stage of layer l for this CTA's slabs of it.  False on a failed wait.
 template <int SPS>
-__device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, int g, int l) {
+__device__ __noinline__ bool gemv_stage(int g, int l) {
+  const DkHot& P = dk_P;
+  Smem& S = dk_S;
+  uint8_t* const smem = dk_smem;
   const i4b_decode_model& m = P.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int ib = 0, n = 0;
@@ -376,7 +381,7 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
   if (!S.flag) return false;
   stamp(P, l, st_id, 1);
   const int K = g == G_DOWN ? m.intermediate : (g == G_O ? P.q_n : m.hidden);
-  stage_x(P, S, smem, g, l, K);
+  stage_x(g, l, K);
   cbar();
   stamp(P, l, st_id, 2);
   // residual inputs of the o_proj / down_proj epilogue: loaded here, consumed after the pieces
@@ -389,9 +394,9 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
 #pragma unroll
     for (int k = 0; k < kRes; ++k) {
       const int idx = tid + k * kCT;
-      if (idx < n * B * 32) {
-        const int i = idx / (B * 32), rem = idx - i * B * 32, b = rem / 32, col = rem % 32;
-        const int64_t nn = int64_t(S.slab[ib + i]) * 32 + col;
+      if (idx < n * B * kSlabW) {
+        const int i = idx / (B * kSlabW), rem = idx - i * B * kSlabW, b = rem / kSlabW, col = rem % kSlabW;
+        const int64_t nn = int64_t(S.slab[ib + i]) * kSlabW + col;
         if (g == G_O && l == 0) {
           int64_t id = m.tokens[b];
           if (id < 0 || id >= m.vocab) id = 0;
@@ -409,17 +414,15 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
   const int r = lane >> 2, c = lane & 3;
   const uint8_t* xl = smem + P.off_x + min(r, B - 1) * P.xpitch + 16 * c;
   bool ok = true;
-  float acc[2][4];
+  float acc[4];
   int cur = -1, cur_j = 0;
   auto flush = [&](int i, int j) {
-    float* pp = part + (i * J + j) * (B * 32);
+    float* pp = part + (i * J + j) * (B * kSlabW);
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int col = 4 * r + 2 * t + (e >> 1), tok = 2 * c + (e & 1);
-        if (tok < B) pp[tok * 32 + col] = acc[t][e];
-      }
+    for (int e = 0; e < 4; ++e) {
+      const int col = r + 8 * (e >> 1), tok = 2 * c + (e & 1);
+      if (tok < B) pp[tok * kSlabW + col] = acc[e];
+    }
   };
   const int total = n * ppi;
   const int seq0 = l * S.ppl;
@@ -434,9 +437,7 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
       cur = i;
       cur_j = pl % kCW;
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[t][e] = 0.0f;
+      for (int e = 0; e < 4; ++e) acc[e] = 0.0f;
     }
     const int seq = seq0 + S.poff[ib + i] + pl;
     const int slot = seq % P.nslot;
@@ -454,6 +455,7 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
     if (lane == 0) mbar_arrive(&S.empty[slot]);
   }
   if (ok && cur >= 0) flush(cur, cur_j);
+  if (P.trace && lane == 0) S.wexit[warp] = clock64();
   if (tid == 0) {
     trace_put(P, l, st_id, 8, t_wait);
     trace_put(P, l, st_id, 9, t_mma);
@@ -461,33 +463,45 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
   }
   if (!ok && lane == 0) S.flag = 0;
   cbar();
+  if (P.trace && tid == 0) {  // first and last warp to finish its pieces, and which warp was last
+    long long lo = S.wexit[0], hi = S.wexit[0];
+    int wl = 0;
+    for (int w = 1; w < kCW; ++w) {
+      lo = min(lo, S.wexit[w]);
+      if (S.wexit[w] > hi) hi = S.wexit[w], wl = w;
+    }
+    trace_put(P, l, st_id, 12, lo);
+    trace_put(P, l, st_id, 13, hi);
+    trace_put(P, l, st_id, 14, wl);
+  }
   if (!S.flag) return false;
   stamp(P, l, st_id, 3);
 
   // ---- epilogue: fixed-order sum of the partials of each slab, then the stage's output operation
   if (g == G_GU) {
 #pragma unroll 1
-    for (int idx = tid; idx < n * B * 16; idx += kCT) {
-      const int i = idx / (B * 16), rem = idx - i * B * 16, b = rem / 16, pr = rem % 16;
+    for (int idx = tid; idx < n * B * (kSlabW / 2); idx += kCT) {
+      constexpr int kH = kSlabW / 2;  // gate / up column pairs of a slab
+      const int i = idx / (B * kH), rem = idx - i * B * kH, b = rem / kH, pr = rem % kH;
       float gs = 0.0f, us = 0.0f;
       for (int j = 0; j < J; ++j) {
-        const float* pp = part + (i * J + j) * (B * 32) + b * 32;
+        const float* pp = part + (i * J + j) * (B * kSlabW) + b * kSlabW;
         gs += pp[2 * pr];
         us += pp[2 * pr + 1];
       }
       const float gt = bfv(bfr(gs)), up = bfv(bfr(us));
       const float sl = bfv(bfr(gt / (1.0f + expf(-gt))));
-      P.act[int64_t(b) * m.intermediate + int64_t(S.slab[ib + i]) * 16 + pr] = uint16_t(bfr(sl * up));
+      P.act[int64_t(b) * m.intermediate + int64_t(S.slab[ib + i]) * kH + pr] = uint16_t(bfr(sl * up));
     }
   } else {
 #pragma unroll
     for (int k = 0; k < kRes; ++k) {
       const int idx = tid + k * kCT;
-      if (idx >= n * B * 32) break;
-      const int i = idx / (B * 32), rem = idx - i * B * 32, b = rem / 32, col = rem % 32;
+      if (idx >= n * B * kSlabW) break;
+      const int i = idx / (B * kSlabW), rem = idx - i * B * kSlabW, b = rem / kSlabW, col = rem % kSlabW;
       float sum = 0.0f;
-      for (int j = 0; j < J; ++j) sum += part[(i * J + j) * (B * 32) + b * 32 + col];
-      const int64_t nn = int64_t(S.slab[ib + i]) * 32 + col;
+      for (int j = 0; j < J; ++j) sum += part[(i * J + j) * (B * kSlabW) + b * kSlabW + col];
+      const int64_t nn = int64_t(S.slab[ib + i]) * kSlabW + col;
       if (g == G_QKV) P.qkv[int64_t(b) * P.qkv_n + nn] = uint16_t(bfr(sum));
       else h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(sum))));
     }
@@ -507,7 +521,10 @@ __device__ __noinline__ bool gemv_stage(const DkHot& P, Smem& S, uint8_t* smem, 
 // Attention item a = (token b, kv head, split j) of layer l: GS query heads over cache positions of split j.
 // Run by the first kAW compute warps (barrier 2); a failure clears the CTA's sticky S.flag.
 template <int GS>
-__device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* smem, int l, int a) {
+__device__ __noinline__ bool attention_item(int l, int a) {
+  const DkHot& P = dk_P;
+  Smem& S = dk_S;
+  uint8_t* const smem = dk_smem;
   const i4b_decode_model& m = P.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nkv = m.kv_heads, nsplit = P.nsplit, nq = m.heads;
@@ -721,15 +738,14 @@ __device__ __noinline__ bool attention_item(const DkHot& P, Smem& S, uint8_t* sm
 
 template <int SPS, int GS>
 __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid_constant__ DkParams Pg) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ Smem S;
-  __shared__ DkHot P_s;
+  uint8_t* const smem = dk_smem;
+  Smem& S = dk_S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   static_assert(sizeof(DkHot) % 4 == 0, "word copy");
   for (int i = tid; i < int(sizeof(DkHot) / 4); i += kThreads)
-    reinterpret_cast<uint32_t*>(&P_s)[i] = reinterpret_cast<const uint32_t*>(&Pg.h)[i];
+    reinterpret_cast<uint32_t*>(&dk_P)[i] = reinterpret_cast<const uint32_t*>(&Pg.h)[i];
   __syncthreads();
-  const DkHot& P = P_s;
+  const DkHot& P = dk_P;
   const i4b_decode_model& m = P.m;
   const unsigned int* abort_word = P.ctr + P.i_abort;
   if (tid == 0) {
@@ -794,13 +810,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     // ---- compute warps: the stages of every layer in order
     const int nattn = m.batch * m.kv_heads * P.nsplit;
     for (int l = 0; l < m.layers && ok; ++l) {
-      ok = gemv_stage<SPS>(P, S, smem, G_QKV, l);
+      ok = gemv_stage<SPS>(G_QKV, l);
       // attention runs on warps 0..kAW-1; the others go on to the o_proj stage, whose barrier they pass
       // only together with them.  A failed attention clears S.flag, which that stage checks.
-      if (ok && int(blockIdx.x) < nattn && warp < kAW) attention_item<GS>(P, S, smem, l, blockIdx.x);
-      ok = ok && gemv_stage<SPS>(P, S, smem, G_O, l);
-      ok = ok && gemv_stage<SPS>(P, S, smem, G_GU, l);
-      ok = ok && gemv_stage<SPS>(P, S, smem, G_DOWN, l);
+      if (ok && int(blockIdx.x) < nattn && warp < kAW) attention_item<GS>(l, blockIdx.x);
+      ok = ok && gemv_stage<SPS>(G_O, l);
+      ok = ok && gemv_stage<SPS>(G_GU, l);
+      ok = ok && gemv_stage<SPS>(G_DOWN, l);
     }
     if (!ok && tid == 0) {
       atomicOr(&g_dk_err, I4B_DEVERR_WAIT_TIMEOUT);
@@ -821,41 +837,40 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
   }
 }
 
-// Re-lay a quantize_int4 tensor triple into pieces: for slab s (columns 32s..32s+31) and piece p (k in
-// [512p, 512p + 512)), 16 steps x 32 lanes x 4 words -- lane (r, c) of step j holds qweight rows
-// 64p + 4j + c at columns 32s + 4r .. +3 -- then 512 / G records of 8 x 16 bytes (s0..s3, z0..z3 of
-// columns 32s + 4r .. +3).  One thread per 16-byte unit.
+// Re-lay a quantize_int4 tensor triple into pieces: for slab s (columns 16s..16s+15) and piece p (k in
+// [512p, 512p + 512)), 16 steps x 32 lanes x 2 words -- lane (r, c) of step j holds qweight row
+// 64p + 4j + c at columns 16s + r and 16s + r + 8 -- then 512 / G groups of 8 records of 8 bytes (scale
+// of column 16s + r, scale of 16s + r + 8, zero of 16s + r, zero of 16s + r + 8).  One thread per
+// 8-byte unit.
 __global__ void tile_w4_kernel(const int32_t* __restrict__ qw, int64_t sqk, const uint16_t* __restrict__ sc,
                                const uint16_t* __restrict__ zr, int64_t ssg, int64_t N, int64_t K, int G,
                                uint8_t* __restrict__ out, int piece_bytes) {
-  const int units_per_piece = piece_bytes / 16;
-  const int64_t npieces = (N / 32) * (K / kPieceK);
-  const int64_t total = npieces * units_per_piece;
+  const int units_per_piece = piece_bytes / 8;
+  const int64_t pk = K / kPieceK;
+  const int64_t total = (N / kSlabW) * pk * units_per_piece;
   for (int64_t u = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; u < total; u += int64_t(gridDim.x) * blockDim.x) {
     const int64_t piece = u / units_per_piece;
     const int w = int(u - piece * units_per_piece);
-    const int64_t pk = K / kPieceK;
     const int64_t s = piece / pk, p = piece - s * pk;
-    uint4 v;
-    if (w < 512) {
+    uint2 v;
+    if (w < kPieceW / 8) {
       const int j = w / 32, lane = w % 32, r = lane >> 2, c = lane & 3;
-      const int32_t* src = qw + (64 * p + 4 * j + c) * sqk + 32 * s + 4 * r;
-      v = make_uint4(uint32_t(src[0]), uint32_t(src[1]), uint32_t(src[2]), uint32_t(src[3]));
+      const int32_t* src = qw + (64 * p + 4 * j + c) * sqk + kSlabW * s + r;
+      v = make_uint2(uint32_t(src[0]), uint32_t(src[8]));
     } else {
-      const int rec = w - 512, gi = rec / 8, r = rec % 8;
+      const int rec = w - kPieceW / 8, gi = rec / 8, r = rec % 8;
       const int64_t g = p * (kPieceK / G) + gi;
-      const uint16_t* s4 = sc + g * ssg + 32 * s + 4 * r;
-      const uint16_t* z4 = zr + g * ssg + 32 * s + 4 * r;
-      v = make_uint4(uint32_t(s4[0]) | (uint32_t(s4[1]) << 16), uint32_t(s4[2]) | (uint32_t(s4[3]) << 16),
-                     uint32_t(z4[0]) | (uint32_t(z4[1]) << 16), uint32_t(z4[2]) | (uint32_t(z4[3]) << 16));
+      const uint16_t* s2 = sc + g * ssg + kSlabW * s + r;
+      const uint16_t* z2 = zr + g * ssg + kSlabW * s + r;
+      v = make_uint2(uint32_t(s2[0]) | (uint32_t(s2[8]) << 16), uint32_t(z2[0]) | (uint32_t(z2[8]) << 16));
     }
-    reinterpret_cast<uint4*>(out)[u] = v;
+    reinterpret_cast<uint2*>(out)[u] = v;
   }
 }
 
 // ------------------------------------------------------------------ host side
 
-int piece_bytes_for(int G) { return kPieceW + (kPieceK / G) * 128; }
+int piece_bytes_for(int G) { return kPieceW + (kPieceK / G) * kRecB; }
 
 struct Sched {
   int max_part = 0;
@@ -865,25 +880,26 @@ struct Sched {
   std::vector<uint16_t> items;  // [grid][kMaxItems]
 };
 
-// Longest-processing-time assignment of one layer's slabs to the CTAs: slabs by decreasing piece count
-// (then stage, then slab), each to the least-loaded CTA (lowest index on ties); each CTA's list is then
-// put in stage order.  The same lists serve every layer.
+// Assignment of one layer's slabs to the CTAs, stage by stage: each stage is its own critical path, so
+// each slab goes to the CTA with the fewest pieces of that stage so far, ties to the fewest pieces over
+// all stages, then to the lowest index.  Each CTA's list is in stage order; the same lists serve every
+// layer.
 Sched build_sched(int grid, const int nslab[4], const int npiece[4]) {
   Sched sc;
   sc.nitems.assign(grid, 0);
   sc.items.assign(size_t(grid) * kMaxItems, 0);
-  std::vector<std::tuple<int, int, int>> all;  // (-pieces, stage, slab)
-  for (int g = 0; g < 4; ++g)
-    for (int s = 0; s < nslab[g]; ++s) all.emplace_back(-npiece[g], g, s);
-  std::sort(all.begin(), all.end());
   std::vector<int64_t> load(grid, 0);
   std::vector<std::vector<std::pair<int, int>>> lists(grid);
-  for (const auto& [neg, g, s] : all) {
-    int best = 0;
-    for (int c = 1; c < grid; ++c)
-      if (load[c] < load[best]) best = c;
-    load[best] += -neg;
-    lists[best].emplace_back(g, s);
+  for (int g = 0; g < 4; ++g) {
+    std::vector<int> st(grid, 0);
+    for (int s = 0; s < nslab[g]; ++s) {
+      int best = 0;
+      for (int c = 1; c < grid; ++c)
+        if (st[c] < st[best] || (st[c] == st[best] && load[c] < load[best])) best = c;
+      st[best] += npiece[g];
+      load[best] += npiece[g];
+      lists[best].emplace_back(g, s);
+    }
   }
   for (int c = 0; c < grid; ++c) {
     auto& L = lists[c];
@@ -931,8 +947,8 @@ int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
   const int64_t N[4] = {qkv_n, m.hidden, 2 * int64_t(m.intermediate), m.hidden};
   const int64_t K[4] = {m.hidden, q_n, m.hidden, m.intermediate};
   for (int g = 0; g < 4; ++g) {
-    if (N[g] / 32 >= (1 << 14)) return I4B_ERR_SHAPE;
-    L->nslab[g] = int(N[g] / 32);
+    if (N[g] / kSlabW >= (1 << 14)) return I4B_ERR_SHAPE;
+    L->nslab[g] = int(N[g] / kSlabW);
     L->npiece[g] = int(K[g] / kPieceK);
     L->layer_bytes[g] = int64_t(L->nslab[g]) * L->npiece[g] * L->piece_bytes;
   }
@@ -989,13 +1005,13 @@ cudaError_t launch_dk_s(const DkParams& p, int grid, size_t smem, cudaStream_t s
 }  // namespace
 
 size_t tile_w4_bytes(int64_t N, int64_t K, int G) {
-  if (N <= 0 || K <= 0 || N % 32 || K % kPieceK || (G != 32 && G != 64 && G != 128)) return 0;
-  return size_t(N / 32) * size_t(K / kPieceK) * size_t(piece_bytes_for(G));
+  if (N <= 0 || K <= 0 || N % kSlabW || K % kPieceK || (G != 32 && G != 64 && G != 128)) return 0;
+  return size_t(N / kSlabW) * size_t(K / kPieceK) * size_t(piece_bytes_for(G));
 }
 
 cudaError_t launch_tile_w4(const int32_t* qw, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg,
                            int64_t N, int64_t K, int G, void* out, cudaStream_t stream) {
-  const int64_t units = int64_t(tile_w4_bytes(N, K, G) / 16);
+  const int64_t units = int64_t(tile_w4_bytes(N, K, G) / 8);
   const int blocks = int(std::min<int64_t>((units + 255) / 256, 148 * 16));
   tile_w4_kernel<<<blocks, 256, 0, stream>>>(qw, sqk, sc, zr, ssg, N, K, G, static_cast<uint8_t*>(out),
                                              piece_bytes_for(G));
@@ -1037,7 +1053,7 @@ int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin,
     sc = &it->second;
   }
   if (!sc->ok) return I4B_ERR_SHAPE;
-  if (sc->max_res * m.batch * 32 > kCT * kResPerThread) return I4B_ERR_SHAPE;
+  if (sc->max_res * m.batch * kSlabW > kCT * kResPerThread) return I4B_ERR_SHAPE;
 
   DkParams p;
   memset(&p, 0, sizeof(p));
@@ -1077,7 +1093,7 @@ int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin,
   const int attn_bytes = std::max(attn_block, L.gqa * kHD * 4 + L.nsplit * L.gqa * kPartRow * 4);
   const int x_bytes = al(std::max(m.batch * p.h.xpitch, attn_bytes));
   const int xs_bytes = 0;
-  const int part_bytes = al(sc->max_part * m.batch * 32 * 4);
+  const int part_bytes = al(sc->max_part * m.batch * kSlabW * 4);
   const int fixed = x_bytes + xs_bytes + part_bytes;
   const int avail = smem_optin - int(sizeof(Smem)) - 1024;
   const int nslot = std::min(kMaxSlots, (avail - fixed) / p.h.piece_bytes);

@@ -167,7 +167,7 @@ def argmax_last(x: torch.Tensor) -> torch.Tensor:
 
 def tile_w4(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
             out: torch.Tensor | None = None) -> torch.Tensor:
-    """The quantize_int4 triple re-laid into the 32-column x 512-k pieces the persistent decode streams.
+    """The quantize_int4 triple re-laid into the 16-column x 512-k pieces the persistent decode streams.
 
     ``out`` (uint8, 16-byte aligned, at least ``tile_w4_bytes`` long) receives the pieces when given.
     """
@@ -176,7 +176,7 @@ def tile_w4(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
     L = _lib.lib()
     nbytes = L.i4b_tile_w4_bytes(N, K, G)
     if nbytes == 0:
-        raise ValueError(f"tile_w4: N={N} must be a multiple of 32, K={K} of 512, group size {G} in (32, 64, 128)")
+        raise ValueError(f"tile_w4: N={N} must be a multiple of 16, K={K} of 512, group size {G} in (32, 64, 128)")
     if out is None:
         out = torch.empty(nbytes, dtype=torch.uint8, device=qweight.device)
     assert out.dtype == torch.uint8 and out.numel() >= nbytes and out.is_contiguous()
@@ -247,7 +247,8 @@ class PersistentDecoder:
 
         Projection stages: ``wait`` (entry to dependency met), ``stage_x`` (inputs staged), ``pieces``,
         ``epilogue``, ``publish``; warp 0's ``weight_wait`` / ``mma`` per piece; ``producer_lead`` (pieces
-        the producer had issued ahead of the stage).  Attention: ``wait``, ``queries``, ``blocks``,
+        the producer had issued ahead of the stage); ``first_warp_done`` / ``last_warp_done`` (from the
+        start of the pieces) and ``last_warp``.  Attention: ``wait``, ``queries``, ``blocks``,
         ``fence``, ``ticket``.  ``layer_us``: median CTA's time from one qkv entry to the next.
         """
         import numpy as np
@@ -286,6 +287,9 @@ class PersistentDecoder:
                 d["mma_per_piece"] = round(float(np.median(rows[:, 9] / npc)) / mhz, 3)
                 d["pieces_warp0"] = float(np.median(rows[:, 10]))
                 d["producer_lead"] = float(np.median(rows[:, 11]))
+                d["first_warp_done"] = round(float(np.median(rows[:, 12] - rows[:, 2])) / mhz, 2)
+                d["last_warp_done"] = round(float(np.median(rows[:, 13] - rows[:, 2])) / mhz, 2)
+                d["last_warp"] = float(np.median(rows[:, 14]))
             out["stages"][sname] = d
         g0 = [np.median(t[valid[:, l, 0], l, 0, 7]) for l in range(L) if valid[:, l, 0].any()]
         out["layer_us"] = round(float(np.median(np.diff(g0))) / 1e3, 2) if len(g0) > 1 else None

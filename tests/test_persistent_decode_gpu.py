@@ -57,8 +57,8 @@ def _ids(B, S, seed, vocab=512):
 
 @pytest.mark.parametrize("G", [32, 64, 128])
 def test_tile_w4_layout(cuda_device, G):
-    """Piece (slab s, piece p): step j, lane (r, c) holds qweight[64p + 4j + c, 32s + 4r .. +3]; then the scale and
-    zero records of the piece's groups."""
+    """Piece (slab s, piece p): step j, lane (r, c) holds qweight[64p + 4j + c, 16s + r] and [.., 16s + r + 8]; then
+    per group of the piece, record r holds the scales and then the zeros of columns 16s + r and 16s + r + 8."""
     import int4_b200
     from int4_b200.decode import tile_w4
 
@@ -66,17 +66,17 @@ def test_tile_w4_layout(cuda_device, G):
     w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
     qw, sc, zr = int4_b200.quantize_int4(w, G)
     blob = tile_w4(qw, sc, zr)
-    S, P = N // 32, K // 512
-    pb = 8192 + (512 // G) * 128
+    S, P = N // 16, K // 512
+    pb = 4096 + (512 // G) * 64
     assert blob.numel() == S * P * pb
     b = blob.view(S, P, pb)
-    words = b[:, :, :8192].contiguous().view(torch.int32).view(S, P, 16, 8, 4, 4)  # s p j r c e
-    want = qw.view(P, 16, 4, S, 8, 4).permute(3, 0, 1, 4, 2, 5)  # (p j c s r e) -> s p j r c e
+    words = b[:, :, :4096].contiguous().view(torch.int32).view(S, P, 16, 8, 4, 2)  # s p j r c e
+    want = qw.view(P, 16, 4, S, 2, 8).permute(3, 0, 1, 5, 2, 4)  # (p j c s e r) -> s p j r c e
     assert torch.equal(words, want)
-    rec = b[:, :, 8192:].contiguous().view(torch.float16).view(S, P, 512 // G, 8, 2, 4)  # s p gi r (s|z) e
+    rec = b[:, :, 4096:].contiguous().view(torch.float16).view(S, P, 512 // G, 8, 2, 2)  # s p gi r (s|z) e
     gp = 512 // G
-    assert torch.equal(rec[..., 0, :], sc.view(P, gp, S, 8, 4).permute(2, 0, 1, 3, 4))
-    assert torch.equal(rec[..., 1, :], zr.view(P, gp, S, 8, 4).permute(2, 0, 1, 3, 4))
+    assert torch.equal(rec[..., 0, :], sc.view(P, gp, S, 2, 8).permute(2, 0, 1, 4, 3))
+    assert torch.equal(rec[..., 1, :], zr.view(P, gp, S, 2, 8).permute(2, 0, 1, 4, 3))
 
 
 def _noise_floor_bound(floor_model, tok, pos, ref):
@@ -177,7 +177,7 @@ def test_persistent_decode_replays_bit_identically_from_a_cuda_graph(small):
 @torch.no_grad()
 @pytest.mark.parametrize("B", [1, 4])
 def test_persistent_decode_on_llama_1b_widths(cuda_device, B):
-    """Two layers at the Llama-3.2-1B widths: 96 / 64 / 512 / 64 slabs per stage, several attention blocks per
+    """Two layers at the Llama-3.2-1B widths: 192 / 128 / 1024 / 128 slabs per stage, several attention blocks per
     split.
 
     At these widths a cached single-token step differs from the reference's full recompute by bf16 rounding
