@@ -225,8 +225,8 @@ typedef struct i4b_decode_model {
 size_t i4b_tile_w4_bytes(int64_t N, int64_t K, int group_size);
 
 /* Re-lay qweight[K/8, N] (+ scales / zeros [K/G, N]) into 16-column x 512-k pieces of packed words (4 KB)
- * followed by their scales and zeros (64 bytes per group), slab by slab, the order in which the persistent
- * decode streams them. */
+ * followed by each group's dequantization constants (128 bytes per group: bf16 128 + zero, the scale's top
+ * 8 bits, the scale's remainder), slab by slab, the order in which the persistent decode streams them. */
 int i4b_tile_w4(const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales, const uint16_t* zeros,
                 int64_t stride_sg, int64_t K, int group_size, void* out, void* stream);
 

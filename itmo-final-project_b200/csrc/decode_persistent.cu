@@ -63,7 +63,7 @@ constexpr int kAT = kAW * 32;
 constexpr int kSlabW = 16;           // output columns of one slab (the rows of one m16n8k16 tile)
 constexpr int kPieceK = 512;         // k of one weight piece
 constexpr int kPieceW = 4096;        // packed-word bytes of one piece (16 columns x 512 k x 4 bit)
-constexpr int kRecB = 64;            // bytes of one group's scale / zero records in a piece (16 columns x 2 x fp16)
+constexpr int kRecB = 128;           // bytes of one group's dequantization records in a piece (8 x 16 bytes)
 constexpr int kMaxSlots = 48;
 constexpr int kMaxCtas = 160;
 constexpr int kMaxItems = 24;        // slabs per CTA per layer
@@ -202,11 +202,13 @@ __device__ __forceinline__ void mma_bf16_first(float (&d)[4], const uint32_t (&a
 // A fragment.  wb: the piece in shared memory; xb: this lane's activations at the piece's first k.
 // Every weight is dequantized exactly as the reference does -- (q - z) * s rounded once to bf16
 // (dq_pair) -- so y = sum_k x_k * bf16(w_k) with fp32 accumulation.  The two k16 halves of a step
-// accumulate in separate registers (two independent MMA chains).
+// accumulate in separate registers, acc and a1 (two independent MMA chains), which the caller carries
+// from piece to piece of a slab and adds only when it stores the slab's partial: no piece waits for the
+// previous one's last MMA.
 template <int SPS>
-__device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, int lane, float (&acc)[4]) {
+__device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, int lane, float (&acc)[4],
+                                          float (&a1)[4]) {
   const int r = lane >> 2;
-  float a1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   DqParams dp[2];
   // four blocks of four 32-k steps: the loads of a block are scheduled together, the block loop is not
   // unrolled (instruction cache); SPS divides 4, so group boundaries fall inside blocks
@@ -215,10 +217,14 @@ __device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, 
 #pragma unroll
   for (int jj = 0; jj < 4; ++jj) {
     const int j = j0 + jj;
-    if (jj % SPS == 0) {  // a new group: scale / zero of columns r and r + 8
-      const uint2 sz = *reinterpret_cast<const uint2*>(wb + kPieceW + ((j / SPS) * 8 + r) * 8);
-      dp[0] = dq_params<false>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.y & 0xFFFFu));
-      dp[1] = dq_params<false>(uint16_t(sz.x >> 16), uint16_t(sz.y >> 16));
+    if (jj % SPS == 0) {  // a new group: the dequantization constants of columns r (low halves), r + 8 (high)
+      const uint4 rc = *reinterpret_cast<const uint4*>(wb + kPieceW + ((j / SPS) * 8 + r) * 16);
+      dp[0].zz = __byte_perm(rc.x, 0u, 0x1010);
+      dp[0].shi = __byte_perm(rc.y, 0u, 0x1010);
+      dp[0].slo = __byte_perm(rc.z, 0u, 0x1010);
+      dp[1].zz = __byte_perm(rc.x, 0u, 0x3232);
+      dp[1].shi = __byte_perm(rc.y, 0u, 0x3232);
+      dp[1].slo = __byte_perm(rc.z, 0u, 0x3232);
     }
     const uint2 w2 = *reinterpret_cast<const uint2*>(wb + (j * 32 + lane) * 8);
     uint32_t af[2][4];
@@ -233,8 +239,6 @@ __device__ __forceinline__ void piece_mma(const uint8_t* wb, const uint8_t* xb, 
     mma_bf16(acc, af[0], b.x, b.y);
     mma_bf16(a1, af[1], b.z, b.w);
   }
-#pragma unroll
-  for (int e = 0; e < 4; ++e) acc[e] += a1[e];
 }
 
 struct Smem {
@@ -292,7 +296,6 @@ __device__ __noinline__ void stage_x(int g, int l, int K) {
       row = static_cast<const uint16_t*>(m.embed) + id * H;
     }
     cp_async_16(sx + t * P.xpitch + ch * 16, row + 8 * ch, 16);
-    if (norm) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + 8 * ch));  // read in step (3)
   }
   cp_async_commit();
   cp_async_wait<0>();
@@ -362,6 +365,11 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
   const int st_id = g == G_QKV ? C_QKV : g == G_O ? C_O : g == G_GU ? C_GU : C_DOWN;
   stamp(P, l, st_id, 0);
   const unsigned int* abort_word = P.ctr + P.i_abort;
+  if (g == G_QKV || g == G_GU) {  // the RMSNorm weights do not depend on the previous stage: fetch them now
+    const uint16_t* nw = static_cast<const uint16_t*>(g == G_QKV ? m.ln1 : m.ln2) + int64_t(l) * m.hidden;
+#pragma unroll 1
+    for (int ch = tid; ch < m.hidden / 8; ch += kCT) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + 8 * ch));
+  }
   // ---- dependency: every output of the previous stage
   if (tid == 0) {
     const unsigned int* c = nullptr;
@@ -408,23 +416,24 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
     }
   }
 
-  // ---- pieces: piece q = i * ppi + p of this stage goes to warp q % kCW
+  // ---- pieces: piece q = i * ppi + p (slab i, k-piece p) of this stage goes to warp q % kCW; warp w's
+  // sum over its pieces of slab i is partial row (i, p % kCW) of J per slab
   const int ppi = P.npiece[g], J = ppi < kCW ? ppi : kCW;
   float* part = reinterpret_cast<float*>(smem + P.off_part);
   const int r = lane >> 2, c = lane & 3;
   const uint8_t* xl = smem + P.off_x + min(r, B - 1) * P.xpitch + 16 * c;
+  const int total = n * ppi;
   bool ok = true;
-  float acc[4];
+  float acc[4], a1[4];
   int cur = -1, cur_j = 0;
   auto flush = [&](int i, int j) {
     float* pp = part + (i * J + j) * (B * kSlabW);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int col = r + 8 * (e >> 1), tok = 2 * c + (e & 1);
-      if (tok < B) pp[tok * kSlabW + col] = acc[e];
+      if (tok < B) pp[tok * kSlabW + col] = acc[e] + a1[e];
     }
   };
-  const int total = n * ppi;
   const int seq0 = l * S.ppl;
   if (tid == 0) trace_put(P, l, st_id, 11, S.prod_seq - (seq0 + S.poff[ib]));
   long long t_wait = 0, t_mma = 0;
@@ -437,7 +446,7 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
       cur = i;
       cur_j = pl % kCW;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] = 0.0f;
+      for (int e = 0; e < 4; ++e) acc[e] = a1[e] = 0.0f;
     }
     const int seq = seq0 + S.poff[ib + i] + pl;
     const int slot = seq % P.nslot;
@@ -447,7 +456,7 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
       break;
     }
     const long long c1 = clock64();
-    piece_mma<SPS>(smem + slot * P.piece_bytes, xl + p * (kPieceK / 32) * 64, lane, acc);
+    piece_mma<SPS>(smem + slot * P.piece_bytes, xl + p * (kPieceK / 32) * 64, lane, acc, a1);
     t_wait += c1 - c0;
     t_mma += clock64() - c1;
     ++npc;
@@ -537,12 +546,8 @@ __device__ __noinline__ bool attention_item(int l, int a) {
   const int ns = max(1, min(nsplit, (Lp + kAttnMinSplit - 1) / kAttnMinSplit));
   if (j >= ns) return true;
   stamp(P, l, C_ATTN, 0);
-  if (tid == 0 && !wait_counter(P.ctr + l * C_LAYER + C_QKV, unsigned(P.nslab[G_QKV]), abort_word)) S.flag = 0;
-  abar();
-  if (!S.flag) return false;
-  stamp(P, l, C_ATTN, 1);
   // scratch (the activation staging area): rotated queries, this block's keys and values, probabilities,
-  // running max / sum / rescale per head
+  // running max / sum / rescale per head, the new position's key and value
   constexpr int KP = 33;  // words per staged key row: 32 bf16 pairs + 1, so that 32 positions hit 32 banks
   float* qs = reinterpret_cast<float*>(smem + P.off_x);   // [GS][64]
   uint32_t* ks = reinterpret_cast<uint32_t*>(qs + GS * kHD);  // [64][KP] bf16 pairs
@@ -551,15 +556,39 @@ __device__ __noinline__ bool attention_item(int l, int a) {
   float* sm = pr + GS * kHD;                                  // [GS] running max
   float* sl = sm + GS;                                        // [GS] running sum
   float* scr = sl + GS;                                       // [GS] rescale of this block
+  uint16_t* newkv = reinterpret_cast<uint16_t*>(scr + GS);    // [2][64] rotated key, value of position pos
   const int chunk = (Lp + ns - 1) / ns;
   const int i0 = j * chunk, i1 = min(Lp, i0 + chunk);
-  const uint16_t* qrow = P.qkv + int64_t(b) * P.qkv_n;
-  const uint16_t* cosT = static_cast<const uint16_t*>(m.cos_table);
-  const uint16_t* sinT = static_cast<const uint16_t*>(m.sin_table);
   const int64_t head_stride = int64_t(m.max_seq) * kHD;
   const int64_t cache_off = ((int64_t(l) * m.cache_batch + b) * nkv + kvh) * head_stride;
   uint16_t* kc = static_cast<uint16_t*>(m.k_cache) + cache_off;
   uint16_t* vc = static_cast<uint16_t*>(m.v_cache) + cache_off;
+  // keys (4-byte copies into conflict-free rows) and values (16-byte copies) of cached positions
+  // [blk, blk + nb), all in flight at once.  Every position but pos was written by an earlier step, so the
+  // first block goes out before the wait for this layer's q / k / v; row pos comes from newkv.
+  auto issue_block = [&](int blk, int nb) {
+#pragma unroll 1
+    for (int cc = tid; cc < nb * 32; cc += kAT)
+      if (blk + (cc >> 5) != pos)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ks + (cc >> 5) * KP + (cc & 31))),
+                     "l"(kc + int64_t(blk) * kHD + 2 * cc)
+                     : "memory");
+#pragma unroll 1
+    for (int cc = tid; cc < nb * 8; cc += kAT)
+      if (blk + (cc >> 3) != pos) cp_async_16(vs + cc * 8, vc + int64_t(blk) * kHD + cc * 8, 16);
+    cp_async_commit();
+  };
+  if (i1 > i0) issue_block(i0, min(64, i1 - i0));
+  if (tid == 0 && !wait_counter(P.ctr + l * C_LAYER + C_QKV, unsigned(P.nslab[G_QKV]), abort_word)) S.flag = 0;
+  abar();
+  if (!S.flag) {
+    cp_async_wait<0>();  // nothing may land in shared memory after the CTA has moved on
+    return false;
+  }
+  stamp(P, l, C_ATTN, 1);
+  const uint16_t* qrow = P.qkv + int64_t(b) * P.qkv_n;
+  const uint16_t* cosT = static_cast<const uint16_t*>(m.cos_table);
+  const uint16_t* sinT = static_cast<const uint16_t*>(m.sin_table);
   // rotary embedding, apply_rotary_pos_emb's rounding: bf16(bf16(t * cos) + bf16(rotate_half(t) * sin))
   float c0 = 0.f, c1 = 0.f, s0 = 0.f, s1 = 0.f;
   if (pvalid) {
@@ -579,12 +608,19 @@ __device__ __noinline__ bool attention_item(int l, int a) {
     if (warp == kAW - 1) {
       const uint16_t* src = qrow + (nq + kvh) * kHD;
       const float x0 = bfv(ldcg16(src + lane)), x1 = bfv(ldcg16(src + lane + 32));
-      kc[pos * kHD + lane] = uint16_t(bfr(bfv(bfr(x0 * c0)) + bfv(bfr(-x1 * s0))));
-      kc[pos * kHD + lane + 32] = uint16_t(bfr(bfv(bfr(x1 * c1)) + bfv(bfr(x0 * s1))));
+      const uint16_t k0 = uint16_t(bfr(bfv(bfr(x0 * c0)) + bfv(bfr(-x1 * s0))));
+      const uint16_t k1 = uint16_t(bfr(bfv(bfr(x1 * c1)) + bfv(bfr(x0 * s1))));
+      kc[pos * kHD + lane] = k0;
+      kc[pos * kHD + lane + 32] = k1;
+      newkv[lane] = k0;
+      newkv[lane + 32] = k1;
     } else if (warp == kAW - 2) {
       const uint16_t* src = qrow + (nq + nkv + kvh) * kHD;
-      vc[pos * kHD + lane] = ldcg16(src + lane);
-      vc[pos * kHD + lane + 32] = ldcg16(src + lane + 32);
+      const uint16_t v0 = ldcg16(src + lane), v1 = ldcg16(src + lane + 32);
+      vc[pos * kHD + lane] = v0;
+      vc[pos * kHD + lane + 32] = v1;
+      newkv[kHD + lane] = v0;
+      newkv[kHD + lane + 32] = v1;
     }
   }
   if (tid < GS) {
@@ -604,15 +640,12 @@ __device__ __noinline__ bool attention_item(int l, int a) {
 #pragma unroll 1
   for (int blk = i0; blk < i1; blk += 64) {
     const int nb = min(64, i1 - blk);
-    // keys (4-byte copies into conflict-free rows) and values (16-byte copies), all in flight at once
-#pragma unroll 1
-    for (int c = tid; c < nb * 32; c += kAT)
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ks + (c >> 5) * KP + (c & 31))),
-                   "l"(kc + int64_t(blk) * kHD + 2 * c)
-                   : "memory");
-#pragma unroll 1
-    for (int c = tid; c < nb * 8; c += kAT) cp_async_16(vs + c * 8, vc + int64_t(blk) * kHD + c * 8, 16);
-    cp_async_commit();
+    if (blk != i0) issue_block(blk, nb);
+    if (pos >= blk && pos < blk + nb) {  // the new position's row, from newkv (written before the last barrier)
+      const int t = int(pos - blk);
+      if (tid < 32) ks[t * KP + tid] = reinterpret_cast<const uint32_t*>(newkv)[tid];
+      else if (tid < 32 + kHD) vs[t * kHD + tid - 32] = newkv[kHD + tid - 32];
+    }
     cp_async_wait<0>();
     abar();
     // scores s[hh][x] = q[hh] . k[x] * scale
@@ -839,32 +872,42 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
 
 // Re-lay a quantize_int4 tensor triple into pieces: for slab s (columns 16s..16s+15) and piece p (k in
 // [512p, 512p + 512)), 16 steps x 32 lanes x 2 words -- lane (r, c) of step j holds qweight row
-// 64p + 4j + c at columns 16s + r and 16s + r + 8 -- then 512 / G groups of 8 records of 8 bytes (scale
-// of column 16s + r, scale of 16s + r + 8, zero of 16s + r, zero of 16s + r + 8).  One thread per
-// 8-byte unit.
+// 64p + 4j + c at columns 16s + r and 16s + r + 8 -- then, per group of the piece, 8 records of 16 bytes:
+// record r holds the dequantization constants (dq_params) of columns 16s + r (low halves) and 16s + r + 8
+// (high halves) as bf16 pairs: 128 + zero, the scale's high part, the scale's remainder, and 4 zero bytes.
+// One thread per 16-byte unit.
 __global__ void tile_w4_kernel(const int32_t* __restrict__ qw, int64_t sqk, const uint16_t* __restrict__ sc,
                                const uint16_t* __restrict__ zr, int64_t ssg, int64_t N, int64_t K, int G,
                                uint8_t* __restrict__ out, int piece_bytes) {
-  const int units_per_piece = piece_bytes / 8;
+  const int units_per_piece = piece_bytes / 16;
   const int64_t pk = K / kPieceK;
   const int64_t total = (N / kSlabW) * pk * units_per_piece;
   for (int64_t u = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; u < total; u += int64_t(gridDim.x) * blockDim.x) {
     const int64_t piece = u / units_per_piece;
     const int w = int(u - piece * units_per_piece);
     const int64_t s = piece / pk, p = piece - s * pk;
-    uint2 v;
-    if (w < kPieceW / 8) {
-      const int j = w / 32, lane = w % 32, r = lane >> 2, c = lane & 3;
-      const int32_t* src = qw + (64 * p + 4 * j + c) * sqk + kSlabW * s + r;
-      v = make_uint2(uint32_t(src[0]), uint32_t(src[8]));
+    uint4 v;
+    if (w < kPieceW / 16) {  // lanes 2h and 2h + 1 of step j
+      const int j = w / 16, h = w % 16;
+      uint32_t t[4];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int lane = 2 * h + e, r = lane >> 2, c = lane & 3;
+        const int32_t* src = qw + (64 * p + 4 * j + c) * sqk + kSlabW * s + r;
+        t[2 * e] = uint32_t(src[0]);
+        t[2 * e + 1] = uint32_t(src[8]);
+      }
+      v = make_uint4(t[0], t[1], t[2], t[3]);
     } else {
-      const int rec = w - kPieceW / 8, gi = rec / 8, r = rec % 8;
+      const int rec = w - kPieceW / 16, gi = rec / 8, r = rec % 8;
       const int64_t g = p * (kPieceK / G) + gi;
       const uint16_t* s2 = sc + g * ssg + kSlabW * s + r;
       const uint16_t* z2 = zr + g * ssg + kSlabW * s + r;
-      v = make_uint2(uint32_t(s2[0]) | (uint32_t(s2[8]) << 16), uint32_t(z2[0]) | (uint32_t(z2[8]) << 16));
+      const DqParams a = dq_params<false>(s2[0], z2[0]), b = dq_params<false>(s2[8], z2[8]);
+      v = make_uint4((a.zz & 0xFFFFu) | (b.zz << 16), (a.shi & 0xFFFFu) | (b.shi << 16),
+                     (a.slo & 0xFFFFu) | (b.slo << 16), 0u);
     }
-    reinterpret_cast<uint2*>(out)[u] = v;
+    reinterpret_cast<uint4*>(out)[u] = v;
   }
 }
 
@@ -1011,7 +1054,7 @@ size_t tile_w4_bytes(int64_t N, int64_t K, int G) {
 
 cudaError_t launch_tile_w4(const int32_t* qw, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg,
                            int64_t N, int64_t K, int G, void* out, cudaStream_t stream) {
-  const int64_t units = int64_t(tile_w4_bytes(N, K, G) / 8);
+  const int64_t units = int64_t(tile_w4_bytes(N, K, G) / 16);
   const int blocks = int(std::min<int64_t>((units + 255) / 256, 148 * 16));
   tile_w4_kernel<<<blocks, 256, 0, stream>>>(qw, sqk, sc, zr, ssg, N, K, G, static_cast<uint8_t*>(out),
                                              piece_bytes_for(G));
@@ -1088,8 +1131,9 @@ int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin,
   const int kmax = std::max(std::max(m.hidden, m.intermediate), L.q_n);
   p.h.xpitch = 2 * kmax + 16;
   auto al = [](int v) { return (v + 127) & ~127; };
-  // attention: queries, scores, running max / sum / rescale, then the partials of all splits when combining
-  const int attn_block = (2 * L.gqa * kHD + 3 * L.gqa) * 4 + 64 * 33 * 4 + 64 * kHD * 2;
+  // attention: queries, keys, values, probabilities, running max / sum / rescale, the new key and value; then
+  // the partials of all splits when combining
+  const int attn_block = (2 * L.gqa * kHD + 3 * L.gqa) * 4 + 64 * 33 * 4 + 64 * kHD * 2 + 2 * kHD * 2;
   const int attn_bytes = std::max(attn_block, L.gqa * kHD * 4 + L.nsplit * L.gqa * kPartRow * 4);
   const int x_bytes = al(std::max(m.batch * p.h.xpitch, attn_bytes));
   const int xs_bytes = 0;

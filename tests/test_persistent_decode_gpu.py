@@ -58,7 +58,8 @@ def _ids(B, S, seed, vocab=512):
 @pytest.mark.parametrize("G", [32, 64, 128])
 def test_tile_w4_layout(cuda_device, G):
     """Piece (slab s, piece p): step j, lane (r, c) holds qweight[64p + 4j + c, 16s + r] and [.., 16s + r + 8]; then
-    per group of the piece, record r holds the scales and then the zeros of columns 16s + r and 16s + r + 8."""
+    per group of the piece, record r holds the bf16 dequantization constants of columns 16s + r and 16s + r + 8:
+    128 + zero, the scale's top 8 bits and the scale's remainder (exact: an fp16 scale has 11 significant bits)."""
     import int4_b200
     from int4_b200.decode import tile_w4
 
@@ -67,16 +68,21 @@ def test_tile_w4_layout(cuda_device, G):
     qw, sc, zr = int4_b200.quantize_int4(w, G)
     blob = tile_w4(qw, sc, zr)
     S, P = N // 16, K // 512
-    pb = 4096 + (512 // G) * 64
+    pb = 4096 + (512 // G) * 128
     assert blob.numel() == S * P * pb
     b = blob.view(S, P, pb)
     words = b[:, :, :4096].contiguous().view(torch.int32).view(S, P, 16, 8, 4, 2)  # s p j r c e
     want = qw.view(P, 16, 4, S, 2, 8).permute(3, 0, 1, 5, 2, 4)  # (p j c s e r) -> s p j r c e
     assert torch.equal(words, want)
-    rec = b[:, :, 4096:].contiguous().view(torch.float16).view(S, P, 512 // G, 8, 2, 2)  # s p gi r (s|z) e
     gp = 512 // G
-    assert torch.equal(rec[..., 0, :], sc.view(P, gp, S, 2, 8).permute(2, 0, 1, 4, 3))
-    assert torch.equal(rec[..., 1, :], zr.view(P, gp, S, 2, 8).permute(2, 0, 1, 4, 3))
+    rec = b[:, :, 4096:].contiguous().view(torch.bfloat16).view(S, P, gp, 8, 4, 2)  # s p gi r (zz|hi|lo|0) e
+    s32 = sc.float()
+    hi = (s32.view(torch.int32) & -65536).view(torch.float32)
+    want_rec = {0: (128.0 + zr.float()).to(torch.bfloat16), 1: hi.to(torch.bfloat16), 2: (s32 - hi).to(torch.bfloat16)}
+    for k, v in want_rec.items():
+        assert torch.equal(rec[..., k, :].view(torch.int16), v.view(P, gp, S, 2, 8).permute(2, 0, 1, 4, 3).view(torch.int16))
+    assert torch.equal(hi + (s32 - hi), s32)  # the split is exact
+    assert not rec[..., 3, :].view(torch.int16).any()
 
 
 def _noise_floor_bound(floor_model, tok, pos, ref):
