@@ -278,15 +278,29 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const uint16_t* __restrict
   int64_t bi = n;
   const bool vec = (reinterpret_cast<uintptr_t>(xr) % 16 == 0);
   const int64_t n8 = vec ? n / 8 * 8 : 0;
-  for (int64_t c = int64_t(threadIdx.x) * 8; c < n8; c += int64_t(blockDim.x) * 8) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + c));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const int64_t nch = n8 / 8;  // 16-byte chunks
+  // kU chunks per thread in flight before any is compared (one memory round trip per kU chunks, not per
+  // chunk); a thread visits its chunks in increasing index order
+  constexpr int kU = 8;
+  for (int64_t base = 0; base < nch; base += int64_t(blockDim.x) * kU) {
+    uint4 v[kU];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float f = bf(uint16_t(w[e >> 1] >> (16 * (e & 1))));
-      if (f > best) {  // strictly greater: the first index wins within a thread
-        best = f;
-        bi = c + e;
+    for (int u = 0; u < kU; ++u) {
+      const int64_t ch = base + int64_t(u) * blockDim.x + threadIdx.x;
+      v[u] = ch < nch ? __ldg(reinterpret_cast<const uint4*>(xr) + ch) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t ch = base + int64_t(u) * blockDim.x + threadIdx.x;
+      if (ch >= nch) break;
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = bf(uint16_t(w[e >> 1] >> (16 * (e & 1))));
+        if (f > best) {  // strictly greater: the first index wins within a thread
+          best = f;
+          bi = ch * 8 + e;
+        }
       }
     }
   }
