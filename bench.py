@@ -191,27 +191,36 @@ def block_weights(rank: int, world: int, copies: int, dev):
     return [stack([0, 1, 2]), layers[3] + ([layers[3][1]],), stack([4, 5]), layers[6] + ([layers[6][1]],)]
 
 
-def block_step(x, layers, copy: int, world: int):
-    """The block's dataflow as four launches: q|k|v, o_proj, gate|up, down_proj (+ all-reduces under TP)."""
+def block_step(x, layers, copy: int, world: int, peers=None):
+    """The block's dataflow as four launches: q|k|v, o_proj, gate|up, down_proj.
+
+    Under TP the row-parallel o / down outputs are summed over the ranks inside their matmuls when a peer
+    group is given (``w4a16_matmul_allreduce``: fp32 partials through peer exchange buffers), else by an
+    NCCL all-reduce after them.
+    """
     import int4_b200 as ib
+    from int4_b200.peer import w4a16_matmul_allreduce
 
     def mm(i, inp):
         qw, s, z = layers[i][3][copy]
         return ib.w4a16_matmul(inp, qw, s, z)
 
+    def mm_sum(i, inp):
+        if world == 1:
+            return mm(i, inp)
+        if peers is not None:
+            qw, s, z = layers[i][3][copy]
+            return w4a16_matmul_allreduce(peers, inp, qw, s, z)
+        import torch.distributed as dist
+
+        out = mm(i, inp)
+        dist.all_reduce(out)
+        return out
+
     qkv = mm(0, x)
-    o = mm(1, qkv[:, :layers[0][4][0]])
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.all_reduce(o)
+    o = mm_sum(1, qkv[:, :layers[0][4][0]])
     gu = mm(2, o)
-    d = mm(3, gu[:, :layers[2][4][0]])
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.all_reduce(d)
-    return d
+    return mm_sum(3, gu[:, :layers[2][4][0]])
 
 
 def run_block(args, world, rank, local):
@@ -227,6 +236,11 @@ def run_block(args, world, rank, local):
     layers = block_weights(rank, world, copies, dev)
     g = torch.Generator().manual_seed(1)
     x = torch.randn((M, 2048), generator=g).to(torch.bfloat16).to(dev)
+    peers = None
+    if world > 1 and args.peer_allreduce and M <= 32:
+        from int4_b200.peer import PeerGroup
+
+        peers = PeerGroup(None, capacity=M * 2048)
 
     # One graph holds `chunk` steps (a divisor of K, at most 200); the timed
     # region replays it K / chunk times, i.e. exactly K steps.
@@ -236,7 +250,7 @@ def run_block(args, world, rank, local):
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):  # warm-up (eager) on the capture stream: workspace, module load
         for i in range(args.warmup):
-            block_step(x, layers, i % copies, world)
+            block_step(x, layers, i % copies, world, peers)
     torch.cuda.synchronize()
 
     def capture(fn):
@@ -264,13 +278,13 @@ def run_block(args, world, rank, local):
         barrier(world)
         return e0.elapsed_time(e1) * 1e-3, wall
 
-    graph = capture(lambda i: block_step(x, layers, i % copies, world))
+    graph = capture(lambda i: block_step(x, layers, i % copies, world, peers))
     with ClockSampler(local) as clk:
         t_dev, _ = timed(graph)
     us_per_step = max_over_ranks(t_dev, world) * 1e6 / args.steps
 
     # L2-hot variant (the reference's timing method: the same weights every step)
-    graph_hot = capture(lambda i: block_step(x, layers, 0, world))
+    graph_hot = capture(lambda i: block_step(x, layers, 0, world, peers))
     hot_us = max_over_ranks(timed(graph_hot)[0], world) * 1e6 / args.steps
 
     # End to end through the public API: pinned host x in, block output back to the host, every step.
@@ -280,7 +294,7 @@ def run_block(args, world, rank, local):
 
     def e2e_step(i):
         x_dev.copy_(x_host, non_blocking=True)
-        d = block_step(x_dev, layers, i % copies, world)
+        d = block_step(x_dev, layers, i % copies, world, peers)
         y_host.copy_(d, non_blocking=True)
 
     graph_e2e = capture(e2e_step)
@@ -288,6 +302,10 @@ def run_block(args, world, rank, local):
     e2e_us = max_over_ranks(max(t_dev, wall), world) * 1e6 / args.steps
 
     flags = _lib.device_error_flags(local)
+    if peers is not None:
+        del graph, graph_hot, graph_e2e
+        graph = graph_hot = graph_e2e = None
+        peers.close()
     # algorithmic bytes / flops of the seven linears (shard shapes), as the metric defines them
     shards = [((N // world if c else N), (K if c else K // world)) for (_, N, K, c) in BLOCK]
     total_bytes = sum(alg_bytes(M, n, k) for (n, k) in shards)
@@ -297,6 +315,8 @@ def run_block(args, world, rank, local):
         "us_per_step": us_per_step, "hot_us": hot_us, "e2e_us": e2e_us, "clocks": clk.summary(),
         "bytes_per_step_rank": total_bytes, "flops_per_step_rank": total_flops, "copies": copies,
         "launches_per_step": len(layers), "device_error_flags": flags,
+        "tp_sum": "none" if world == 1 else ("in the o/down matmuls (peer buffers)" if peers is not None
+                                            else "NCCL all-reduce"),
         "h2d": M * 2048 * 2, "d2h": M * 2048 * 2,
     }
 
@@ -431,12 +451,15 @@ def run_model(args, world, rank, local):
     for label, w4 in (("w4", True), ("bf16", False)):
         persistent = None if args.persistent < 0 else bool(args.persistent) and w4
         m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world, persistent=persistent,
+                    peer_allreduce=bool(args.peer_allreduce),
                     max_seq=prompt + steps + args.warmup + 8, max_batch=B, device=dev)
         with ClockSampler(local) as clk:
             r = time_decode(m, B, prompt, steps, args.warmup, world, dev, LLAMA_1B["vocab_size"],
                             trace=bool(args.trace) and w4)
         r["clocks"] = clk.summary()
         r["persistent"] = m.persistent is not None
+        r["peer_allreduce"] = m.peers is not None
+        m.close()
         # bytes one decode step must read on this rank: projection weights + the KV cache up to the mean position
         mean_pos = prompt + steps / 2
         kv = 2 * len(m.layers) * m.nkv_l * m.hd * 2 * B * mean_pos
@@ -510,7 +533,9 @@ def main_model(args, world, rank, local, threads):
         "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "w4a16-bf16", "data": "synthetic (random-init weights, random token ids)",
         "config": dict(model_config(args), decode="one launch for all layers (i4b_decode_layers)"
-                       if w4["persistent"] else "one launch per projection / glue op"),
+                       if w4["persistent"] else "one launch per projection / glue op",
+                       tp_sum="none" if world == 1 else ("inside the o/down matmuls (peer buffers)"
+                                                         if w4["peer_allreduce"] else "NCCL all-reduce")),
         "bf16_tokens_per_s": args.m * args.steps / bf["decode_s"],
         "w4_over_bf16": bf["decode_s"] / w4["decode_s"],
         "prefill_ms": {"w4": w4["prefill_ms"], "bf16": bf["prefill_ms"]},
@@ -544,6 +569,9 @@ def main():
     ap.add_argument("--persistent", type=int, default=-1,
                     help="model workload: 1 = all decoder layers of a step in one launch (i4b_decode_layers), "
                          "0 = one launch per projection / glue op, -1 = whichever the model qualifies for")
+    ap.add_argument("--peer-allreduce", type=int, default=1,
+                    help="tensor-parallel runs: sum the row-parallel outputs inside the W4 matmuls through peer "
+                         "exchange buffers (1) or with an NCCL all-reduce after them (0)")
     ap.add_argument("--pdl", type=int, default=1,
                     help="programmatic dependent launch for the small-M kernels (weights fetched before the wait)")
     args = ap.parse_args()

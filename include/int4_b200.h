@@ -155,6 +155,55 @@ int i4b_w4a16_matmul_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, i
                              const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
                              void* stream);
 
+/* ---- Tensor-parallel all-reduce fused into the small-M W4 matmul (peer memory over NVLink) ----
+ *
+ * The reference runs on one GPU.  Its tensor-parallel form shards o_proj and down_proj along K
+ * (row-parallel): every rank computes a partial product over its slice of K and the ranks' partials
+ * are summed.  i4b_w4a16_matmul_allreduce does that sum inside the matmul's epilogue. Each CTA:
+ *   - stores its fp32 partial outputs into every rank's exchange buffer (plain stores through
+ *     CUDA-IPC mappings);
+ *   - raises one flag per rank;
+ *   - waits, bounded, for the same CTA of every other rank;
+ *   - adds the ranks' partials in rank order and writes y.
+ * It replaces w4a16_matmul (int4_triton/gemm.py:303-309) followed by a separate all-reduce launch.
+ * Every rank ends with bit-identical y.  All ranks must make the same sequence of calls on one
+ * peer group; a group's calls must not overlap in time on a rank.  A wait that gives up after
+ * I4B_WAIT_LIMIT_NS sets bit 1 of i4b_device_error_flags, and later waits on that device then
+ * return at once. */
+#define I4B_PEER_MAX_RANKS 8
+#define I4B_IPC_HANDLE_BYTES 64
+typedef struct i4b_peer_group {
+  int32_t world;    /* ranks, 1..I4B_PEER_MAX_RANKS */
+  int32_t rank;     /* this process's rank, 0..world-1 */
+  int64_t capacity; /* outputs (M * N) one call may exchange: what the buffers were allocated for */
+  void* buffers[I4B_PEER_MAX_RANKS]; /* rank p's exchange buffer as mapped in this process */
+} i4b_peer_group;
+
+/* Bytes of one exchange buffer holding `capacity` outputs per call. */
+size_t i4b_peer_buffer_bytes(int64_t capacity);
+/* Set-up calls (they allocate and synchronise, unlike the rest of the ABI): cudaMalloc a zero-filled
+ * exchange buffer on the current device / free it. */
+int i4b_peer_buffer_alloc(int64_t capacity, void** buffer);
+int i4b_peer_buffer_free(void* buffer);
+/* CUDA-IPC handle (I4B_IPC_HANDLE_BYTES opaque bytes) of an exchange buffer, for the other ranks; open a
+ * handle received from another rank (peer access enabled); close a mapping opened that way. */
+int i4b_ipc_get_handle(void* buffer, void* handle);
+int i4b_ipc_open_handle(const void* handle, void** buffer);
+int i4b_ipc_close_handle(void* buffer);
+
+/* y[M, N] = sum over the group's ranks of (this rank's x @ W_hat^T), in x's dtype.  prologue 0: x[M, K]
+ * rows of stride_xm, x_dtype I4B_BF16 or I4B_F16, unit stride along K; I4B_PROLOGUE_SWIGLU: x = silu(g) * u
+ * of src = x = (g | u) rows [M, 2K], as i4b_w4a16_matmul_prologue does (bf16; delta, norm_weight and
+ * resid_out unused).  I4B_PROLOGUE_RMSNORM is rejected: a K shard does not hold the whole row the norm
+ * needs.  1 <= M <= 32 and M * N <= capacity.  Needs no
+ * workspace; sizes that would need the workspace split-K (K > 8192) or more CTAs than the device has SMs
+ * return I4B_ERR_SHAPE.  world == 1 skips the exchange. */
+int i4b_w4a16_matmul_allreduce(const i4b_peer_group* group, int prologue, const void* x, int x_dtype,
+                               const void* delta, const void* norm_weight, float eps, void* resid_out, int64_t M,
+                               int64_t K, int64_t stride_xm, const int32_t* qweight, int64_t N, int64_t stride_qk,
+                               const uint16_t* scales, const uint16_t* zeros, int64_t stride_sg, int group_size,
+                               void* y, int64_t stride_ym, void* stream);
+
 /* ---- Decode-step glue of a Llama layer (bf16, head_dim 64), for the model-level caller of the
  * matmuls.  No counterpart in the reference, which runs these steps as transformers' torch ops
  * (benchmarks/eval_llama.py:121-183); each reproduces transformers' bf16 rounding points.
@@ -253,7 +302,8 @@ void i4b_set_decode_trace(void* buffer, size_t bytes);
 void i4b_set_gemm_override(int tile, int splits);
 
 /* Device-side error flags raised by kernels of this library on `device`
- * (a bounded wait that expired sets bit 0).  Synchronises that device;
+ * (a bounded wait that expired sets bit 0; a wait for another rank of a peer
+ * group that expired sets bit 1).  Synchronises that device;
  * clear != 0 resets the flags.  Returns -1 if the flags cannot be read. */
 int i4b_device_error_flags(int device, int clear);
 

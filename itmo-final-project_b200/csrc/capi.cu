@@ -87,6 +87,10 @@ constexpr int64_t kSmallM = kSkinnyMaxM;
 
 }  // namespace
 
+namespace i4b {
+int cuda_error_status(cudaError_t e) { return fail_cuda(e); }
+}  // namespace i4b
+
 extern "C" {
 
 const char* i4b_status_string(int status) {
@@ -251,6 +255,54 @@ int i4b_w4a16_matmul_prologue(int prologue, const void* src, const void* delta, 
   const W4Prologue pro{prologue, delta, norm_weight, resid_out, eps};
   cudaError_t e = launch_w4(false, src, M, K, stride_src, 1, qweight, N, stride_qk, scales, zeros, stride_sg, G, y,
                             stride_ym, workspace, p, g_pdl, static_cast<cudaStream_t>(stream), &pro);
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
+int i4b_w4a16_matmul_allreduce(const i4b_peer_group* group, int prologue, const void* x, int x_dtype,
+                               const void* delta, const void* norm_weight, float eps, void* resid_out, int64_t M,
+                               int64_t K, int64_t stride_xm, const int32_t* qweight, int64_t N, int64_t stride_qk,
+                               const uint16_t* scales, const uint16_t* zeros, int64_t stride_sg, int group_size,
+                               void* y, int64_t stride_ym, void* stream) {
+  if (!group || group->world < 1 || group->world > I4B_PEER_MAX_RANKS || group->rank < 0 ||
+      group->rank >= group->world || group->capacity < 0)
+    return I4B_ERR_INVALID_ARG;
+  // RMSNorm needs the statistics of the whole row, which a K shard does not hold: plain or SwiGLU only
+  if (prologue != 0 && prologue != I4B_PROLOGUE_SWIGLU) return I4B_ERR_INVALID_ARG;
+  if (x_dtype != I4B_BF16 && (x_dtype != I4B_F16 || prologue != 0)) return I4B_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return I4B_ERR_INVALID_ARG;
+  if (M > kW4MaxM || K % 8 != 0) return I4B_ERR_SHAPE;
+  const int G = group_size;
+  if (G <= 0 || G % 32 != 0 || K % G != 0) return I4B_ERR_GROUP;
+  if (M == 0 || N == 0) return I4B_OK;
+  if (!x || !qweight || !scales || !zeros || !y) return I4B_ERR_INVALID_ARG;
+  if (prologue == I4B_PROLOGUE_RMSNORM && !norm_weight) return I4B_ERR_INVALID_ARG;
+  if (N > INT32_MAX || K > INT32_MAX || M * N > group->capacity) return I4B_ERR_SHAPE;
+  if (stride_qk < N || stride_sg < N || stride_ym < N) return I4B_ERR_LAYOUT;
+  if (prologue != 0) {
+    const int64_t row = prologue == I4B_PROLOGUE_SWIGLU ? 2 * K : K;
+    if (stride_xm < row || stride_xm % 8 != 0 || !aligned16(x) || (delta && !aligned16(delta)) ||
+        (norm_weight && !aligned16(norm_weight)) || (resid_out && !aligned16(resid_out)))
+      return I4B_ERR_LAYOUT;
+  } else if (stride_xm < K) {
+    return I4B_ERR_LAYOUT;
+  }
+  for (int q = 0; q < group->world; ++q)
+    if (!group->buffers[q] || reinterpret_cast<uintptr_t>(group->buffers[q]) % 256 != 0) return I4B_ERR_INVALID_ARG;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const W4Plan p = plan_w4(M, N, K, G, d.sms);
+  // every CTA waits for the same CTA of the other ranks, so the whole grid must be resident at once
+  if (p.mode != 0 && p.mode != 1) return I4B_ERR_SHAPE;
+  if (p.ntiles * p.S > std::min<int64_t>(d.sms, kArMaxCtas)) return I4B_ERR_SHAPE;
+  W4AllReduce ar{};
+  for (int q = 0; q < group->world; ++q) ar.buffers[q] = group->buffers[q];
+  ar.capacity = group->capacity;
+  ar.world = group->world;
+  ar.rank = group->rank;
+  const W4Prologue pro{prologue, delta, norm_weight, resid_out, eps};
+  cudaError_t e = launch_w4(x_dtype == I4B_F16, x, M, K, stride_xm, 1, qweight, N, stride_qk, scales, zeros, stride_sg,
+                            G, y, stride_ym, nullptr, p, g_pdl, static_cast<cudaStream_t>(stream),
+                            prologue ? &pro : nullptr, &ar);
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
@@ -439,7 +491,8 @@ int i4b_device_error_flags(int device, int clear) {
   if (cudaSetDevice(device) != cudaSuccess) return -1;
   int flags = -1;
   if (cudaDeviceSynchronize() == cudaSuccess) {
-    flags = int(read_quant_error(clear != 0) | read_tc_error(clear != 0) | read_dk_error(clear != 0));
+    flags = int(read_quant_error(clear != 0) | read_tc_error(clear != 0) | read_dk_error(clear != 0) |
+                read_w4_error(clear != 0));
   }
   cudaSetDevice(prev);
   return flags;

@@ -28,6 +28,7 @@
 
 // Device-side error codes (bit flags OR-ed into a per-file __device__ word).
 #define I4B_DEVERR_WAIT_TIMEOUT 1u
+#define I4B_DEVERR_PEER_TIMEOUT 2u  // a wait for another rank of a peer group gave up
 
 namespace i4b {
 

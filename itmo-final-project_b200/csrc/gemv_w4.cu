@@ -69,9 +69,96 @@ struct W4SArgs {
   const uint16_t* norm_w;
   uint16_t* resid_out;
   float eps;
+  // fused tensor-parallel all-reduce of y (ar_world > 1): every rank's exchange buffer, mapped here
+  uint8_t* ar_buf[kArMaxRanks];
+  int64_t ar_cap;
+  int ar_world, ar_rank;
 };
 
 enum { kProPlain = 0, kProRmsNorm = 1, kProSwiGlu = 2 };
+
+__device__ unsigned int g_w4_err = 0;
+
+// ---- fused all-reduce over peer exchange buffers (layout in kernels.h)
+
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// fp32 outputs of source rank `src` in rank p's buffer
+__device__ __forceinline__ float* ar_data(const W4SArgs& a, int p, uint32_t slot, int src) {
+  return reinterpret_cast<float*>(a.ar_buf[p] + kArDataOff) + (int64_t(slot) * kArMaxRanks + src) * a.ar_cap;
+}
+__device__ __forceinline__ unsigned int* ar_flag(const W4SArgs& a, int p, uint32_t slot, int src, int cta) {
+  return reinterpret_cast<unsigned int*>(a.ar_buf[p] + kArCtlBytes) + (int(slot) * kArMaxRanks + src) * kArMaxCtas +
+         cta;
+}
+// The call's epoch, read once per CTA (after the previous kernel of the stream has completed).
+__device__ __forceinline__ uint32_t ar_epoch(const W4SArgs& a, uint32_t* s_ep) {
+  if (threadIdx.x == 0) *s_ep = *reinterpret_cast<volatile unsigned int*>(a.ar_buf[a.ar_rank]);
+  __syncthreads();
+  return *s_ep;
+}
+// Push one output (offset tok * N + n) to every rank's buffer, slot of this epoch, region of this rank.
+__device__ __forceinline__ void ar_push(const W4SArgs& a, uint32_t slot, int64_t off, float v) {
+  for (int p = 0; p < a.ar_world; ++p) ar_data(a, p, slot, a.ar_rank)[off] = v;
+}
+// Sum over source ranks, in rank order, of one output in this rank's buffer.
+__device__ __forceinline__ float ar_sum(const W4SArgs& a, uint32_t slot, int64_t off) {
+  float t[kArMaxRanks];
+#pragma unroll
+  for (int q = 0; q < kArMaxRanks; ++q) t[q] = q < a.ar_world ? __ldcg(ar_data(a, a.ar_rank, slot, q) + off) : 0.0f;
+  float v = t[0];
+#pragma unroll
+  for (int q = 1; q < kArMaxRanks; ++q)
+    if (q < a.ar_world) v += t[q];
+  return v;
+}
+// After every thread of the CTA has pushed: raise this CTA's flag in every other rank's buffer, then wait
+// (bounded) for the same CTA of every other rank.  A wait that gives up sets I4B_DEVERR_PEER_TIMEOUT; once
+// set, later waits on this device return at once.
+__device__ __forceinline__ void ar_publish_wait(const W4SArgs& a, uint32_t ep, int cta) {
+  __threadfence_system();  // this thread's pushes reach every rank before the flags below
+  __syncthreads();
+  const uint32_t slot = ep & 1u;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < a.ar_world; ++p)
+      if (p != a.ar_rank) st_release_sys(ar_flag(a, p, slot, a.ar_rank, cta), ep + 1);
+  }
+  const int src = int(threadIdx.x);
+  if (src < a.ar_world && src != a.ar_rank) {
+    const unsigned int* f = ar_flag(a, a.ar_rank, slot, src, cta);
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while (int(ld_acquire_sys(f) - (ep + 1)) < 0) {
+      if ((++it & 255u) == 0) {
+        if (*reinterpret_cast<volatile unsigned int*>(&g_w4_err) & I4B_DEVERR_PEER_TIMEOUT) break;
+        if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) {
+          atomicOr(&g_w4_err, I4B_DEVERR_PEER_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+// The last CTA of the call advances this rank's epoch (read by the next call on the group).
+__device__ __forceinline__ void ar_finish(const W4SArgs& a, uint32_t ep) {
+  if (threadIdx.x == 0) {
+    unsigned int* ctl = reinterpret_cast<unsigned int*>(a.ar_buf[a.ar_rank]);
+    const unsigned int prev = atomicAdd(ctl + 1, 1u);
+    if (prev == gridDim.x * gridDim.y - 1) {
+      atomicExch(ctl + 1, 0u);
+      __threadfence();
+      atomicExch(ctl, ep + 1);
+    }
+  }
+}
 
 __device__ __forceinline__ float bfv(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 __device__ __forceinline__ uint32_t bfr(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
@@ -410,6 +497,35 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
 
   // ---- outputs: acc[t][mt][e] is (token mt*8 + 2c + (e & 1), column 32*warp + 4r + 2t + (e >> 1))
   uint16_t* y = a.y;
+  __shared__ uint32_t s_ep;
+  if (a.ar_world > 1 && a.mode == 0) {
+    // Tensor-parallel sum of the ranks' outputs: push, publish, wait for the other ranks, add in rank order.
+    const uint32_t ep = ar_epoch(a, &s_ep);
+    const uint32_t slot = ep & 1u;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = mt * 8 + 2 * c + (e & 1);
+          const int64_t n = n_lane + 2 * t + (e >> 1);
+          if (tok < M && n < a.N) ar_push(a, slot, int64_t(tok) * a.N + n, acc[t][mt][e]);
+        }
+    ar_publish_wait(a, ep, int(blockIdx.y * gridDim.x + blockIdx.x));
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = mt * 8 + 2 * c + (e & 1);
+          const int64_t n = n_lane + 2 * t + (e >> 1);
+          if (tok < M && n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(ar_sum(a, slot, int64_t(tok) * a.N + n));
+        }
+    ar_finish(a, ep);
+    return;
+  }
   if (a.mode == 0) {
 #pragma unroll
     for (int t = 0; t < 2; ++t)
@@ -434,8 +550,35 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
       }
   if (a.mode == 1) {
     // Cluster of S CTAs along K: rank q adds outputs q*128 + tid, (q + S)*128 + tid, ... over all ranks in order.
+    const uint32_t ep = a.ar_world > 1 ? ar_epoch(a, &s_ep) : 0u;
     cluster_sync();
     const uint32_t rank = cluster_ctarank();
+    if (a.ar_world > 1) {
+      // The cluster's sums are this rank's partials: push them, then the tensor-parallel sum as in mode 0.
+      const uint32_t slot = ep & 1u;
+      for (int idx = int(rank) * kBN + tid; idx < M * kBN; idx += a.S * kBN) {
+        const uint32_t addr = smem_u32(sP + idx);
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = q < a.S ? ld_shared_cluster_f32(mapa_shared(addr, uint32_t(q))) : 0.0f;
+        float v = t[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q)
+          if (q < a.S) v += t[q];
+        const int tok = idx / kBN;
+        const int64_t n = n0 + idx % kBN;
+        if (n < a.N) ar_push(a, slot, int64_t(tok) * a.N + n, v);
+      }
+      cluster_sync();  // remote shared-memory reads done before any CTA of the cluster moves on
+      ar_publish_wait(a, ep, int(blockIdx.y * gridDim.x + blockIdx.x));
+      for (int idx = int(rank) * kBN + tid; idx < M * kBN; idx += a.S * kBN) {
+        const int tok = idx / kBN;
+        const int64_t n = n0 + idx % kBN;
+        if (n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(ar_sum(a, slot, int64_t(tok) * a.N + n));
+      }
+      ar_finish(a, ep);
+      return;
+    }
     for (int idx = int(rank) * kBN + tid; idx < M * kBN; idx += a.S * kBN) {
       const uint32_t addr = smem_u32(sP + idx);
       float t[8];  // all S (<= 8) remote loads in flight, then added in rank order
@@ -852,7 +995,8 @@ static cudaError_t launch_stream(bool f16, const W4SArgs& a, int sps, int num_sm
 
 cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
                       int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
-                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream, const W4Prologue* pro) {
+                      int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream, const W4Prologue* pro,
+                      const W4AllReduce* ar) {
   if (p.mode == 3) return cudaErrorInvalidConfiguration;
   W4SArgs a{};
   if (pro) {
@@ -891,9 +1035,16 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   const int L = 32 * p.SPS;
   a.gpl = G / L;  // L divides G
   a.gpl_shift = (a.gpl & (a.gpl - 1)) == 0 ? __builtin_ctz(unsigned(a.gpl)) : -1;
+  if (ar && ar->world > 1) {
+    if (p.mode != 0 && p.mode != 1) return cudaErrorInvalidConfiguration;
+    for (int q = 0; q < kArMaxRanks; ++q) a.ar_buf[q] = static_cast<uint8_t*>(ar->buffers[q]);
+    a.ar_cap = ar->capacity;
+    a.ar_world = ar->world;
+    a.ar_rank = ar->rank;
+  }
   int sms = 0, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (sms > 0 && stream_eligible(a, p, sms)) return launch_stream(f16, a, p.SPS, sms, stream);
+  if (sms > 0 && a.ar_world <= 1 && stream_eligible(a, p, sms)) return launch_stream(f16, a, p.SPS, sms, stream);
   const int spst = p.SPS > 4 ? p.SPS : 4;  // steps per stage, as in the kernel
   const int nsteps = p.KC / 32;
   a.nstages = (nsteps + spst - 1) / spst;
@@ -915,6 +1066,16 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
     case 2: return f16 ? launch_w4_sps<2, true>(a, p, smem, stream) : launch_w4_sps<2, false>(a, p, smem, stream);
     default: return f16 ? launch_w4_sps<4, true>(a, p, smem, stream) : launch_w4_sps<4, false>(a, p, smem, stream);
   }
+}
+
+unsigned int read_w4_error(bool clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_w4_err, sizeof(v)) != cudaSuccess) return 0;
+  if (clear && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_w4_err, &z, sizeof(z));
+  }
+  return v;
 }
 
 }  // namespace i4b

@@ -58,11 +58,30 @@ struct W4Prologue {
   void* resid_out;
   float eps;
 };
+// Peer exchange buffer of the fused tensor-parallel all-reduce (i4b_peer_group), per rank:
+//   [control: epoch u32, done-ticket u32 | 256 B][flags u32 [2 slots][8 source ranks][kArMaxCtas]]
+//   [data fp32 [2 slots][8 source ranks][capacity]]
+// A call of epoch e uses slot e & 1 and raises flags to e + 1.
+constexpr size_t kArCtlBytes = 256;
+constexpr int kArMaxRanks = 8;
+constexpr int kArMaxCtas = 1024;
+constexpr size_t kArDataOff = kArCtlBytes + size_t(2) * kArMaxRanks * kArMaxCtas * 4;
+inline size_t ar_buffer_bytes(int64_t capacity) {
+  return kArDataOff + size_t(2) * kArMaxRanks * size_t(capacity) * 4;
+}
+struct W4AllReduce {
+  void* buffers[kArMaxRanks];
+  int64_t capacity;
+  int world, rank;
+};
 cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
                       int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
                       int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream,
-                      const W4Prologue* pro = nullptr);
+                      const W4Prologue* pro = nullptr, const W4AllReduce* ar = nullptr);
 void set_w4_split_override(int splits);
+unsigned int read_w4_error(bool clear);
+// capi.cu: records e for i4b_last_cuda_error and returns I4B_ERR_CUDA
+int cuda_error_status(cudaError_t e);
 
 // gemm_tc.cu (M > 64)
 struct TcOperands {

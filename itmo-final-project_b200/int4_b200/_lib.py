@@ -53,6 +53,15 @@ _SIGNATURES = {
     "i4b_decode_workspace_size": (_c_int, [_c_vp, ctypes.POINTER(_c_size)]),
     "i4b_decode_layers": (_c_int, [_c_vp, _c_vp, _c_size, _c_vp]),
     "i4b_set_decode_trace": (None, [_c_vp, _c_size]),
+    "i4b_peer_buffer_bytes": (_c_size, [_c_i64]),
+    "i4b_peer_buffer_alloc": (_c_int, [_c_i64, ctypes.POINTER(_c_vp)]),
+    "i4b_peer_buffer_free": (_c_int, [_c_vp]),
+    "i4b_ipc_get_handle": (_c_int, [_c_vp, _c_vp]),
+    "i4b_ipc_open_handle": (_c_int, [_c_vp, ctypes.POINTER(_c_vp)]),
+    "i4b_ipc_close_handle": (_c_int, [_c_vp]),
+    "i4b_w4a16_matmul_allreduce": (_c_int, [_c_vp, _c_int, _c_vp, _c_int, _c_vp, _c_vp, ctypes.c_float, _c_vp, _c_i64,
+                                            _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_int, _c_vp,
+                                            _c_i64, _c_vp]),
 }
 
 

@@ -8,7 +8,9 @@ the projections laid out for the kernels and for tensor parallelism:
 
 * q/k/v are one column-parallel projection per layer (this rank's heads of
   q, k and v stacked along N), gate/up likewise; o_proj and down_proj are
-  row-parallel (this rank's slice of K) followed by a bf16 all-reduce;
+  row-parallel (this rank's slice of K) followed by an all-reduce -- in a
+  W4 decode step the sum runs inside the o / down matmul itself
+  (``peer.w4a16_matmul_allreduce``), elsewhere it is NCCL's;
 * the lm_head is vocab-parallel followed by an all-gather of the logits;
 * every INT4 weight is quantized per shard -- for column shards that is the
   same bits as slicing the fully quantized tensor, and for row shards too as
@@ -32,6 +34,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .gemm import w4a16_matmul
+from .peer import w4a16_matmul_allreduce
 from .quantize import quantize_int4
 
 
@@ -323,11 +326,15 @@ class LlamaTP:
     transformers uses.  ``persistent`` (default: whenever the model qualifies --
     W4, one rank, fused, batch <= 8, widths multiples of 2048) runs all decoder
     layers of a decode step as one launch of ``i4b_decode_layers``.
+    ``peer_allreduce`` (tensor-parallel W4 decode steps of <= 32 tokens) sums
+    the row-parallel o / down outputs inside those matmuls through peer
+    exchange buffers (``i4b_w4a16_matmul_allreduce``) instead of NCCL.
     """
 
     def __init__(self, hf_model, *, w4: bool = True, group_size: int = 128, quantize_lm_head: bool = False,
                  rank: int = 0, world: int = 1, group=None, max_seq: int = 2048, max_batch: int = 1,
-                 device: torch.device | None = None, fused: bool = True, persistent: bool | None = None):
+                 device: torch.device | None = None, fused: bool = True, persistent: bool | None = None,
+                 peer_allreduce: bool = True):
         cfg = hf_model.config
         self.fused = fused
         self.cfg = cfg
@@ -403,6 +410,19 @@ class LlamaTP:
         if qualifies and persistent is not False:
             self.persistent = PersistentDecoder(
                 self, [{k: L[k].q for k in ("qkv", "o", "gu", "down")} for L in self.layers], group_size)
+        # Under tensor parallelism the W4 decode step sums the row-parallel o / down outputs inside their
+        # matmuls (peer exchange buffers over NVLink) instead of a separate NCCL all-reduce.
+        self.peers = None
+        if world > 1 and w4 and fused and peer_allreduce:
+            from .peer import PeerGroup
+
+            self.peers = PeerGroup(group, capacity=max_batch * H)
+
+    def close(self) -> None:
+        """Release the peer exchange buffers (collective when tensor-parallel)."""
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     # ------------------------------------------------------------------ collectives
 
@@ -512,12 +532,19 @@ class LlamaTP:
                 qkv = L["qkv"](x)
             rope_kv_cache(qkv, self.cos, self.sin, pos, q, kc, vc, nq, nkv)
             decode_attention(q, kc, vc, pos, att, nq, nkv, hd ** -0.5)
-            o = self._all_reduce(L["o"](att))
+            fused_ar = fold and self.peers is not None
+            if fused_ar:
+                o = w4a16_matmul_allreduce(self.peers, att, *L["o"].q)
+            else:
+                o = self._all_reduce(L["o"](att))
             if fold:
                 gu = w4a16_matmul_prologue(PROLOGUE_RMSNORM, cur, *L["gu"].q, delta=o, norm_weight=L["ln2"],
                                            eps=self.eps, resid_out=other)
                 cur, other = other, cur
-                delta = self._all_reduce(w4a16_matmul_prologue(PROLOGUE_SWIGLU, gu, *L["down"].q))
+                if fused_ar:
+                    delta = w4a16_matmul_allreduce(self.peers, gu, *L["down"].q, prologue=PROLOGUE_SWIGLU)
+                else:
+                    delta = self._all_reduce(w4a16_matmul_prologue(PROLOGUE_SWIGLU, gu, *L["down"].q))
             else:
                 add_rmsnorm(cur, o, L["ln2"], x, self.eps)
                 silu_mul(L["gu"](x), act)

@@ -63,3 +63,34 @@ def test_argument_validation_before_any_device_call(L):
     # empty problems are a no-op
     assert L.i4b_w4a16_matmul(None, 1, 0, 256, 256, 1, None, 8, 8, None, None, 8, 128, None, 8, None, 0, None) == 0
     assert L.i4b_w4a16_workspace_size(1, 8, 256, 16) == 0
+
+
+def test_fused_allreduce_validation_before_any_device_call(L):
+    import ctypes
+
+    from int4_b200.peer import MAX_RANKS, PeerGroupStruct
+
+    fake = [0x100000 * (i + 1) for i in range(2)]  # never dereferenced: every case below fails validation first
+
+    def call(grp, prologue=0, dtype=1, M=1, N=64, K=256, G=128):
+        return L.i4b_w4a16_matmul_allreduce(ctypes.byref(grp), prologue, 0x1000, dtype, None, None, 0.0, None, M, K, K,
+                                            0x2000, N, N, 0x3000, 0x4000, N, G, 0x5000, N, None)
+
+    def grp(world, rank, cap, bufs):
+        return PeerGroupStruct(world, rank, cap, (ctypes.c_void_p * MAX_RANKS)(*(bufs + [None] * (MAX_RANKS - len(bufs)))))
+
+    assert L.i4b_w4a16_matmul_allreduce(None, 0, None, 1, None, None, 0.0, None, 1, 256, 256, None, 64, 64, None,
+                                        None, 64, 128, None, 64, None) == 1  # no group
+    assert call(grp(9, 0, 64, fake)) == 1            # more ranks than a group holds
+    assert call(grp(2, 2, 64, fake)) == 1            # rank outside the group
+    assert call(grp(2, 0, 64, fake), prologue=1) == 1  # RMSNorm of a K shard is rejected
+    assert call(grp(2, 0, 64, fake), dtype=0, prologue=2) == 1  # SwiGLU prologue is bf16 only
+    assert call(grp(2, 0, 63, fake)) == 2            # M * N beyond the buffers' capacity
+    assert call(grp(2, 0, 64, fake), M=33) == 2       # beyond the small-M kernel
+    assert call(grp(2, 0, 64, fake), G=96) == 3
+    assert call(grp(2, 0, 64, [fake[0]])) == 1        # a rank without a buffer
+    assert call(grp(2, 0, 64, [fake[0], fake[1] + 16])) == 1  # buffers are 256-byte aligned allocations
+    assert call(grp(2, 0, 64, fake), M=0) == 0        # empty: no-op
+    assert L.i4b_peer_buffer_bytes(0) == 256 + 2 * 8 * 1024 * 4
+    assert L.i4b_peer_buffer_bytes(1000) == 256 + 2 * 8 * 1024 * 4 + 2 * 8 * 1000 * 4
+    assert L.i4b_ipc_get_handle(None, None) == 1 and L.i4b_ipc_open_handle(None, None) == 1

@@ -1,9 +1,14 @@
 """One rank of the two-GPU tensor-parallel decode check (launched by tests/test_decode_gpu.py via torchrun).
 
-Every rank builds the same seeded tiny Llama, runs its ``LlamaTP`` shard (NCCL
-all-reduce after o/down, all-gather of the vocab-parallel logits) for a prompt
-and three cached decode steps, and compares with a one-rank ``LlamaTP`` of the
-same weights.  Exit status 0 only if every rank stays within 2e-2 max-abs.
+Every rank builds the same seeded tiny Llama, runs its ``LlamaTP`` shard for a
+prompt and three cached decode steps, and compares with a one-rank ``LlamaTP``
+of the same weights.  The row-parallel o/down outputs of the decode steps are
+summed inside the W4 matmuls through peer exchange buffers
+(``w4a16_matmul_allreduce``), or by an NCCL all-reduce (``peer_allreduce=False``);
+the prompt always uses NCCL; the vocab-parallel logits are all-gathered.  With
+the fused sum, three more steps replayed from one CUDA graph must equal the
+eager steps bit for bit.  Exit status 0 only if every rank stays within 2e-2
+max-abs and no kernel's bounded wait expired.
 """
 from __future__ import annotations
 
@@ -30,29 +35,57 @@ def main() -> int:
     from int4_b200.decode import LlamaTP
     from test_decode_gpu import build_hf
 
-    worst = 0.0
+    from int4_b200 import _lib
+
+    worst, graph_diff = 0.0, 0.0
     with torch.no_grad():
         hf = build_hf(0)
         g = torch.Generator().manual_seed(3)
         ids = torch.randint(0, 512, (1, 24), generator=g).to(dev)
-        for lm_w4 in (False, True):
-            tp = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=rank, world=world, max_seq=64, device=dev)
+        for lm_w4, peer in ((False, True), (True, True), (False, False)):
+            tp = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=rank, world=world, max_seq=64, device=dev,
+                         peer_allreduce=peer)
+            assert (tp.peers is not None) == peer
             one = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev)
             a, b = tp.prefill(ids, all_logits=True), one.prefill(ids, all_logits=True)
             worst = max(worst, (a.float() - b.float()).abs().max().item())
             tok = b[:, -1].argmax(-1, keepdim=True)
+            eager = []
             for step in range(3):
                 pos = torch.tensor([24 + step], device=dev)
                 a, b = tp.decode_step(tok, pos), one.decode_step(tok, pos)
                 worst = max(worst, (a.float() - b.float()).abs().max().item())
+                eager.append(a.clone())
                 tok = b[:, -1].argmax(-1, keepdim=True)
-    t = torch.tensor([worst], device=dev)
+            if peer:
+                # the same three steps replayed from one captured step: identical logits
+                first = one.prefill(ids)[:, -1].argmax(-1, keepdim=True)
+                tp.prefill(ids)
+                tok_g = first.clone()
+                pos_g = torch.tensor([24], device=dev)
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    out = tp.decode_step(tok_g, pos_g)
+                tp.prefill(ids)
+                for step in range(3):
+                    graph.replay()
+                    graph_diff = max(graph_diff, (out.float() - eager[step].float()).abs().max().item())
+                    tok_g.copy_(one.decode_step(tok_g, pos_g)[:, -1].argmax(-1, keepdim=True))
+                    pos_g += 1
+                torch.cuda.synchronize()
+                del graph
+            tp.close()
+    flags = _lib.device_error_flags(local)
+    t = torch.tensor([worst, graph_diff, float(flags != 0)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     torch.cuda.synchronize()
     dist.destroy_process_group()
     if rank == 0:
-        print(f"max |logits(tp{world}) - logits(tp1)| = {t.item():.3e}")
-    return 0 if t.item() <= 2e-2 else 1
+        print(f"max |logits(tp{world}) - logits(tp1)| = {t[0].item():.3e}, graph vs eager {t[1].item():.3e}, "
+              f"device error flags {'set' if t[2].item() else 'clear'}")
+    return 0 if t[0].item() <= 2e-2 and t[1].item() == 0.0 and t[2].item() == 0.0 else 1
 
 
 if __name__ == "__main__":
