@@ -268,7 +268,17 @@ typedef struct i4b_decode_model {
   void* k_cache;         /* bf16 [layers, cache_batch, kv_heads, max_seq, 64] */
   void* v_cache;         /* bf16 [layers, cache_batch, kv_heads, max_seq, 64] */
   void* h_out;           /* bf16 [batch, hidden]: the residual stream after the last layer */
+  /* Tensor parallelism: NULL (or world 1) for one rank.  Otherwise heads, kv_heads and intermediate are
+   * this rank's shares, the weights its shards (q/k/v and gate/up split along N, o and down along K) and
+   * the caches hold its kv heads.  The o / down epilogues then store their fp32 partial outputs into
+   * every rank's exchange buffer (each of at least i4b_decode_peer_capacity outputs, used by no other
+   * call), and the stages that consume the residual stream add the ranks' partials in rank order: every
+   * rank ends with the same h_out.  All ranks must make the same sequence of calls on one group. */
+  const i4b_peer_group* peers;
 } i4b_decode_model;
+
+/* Capacity (outputs) of each exchange buffer of a tensor-parallel i4b_decode_layers group. */
+int64_t i4b_decode_peer_capacity(int32_t layers, int32_t world, int32_t hidden);
 
 /* Bytes of the tiled form of a quantize_int4 triple; 0 when N % 16, K % 512 or G is unsupported. */
 size_t i4b_tile_w4_bytes(int64_t N, int64_t K, int group_size);

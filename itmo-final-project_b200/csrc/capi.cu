@@ -485,6 +485,11 @@ int i4b_decode_layers(const i4b_decode_model* model, void* workspace, size_t wor
 
 void i4b_set_decode_trace(void* buffer, size_t bytes) { set_decode_trace(buffer, bytes); }
 
+int64_t i4b_decode_peer_capacity(int32_t layers, int32_t world, int32_t hidden) {
+  if (layers <= 0 || world <= 0 || hidden <= 0) return 0;
+  return decode_peer_capacity(layers, world, hidden);
+}
+
 int i4b_device_error_flags(int device, int clear) {
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess) return -1;

@@ -89,6 +89,14 @@ struct DkHot {
   uint16_t* att;      // [B][q_n]
   uint16_t* act;      // [B][intermediate]
   unsigned long long* trace;  // optional: [grid][layers][5 stages][8] %globaltimer stamps, or null
+  // Tensor parallelism (tp_world > 1): every rank's exchange buffer as mapped here (layout below), this
+  // rank, the CTA that stores the summed residual rows in stages G_QKV / G_GU, and the residual rows
+  // [kMaxTok][hidden] after update u in hbuf[u & 1].  Update u = 2l adds layer l's o_proj outputs of all
+  // ranks, u = 2l + 1 its down_proj outputs.
+  uint8_t* xb[kArMaxRanks];
+  int tp_world, tp_rank;
+  int writer[4];
+  uint16_t* hbuf[2];
 };
 
 struct DkParams {
@@ -164,6 +172,64 @@ __device__ bool wait_counter(const unsigned int* c, unsigned int target, const u
       if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
     }
   }
+}
+
+// ---- tensor parallelism: exchange buffer of rank p (i4b_peer_group), as this launch uses it:
+//   [epoch u32 | 256 B][counters u32 [layers][2]: o_proj, down_proj partials received from the other ranks]
+//   [fp32 partial outputs [layers][2][world][kMaxTok][hidden], at kArDataOff]
+// The counters only grow: step e (the epoch) waits for (e + 1) * (world - 1) * slabs of the stage.
+__device__ __forceinline__ float* xdata(const DkHot& P, int p, int l, int s, int src) {
+  return reinterpret_cast<float*>(P.xb[p] + kArDataOff) +
+         int64_t((l * 2 + s) * P.tp_world + src) * kMaxTok * P.m.hidden;
+}
+__device__ __forceinline__ unsigned int* xctr(const DkHot& P, int p, int l, int s) {
+  return reinterpret_cast<unsigned int*>(P.xb[p] + kArCtlBytes) + l * 2 + s;
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until the counter another GPU raises reaches target (wrap-around order; acquire at system scope).
+__device__ bool wait_counter_sys(const unsigned int* c, unsigned int target, const unsigned int* abort_word) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (int(ld_acquire_sys_u32(c) - target) >= 0) return true;
+    if ((i & 31u) == 0) {
+      if (ld_relaxed_u32(abort_word)) return false;
+      if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
+    }
+  }
+}
+// Eight residual values (token t, columns 8ch..8ch+7) after update u: bf16(h_{u-1} + bf16(sum over ranks,
+// in rank order, of their fp32 partials)) -- the one-rank epilogue's rounding, bf16(h + bf16(sum)).
+// h_{-1} is the token's embedding row.
+__device__ __forceinline__ uint4 residual_chunk(const DkHot& P, int u, int t, int ch) {
+  const i4b_decode_model& m = P.m;
+  const int H = m.hidden;
+  uint4 hv;
+  if (u == 0) {
+    int64_t id = m.tokens[t];
+    if (id < 0 || id >= m.vocab) id = 0;
+    hv = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(m.embed) + id * H + 8 * ch));
+  } else {
+    hv = ldcg128(P.hbuf[(u - 1) & 1] + int64_t(t) * H + 8 * ch);
+  }
+  float sm[8];
+#pragma unroll 1
+  for (int r = 0; r < P.tp_world; ++r) {
+    const float* d = xdata(P, P.tp_rank, u >> 1, u & 1, r) + int64_t(t) * H + 8 * ch;
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(d)), b = __ldcg(reinterpret_cast<const float4*>(d + 4));
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sm[i] = r == 0 ? v[i] : sm[i] + v[i];
+  }
+  const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    o[i] = bfr(bfv(hw[i] & 0xFFFFu) + bfv(bfr(sm[2 * i]))) | (bfr(bfv(hw[i] >> 16) + bfv(bfr(sm[2 * i + 1]))) << 16);
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // mbarrier phase wait, bounded, giving up early when another CTA aborted.  Each probe lets the thread
@@ -251,6 +317,7 @@ struct Smem {
   uint16_t poff[kMaxItems];  // piece offset of each item inside the CTA's layer sequence
   int nit, ppl;
   int flag;   // 1 until a wait fails in this CTA (then 0 for the rest of the launch)
+  unsigned int ep;  // tensor parallelism: this launch's epoch (steps this rank's group has completed)
   int tflag;  // the attention ticket said: this CTA combines
   volatile int prod_seq;  // pieces issued by the producer so far (diagnostics)
   long long wexit[kCW];   // each compute warp's clock at the end of its pieces (diagnostics)
@@ -286,20 +353,35 @@ __device__ __noinline__ void stage_x(int g, int l, int K) {
   const int64_t stride = g == G_O ? P.q_n : g == G_DOWN ? m.intermediate : H;
   uint8_t* sx = smem + P.off_x;
   const int nch = K / 8, lg = 31 - __clz(nch), total = B << lg;  // chunks per row: a power of two
+  if (P.tp_world > 1 && (g == G_GU || (g == G_QKV && l > 0))) {
+    // tensor parallelism: the residual rows are the previous update's rows plus all ranks' partials;
+    // one CTA also stores them for the next update
+    const int u = g == G_GU ? 2 * l : 2 * l - 1;
+    uint16_t* hout = int(blockIdx.x) == P.writer[g] ? P.hbuf[u & 1] : nullptr;
 #pragma unroll 1
-  for (int idx = tid; idx < total; idx += kCT) {
-    const int t = idx >> lg, ch = idx & (nch - 1);
-    const uint16_t* row = src + t * stride;
-    if (emb) {
-      int64_t id = m.tokens[t];
-      if (id < 0 || id >= m.vocab) id = 0;
-      row = static_cast<const uint16_t*>(m.embed) + id * H;
+    for (int idx = tid; idx < total; idx += kCT) {
+      const int t = idx >> lg, ch = idx & (nch - 1);
+      const uint4 v = residual_chunk(P, u, t, ch);
+      *reinterpret_cast<uint4*>(sx + t * P.xpitch + ch * 16) = v;
+      if (hout) *reinterpret_cast<uint4*>(hout + int64_t(t) * H + 8 * ch) = v;
     }
-    cp_async_16(sx + t * P.xpitch + ch * 16, row + 8 * ch, 16);
+    cbar();
+  } else {
+#pragma unroll 1
+    for (int idx = tid; idx < total; idx += kCT) {
+      const int t = idx >> lg, ch = idx & (nch - 1);
+      const uint16_t* row = src + t * stride;
+      if (emb) {
+        int64_t id = m.tokens[t];
+        if (id < 0 || id >= m.vocab) id = 0;
+        row = static_cast<const uint16_t*>(m.embed) + id * H;
+      }
+      cp_async_16(sx + t * P.xpitch + ch * 16, row + 8 * ch, 16);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    cbar();
   }
-  cp_async_commit();
-  cp_async_wait<0>();
-  cbar();
   if (norm) {
 #pragma unroll 1
     for (int t = 0; t < B; ++t) {
@@ -384,6 +466,11 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
       c = P.ctr + l * C_LAYER + C_GU, target = unsigned(P.nslab[G_GU]);
     }
     if (c != nullptr && !wait_counter(c, target, abort_word)) S.flag = 0;  // sticky: errors are never cleared
+    if (S.flag && P.tp_world > 1 && (g == G_GU || (g == G_QKV && l > 0))) {
+      const int lu = g == G_GU ? l : l - 1, su = g == G_GU ? 0 : 1;
+      const unsigned int xt = (S.ep + 1u) * unsigned(P.tp_world - 1) * unsigned(P.nslab[su ? G_DOWN : G_O]);
+      if (!wait_counter_sys(xctr(P, P.tp_rank, lu, su), xt, abort_word)) S.flag = 0;
+    }
   }
   cbar();
   if (!S.flag) return false;
@@ -398,7 +485,8 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
   const int B = m.batch;
   constexpr int kRes = kResPerThread;
   uint16_t res[kRes];
-  if (g == G_O || g == G_DOWN) {
+  const bool tp_out = P.tp_world > 1 && (g == G_O || g == G_DOWN);
+  if ((g == G_O || g == G_DOWN) && !tp_out) {
 #pragma unroll
     for (int k = 0; k < kRes; ++k) {
       const int idx = tid + k * kCT;
@@ -511,9 +599,16 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
       float sum = 0.0f;
       for (int j = 0; j < J; ++j) sum += part[(i * J + j) * (B * kSlabW) + b * kSlabW + col];
       const int64_t nn = int64_t(S.slab[ib + i]) * kSlabW + col;
-      if (g == G_QKV) P.qkv[int64_t(b) * P.qkv_n + nn] = uint16_t(bfr(sum));
-      else h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(sum))));
+      if (g == G_QKV) {
+        P.qkv[int64_t(b) * P.qkv_n + nn] = uint16_t(bfr(sum));
+      } else if (tp_out) {  // this rank's fp32 partial, into every rank's buffer
+        const int s2 = g == G_O ? 0 : 1;
+        for (int p = 0; p < P.tp_world; ++p) xdata(P, p, l, s2, P.tp_rank)[int64_t(b) * H + nn] = sum;
+      } else {
+        h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(sum))));
+      }
     }
+    if (tp_out) __threadfence_system();  // the pushes reach every rank before the counters below
   }
   cbar();
   stamp(P, l, st_id, 4);
@@ -522,6 +617,12 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
     // release: the CTA's output stores (ordered before by the barrier) are visible before the count
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.ctr + l * C_LAYER + st_id), "r"(unsigned(n))
                  : "memory");
+    if (tp_out)
+      for (int p = 0; p < P.tp_world; ++p)
+        if (p != P.tp_rank)
+          asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(xctr(P, p, l, g == G_O ? 0 : 1)),
+                       "r"(unsigned(n))
+                       : "memory");
   }
   stamp(P, l, st_id, 6);
   return true;
@@ -769,6 +870,32 @@ __device__ __noinline__ bool attention_item(int l, int a) {
   return true;
 }
 
+// Tensor parallelism, one CTA: h_out = the residual rows after the last update (layer L-1's down_proj
+// outputs of all ranks added), once every rank's partials have arrived.
+__device__ __noinline__ bool tp_finalize() {
+  const DkHot& P = dk_P;
+  Smem& S = dk_S;
+  const i4b_decode_model& m = P.m;
+  const int tid = threadIdx.x, L = m.layers, H = m.hidden;
+  const unsigned int* abort_word = P.ctr + P.i_abort;
+  if (tid == 0) {
+    const unsigned int xt = (S.ep + 1u) * unsigned(P.tp_world - 1) * unsigned(P.nslab[G_DOWN]);
+    if (!wait_counter(P.ctr + (L - 1) * C_LAYER + C_DOWN, unsigned(P.nslab[G_DOWN]), abort_word) ||
+        !wait_counter_sys(xctr(P, P.tp_rank, L - 1, 1), xt, abort_word))
+      S.flag = 0;
+  }
+  cbar();
+  if (!S.flag) return false;
+  uint16_t* out = static_cast<uint16_t*>(m.h_out);
+  const int nch = H / 8;
+#pragma unroll 1
+  for (int idx = tid; idx < m.batch * nch; idx += kCT) {
+    const int t = idx / nch, ch = idx - t * nch;
+    *reinterpret_cast<uint4*>(out + int64_t(t) * H + 8 * ch) = residual_chunk(P, 2 * L - 1, t, ch);
+  }
+  return true;
+}
+
 template <int SPS, int GS>
 __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid_constant__ DkParams Pg) {
   uint8_t* const smem = dk_smem;
@@ -795,6 +922,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     S.nit = nit;
     S.ppl = off;
     S.flag = 1;
+    S.ep = P.tp_world > 1 ? *reinterpret_cast<volatile unsigned int*>(P.xb[P.tp_rank]) : 0u;
     S.prod_seq = 0;
     for (int s = 0; s < P.nslot; ++s) {
       mbar_init(&S.full[s], 1);
@@ -851,6 +979,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
       ok = ok && gemv_stage<SPS>(G_GU, l);
       ok = ok && gemv_stage<SPS>(G_DOWN, l);
     }
+    if (ok && P.tp_world > 1 && blockIdx.x == 0) ok = tp_finalize();
     if (!ok && tid == 0) {
       atomicOr(&g_dk_err, I4B_DEVERR_WAIT_TIMEOUT);
       atomicExch(P.ctr + P.i_abort, 1u);
@@ -865,6 +994,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     __threadfence();
     if (atomicAdd(P.ctr + P.i_done, 1u) == gridDim.x - 1) {  // the last CTA out resets the workspace counters
       for (int i = 0; i < P.n_ctr; ++i) P.ctr[i] = 0u;
+      // and, under tensor parallelism, advances this rank's epoch for the next launch
+      if (P.tp_world > 1) *reinterpret_cast<volatile unsigned int*>(P.xb[P.tp_rank]) = S.ep + 1u;
       __threadfence();
     }
   }
@@ -966,7 +1097,7 @@ struct Layout {
   int64_t layer_bytes[4];
   int piece_bytes, gqa, nsplit, qkv_n, q_n;
   int n_ctr, i_ticket, i_done, i_abort;
-  size_t off_apart, off_qkv, off_att, off_act, total;
+  size_t off_apart, off_qkv, off_att, off_act, off_hbuf, total;
 };
 
 int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
@@ -980,8 +1111,8 @@ int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
   const int gqa = m.heads / m.kv_heads;
   if (gqa != 1 && gqa != 2 && gqa != 4 && gqa != 8) return I4B_ERR_SHAPE;
   const int q_n = m.heads * kHD, qkv_n = (m.heads + 2 * m.kv_heads) * kHD;
-  // every projection input width is a power-of-two number of 8-value chunks, at least 256
-  auto pow2_chunks = [](int k) { return k >= 2048 && k % 8 == 0 && ((k / 8) & (k / 8 - 1)) == 0; };
+  // every projection input width is a power-of-two number of 8-value chunks, at least one 512-k piece
+  auto pow2_chunks = [](int k) { return k >= kPieceK && k % 8 == 0 && ((k / 8) & (k / 8 - 1)) == 0; };
   if (!pow2_chunks(m.hidden) || !pow2_chunks(m.intermediate) || !pow2_chunks(q_n)) return I4B_ERR_SHAPE;
   L->gqa = gqa;
   L->q_n = q_n;
@@ -1013,6 +1144,8 @@ int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
   off = al(off + size_t(m.batch) * q_n * 2);
   L->off_act = off;
   off = al(off + size_t(m.batch) * m.intermediate * 2);
+  L->off_hbuf = off;  // tensor parallelism: the residual rows of two consecutive updates
+  off = al(off + size_t(2) * kMaxTok * m.hidden * 2);
   L->total = off;
   return I4B_OK;
 }
@@ -1046,6 +1179,12 @@ cudaError_t launch_dk_s(const DkParams& p, int grid, size_t smem, cudaStream_t s
 }
 
 }  // namespace
+
+int64_t decode_peer_capacity(int layers, int world, int hidden) {
+  // fp32 partials [layers][2][world][kMaxTok][hidden] in the 2 x kArMaxRanks x capacity data area
+  const int64_t floats = int64_t(layers) * 2 * world * kMaxTok * hidden;
+  return (floats + 2 * kArMaxRanks - 1) / (2 * kArMaxRanks);
+}
 
 size_t tile_w4_bytes(int64_t N, int64_t K, int G) {
   if (N <= 0 || K <= 0 || N % kSlabW || K % kPieceK || (G != 32 && G != 64 && G != 128)) return 0;
@@ -1121,6 +1260,31 @@ int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin,
   p.h.qkv = reinterpret_cast<uint16_t*>(w + L.off_qkv);
   p.h.att = reinterpret_cast<uint16_t*>(w + L.off_att);
   p.h.act = reinterpret_cast<uint16_t*>(w + L.off_act);
+  p.h.tp_world = 1;
+  if (m.peers && m.peers->world > 1) {
+    const i4b_peer_group& pg = *m.peers;
+    if (pg.world > kArMaxRanks || pg.rank < 0 || pg.rank >= pg.world) return I4B_ERR_INVALID_ARG;
+    if (pg.capacity < decode_peer_capacity(m.layers, pg.world, m.hidden)) return I4B_ERR_SHAPE;
+    for (int q = 0; q < pg.world; ++q) {
+      if (!pg.buffers[q] || reinterpret_cast<uintptr_t>(pg.buffers[q]) % 256 != 0) return I4B_ERR_INVALID_ARG;
+      p.h.xb[q] = static_cast<uint8_t*>(pg.buffers[q]);
+    }
+    p.h.tp_world = pg.world;
+    p.h.tp_rank = pg.rank;
+    p.h.hbuf[0] = reinterpret_cast<uint16_t*>(w + L.off_hbuf);
+    p.h.hbuf[1] = p.h.hbuf[0] + size_t(kMaxTok) * m.hidden;
+    // the residual rows of an update are stored by a CTA that runs the stage consuming them
+    for (int g = 0; g < 4; ++g) {
+      p.h.writer[g] = -1;
+      for (int c = 0; c < grid && p.h.writer[g] < 0; ++c)
+        for (int i = 0; i < sc->nitems[c]; ++i)
+          if ((sc->items[size_t(c) * kMaxItems + i] >> 14) == g) {
+            p.h.writer[g] = c;
+            break;
+          }
+    }
+    if (p.h.writer[G_QKV] < 0 || p.h.writer[G_GU] < 0) return I4B_ERR_SHAPE;
+  }
   if (g_dk_trace && g_dk_trace_bytes >= size_t(grid) * m.layers * 5 * kTraceSlots * 8) p.h.trace = g_dk_trace;
   for (int c = 0; c < grid; ++c) {
     p.nitems[c] = sc->nitems[c];

@@ -122,6 +122,7 @@ size_t tile_w4_bytes(int64_t N, int64_t K, int G);
 cudaError_t launch_tile_w4(const int32_t* qw, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg,
                            int64_t N, int64_t K, int G, void* out, cudaStream_t stream);
 int decode_layers_workspace(const i4b_decode_model& m, int num_sms, size_t* bytes);
+int64_t decode_peer_capacity(int layers, int world, int hidden);
 int launch_decode_layers(const i4b_decode_model& m, int num_sms, int smem_optin, void* ws, size_t ws_bytes,
                          cudaStream_t stream, cudaError_t* err);
 unsigned int read_dk_error(bool clear);

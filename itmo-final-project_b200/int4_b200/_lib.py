@@ -54,6 +54,7 @@ _SIGNATURES = {
     "i4b_decode_layers": (_c_int, [_c_vp, _c_vp, _c_size, _c_vp]),
     "i4b_set_decode_trace": (None, [_c_vp, _c_size]),
     "i4b_peer_buffer_bytes": (_c_size, [_c_i64]),
+    "i4b_decode_peer_capacity": (_c_i64, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "i4b_peer_buffer_alloc": (_c_int, [_c_i64, ctypes.POINTER(_c_vp)]),
     "i4b_peer_buffer_free": (_c_int, [_c_vp]),
     "i4b_ipc_get_handle": (_c_int, [_c_vp, _c_vp]),
@@ -72,7 +73,8 @@ class DecodeModel(ctypes.Structure):
                                               "vocab", "group_size", "batch", "max_seq", "cache_batch")] + \
                [("eps", ctypes.c_float), ("attn_scale", ctypes.c_float)] + \
                [(n, ctypes.c_void_p) for n in ("tokens", "pos", "embed", "w_qkv", "w_o", "w_gu", "w_down", "ln1",
-                                               "ln2", "cos_table", "sin_table", "k_cache", "v_cache", "h_out")]
+                                               "ln2", "cos_table", "sin_table", "k_cache", "v_cache", "h_out",
+                                               "peers")]
 
 
 class Int4B200Error(RuntimeError):

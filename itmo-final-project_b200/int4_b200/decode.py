@@ -203,7 +203,10 @@ class PersistentDecoder:
     """Every decoder layer of a single-token decode step in one launch (``i4b_decode_layers``).
 
     Holds the tiled weights of all layers (one buffer per projection kind), the stacked norm weights,
-    the residual-stream buffer and the workspace (zeroed once; every launch leaves it zero).
+    the residual-stream buffer and the workspace (zeroed once; every launch leaves it zero).  Under
+    tensor parallelism it also holds a peer group of its own: the o_proj / down_proj epilogues store
+    their partial outputs into every rank's exchange buffer, and the stages that consume the residual
+    stream add them up (collective set-up; ``close`` releases it).
     """
 
     def __init__(self, model: "LlamaTP", layer_q: list, group_size: int):
@@ -238,6 +241,12 @@ class PersistentDecoder:
         m.cos_table, m.sin_table = model.cos.data_ptr(), model.sin.data_ptr()
         m.k_cache, m.v_cache = model.k_cache.data_ptr(), model.v_cache.data_ptr()
         m.h_out = self.h.data_ptr()
+        self.peers = None
+        if model.world > 1:
+            from .peer import PeerGroup
+
+            self.peers = PeerGroup(model.group, capacity=L.i4b_decode_peer_capacity(Lc, model.world, H))
+            m.peers = ctypes.addressof(self.peers.struct)
         self.m = m
         nbytes = ctypes.c_size_t(0)
         _lib.check(L.i4b_decode_workspace_size(ctypes.byref(m), ctypes.byref(nbytes)), "decode_workspace_size")
@@ -298,6 +307,12 @@ class PersistentDecoder:
         out["layer_us"] = round(float(np.median(np.diff(g0))) / 1e3, 2) if len(g0) > 1 else None
         return out
 
+    def close(self) -> None:
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
+            self.m.peers = None
+
     def run(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """Residual stream [B, H] after the last layer for token ids[B, 1] at position pos (device int64)."""
         B = ids.shape[0]
@@ -324,8 +339,10 @@ class LlamaTP:
     ``fused`` runs a decode step's norms, rotary embedding, attention and SwiGLU
     as the library's fused kernels; ``fused=False`` runs them as the torch ops
     transformers uses.  ``persistent`` (default: whenever the model qualifies --
-    W4, one rank, fused, batch <= 8, widths multiples of 2048) runs all decoder
-    layers of a decode step as one launch of ``i4b_decode_layers``.
+    W4, fused, batch <= 8, hidden and per-rank widths of 512 * 2^k, and under
+    tensor parallelism the peer all-reduce) runs all decoder layers of a decode
+    step as one launch of ``i4b_decode_layers``; tensor-parallel ranks then add
+    each other's o / down partials inside that launch.
     ``peer_allreduce`` (tensor-parallel W4 decode steps of <= 32 tokens) sums
     the row-parallel o / down outputs inside those matmuls through peer
     exchange buffers (``i4b_w4a16_matmul_allreduce``) instead of NCCL.
@@ -400,12 +417,17 @@ class LlamaTP:
         self.v_cache = torch.zeros_like(self.k_cache)
         self.positions = torch.arange(max_seq, device=dev)
 
-        qualifies = (w4 and world == 1 and fused and hd == 64 and max_batch <= 8 and group_size in (32, 64, 128)
-                     and H % 2048 == 0 and self.inter_l % 2048 == 0 and (self.nh_l * hd) % 2048 == 0
+        def pow2_chunks(k: int) -> bool:  # a power-of-two number of 8-value chunks, at least one 512-k piece
+            return k >= 512 and k % 8 == 0 and (k // 8) & (k // 8 - 1) == 0
+
+        qualifies = (w4 and (world == 1 or peer_allreduce) and fused and hd == 64 and max_batch <= 8
+                     and group_size in (32, 64, 128) and world <= 8
+                     and pow2_chunks(H) and pow2_chunks(self.inter_l) and pow2_chunks(self.nh_l * hd)
                      and self.nh_l // self.nkv_l in (1, 2, 4, 8) and self.nh_l % self.nkv_l == 0)
         if persistent and not qualifies:
-            raise ValueError("persistent decode needs W4 (G 32/64/128), one rank, fused kernels, head_dim 64, "
-                             "batch <= 8 and hidden / intermediate / q widths that are multiples of 2048")
+            raise ValueError("persistent decode needs W4 (G 32/64/128), fused kernels, head_dim 64, batch <= 8, "
+                             "hidden and per-rank intermediate / q widths of 512 * 2^k, and under tensor "
+                             "parallelism the peer all-reduce")
         self.persistent = None
         if qualifies and persistent is not False:
             self.persistent = PersistentDecoder(
@@ -420,6 +442,8 @@ class LlamaTP:
 
     def close(self) -> None:
         """Release the peer exchange buffers (collective when tensor-parallel)."""
+        if self.persistent is not None:
+            self.persistent.close()
         if self.peers is not None:
             self.peers.close()
             self.peers = None

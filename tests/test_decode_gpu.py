@@ -37,12 +37,12 @@ def tiny_config():
                                      "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
 
 
-def build_hf(seed: int = 0):
+def build_hf(seed: int = 0, config=None):
     from transformers import LlamaForCausalLM
 
     torch.manual_seed(seed)
     with torch.device("cuda"):
-        model = LlamaForCausalLM(tiny_config())
+        model = LlamaForCausalLM(config if config is not None else tiny_config())
     return model.to(torch.bfloat16).eval()
 
 

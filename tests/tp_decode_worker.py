@@ -1,14 +1,16 @@
 """One rank of the two-GPU tensor-parallel decode check (launched by tests/test_decode_gpu.py via torchrun).
 
-Every rank builds the same seeded tiny Llama, runs its ``LlamaTP`` shard for a
+Every rank builds the same seeded Llama, runs its ``LlamaTP`` shard for a
 prompt and three cached decode steps, and compares with a one-rank ``LlamaTP``
 of the same weights.  The row-parallel o/down outputs of the decode steps are
 summed inside the W4 matmuls through peer exchange buffers
-(``w4a16_matmul_allreduce``), or by an NCCL all-reduce (``peer_allreduce=False``);
-the prompt always uses NCCL; the vocab-parallel logits are all-gathered.  With
-the fused sum, three more steps replayed from one CUDA graph must equal the
-eager steps bit for bit.  Exit status 0 only if every rank stays within 2e-2
-max-abs and no kernel's bounded wait expired.
+(``w4a16_matmul_allreduce``), by an NCCL all-reduce (``peer_allreduce=False``),
+or -- for the wider model, whose shards qualify -- inside the persistent decode
+launch, which exchanges the partials itself; the prompt always uses NCCL; the
+vocab-parallel logits are all-gathered.  With the fused sums, three more steps
+replayed from one CUDA graph must equal the eager steps bit for bit.  Exit
+status 0 only if every rank stays within 2e-2 max-abs and no kernel's bounded
+wait expired.
 """
 from __future__ import annotations
 
@@ -33,19 +35,32 @@ def main() -> int:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     from int4_b200.decode import LlamaTP
-    from test_decode_gpu import build_hf
+    from test_decode_gpu import build_hf, tiny_config
+
+    def mid_config():
+        """Widths at which the tensor-parallel shards still run the persistent decode (per-rank q width and
+        intermediate of at least 512 at two ranks)."""
+        c = tiny_config()
+        c.hidden_size, c.intermediate_size, c.num_hidden_layers = 1024, 2048, 3
+        c.num_attention_heads, c.num_key_value_heads = 16, 4
+        return c
 
     from int4_b200 import _lib
 
     worst, graph_diff = 0.0, 0.0
     with torch.no_grad():
-        hf = build_hf(0)
+        hf_tiny = build_hf(0)
+        hf_mid = build_hf(0, mid_config())
         g = torch.Generator().manual_seed(3)
         ids = torch.randint(0, 512, (1, 24), generator=g).to(dev)
-        for lm_w4, peer in ((False, True), (True, True), (False, False)):
+        # (model, quantized lm_head, peer all-reduce, persistent decode expected)
+        runs = ((hf_tiny, False, True, False), (hf_tiny, True, True, False), (hf_tiny, False, False, False),
+                (hf_mid, False, True, True))
+        for hf, lm_w4, peer, persistent in runs:
             tp = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=rank, world=world, max_seq=64, device=dev,
                          peer_allreduce=peer)
             assert (tp.peers is not None) == peer
+            assert (tp.persistent is not None) == persistent
             one = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev)
             a, b = tp.prefill(ids, all_logits=True), one.prefill(ids, all_logits=True)
             worst = max(worst, (a.float() - b.float()).abs().max().item())
