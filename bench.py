@@ -448,7 +448,7 @@ def run_model(args, world, rank, local):
     B, prompt, steps = args.m, args.prompt, args.steps
     hf = build_llama(dev)
     res = {}
-    for label, w4 in (("w4", True), ("bf16", False)):
+    for label, w4 in (("w4", True), ("bf16", False))[:2 if args.compare_bf16 else 1]:
         persistent = None if args.persistent < 0 else bool(args.persistent) and w4
         m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world, persistent=persistent,
                     peer_allreduce=bool(args.peer_allreduce),
@@ -518,7 +518,7 @@ def main_model(args, world, rank, local, threads):
     if rank != 0:
         return
     pk = peaks()
-    w4, bf = res["w4"], res["bf16"]
+    w4, bf = res["w4"], res.get("bf16")
     if "trace" in w4:
         print(json.dumps({"persistent_decode_trace": w4["trace"]}), file=sys.stderr, flush=True)
     tps = args.m * args.steps / w4["decode_s"]
@@ -536,9 +536,9 @@ def main_model(args, world, rank, local, threads):
                        if w4["persistent"] else "one launch per projection / glue op",
                        tp_sum="none" if world == 1 else ("inside the o/down matmuls (peer buffers)"
                                                          if w4["peer_allreduce"] else "NCCL all-reduce")),
-        "bf16_tokens_per_s": args.m * args.steps / bf["decode_s"],
-        "w4_over_bf16": bf["decode_s"] / w4["decode_s"],
-        "prefill_ms": {"w4": w4["prefill_ms"], "bf16": bf["prefill_ms"]},
+        "bf16_tokens_per_s": args.m * args.steps / bf["decode_s"] if bf else None,
+        "w4_over_bf16": bf["decode_s"] / w4["decode_s"] if bf else None,
+        "prefill_ms": {"w4": w4["prefill_ms"], "bf16": bf["prefill_ms"] if bf else None},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "traffic": None,
                      "kernel": "whole decode step (projection weights + KV cache bytes / step time)",
@@ -569,6 +569,8 @@ def main():
     ap.add_argument("--persistent", type=int, default=-1,
                     help="model workload: 1 = all decoder layers of a step in one launch (i4b_decode_layers), "
                          "0 = one launch per projection / glue op, -1 = whichever the model qualifies for")
+    ap.add_argument("--compare-bf16", type=int, default=1,
+                    help="model workload: also time the same decode loop with bf16 projections")
     ap.add_argument("--peer-allreduce", type=int, default=1,
                     help="tensor-parallel runs: sum the row-parallel outputs inside the W4 matmuls through peer "
                          "exchange buffers (1) or with an NCCL all-reduce after them (0)")
