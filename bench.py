@@ -384,8 +384,7 @@ def time_decode(m, B: int, prompt: int, steps: int, warmup: int, world: int, dev
     pos = torch.tensor([prompt], device=dev)
 
     def step():
-        out = m.decode_step(tok, pos)
-        tok.copy_(argmax_last(out[:, -1]))
+        tok.copy_(m.decode_greedy(tok, pos))
         pos.add_(1)
 
     side = torch.cuda.Stream(dev)

@@ -204,6 +204,16 @@ int i4b_w4a16_matmul_allreduce(const i4b_peer_group* group, int prologue, const 
                                const uint16_t* scales, const uint16_t* zeros, int64_t stride_sg, int group_size,
                                void* y, int64_t stride_ym, void* stream);
 
+/* Greedy next token of rows whose vocabulary is split over the ranks of a peer group (vocab-parallel
+ * lm_head): out[r] = index of the first maximum of the concatenated row, where this rank holds bf16 columns
+ * [offset, offset + n) at x + r * stride_x.  Each rank finds its own first maximum; the candidates are
+ * exchanged through the exchange buffers (two fp32 words per row) and compared in rank order, so every rank
+ * gets torch.argmax of the full row without gathering the logits.  rows <= SMs and 2 * rows <= capacity.
+ * Replaces, under tensor parallelism, the all-gather of the logits and the argmax of the reference's greedy
+ * decode loop (benchmarks/eval_llama.py:121-183, logits[:, -1].argmax(-1)); same group rules as above. */
+int i4b_argmax_allreduce(const i4b_peer_group* group, const void* x, int64_t rows, int64_t n, int64_t stride_x,
+                         int64_t offset, int64_t* out, void* stream);
+
 /* ---- Decode-step glue of a Llama layer (bf16, head_dim 64), for the model-level caller of the
  * matmuls.  No counterpart in the reference, which runs these steps as transformers' torch ops
  * (benchmarks/eval_llama.py:121-183); each reproduces transformers' bf16 rounding points.

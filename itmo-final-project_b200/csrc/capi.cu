@@ -306,6 +306,30 @@ int i4b_w4a16_matmul_allreduce(const i4b_peer_group* group, int prologue, const 
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
+int i4b_argmax_allreduce(const i4b_peer_group* group, const void* x, int64_t rows, int64_t n, int64_t stride_x,
+                         int64_t offset, int64_t* out, void* stream) {
+  if (!group || group->world < 1 || group->world > I4B_PEER_MAX_RANKS || group->rank < 0 ||
+      group->rank >= group->world)
+    return I4B_ERR_INVALID_ARG;
+  if (rows < 0 || n <= 0 || stride_x < n || offset < 0 || offset + n > INT32_MAX) return I4B_ERR_SHAPE;
+  if (rows == 0) return I4B_OK;
+  if (!x || !out) return I4B_ERR_INVALID_ARG;
+  if (2 * rows > group->capacity || rows > kArMaxCtas) return I4B_ERR_SHAPE;
+  for (int q = 0; q < group->world; ++q)
+    if (!group->buffers[q] || reinterpret_cast<uintptr_t>(group->buffers[q]) % 256 != 0) return I4B_ERR_INVALID_ARG;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  if (rows > d.sms) return I4B_ERR_SHAPE;  // every CTA waits for another GPU: all must be resident
+  W4AllReduce ar{};
+  for (int q = 0; q < group->world; ++q) ar.buffers[q] = group->buffers[q];
+  ar.capacity = group->capacity;
+  ar.world = group->world;
+  ar.rank = group->rank;
+  const cudaError_t e = launch_argmax_allreduce(static_cast<const uint16_t*>(x), rows, n, stride_x, offset, out, ar,
+                                                static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
 size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   DevInfo d;

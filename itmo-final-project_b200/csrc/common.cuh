@@ -405,4 +405,77 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t p, const DqParams& dp) {
   return w;
 }
 
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+// First maximum of the bf16 row xr[0, n) over the CTA (blockDim.x a multiple of 32, <= 1024): on thread 0,
+// *best_out = the maximum and *idx_out = its first index (n when no element compares above -inf, e.g. all
+// NaN).  kU 16-byte chunks per thread are in flight before any is compared; each thread visits its chunks in
+// increasing index order and ties go to the lower index at every step.
+__device__ __forceinline__ void block_row_argmax(const uint16_t* __restrict__ xr, int64_t n, float* best_out,
+                                                 int64_t* idx_out) {
+  __shared__ float vmax[32];
+  __shared__ int64_t vidx[32];
+  float best = -INFINITY;
+  int64_t bi = n;
+  const bool vec = (reinterpret_cast<uintptr_t>(xr) % 16 == 0);
+  const int64_t n8 = vec ? n / 8 * 8 : 0;
+  const int64_t nch = n8 / 8;  // 16-byte chunks
+  // kU chunks per thread in flight before any is compared (one memory round trip per kU chunks, not per
+  // chunk); a thread visits its chunks in increasing index order
+  constexpr int kU = 8;
+  for (int64_t base = 0; base < nch; base += int64_t(blockDim.x) * kU) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t ch = base + int64_t(u) * blockDim.x + threadIdx.x;
+      v[u] = ch < nch ? __ldg(reinterpret_cast<const uint4*>(xr) + ch) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t ch = base + int64_t(u) * blockDim.x + threadIdx.x;
+      if (ch >= nch) break;
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = bf16_bits_to_f32(uint16_t(w[e >> 1] >> (16 * (e & 1))));
+        if (f > best) {  // strictly greater: the first index wins within a thread
+          best = f;
+          bi = ch * 8 + e;
+        }
+      }
+    }
+  }
+  for (int64_t c = n8 + threadIdx.x; c < n; c += blockDim.x) {
+    const float f = bf16_bits_to_f32(xr[c]);
+    if (f > best) {
+      best = f;
+      bi = c;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    vmax[warp] = best;
+    vidx[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < int(blockDim.x >> 5); ++w)
+      if (vmax[w] > best || (vmax[w] == best && vidx[w] < bi)) {
+        best = vmax[w];
+        bi = vidx[w];
+      }
+    *best_out = best;
+    *idx_out = bi;
+  }
+}
+
 }  // namespace i4b

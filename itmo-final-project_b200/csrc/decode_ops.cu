@@ -270,70 +270,11 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const uint16_
 
 // Row-wise argmax of bf16 values (first index of the maximum, as torch.argmax): one CTA per row.
 __global__ void __launch_bounds__(1024) argmax_kernel(const uint16_t* __restrict__ x, int64_t n, int64_t* __restrict__ out) {
-  __shared__ float vmax[32];
-  __shared__ int64_t vidx[32];
   const int64_t row = blockIdx.x;
-  const uint16_t* xr = x + row * n;
-  float best = -INFINITY;
-  int64_t bi = n;
-  const bool vec = (reinterpret_cast<uintptr_t>(xr) % 16 == 0);
-  const int64_t n8 = vec ? n / 8 * 8 : 0;
-  const int64_t nch = n8 / 8;  // 16-byte chunks
-  // kU chunks per thread in flight before any is compared (one memory round trip per kU chunks, not per
-  // chunk); a thread visits its chunks in increasing index order
-  constexpr int kU = 8;
-  for (int64_t base = 0; base < nch; base += int64_t(blockDim.x) * kU) {
-    uint4 v[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int64_t ch = base + int64_t(u) * blockDim.x + threadIdx.x;
-      v[u] = ch < nch ? __ldg(reinterpret_cast<const uint4*>(xr) + ch) : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int64_t ch = base + int64_t(u) * blockDim.x + threadIdx.x;
-      if (ch >= nch) break;
-      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float f = bf(uint16_t(w[e >> 1] >> (16 * (e & 1))));
-        if (f > best) {  // strictly greater: the first index wins within a thread
-          best = f;
-          bi = ch * 8 + e;
-        }
-      }
-    }
-  }
-  for (int64_t c = n8 + threadIdx.x; c < n; c += blockDim.x) {
-    const float f = bf(xr[c]);
-    if (f > best) {
-      best = f;
-      bi = c;
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-    const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-    if (ob > best || (ob == best && oi < bi)) {
-      best = ob;
-      bi = oi;
-    }
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    vmax[warp] = best;
-    vidx[warp] = bi;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < int(blockDim.x >> 5); ++w)
-      if (vmax[w] > best || (vmax[w] == best && vidx[w] < bi)) {
-        best = vmax[w];
-        bi = vidx[w];
-      }
-    out[row] = bi < n ? bi : 0;
-  }
+  float best;
+  int64_t bi;
+  block_row_argmax(x + row * n, n, &best, &bi);
+  if (threadIdx.x == 0) out[row] = bi < n ? bi : 0;
 }
 
 __global__ void silu_mul_kernel(const uint16_t* __restrict__ gu, uint16_t* __restrict__ y, int B, int I) {

@@ -79,7 +79,8 @@ enum { kProPlain = 0, kProRmsNorm = 1, kProSwiGlu = 2 };
 
 __device__ unsigned int g_w4_err = 0;
 
-// ---- fused all-reduce over peer exchange buffers (layout in kernels.h)
+// ---- fused all-reduce over peer exchange buffers (layout in kernels.h).  The helpers take any argument
+// struct with the fields ar_buf, ar_cap, ar_world and ar_rank.
 
 __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -90,25 +91,30 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
   return v;
 }
 // fp32 outputs of source rank `src` in rank p's buffer
-__device__ __forceinline__ float* ar_data(const W4SArgs& a, int p, uint32_t slot, int src) {
+template <class A>
+__device__ __forceinline__ float* ar_data(const A& a, int p, uint32_t slot, int src) {
   return reinterpret_cast<float*>(a.ar_buf[p] + kArDataOff) + (int64_t(slot) * kArMaxRanks + src) * a.ar_cap;
 }
-__device__ __forceinline__ unsigned int* ar_flag(const W4SArgs& a, int p, uint32_t slot, int src, int cta) {
+template <class A>
+__device__ __forceinline__ unsigned int* ar_flag(const A& a, int p, uint32_t slot, int src, int cta) {
   return reinterpret_cast<unsigned int*>(a.ar_buf[p] + kArCtlBytes) + (int(slot) * kArMaxRanks + src) * kArMaxCtas +
          cta;
 }
 // The call's epoch, read once per CTA (after the previous kernel of the stream has completed).
-__device__ __forceinline__ uint32_t ar_epoch(const W4SArgs& a, uint32_t* s_ep) {
+template <class A>
+__device__ __forceinline__ uint32_t ar_epoch(const A& a, uint32_t* s_ep) {
   if (threadIdx.x == 0) *s_ep = *reinterpret_cast<volatile unsigned int*>(a.ar_buf[a.ar_rank]);
   __syncthreads();
   return *s_ep;
 }
 // Push one output (offset tok * N + n) to every rank's buffer, slot of this epoch, region of this rank.
-__device__ __forceinline__ void ar_push(const W4SArgs& a, uint32_t slot, int64_t off, float v) {
+template <class A>
+__device__ __forceinline__ void ar_push(const A& a, uint32_t slot, int64_t off, float v) {
   for (int p = 0; p < a.ar_world; ++p) ar_data(a, p, slot, a.ar_rank)[off] = v;
 }
 // Sum over source ranks, in rank order, of one output in this rank's buffer.
-__device__ __forceinline__ float ar_sum(const W4SArgs& a, uint32_t slot, int64_t off) {
+template <class A>
+__device__ __forceinline__ float ar_sum(const A& a, uint32_t slot, int64_t off) {
   float t[kArMaxRanks];
 #pragma unroll
   for (int q = 0; q < kArMaxRanks; ++q) t[q] = q < a.ar_world ? __ldcg(ar_data(a, a.ar_rank, slot, q) + off) : 0.0f;
@@ -121,7 +127,8 @@ __device__ __forceinline__ float ar_sum(const W4SArgs& a, uint32_t slot, int64_t
 // After every thread of the CTA has pushed: raise this CTA's flag in every other rank's buffer, then wait
 // (bounded) for the same CTA of every other rank.  A wait that gives up sets I4B_DEVERR_PEER_TIMEOUT; once
 // set, later waits on this device return at once.
-__device__ __forceinline__ void ar_publish_wait(const W4SArgs& a, uint32_t ep, int cta) {
+template <class A>
+__device__ __forceinline__ void ar_publish_wait(const A& a, uint32_t ep, int cta) {
   __threadfence_system();  // this thread's pushes reach every rank before the flags below
   __syncthreads();
   const uint32_t slot = ep & 1u;
@@ -148,7 +155,8 @@ __device__ __forceinline__ void ar_publish_wait(const W4SArgs& a, uint32_t ep, i
   __syncthreads();
 }
 // The last CTA of the call advances this rank's epoch (read by the next call on the group).
-__device__ __forceinline__ void ar_finish(const W4SArgs& a, uint32_t ep) {
+template <class A>
+__device__ __forceinline__ void ar_finish(const A& a, uint32_t ep) {
   if (threadIdx.x == 0) {
     unsigned int* ctl = reinterpret_cast<unsigned int*>(a.ar_buf[a.ar_rank]);
     const unsigned int prev = atomicAdd(ctl + 1, 1u);
@@ -1066,6 +1074,68 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
     case 2: return f16 ? launch_w4_sps<2, true>(a, p, smem, stream) : launch_w4_sps<2, false>(a, p, smem, stream);
     default: return f16 ? launch_w4_sps<4, true>(a, p, smem, stream) : launch_w4_sps<4, false>(a, p, smem, stream);
   }
+}
+
+// ------------------------------------------------------------------ greedy token over tensor-parallel ranks
+
+namespace {
+struct ArgmaxArArgs {
+  const uint16_t* x;  // [rows] rows of this rank's logits, bf16, n columns, row stride sx
+  int64_t sx, n, offset;
+  int64_t* out;       // [rows] global index of the first maximum over all ranks
+  uint8_t* ar_buf[kArMaxRanks];
+  int64_t ar_cap;
+  int ar_world, ar_rank;
+};
+
+// One CTA per row: this rank's first maximum (value, global index), exchanged through the peer buffers as
+// two fp32 words; the ranks' candidates are compared in rank order with a strict '>', so equal maxima go
+// to the lower rank, whose columns come first: the result is torch.argmax over the concatenated row.
+__global__ void __launch_bounds__(1024) argmax_allreduce_kernel(const ArgmaxArArgs a) {
+  __shared__ uint32_t s_ep;
+  const int row = blockIdx.x;
+  float best;
+  int64_t bi;
+  block_row_argmax(a.x + int64_t(row) * a.sx, a.n, &best, &bi);
+  const uint32_t ep = ar_epoch(a, &s_ep);
+  const uint32_t slot = ep & 1u;
+  if (threadIdx.x == 0) {
+    const int gi = bi < a.n ? int(a.offset + bi) : -1;  // -1: nothing above -inf on this rank
+    ar_push(a, slot, 2 * int64_t(row), best);
+    ar_push(a, slot, 2 * int64_t(row) + 1, __int_as_float(gi));
+  }
+  ar_publish_wait(a, ep, row);
+  if (threadIdx.x == 0) {
+    float bv = 0.0f;
+    int gi = -1;
+    for (int q = 0; q < a.ar_world; ++q) {
+      const float v = __ldcg(ar_data(a, a.ar_rank, slot, q) + 2 * row);
+      const int i = __float_as_int(__ldcg(ar_data(a, a.ar_rank, slot, q) + 2 * row + 1));
+      if (i >= 0 && (gi < 0 || v > bv)) {
+        bv = v;
+        gi = i;
+      }
+    }
+    a.out[row] = gi < 0 ? 0 : gi;
+  }
+  ar_finish(a, ep);
+}
+}  // namespace
+
+cudaError_t launch_argmax_allreduce(const uint16_t* x, int64_t rows, int64_t n, int64_t sx, int64_t offset,
+                                    int64_t* out, const W4AllReduce& ar, cudaStream_t stream) {
+  ArgmaxArArgs a{};
+  a.x = x;
+  a.sx = sx;
+  a.n = n;
+  a.offset = offset;
+  a.out = out;
+  for (int q = 0; q < kArMaxRanks; ++q) a.ar_buf[q] = static_cast<uint8_t*>(ar.buffers[q]);
+  a.ar_cap = ar.capacity;
+  a.ar_world = ar.world;
+  a.ar_rank = ar.rank;
+  argmax_allreduce_kernel<<<unsigned(rows), 1024, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 unsigned int read_w4_error(bool clear) {

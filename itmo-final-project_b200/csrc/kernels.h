@@ -80,6 +80,9 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
                       const W4Prologue* pro = nullptr, const W4AllReduce* ar = nullptr);
 void set_w4_split_override(int splits);
 unsigned int read_w4_error(bool clear);
+// Greedy token of rows split over the ranks of a peer group (columns [offset, offset + n) on this rank).
+cudaError_t launch_argmax_allreduce(const uint16_t* x, int64_t rows, int64_t n, int64_t sx, int64_t offset,
+                                    int64_t* out, const W4AllReduce& ar, cudaStream_t stream);
 // capi.cu: records e for i4b_last_cuda_error and returns I4B_ERR_CUDA
 int cuda_error_status(cudaError_t e);
 

@@ -54,6 +54,7 @@ _SIGNATURES = {
     "i4b_decode_layers": (_c_int, [_c_vp, _c_vp, _c_size, _c_vp]),
     "i4b_set_decode_trace": (None, [_c_vp, _c_size]),
     "i4b_peer_buffer_bytes": (_c_size, [_c_i64]),
+    "i4b_argmax_allreduce": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp]),
     "i4b_decode_peer_capacity": (_c_i64, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "i4b_peer_buffer_alloc": (_c_int, [_c_i64, ctypes.POINTER(_c_vp)]),
     "i4b_peer_buffer_free": (_c_int, [_c_vp]),

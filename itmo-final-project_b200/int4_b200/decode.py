@@ -34,7 +34,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .gemm import w4a16_matmul
-from .peer import w4a16_matmul_allreduce
+from .peer import argmax_allreduce, w4a16_matmul_allreduce
 from .quantize import quantize_int4
 
 
@@ -514,22 +514,37 @@ class LlamaTP:
     @torch.no_grad()
     def decode_step(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """One token per sequence: ids[B, 1] at position ``pos`` (a one-element int64 device tensor); logits [B, 1, V]."""
-        if self.persistent is not None and ids.shape[0] <= self.max_batch:
-            B = ids.shape[0]
+        B = ids.shape[0]
+        return self._gather_vocab(self._decode_local(ids, pos)).view(B, 1, -1)
+
+    @torch.no_grad()
+    def decode_greedy(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """``decode_step`` followed by the greedy choice: next token ids [B, 1] (first maximum of the logits,
+        as ``logits[:, -1].argmax(-1)`` in the reference's decode loop).  Under tensor parallelism with the peer
+        all-reduce, each rank picks the first maximum of its vocabulary shard and the ranks exchange those
+        candidates (``argmax_allreduce``) instead of all-gathering the logits."""
+        local = self._decode_local(ids, pos)
+        if self.world > 1 and self.peers is not None:
+            return argmax_allreduce(self.peers, local, self.rank * local.shape[-1])
+        return argmax_last(self._gather_vocab(local))
+
+    def _decode_local(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """This rank's logits [B, V / world] of one decode step."""
+        B = ids.shape[0]
+        if self.persistent is not None and B <= self.max_batch:
             h = self.persistent.run(ids, pos)
             x = torch.empty_like(h)
             add_rmsnorm(h, None, self.norm, x, self.eps)
-            return self._gather_vocab(self.lm_head(x)).view(B, 1, -1)
+            return self.lm_head(x)
         if self.fused:
             return self._decode_step_fused(ids, pos)
-        B = ids.shape[0]
         h = F.embedding(ids, self.embed)
         cos = self.cos.index_select(0, pos)
         sin = self.sin.index_select(0, pos)
         mask = (self.positions <= pos)[None, None, None, :]
         for i in range(len(self.layers)):
             h = self._layer(i, h, cos, sin, pos, mask)
-        return self._head(h)
+        return self.lm_head(rms_norm(h, self.norm, self.eps)).view(B, -1)
 
     def _decode_step_fused(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         B = ids.shape[0]
@@ -574,4 +589,4 @@ class LlamaTP:
                 silu_mul(L["gu"](x), act)
                 delta = self._all_reduce(L["down"](act))
         add_rmsnorm(cur, delta, self.norm, x, self.eps)
-        return self._gather_vocab(self.lm_head(x)).view(B, 1, -1)
+        return self.lm_head(x)

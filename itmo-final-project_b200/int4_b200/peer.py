@@ -118,3 +118,18 @@ def w4a16_matmul_allreduce(peers: PeerGroup, x: torch.Tensor, qweight: torch.Ten
         _lib.stream_handle(x.device))
     _lib.check(st, "w4a16_matmul_allreduce")
     return y
+
+
+def argmax_allreduce(peers: PeerGroup, x: torch.Tensor, offset: int) -> torch.Tensor:
+    """Greedy token of rows split over the ranks: x [rows, n] holds columns [offset, offset + n) of each row.
+
+    Returns int64 [rows, 1], the first index of the maximum of the whole row (torch.argmax), the same on every
+    rank, without gathering the rows.
+    """
+    assert x.is_cuda and x.dim() == 2 and x.dtype == torch.bfloat16 and x.stride(-1) == 1
+    rows, n = x.shape
+    out = torch.empty((rows, 1), dtype=torch.int64, device=x.device)
+    st = peers._lib.i4b_argmax_allreduce(ctypes.byref(peers.struct), x.data_ptr(), rows, n, x.stride(0), offset,
+                                         out.data_ptr(), _lib.stream_handle(x.device))
+    _lib.check(st, "argmax_allreduce")
+    return out

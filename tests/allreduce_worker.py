@@ -13,7 +13,9 @@ of x must then give, on every rank:
 * the same bits when replayed from a CUDA graph.
 
 The SwiGLU prologue (down_proj of a Llama MLP, gate | up sliced per rank) is
-checked the same way against torch's ``silu(g) * u``.  Exit status 0 only if
+checked the same way against torch's ``silu(g) * u``; ``argmax_allreduce`` of
+rows split over the ranks against torch.argmax of the whole row (ties across
+and within ranks, an all -inf row).  Exit status 0 only if
 every check holds on every rank and no bounded wait expired.
 """
 from __future__ import annotations
@@ -121,6 +123,23 @@ def main() -> int:
                 failures.append("graph replay differs from the eager call")
                 break
         del graph
+        # greedy token of rows split over the ranks (vocab-parallel lm_head), against torch.argmax of the row
+        from int4_b200.peer import argmax_allreduce
+
+        V = 1000 * world + 8 * world  # each rank holds V / world columns
+        vl = V // world
+        full = cases.activations(6, V, "bfloat16", seed=21).to(dev)
+        full[1, :] = float("-inf")                        # nothing above -inf: index 0, as torch.argmax
+        full[2, 5] = full[2, vl + 7] = 30.0               # equal maxima on two ranks: the lower index
+        full[3, vl * (world - 1) + 3] = 40.0              # the maximum on the last rank
+        full[4, 10] = full[4, 11] = 50.0                  # equal maxima inside one rank
+        full[5, V - 1] = 60.0                             # the last column
+        ref = full.float().argmax(-1, keepdim=True)
+        for _ in range(2):
+            got = argmax_allreduce(peers, full[:, rank * vl:(rank + 1) * vl].contiguous(), rank * vl)
+            if not torch.equal(got, ref):
+                failures.append(f"argmax_allreduce {got.view(-1).tolist()} != {ref.view(-1).tolist()}")
+                break
     flags = _lib.device_error_flags(local)
     if flags:
         failures.append(f"device error flags {flags}")

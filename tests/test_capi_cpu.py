@@ -94,3 +94,18 @@ def test_fused_allreduce_validation_before_any_device_call(L):
     assert L.i4b_peer_buffer_bytes(0) == 256 + 2 * 8 * 1024 * 4
     assert L.i4b_peer_buffer_bytes(1000) == 256 + 2 * 8 * 1024 * 4 + 2 * 8 * 1000 * 4
     assert L.i4b_ipc_get_handle(None, None) == 1 and L.i4b_ipc_open_handle(None, None) == 1
+
+
+def test_argmax_allreduce_validation_before_any_device_call(L):
+    import ctypes
+
+    from int4_b200.peer import MAX_RANKS, PeerGroupStruct
+
+    bufs = [0x100000, 0x200000]
+    grp = PeerGroupStruct(2, 1, 16, (ctypes.c_void_p * MAX_RANKS)(*(bufs + [None] * (MAX_RANKS - 2))))
+    call = L.i4b_argmax_allreduce
+    assert call(None, 0x1000, 4, 100, 100, 0, 0x2000, None) == 1             # no group
+    assert call(ctypes.byref(grp), 0x1000, 4, 100, 99, 0, 0x2000, None) == 2  # row stride below n
+    assert call(ctypes.byref(grp), 0x1000, 9, 100, 100, 0, 0x2000, None) == 2  # 2 * rows beyond capacity
+    assert call(ctypes.byref(grp), None, 4, 100, 100, 0, 0x2000, None) == 1
+    assert call(ctypes.byref(grp), 0x1000, 0, 100, 100, 0, 0x2000, None) == 0   # no rows: no-op

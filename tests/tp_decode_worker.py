@@ -7,7 +7,8 @@ summed inside the W4 matmuls through peer exchange buffers
 (``w4a16_matmul_allreduce``), by an NCCL all-reduce (``peer_allreduce=False``),
 or -- for the wider model, whose shards qualify -- inside the persistent decode
 launch, which exchanges the partials itself; the prompt always uses NCCL; the
-vocab-parallel logits are all-gathered.  With the fused sums, three more steps
+vocab-parallel logits are all-gathered, and the greedy token computed without
+that all-gather (``decode_greedy``) must be their first maximum.  With the fused sums, three more steps
 replayed from one CUDA graph must equal the eager steps bit for bit.  Exit
 status 0 only if every rank stays within 2e-2 max-abs and no kernel's bounded
 wait expired.
@@ -47,7 +48,7 @@ def main() -> int:
 
     from int4_b200 import _lib
 
-    worst, graph_diff = 0.0, 0.0
+    worst, graph_diff, greedy_bad = 0.0, 0.0, 0
     with torch.no_grad():
         hf_tiny = build_hf(0)
         hf_mid = build_hf(0, mid_config())
@@ -71,6 +72,11 @@ def main() -> int:
                 a, b = tp.decode_step(tok, pos), one.decode_step(tok, pos)
                 worst = max(worst, (a.float() - b.float()).abs().max().item())
                 eager.append(a.clone())
+                # the same step again (same position, same cache writes), choosing the token without the
+                # logits all-gather: the first maximum of the gathered logits
+                greedy = tp.decode_greedy(tok, pos)
+                if not torch.equal(greedy, a[:, -1].float().argmax(-1, keepdim=True)):
+                    greedy_bad += 1
                 tok = b[:, -1].argmax(-1, keepdim=True)
             if peer:
                 # the same three steps replayed from one captured step: identical logits
@@ -93,14 +99,14 @@ def main() -> int:
                 del graph
             tp.close()
     flags = _lib.device_error_flags(local)
-    t = torch.tensor([worst, graph_diff, float(flags != 0)], device=dev)
+    t = torch.tensor([worst, graph_diff, float(flags != 0), float(greedy_bad)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     torch.cuda.synchronize()
     dist.destroy_process_group()
     if rank == 0:
         print(f"max |logits(tp{world}) - logits(tp1)| = {t[0].item():.3e}, graph vs eager {t[1].item():.3e}, "
-              f"device error flags {'set' if t[2].item() else 'clear'}")
-    return 0 if t[0].item() <= 2e-2 and t[1].item() == 0.0 and t[2].item() == 0.0 else 1
+              f"device error flags {'set' if t[2].item() else 'clear'}, greedy mismatches {int(t[3].item())}")
+    return 0 if t[0].item() <= 2e-2 and t[1].item() == 0.0 and t[2].item() == 0.0 and t[3].item() == 0 else 1
 
 
 if __name__ == "__main__":
