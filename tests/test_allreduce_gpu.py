@@ -114,3 +114,27 @@ def _dequant(q, s, z):
     from int4_b200 import dequantize_int4_ref
 
     return dequantize_int4_ref(q, s, z, torch.float32)
+
+
+def test_argmax_exchange_of_one_rank_is_torch_argmax(cuda_device):
+    import cases
+    from int4_b200 import _lib
+    from int4_b200.peer import argmax_allreduce
+
+    L = _lib.lib()
+    x = cases.activations(5, 128256, "bfloat16", seed=8).to(cuda_device)
+    x[1, 77] = x[1, 99] = 20.0  # equal maxima: the first index
+    x[2, :] = float("-inf")
+    buf = _alloc(L, 64)
+    try:
+
+        class One:  # a peer group of one rank, built straight from the C ABI
+            _lib = L
+            struct = _group(1, 0, 64, [buf])
+
+        for _ in range(2):
+            got = argmax_allreduce(One, x, 0)
+            assert torch.equal(got, x.float().argmax(-1, keepdim=True)), got.view(-1).tolist()
+    finally:
+        torch.cuda.synchronize()
+        L.i4b_peer_buffer_free(buf)
