@@ -339,6 +339,7 @@ constexpr int kResPerThread = 4;  // residual values per thread: o / down slabs 
 // take per-token sums of squares over the staged rows (fixed order: lanes, then warps); (3) each thread
 // rewrites its chunks in place: x = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) (LlamaRMSNorm) where
 // needed, then the permutation.
+template <bool TP>
 __device__ __noinline__ void stage_x(int g, int l, int K) {
   const DkHot& P = dk_P;
   Smem& S = dk_S;
@@ -353,7 +354,7 @@ __device__ __noinline__ void stage_x(int g, int l, int K) {
   const int64_t stride = g == G_O ? P.q_n : g == G_DOWN ? m.intermediate : H;
   uint8_t* sx = smem + P.off_x;
   const int nch = K / 8, lg = 31 - __clz(nch), total = B << lg;  // chunks per row: a power of two
-  if (P.tp_world > 1 && (g == G_GU || (g == G_QKV && l > 0))) {
+  if (TP && (g == G_GU || (g == G_QKV && l > 0))) {
     // tensor parallelism: the residual rows are the previous update's rows plus all ranks' partials;
     // one CTA also stores them for the next update
     const int u = g == G_GU ? 2 * l : 2 * l - 1;
@@ -431,7 +432,7 @@ __device__ __noinline__ void stage_x(int g, int l, int K) {
 }
 
 // One GEMV stage of layer l for this CTA's slabs of it.  False on a failed wait.
-template <int SPS>
+template <int SPS, bool TP>
 __device__ __noinline__ bool gemv_stage(int g, int l) {
   const DkHot& P = dk_P;
   Smem& S = dk_S;
@@ -466,7 +467,7 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
       c = P.ctr + l * C_LAYER + C_GU, target = unsigned(P.nslab[G_GU]);
     }
     if (c != nullptr && !wait_counter(c, target, abort_word)) S.flag = 0;  // sticky: errors are never cleared
-    if (S.flag && P.tp_world > 1 && (g == G_GU || (g == G_QKV && l > 0))) {
+    if (TP && S.flag && (g == G_GU || (g == G_QKV && l > 0))) {
       const int lu = g == G_GU ? l : l - 1, su = g == G_GU ? 0 : 1;
       const unsigned int xt = (S.ep + 1u) * unsigned(P.tp_world - 1) * unsigned(P.nslab[su ? G_DOWN : G_O]);
       if (!wait_counter_sys(xctr(P, P.tp_rank, lu, su), xt, abort_word)) S.flag = 0;
@@ -476,7 +477,7 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
   if (!S.flag) return false;
   stamp(P, l, st_id, 1);
   const int K = g == G_DOWN ? m.intermediate : (g == G_O ? P.q_n : m.hidden);
-  stage_x(g, l, K);
+  stage_x<TP>(g, l, K);
   cbar();
   stamp(P, l, st_id, 2);
   // residual inputs of the o_proj / down_proj epilogue: loaded here, consumed after the pieces
@@ -485,7 +486,7 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
   const int B = m.batch;
   constexpr int kRes = kResPerThread;
   uint16_t res[kRes];
-  const bool tp_out = P.tp_world > 1 && (g == G_O || g == G_DOWN);
+  const bool tp_out = TP && (g == G_O || g == G_DOWN);
   if ((g == G_O || g == G_DOWN) && !tp_out) {
 #pragma unroll
     for (int k = 0; k < kRes; ++k) {
@@ -896,7 +897,7 @@ __device__ __noinline__ bool tp_finalize() {
   return true;
 }
 
-template <int SPS, int GS>
+template <int SPS, int GS, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid_constant__ DkParams Pg) {
   uint8_t* const smem = dk_smem;
   Smem& S = dk_S;
@@ -922,7 +923,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     S.nit = nit;
     S.ppl = off;
     S.flag = 1;
-    S.ep = P.tp_world > 1 ? *reinterpret_cast<volatile unsigned int*>(P.xb[P.tp_rank]) : 0u;
+    S.ep = TP ? *reinterpret_cast<volatile unsigned int*>(P.xb[P.tp_rank]) : 0u;
     S.prod_seq = 0;
     for (int s = 0; s < P.nslot; ++s) {
       mbar_init(&S.full[s], 1);
@@ -971,15 +972,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     // ---- compute warps: the stages of every layer in order
     const int nattn = m.batch * m.kv_heads * P.nsplit;
     for (int l = 0; l < m.layers && ok; ++l) {
-      ok = gemv_stage<SPS>(G_QKV, l);
+      ok = gemv_stage<SPS, TP>(G_QKV, l);
       // attention runs on warps 0..kAW-1; the others go on to the o_proj stage, whose barrier they pass
       // only together with them.  A failed attention clears S.flag, which that stage checks.
       if (ok && int(blockIdx.x) < nattn && warp < kAW) attention_item<GS>(l, blockIdx.x);
-      ok = ok && gemv_stage<SPS>(G_O, l);
-      ok = ok && gemv_stage<SPS>(G_GU, l);
-      ok = ok && gemv_stage<SPS>(G_DOWN, l);
+      ok = ok && gemv_stage<SPS, TP>(G_O, l);
+      ok = ok && gemv_stage<SPS, TP>(G_GU, l);
+      ok = ok && gemv_stage<SPS, TP>(G_DOWN, l);
     }
-    if (ok && P.tp_world > 1 && blockIdx.x == 0) ok = tp_finalize();
+    if (TP && ok && blockIdx.x == 0) ok = tp_finalize();
     if (!ok && tid == 0) {
       atomicOr(&g_dk_err, I4B_DEVERR_WAIT_TIMEOUT);
       atomicExch(P.ctr + P.i_abort, 1u);
@@ -995,7 +996,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     if (atomicAdd(P.ctr + P.i_done, 1u) == gridDim.x - 1) {  // the last CTA out resets the workspace counters
       for (int i = 0; i < P.n_ctr; ++i) P.ctr[i] = 0u;
       // and, under tensor parallelism, advances this rank's epoch for the next launch
-      if (P.tp_world > 1) *reinterpret_cast<volatile unsigned int*>(P.xb[P.tp_rank]) = S.ep + 1u;
+      if (TP) *reinterpret_cast<volatile unsigned int*>(P.xb[P.tp_rank]) = S.ep + 1u;
       __threadfence();
     }
   }
@@ -1152,7 +1153,8 @@ int make_layout(const i4b_decode_model& m, int grid, Layout* L) {
 
 template <int SPS, int GS>
 cudaError_t launch_dk_t(const DkParams& p, int grid, size_t smem, cudaStream_t stream) {
-  auto kern = decode_layers_kernel<SPS, GS>;
+  // the one-rank kernel is compiled without the tensor-parallel exchange
+  auto kern = p.h.tp_world > 1 ? decode_layers_kernel<SPS, GS, true> : decode_layers_kernel<SPS, GS, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};

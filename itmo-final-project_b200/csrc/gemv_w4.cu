@@ -29,7 +29,8 @@
 // in fixed rank order.  More than 8 splits (K > 8192) write fp32 partials to
 // the caller's workspace; the last CTA of a column tile (atomic ticket, no
 // spinning) adds them in split order and resets the ticket.  Every path is
-// bit-identical from run to run.  The kernel has no spin-waits.
+// bit-identical from run to run.  The only waits are those of the tensor-parallel
+// epilogue (i4b_w4a16_matmul_allreduce), for the other ranks' flags, each bounded.
 #include <algorithm>
 
 #include "common.cuh"

@@ -10,8 +10,10 @@ launch, which exchanges the partials itself; the prompt always uses NCCL; the
 vocab-parallel logits are all-gathered, and the greedy token computed without
 that all-gather (``decode_greedy``) must be their first maximum.  With the fused sums, three more steps
 replayed from one CUDA graph must equal the eager steps bit for bit.  Exit
-status 0 only if every rank stays within 2e-2 max-abs and no kernel's bounded
-wait expired.
+status 0 only if every rank stays within 2e-2 max-abs (for the wider,
+persistent model: max(2e-2, twice the noise floor of a cached step at that
+width, measured in the run between two one-rank W4 decoders that differ only in
+summation order), and no kernel's bounded wait expired.
 """
 from __future__ import annotations
 
@@ -48,7 +50,8 @@ def main() -> int:
 
     from int4_b200 import _lib
 
-    worst, graph_diff, greedy_bad = 0.0, 0.0, 0
+    graph_diff, greedy_bad = 0.0, 0
+    excess, report = -1.0, []  # max over runs of (difference - bound); per-run "difference / bound"
     with torch.no_grad():
         hf_tiny = build_hf(0)
         hf_mid = build_hf(0, mid_config())
@@ -63,14 +66,24 @@ def main() -> int:
             assert (tp.peers is not None) == peer
             assert (tp.persistent is not None) == persistent
             one = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev)
+            # Noise floor of a cached step at this width: two one-rank W4 decoders whose only difference is
+            # the fp32 summation order (the persistent launch against the per-projection launches).  Where
+            # the tensor-parallel model runs the persistent decode its bound is max(2e-2, twice that floor).
+            floor_ref = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev,
+                                persistent=False) if persistent else None
             a, b = tp.prefill(ids, all_logits=True), one.prefill(ids, all_logits=True)
-            worst = max(worst, (a.float() - b.float()).abs().max().item())
+            worst = (a.float() - b.float()).abs().max().item()
+            floor = 0.0
+            if floor_ref is not None:
+                floor_ref.prefill(ids)
             tok = b[:, -1].argmax(-1, keepdim=True)
             eager = []
             for step in range(3):
                 pos = torch.tensor([24 + step], device=dev)
                 a, b = tp.decode_step(tok, pos), one.decode_step(tok, pos)
                 worst = max(worst, (a.float() - b.float()).abs().max().item())
+                if floor_ref is not None:
+                    floor = max(floor, (floor_ref.decode_step(tok, pos).float() - b.float()).abs().max().item())
                 eager.append(a.clone())
                 # the same step again (same position, same cache writes), choosing the token without the
                 # logits all-gather: the first maximum of the gathered logits
@@ -98,15 +111,19 @@ def main() -> int:
                 torch.cuda.synchronize()
                 del graph
             tp.close()
+            bound = max(2e-2, 2 * floor)
+            excess = max(excess, worst - bound)
+            report.append(f"{worst:.3e}/{bound:.1e}")
     flags = _lib.device_error_flags(local)
-    t = torch.tensor([worst, graph_diff, float(flags != 0), float(greedy_bad)], device=dev)
+    t = torch.tensor([excess, graph_diff, float(flags != 0), float(greedy_bad)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     torch.cuda.synchronize()
     dist.destroy_process_group()
     if rank == 0:
-        print(f"max |logits(tp{world}) - logits(tp1)| = {t[0].item():.3e}, graph vs eager {t[1].item():.3e}, "
-              f"device error flags {'set' if t[2].item() else 'clear'}, greedy mismatches {int(t[3].item())}")
-    return 0 if t[0].item() <= 2e-2 and t[1].item() == 0.0 and t[2].item() == 0.0 and t[3].item() == 0 else 1
+        print(f"max |logits(tp{world}) - logits(tp1)| / bound per run: {', '.join(report)}; "
+              f"graph vs eager {t[1].item():.3e}, device error flags {'set' if t[2].item() else 'clear'}, "
+              f"greedy mismatches {int(t[3].item())}")
+    return 0 if t[0].item() <= 0.0 and t[1].item() == 0.0 and t[2].item() == 0.0 and t[3].item() == 0 else 1
 
 
 if __name__ == "__main__":
