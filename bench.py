@@ -237,7 +237,7 @@ def run_block(args, world, rank, local):
     g = torch.Generator().manual_seed(1)
     x = torch.randn((M, 2048), generator=g).to(torch.bfloat16).to(dev)
     peers = None
-    if world > 1 and args.peer_allreduce and M <= 32:
+    if world > 1 and args.peer_allreduce == 1 and M <= 32:
         from int4_b200.peer import PeerGroup
 
         peers = PeerGroup(None, capacity=M * 2048)
@@ -450,14 +450,23 @@ def run_model(args, world, rank, local):
     for label, w4 in (("w4", True), ("bf16", False))[:2 if args.compare_bf16 else 1]:
         persistent = None if args.persistent < 0 else bool(args.persistent) and w4
         m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world, persistent=persistent,
-                    peer_allreduce=bool(args.peer_allreduce),
+                    peer_allreduce=args.peer_allreduce != 0, matmul_allreduce=args.peer_allreduce == 1,
                     max_seq=prompt + steps + args.warmup + 8, max_batch=B, device=dev)
         with ClockSampler(local) as clk:
             r = time_decode(m, B, prompt, steps, args.warmup, world, dev, LLAMA_1B["vocab_size"],
                             trace=bool(args.trace) and w4)
         r["clocks"] = clk.summary()
         r["persistent"] = m.persistent is not None
-        r["peer_allreduce"] = m.peers is not None
+        if world == 1:
+            r["tp_sum"] = "none"
+        elif m.persistent is not None:
+            r["tp_sum"] = "inside the persistent decode launch (peer buffers)"
+        elif m.peers is not None and m.matmul_allreduce:
+            r["tp_sum"] = "inside the o/down matmuls (peer buffers)"
+        else:
+            r["tp_sum"] = "NCCL all-reduce"
+        r["greedy"] = "argmax exchange (peer buffers)" if world > 1 and m.peers is not None else \
+            ("logits all-gather + argmax" if world > 1 else "argmax")
         m.close()
         # bytes one decode step must read on this rank: projection weights + the KV cache up to the mean position
         mean_pos = prompt + steps / 2
@@ -533,8 +542,7 @@ def main_model(args, world, rank, local, threads):
         "vs_baseline": None, "dtype": "w4a16-bf16", "data": "synthetic (random-init weights, random token ids)",
         "config": dict(model_config(args), decode="one launch for all layers (i4b_decode_layers)"
                        if w4["persistent"] else "one launch per projection / glue op",
-                       tp_sum="none" if world == 1 else ("inside the o/down matmuls (peer buffers)"
-                                                         if w4["peer_allreduce"] else "NCCL all-reduce")),
+                       tp_sum=w4["tp_sum"], greedy=w4["greedy"]),
         "bf16_tokens_per_s": args.m * args.steps / bf["decode_s"] if bf else None,
         "w4_over_bf16": bf["decode_s"] / w4["decode_s"] if bf else None,
         "prefill_ms": {"w4": w4["prefill_ms"], "bf16": bf["prefill_ms"] if bf else None},
@@ -570,9 +578,11 @@ def main():
                          "0 = one launch per projection / glue op, -1 = whichever the model qualifies for")
     ap.add_argument("--compare-bf16", type=int, default=1,
                     help="model workload: also time the same decode loop with bf16 projections")
-    ap.add_argument("--peer-allreduce", type=int, default=1,
-                    help="tensor-parallel runs: sum the row-parallel outputs inside the W4 matmuls through peer "
-                         "exchange buffers (1) or with an NCCL all-reduce after them (0)")
+    ap.add_argument("--peer-allreduce", type=int, default=-1,
+                    help="tensor-parallel runs: 1 = sum the row-parallel outputs inside every W4 matmul through peer "
+                         "exchange buffers; 0 = NCCL all-reduces only; -1 (default) = what measured fastest at two "
+                         "ranks: NCCL after the per-projection matmuls, the peer exchange inside the persistent "
+                         "decode and for the greedy token")
     ap.add_argument("--pdl", type=int, default=1,
                     help="programmatic dependent launch for the small-M kernels (weights fetched before the wait)")
     args = ap.parse_args()

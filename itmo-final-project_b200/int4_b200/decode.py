@@ -343,15 +343,19 @@ class LlamaTP:
     tensor parallelism the peer all-reduce) runs all decoder layers of a decode
     step as one launch of ``i4b_decode_layers``; tensor-parallel ranks then add
     each other's o / down partials inside that launch.
-    ``peer_allreduce`` (tensor-parallel W4 decode steps of <= 32 tokens) sums
-    the row-parallel o / down outputs inside those matmuls through peer
-    exchange buffers (``i4b_w4a16_matmul_allreduce``) instead of NCCL.
+    ``peer_allreduce`` (tensor parallelism) sets up the peer exchange buffers:
+    the persistent decode sums the ranks' o / down partials inside its launch,
+    and ``decode_greedy`` exchanges the ranks' best tokens instead of
+    all-gathering the logits.  ``matmul_allreduce`` additionally sums the o /
+    down outputs of the per-launch decode (<= 32 tokens) inside those matmuls
+    (``i4b_w4a16_matmul_allreduce``) instead of an NCCL all-reduce; it is off by
+    default because, measured at two ranks, NCCL's all-reduce is faster there.
     """
 
     def __init__(self, hf_model, *, w4: bool = True, group_size: int = 128, quantize_lm_head: bool = False,
                  rank: int = 0, world: int = 1, group=None, max_seq: int = 2048, max_batch: int = 1,
                  device: torch.device | None = None, fused: bool = True, persistent: bool | None = None,
-                 peer_allreduce: bool = True):
+                 peer_allreduce: bool = True, matmul_allreduce: bool = False):
         cfg = hf_model.config
         self.fused = fused
         self.cfg = cfg
@@ -434,6 +438,7 @@ class LlamaTP:
                 self, [{k: L[k].q for k in ("qkv", "o", "gu", "down")} for L in self.layers], group_size)
         # Under tensor parallelism the W4 decode step sums the row-parallel o / down outputs inside their
         # matmuls (peer exchange buffers over NVLink) instead of a separate NCCL all-reduce.
+        self.matmul_allreduce = matmul_allreduce
         self.peers = None
         if world > 1 and w4 and fused and peer_allreduce:
             from .peer import PeerGroup
@@ -571,7 +576,7 @@ class LlamaTP:
                 qkv = L["qkv"](x)
             rope_kv_cache(qkv, self.cos, self.sin, pos, q, kc, vc, nq, nkv)
             decode_attention(q, kc, vc, pos, att, nq, nkv, hd ** -0.5)
-            fused_ar = fold and self.peers is not None
+            fused_ar = fold and self.peers is not None and self.matmul_allreduce
             if fused_ar:
                 o = w4a16_matmul_allreduce(self.peers, att, *L["o"].q)
             else:

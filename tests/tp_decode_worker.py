@@ -62,7 +62,7 @@ def main() -> int:
                 (hf_mid, False, True, True))
         for hf, lm_w4, peer, persistent in runs:
             tp = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=rank, world=world, max_seq=64, device=dev,
-                         peer_allreduce=peer)
+                         peer_allreduce=peer, matmul_allreduce=peer)
             assert (tp.peers is not None) == peer
             assert (tp.persistent is not None) == persistent
             one = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev)
