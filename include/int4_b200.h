@@ -80,9 +80,13 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
 
 /* y[M, N] = x[M, K] @ W_hat^T in x's dtype (fp32 accumulation).
  * Replaces int4_triton.w4a16_matmul (int4_triton/gemm.py:303-309, dispatch
- * gemm.py:234-300): M == 1 decode GEMV and 2 <= M <= 64 split-K both run the
+ * gemm.py:234-300): M == 1 decode GEMV and 2 <= M <= 32 split-K both run the
  * register-dequant tensor-core kernel with a deterministic in-kernel split-K
- * reduction; M > 64 runs the TMA + tcgen05/TMEM GEMM.
+ * reduction; M > 32 runs the TMA + tcgen05/TMEM GEMM (the reference switches
+ * at 64; on B200 the tcgen05 GEMM is faster from 33 tokens on).
+ * For M > 32 qweight, scales and zeros must meet the TMA rules (16-byte
+ * aligned bases and row strides) unless N % 8 != 0 (then they are copied into
+ * the workspace); otherwise I4B_ERR_LAYOUT.
  * x: element (m, k) at x + m*stride_xm + k*stride_xk, dtype I4B_BF16 or I4B_F16.
  * qweight: row k8 at qweight + k8*stride_qk (unit stride along N).
  * scales/zeros: row g at base + g*stride_sg (unit stride along N).
@@ -115,12 +119,15 @@ size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K);
 /* y[M, N] = x[M, K] @ w[N, K]^T, x and w of the same dtype (bf16 or fp16).
  * Replaces int4_triton.w16a16_matmul (int4_triton/gemm.py:312-317), the
  * full-precision baseline with the same kernel structure as the W4 path.
- * w: element (n, k) at w + n*stride_wn + k*stride_wk. */
+ * w: element (n, k) at w + n*stride_wn + k*stride_wk.  M <= 16 accepts any
+ * strides; for M > 16 (tcgen05 GEMM) w must have unit stride along k and a
+ * 16-byte aligned base and row stride when K % 8 == 0 (otherwise it is copied
+ * into the workspace), else I4B_ERR_LAYOUT. */
 int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
                       const void* w, int64_t N, int64_t stride_wn, int64_t stride_wk, void* y, int64_t stride_ym,
                       void* workspace, size_t workspace_bytes, void* stream);
 
-/* Programmatic dependent launch for the M <= 64 kernels (default off).
+/* Programmatic dependent launch for the small-M kernels (W4 M <= 32, W16 M <= 16; default off).
  * When on, those kernels are launched with programmatic stream
  * serialization: they start while the previous kernel of the stream drains
  * and read qweight / scales / zeros BEFORE waiting for it, x only after.
@@ -129,7 +136,7 @@ int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t st
  * in the reference (its launches are plain Triton launches). */
 void i4b_set_pdl(int enable);
 
-/* Tuning hook for the M <= 64 decomposition: columns per CTA (32*wn),
+/* Tuning hook for the small-M decomposition: columns per CTA (32*wn, W16 only),
  * k-warps per CTA (wk) and K splits; 0 keeps the automatic choice, an
  * unusable value is ignored.  Process-wide.  No counterpart in the reference
  * (which autotunes, int4_triton/gemm.py:51-56). */
@@ -148,8 +155,10 @@ void i4b_set_skinny_override(int wn, int wk, int splits);
  * into the library (held by every GPU that loads it, until exit).  Sizes whose
  * i4b_w4a16_workspace_size exceeds that return I4B_ERR_SCRATCH_LIMIT.  No
  * cudaMalloc / cudaFree is called.  The first call on a device looks up the
- * array's device address, so make it before any stream capture.  All calls on
- * a device share the array: calls that overlap on the GPU race. */
+ * array's device address, so make it before any stream capture; the address is
+ * kept until exit, so cudaDeviceReset between calls is not supported.  Argument
+ * errors are reported before the scratch limit.  All calls on a device share
+ * the array: calls that overlap on the GPU race. */
 int i4b_w4a16_matmul_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
                              const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales,
                              const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,

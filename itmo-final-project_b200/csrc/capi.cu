@@ -6,11 +6,13 @@
 // allocates device memory or synchronises: scratch comes from the caller's
 // workspace, whose layout is
 //   [64 KB split-K tickets, always left zero]
-//   M <= 64 : [fp32 partials S x M x N]
-//   M >  64 : [x copy][qweight copy][scales copy][zeros copy]   (copies only when
+//   small M (W4 <= 32, W16 <= 16): [fp32 partials S x M x N]
+//   larger M: [x copy][weight copies][split-K fp32 partials]   (copies only when
 //             an operand breaks the TMA rules: 16-byte base / row stride)
 #include <algorithm>
 #include <cstring>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -37,10 +39,12 @@ struct DevInfo {
 int current_device_info(DevInfo* out) {
   static DevInfo cache[64];
   static bool filled[64] = {};
+  static std::mutex mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e);
   if (dev < 0 || dev >= 64) return I4B_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(mu);
   if (!filled[dev]) {
     DevInfo d;
     if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return fail_cuda(e);
@@ -89,6 +93,33 @@ constexpr int64_t kSmallM = kSkinnyMaxM;
 
 namespace i4b {
 int cuda_error_status(cudaError_t e) { return fail_cuda(e); }
+
+cudaError_t ensure_dynamic_smem(const void* func, size_t bytes) {
+  struct Entry {
+    const void* func;
+    int dev;
+    size_t bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> set;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  bytes = std::max<size_t>(bytes, 48 * 1024);
+  std::lock_guard<std::mutex> lock(mu);
+  Entry* hit = nullptr;
+  for (Entry& en : set)
+    if (en.func == func && en.dev == dev) hit = &en;
+  if (hit && hit->bytes >= bytes) return cudaSuccess;
+  if ((e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes))) != cudaSuccess)
+    return e;
+  if ((e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
+    return e;
+  if (hit) hit->bytes = bytes;
+  else set.push_back({func, dev, bytes});
+  return cudaSuccess;
+}
 }  // namespace i4b
 
 extern "C" {
@@ -334,7 +365,7 @@ size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
-  if (M <= kSmallM) return skinny_workspace_bytes(plan_skinny(M, N, K, 32, false, d.sms));
+  if (M <= kSmallM) return skinny_workspace_bytes(plan_skinny(M, N, K, d.sms));
   return tc_w16_workspace(M, N, K, d.sms);
 }
 
@@ -360,11 +391,11 @@ int i4b_w16a16_matmul(const void* x, int dtype, int64_t M, int64_t K, int64_t st
     return I4B_OK;
   }
   if (M <= kSmallM) {
-    const SkinnyPlan p = plan_skinny(M, N, K, 32, false, d.sms);
+    const SkinnyPlan p = plan_skinny(M, N, K, d.sms);
     if (p.mode == 3) return I4B_ERR_SHAPE;
     if (skinny_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;
-    cudaError_t e = launch_skinny(false, f16, x, M, K, stride_xm, stride_xk, w, N, stride_wn, stride_wk, nullptr,
-                                  nullptr, 0, 0, y, stride_ym, workspace, p, g_pdl, s);
+    cudaError_t e = launch_skinny(f16, x, M, K, stride_xm, stride_xk, w, N, stride_wn, stride_wk, y, stride_ym,
+                                  workspace, p, g_pdl, s);
     return e == cudaSuccess ? I4B_OK : fail_cuda(e);
   }
   const int64_t Kp = round_up(K, 8);

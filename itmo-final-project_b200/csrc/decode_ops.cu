@@ -319,13 +319,8 @@ cudaError_t launch_decode_attn(const uint16_t* q, const uint16_t* kc, const uint
   int ns = (max_seq + 63) / 64;
   ns = ns < 1 ? 1 : (ns > 8 ? 8 : ns);
   const size_t smem = (size_t(kAttnMaxChunk) + 16 * 64) * sizeof(float);
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  const cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(decode_attn_kernel), smem);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(nq * ns), unsigned(B));
   cfg.blockDim = dim3(kAttnThreads);

@@ -1155,7 +1155,7 @@ template <int SPS, int GS>
 cudaError_t launch_dk_t(const DkParams& p, int grid, size_t smem, cudaStream_t stream) {
   // the one-rank kernel is compiled without the tensor-parallel exchange
   auto kern = p.h.tp_world > 1 ? decode_layers_kernel<SPS, GS, true> : decode_layers_kernel<SPS, GS, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));

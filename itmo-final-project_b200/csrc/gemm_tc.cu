@@ -499,7 +499,7 @@ static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int
   }
   if (!ok) return cudaErrorInvalidValue;
   auto kern = tc_gemm_kernel<INT4, F16, BN, BMT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM));
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), C::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(unsigned(cdiv(N, BN)), unsigned(cdiv(M, C::BM)), unsigned(ksplit));
   kern<<<grid, C::THREADS, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym, ksplit, partials,

@@ -63,7 +63,7 @@ struct W4SArgs {
   int gpl;         // segments per group
   int vec_w, vec_s, vec_x, pdl;
   int xpitch;
-  int off_sz, off_x, off_xs, off_part;
+  int off_sz, off_x, off_part;
   int pro;
   // activation prologue (bf16 only): 1 = x := rmsnorm(x + delta) * norm_w, 2 = x := silu(g) * u with g | u = x
   const uint16_t* delta;
@@ -215,8 +215,7 @@ __device__ __forceinline__ void cp_async_wait_upto(int pending) {
 }  // namespace
 
 // Shared memory: weights [step][warp][lane] x 16 B | scales+zeros [segment][warp][r] x 16 B (s0..s3, z0..z3) |
-// activations [token][k/8] x 16 B (pre-permuted) | segment sums of x [segment][8*MT] fp32 |
-// partial sums [token][128] fp32.  The K range of a CTA is
+// activations [token][k/8] x 16 B (pre-permuted) | partial sums [token][128] fp32.  The K range of a CTA is
 // padded to whole stages with zero weights, zero activations and zero scales, which add nothing.
 template <int MT, bool F16, int SPS, int PRO>
 __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
@@ -311,14 +310,11 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     pdl_wait();
   }
   {
-    // Stage x (permuted) and the per-segment sums X[seg][token] in shared memory.  A segment is C = 4*SPS
-    // consecutive chunks of 8 k held by C consecutive lanes, reduced with xor shuffles in a fixed order.
-    constexpr int C = 4 * SPS;
+    // Stage x in shared memory, each 8-k chunk permuted to the k order of the A fragments.
     constexpr int XB = 4;  // chunks per thread in flight
     const int nch = nstages * SPST * 4;  // chunks of 8 k, padded
     const int nreal = a.KC / 8;
     const int total = M * nch;
-    float* sXS = reinterpret_cast<float*>(smem + a.off_xs);
     __shared__ float s_inv[32];
     if constexpr (PRO == kProRmsNorm) {
       // Full-row statistics of h' = bf16(h + delta) for every token (warp t % 4 owns token t); CTA (0, 0)
@@ -418,22 +414,12 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
         if (base + j * 128 >= total) break;  // uniform over the CTA
         const int t = idx / nch, ch = idx - t * nch;
         const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-        float sum = 0.0f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float lo = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] & 0xFFFFu))) : __uint_as_float(u[q] << 16);
-          const float hi = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] >> 16))) : __uint_as_float(u[q] & 0xFFFF0000u);
-          sum += lo + hi;
-        }
-#pragma unroll
-        for (int o = 1; o < C; o <<= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
         if (idx < total) {
           // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
           asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
                        "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
                        "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
                        : "memory");
-          if (ch % C == 0) sXS[(ch / C) * (8 * MT) + t] = sum;
         }
       }
     }
@@ -654,8 +640,8 @@ constexpr int kStreamSteps = I4B_STREAM_STEPS;  // 32-k steps per stage (at leas
 // For matrices with many more 32-column slabs than warps (an lm_head: N = 128256), a persistent grid of
 // warps streams slabs of 32 columns x the whole K: warp g takes slabs g, g + W, g + 2W, ... (W warps in
 // the grid), keeping kStreamRing stages of 4 (or SPS) 32-k steps in flight through its own cp.async ring, so
-// the weight stream never stops between slabs.  The activations (M <= 8 rows x K) and their segment sums
-// are staged once per CTA.  No K split, hence no cross-CTA reduction; the dequant / MMA / segment
+// the weight stream never stops between slabs.  The activations (M <= 8 rows x K) are staged once per
+// CTA.  No K split, hence no cross-CTA reduction; the dequant / MMA / segment
 // arithmetic is that of w4_skinny_kernel.
 template <bool F16, int SPS, bool ONE>
 __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
@@ -678,7 +664,6 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
 
   const uint32_t s_base = smem_u32(smem);
   const uint32_t s_x = s_base;                                   // [M][xpitch]
-  float* sXS = reinterpret_cast<float*>(smem + a.off_xs);        // [K / L][8]
   const uint32_t s_w = s_base + a.off_sz + warp * RING * (WSTAGE + SZSTAGE);  // this warp's ring
 
   // Issue cursor: the next stage of this warp's stream (slab, stage in the slab, ring slot), kept as
@@ -735,33 +720,16 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
     pdl_wait();
   }
   {
-    constexpr int C = 4 * SPS;
+    // stage x in shared memory, each 8-k chunk permuted to the k order of the A fragments
     const int nch = K / 8;
     const int ntot = M * nch;
-    for (int base = 0; base < ntot; base += 128) {
-      const int idx = base + tid;
+    for (int idx = tid; idx < ntot; idx += 128) {
       const int t = idx / nch, ch = idx - t * nch;
-      uint32_t u[4] = {0u, 0u, 0u, 0u};
-      if (idx < ntot) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.x + int64_t(t) * a.sxm + 8 * ch));
-        u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
-      }
-      float sum = 0.0f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float lo = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] & 0xFFFFu))) : __uint_as_float(u[q] << 16);
-        const float hi = F16 ? __half2float(__ushort_as_half(uint16_t(u[q] >> 16))) : __uint_as_float(u[q] & 0xFFFF0000u);
-        sum += lo + hi;
-      }
-#pragma unroll
-      for (int o = 1; o < C; o <<= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-      if (idx < ntot) {
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
-                     "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
-                     "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
-                     : "memory");
-        if (ch % C == 0) sXS[(ch / C) * 8 + t] = sum;
-      }
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.x + int64_t(t) * a.sxm + 8 * ch));
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
+                   "r"(__byte_perm(v.x, v.z, 0x5410)), "r"(__byte_perm(v.x, v.z, 0x7632)),
+                   "r"(__byte_perm(v.y, v.w, 0x5410)), "r"(__byte_perm(v.y, v.w, 0x7632))
+                   : "memory");
     }
   }
   __syncthreads();
@@ -890,14 +858,7 @@ size_t w4_workspace_bytes(const W4Plan& p) { return p.mode == 2 ? kTicketBytes +
 template <int MT, bool F16, int SPS, int PRO>
 static cudaError_t launch_w4_impl(const W4SArgs& a, const W4Plan& p, size_t smem, cudaStream_t stream) {
   auto kern = w4_skinny_kernel<MT, F16, SPS, PRO>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(std::max<size_t>(smem, 48 * 1024)));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
-    configured = std::max<size_t>(smem, 48 * 1024);
-  }
+  if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(p.ntiles), unsigned(p.S));
   cfg.blockDim = dim3(128);
@@ -956,17 +917,9 @@ static cudaError_t launch_stream_impl(W4SArgs a, int num_sms, cudaStream_t strea
   constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;
   constexpr int SEGST = SPST / SPS;
   a.xpitch = (a.K / 8) % 8 == 0 ? a.K * 2 + 64 : a.K * 2;
-  a.off_xs = int((size_t(a.M) * a.xpitch + 15) / 16 * 16);
-  a.off_sz = int((size_t(a.off_xs) + size_t(a.K / (32 * SPS)) * 8 * 4 + 127) / 128 * 128);  // start of the rings
+  a.off_sz = int((size_t(a.M) * a.xpitch + 127) / 128 * 128);  // start of the rings
   const size_t smem = size_t(a.off_sz) + 4 * kStreamRing * (SPST * 512 + SEGST * 128);
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem)) return e;
   int per_sm = int((227 * 1024) / (smem + 1024));
   per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
   cudaLaunchConfig_t cfg = {};
@@ -1067,8 +1020,6 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   off += size_t(a.nstages) * (spst / p.SPS) * 4 * 8 * 16;
   a.off_x = int(off);
   off += size_t(M) * a.xpitch;
-  a.off_xs = int(off);
-  off += size_t(a.nstages) * (spst / p.SPS) * (8 * p.MT) * 4;
   a.off_part = int(off);
   off += size_t(M) * kBN * 4;
   const size_t smem = off;

@@ -21,7 +21,7 @@ unsigned int read_quant_error(bool clear);
 constexpr size_t kTicketBytes = 64 * 1024;
 constexpr int64_t kMaxTickets = int64_t(kTicketBytes / 4);
 
-// skinny.cu (M <= kSkinnyMaxM)
+// skinny.cu (W16 weights, M <= kSkinnyMaxM)
 constexpr int64_t kSkinnyMaxM = 16;
 struct SkinnyPlan {
   int MT, WN, WK, S, KC, KW, L, xstride;
@@ -30,12 +30,11 @@ struct SkinnyPlan {
   size_t partial_bytes;
   int64_t ntiles;
 };
-SkinnyPlan plan_skinny(int64_t M, int64_t N, int64_t K, int G, bool int4, int num_sms);
+SkinnyPlan plan_skinny(int64_t M, int64_t N, int64_t K, int num_sms);
 size_t skinny_workspace_bytes(const SkinnyPlan& p);
-cudaError_t launch_skinny(bool int4, bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk,
-                          const void* w, int64_t N, int64_t sw0, int64_t sw1, const uint16_t* sc,
-                          const uint16_t* zr, int64_t ssg, int G, void* y, int64_t sym, void* ws,
-                          const SkinnyPlan& p, bool pdl, cudaStream_t stream);
+cudaError_t launch_skinny(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const void* w,
+                          int64_t N, int64_t sw0, int64_t sw1, void* y, int64_t sym, void* ws, const SkinnyPlan& p,
+                          bool pdl, cudaStream_t stream);
 // Tuning override of the automatic decomposition (0 = automatic).
 void set_skinny_override(int wn, int wk, int splits);
 
@@ -85,8 +84,12 @@ cudaError_t launch_argmax_allreduce(const uint16_t* x, int64_t rows, int64_t n, 
                                     int64_t* out, const W4AllReduce& ar, cudaStream_t stream);
 // capi.cu: records e for i4b_last_cuda_error and returns I4B_ERR_CUDA
 int cuda_error_status(cudaError_t e);
+// capi.cu: lets kernel `func` use `bytes` of dynamic shared memory on the CURRENT device (and prefer the
+// maximum shared-memory carveout).  The attribute is per device, so the setting is remembered per
+// (kernel, device) pair, under a lock; a later call asking for no more than was set is free.
+cudaError_t ensure_dynamic_smem(const void* func, size_t bytes);
 
-// gemm_tc.cu (M > 64)
+// gemm_tc.cu (W4 M > 32, W16 M > 16)
 struct TcOperands {
   const void* x;
   int64_t sxm;

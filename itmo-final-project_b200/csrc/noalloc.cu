@@ -15,6 +15,9 @@
 // cudaGetSymbolAddress, with that device current, on the first call made on
 // that device.  Make that first call before any stream capture begins.
 //
+// The looked-up address is kept for the life of the process: cudaDeviceReset
+// between calls is not supported (the module reloads, possibly elsewhere).
+//
 // All calls on a device share the one array and it keeps whatever the last
 // call left in it.  The split-K tickets at its start must read zero when a
 // kernel begins, so each call that uses scratch clears them first.  Two calls
@@ -56,7 +59,15 @@ extern "C" int i4b_w4a16_matmul_noalloc(const void* x, int x_dtype, int64_t M, i
                                         int64_t stride_xk, const int32_t* qweight, int64_t N, int64_t stride_qk,
                                         const uint16_t* scales, const uint16_t* zeros, int64_t stride_sg,
                                         int group_size, void* y, int64_t stride_ym, void* stream) {
-  // Sizes the regular entry point would reject are reported by it, unchanged.
+  // The argument checks of i4b_w4a16_matmul, in its order, come before the scratch limit, so a bad
+  // argument is reported as such whatever the sizes.
+  if (x_dtype != I4B_F16 && x_dtype != I4B_BF16) return I4B_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return I4B_ERR_INVALID_ARG;
+  if (K % 8 != 0) return I4B_ERR_SHAPE;
+  if (group_size <= 0 || group_size % 32 != 0 || K % group_size != 0) return I4B_ERR_GROUP;
+  if (M == 0 || N == 0) return I4B_OK;
+  if (!x || !qweight || !scales || !zeros || !y) return I4B_ERR_INVALID_ARG;
+  // Sizes the regular entry point would reject for other reasons are reported by it, unchanged.
   const size_t need = (M > 0 && N > 0 && K > 0) ? i4b_w4a16_workspace_size(M, N, K, group_size) : 0;
   if (need > I4B_NOALLOC_SCRATCH_BYTES) return I4B_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;

@@ -140,7 +140,7 @@ def device_error_flags(device: int = 0, clear: bool = True) -> int:
 
 
 def set_pdl(enable: bool) -> None:
-    """Programmatic dependent launch for the M <= 64 kernels (see include/int4_b200.h)."""
+    """Programmatic dependent launch for the small-M kernels (see include/int4_b200.h)."""
     lib().i4b_set_pdl(1 if enable else 0)
 
 

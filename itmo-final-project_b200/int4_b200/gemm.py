@@ -2,9 +2,11 @@
 
 Same public functions as ``int4_triton.gemm`` (``gemm.py:303-317``).  The
 dispatch on M happens inside ``libint4_b200.so`` (``i4b_w4a16_matmul``):
-M <= 64 runs the register-dequant tensor-core kernel with its in-kernel
-deterministic split-K reduction (M == 1 is the decode GEMV), M > 64 runs the
-TMA + tcgen05/TMEM GEMM.  Launches are asynchronous on the current stream and
+M <= 32 runs the register-dequant tensor-core kernel with its in-kernel
+deterministic split-K reduction (M == 1 is the decode GEMV), M > 32 runs the
+TMA + tcgen05/TMEM GEMM (the reference switches at M = 64; on B200 the tcgen05
+GEMM is the faster one from 33 tokens on).  ``w16a16_matmul`` switches at
+M = 16.  Launches are asynchronous on the current stream and
 capture into CUDA graphs (no host synchronisation, no allocation outside torch).
 """
 from __future__ import annotations
@@ -14,8 +16,18 @@ import torch
 from . import _lib
 
 
-def _unit_n_stride(t: torch.Tensor) -> torch.Tensor:
-    return t if t.stride(1) == 1 and t.data_ptr() % 16 == 0 else t.contiguous()
+# Above these M the C side runs the TMA + tcgen05 GEMM, whose operands need 16-byte aligned bases and
+# row strides (capi.cu: kW4MaxM, kSkinnyMaxM).
+_W4_SMALL_M, _W16_SMALL_M = 32, 16
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    return t.stride(1) == 1 and t.data_ptr() % 16 == 0 and (t.stride(0) * t.element_size()) % 16 == 0
+
+
+def _unit_n_stride(t: torch.Tensor, tma: bool) -> torch.Tensor:
+    ok = _tma_ok(t) if tma else (t.stride(1) == 1 and t.data_ptr() % 16 == 0)
+    return t if ok else t.contiguous()
 
 
 def w4a16_matmul(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor) -> torch.Tensor:
@@ -32,9 +44,10 @@ def w4a16_matmul(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, z
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     if M == 0 or N == 0:
         return y.reshape(*x.shape[:-1], N)
-    qweight = _unit_n_stride(qweight)
-    scales = _unit_n_stride(scales)
-    zeros = _unit_n_stride(zeros)
+    tma = M > _W4_SMALL_M
+    qweight = _unit_n_stride(qweight, tma)
+    scales = _unit_n_stride(scales, tma)
+    zeros = _unit_n_stride(zeros, tma)
     if scales.stride(0) != zeros.stride(0):
         scales, zeros = scales.contiguous(), zeros.contiguous()
     L = _lib.lib()
@@ -63,7 +76,7 @@ def w16a16_matmul(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     if M == 0 or N == 0:
         return y.reshape(*x.shape[:-1], N)
-    if M > 64 and (w.stride(1) != 1 or w.data_ptr() % 16 or (w.stride(0) * 2) % 16) and K % 8 == 0:
+    if M > _W16_SMALL_M and K % 8 == 0 and not _tma_ok(w):
         w = w.contiguous()
     L = _lib.lib()
     dev = x.device

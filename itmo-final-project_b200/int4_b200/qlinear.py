@@ -13,7 +13,12 @@ from .quantize import dequantize_int4, quantize_int4
 
 
 class Int4Linear(nn.Module):
-    """Drop-in replacement for nn.Linear with int4 group-quantized weights (W4A16)."""
+    """A linear layer whose weight is stored as packed 4-bit groups; activations stay 16-bit.
+
+    ``forward`` runs the B200 W4A16 matmul on the packed weight directly (no
+    dequantized copy is ever materialised).  The buffers carry the reference's
+    names, shapes and dtypes so a state dict saved by one loads in the other.
+    """
 
     def __init__(self, in_features: int, out_features: int, group_size: int = 128, bias: bool = False, device=None):
         super().__init__()
@@ -51,20 +56,28 @@ class Int4Linear(nn.Module):
 
 
 def _iter_linears(model: nn.Module, skip):
-    for name, module in model.named_modules():
-        for child_name, child in module.named_children():
-            full = f"{name}.{child_name}" if name else child_name
-            if isinstance(child, nn.Linear) and not any(s in full for s in skip):
-                yield module, child_name, child
+    """(parent, attribute name, layer) of each nn.Linear whose dotted path contains none of ``skip``.
+
+    The parent is returned so that the caller can swap the layer in place.
+    """
+    for prefix, parent in model.named_modules():
+        for attr, layer in parent.named_children():
+            if not isinstance(layer, nn.Linear):
+                continue
+            path = attr if not prefix else prefix + "." + attr
+            if all(pattern not in path for pattern in skip):
+                yield parent, attr, layer
 
 
 @torch.no_grad()
 def quantize_model_linears(model: nn.Module, group_size: int = 128, skip=("lm_head",), fake: bool = False) -> nn.Module:
-    """Replace every nn.Linear (except names containing ``skip``) with Int4Linear.
+    """Swap the model's nn.Linear layers for Int4Linear, in place; returns the model.
 
-    ``fake=True`` keeps nn.Linear but overwrites its weight with the dequantized
-    int4 weight (the quality reference for the W4 kernels), as the reference's
-    ``quantize_model_linears`` does (``qlinear.py:54-68``).
+    Layers whose dotted name contains one of the ``skip`` substrings keep full
+    precision (by default the lm_head).  With ``fake=True`` nothing is swapped:
+    each weight is replaced by its quantize-then-dequantize round trip, which is
+    the accuracy yardstick the W4 kernels are compared with.  Same semantics as
+    the reference's helper (``qlinear.py:54-68``).
     """
     for parent, child_name, child in list(_iter_linears(model, skip)):
         q = Int4Linear.from_linear(child, group_size)

@@ -101,3 +101,51 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     assert L.i4b_status_string(I4B_ERR_SCRATCH_LIMIT).decode().startswith("sizes exceed")
     torch.cuda.synchronize()
     assert np.count_nonzero(y.float().cpu().numpy()) == 0  # nothing was launched
+
+
+def test_noalloc_split_k_after_a_copy_plan_on_the_shared_array():
+    """The strided large-M call writes its activation copy into the shared scratch; a split-K call straight after
+    it on the same stream must still find its tickets cleared and match the regular entry point."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import int4_b200
+    from int4_b200 import _lib
+
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(5)
+    w1 = (torch.randn(512, 2048, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+    w2 = (torch.randn(64, 65536, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+    q1, q2 = int4_b200.quantize_int4(w1, 128), int4_b200.quantize_int4(w2, 128)
+    x1 = torch.randn(100, 4096, generator=gen).to(torch.bfloat16).to(dev)[:, ::2]
+    x2 = torch.randn(1, 65536, generator=gen).to(torch.bfloat16).to(dev)
+    refs = []
+    for x, q in ((x1, q1), (x2, q2)):
+        need = L.i4b_w4a16_workspace_size(x.shape[0], q[0].shape[1], x.shape[1], 128)
+        ws = torch.zeros(max(need, 1), dtype=torch.uint8, device=dev)
+        y = torch.empty(x.shape[0], q[0].shape[1], dtype=torch.bfloat16, device=dev)
+        assert _call(L, "i4b_w4a16_matmul", x, *q, y, ws) == 0
+        refs.append(y)
+    for _ in range(2):
+        outs = []
+        for x, q in ((x1, q1), (x2, q2)):  # back to back, one stream, no synchronisation in between
+            y = torch.full((x.shape[0], q[0].shape[1]), float("nan"), dtype=torch.bfloat16, device=dev)
+            assert _call(L, "i4b_w4a16_matmul_noalloc", x, *q, y) == 0
+            outs.append(y)
+        torch.cuda.synchronize()
+        for y, r in zip(outs, refs):
+            assert _rel_fro(y, r) < FRO_TOL
+            assert torch.equal(y, r)
+    assert _lib.device_error_flags(0, clear=True) == 0
+
+
+def test_noalloc_reports_a_bad_argument_before_the_scratch_limit():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from int4_b200 import _lib
+
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(torch.device("cuda", 0)).cuda_stream
+    M, N, K = 4096, 256, 8192  # would exceed the scratch, but the dtype code is invalid
+    st = L.i4b_w4a16_matmul_noalloc(None, 7, M, K, K, 1, None, N, N, None, None, N, 128, None, N, stream)
+    assert st == 1  # I4B_ERR_INVALID_ARG
