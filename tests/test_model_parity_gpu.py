@@ -1,0 +1,176 @@
+"""Model-level parity at the real Llama-3.2-1B shape against the reference's fake-quant W4 path.
+
+The north star's model bar: logits within 2e-2 max-abs of the reference W4
+path.  The reference measures decode through transformers' Llama with a
+``StaticCache`` -- a cached single-token step (``benchmarks/eval_llama.py:121-143``)
+-- and quality as the perplexity of the W4 model next to the fake-quant model
+(``eval_ppl``, ``benchmarks/eval_llama.py:77-117``; ``quantize_model_linears(...,
+fake=True)``, ``int4_triton/qlinear.py:54-68``).  Both are restated here:
+
+* the reference model is transformers' ``LlamaForCausalLM`` (16 layers, hidden
+  2048, 32 / 8 heads, intermediate 8192, vocab 128256, tied embeddings,
+  random init) whose decoder linears are fake-quantized by
+  ``oracle/int4_torch.py`` -- the test oracle, not this library's kernels;
+* decode: the same prompt is prefilled into a ``StaticCache`` and into
+  ``LlamaTP``'s cache, then every cached step of ``LlamaTP`` (persistent
+  one-launch decode and per-launch decode) is compared with the reference's
+  cached step on the same token, batch 1, 2 and 4;
+* config 4's quality check: mean next-token NLL over 8 seeded random
+  2048-token sequences, W4 prompt pass (tcgen05 GEMM) against the fake-quant
+  model's forward, as ``eval_ppl`` computes it.  Random tokens on a random-init
+  model stand in for WikiText-2 and the checkpoint, which are not available.
+
+The W4 weights are quantized by the library (``quantize_int4``); the test first
+checks that they are bit-identical to the oracle's on the device, so the
+reference stays independent of the code under test.
+"""
+from __future__ import annotations
+
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2  # max-abs, north star
+NLL_TOL = 1e-3    # |mean NLL (W4) - mean NLL (fake-quant reference)|, nats per token
+GROUP = 128
+
+
+def _llama_cfg(layers=16, vocab=128256):
+    from transformers import LlamaConfig
+
+    return LlamaConfig(vocab_size=vocab, hidden_size=2048, intermediate_size=8192, num_hidden_layers=layers,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=64, max_position_embeddings=131072,
+                       rms_norm_eps=1e-5, tie_word_embeddings=True, rope_theta=500000.0,
+                       rope_scaling={"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                                     "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
+
+
+@pytest.fixture(scope="module")
+def llama1b(cuda_device):
+    """(hf bf16 model, fake-quant reference model built by the test oracle)."""
+    from transformers import LlamaForCausalLM
+
+    from oracle import int4_torch as ot
+
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        hf = LlamaForCausalLM(_llama_cfg())
+    hf = hf.to(torch.bfloat16).eval()
+    fake = copy.deepcopy(hf)
+    ot.fake_quantize_model_(fake, GROUP, skip=("lm_head",))
+    yield hf, fake
+    del hf, fake
+    torch.cuda.empty_cache()
+
+
+def _ids(B, S, seed, vocab=128256):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, vocab, (B, S), generator=g).cuda()
+
+
+def _bits(t):
+    """Raw bits of a quantize triple element (int32 words, fp16 as int16) as a numpy array."""
+    t = t.detach().cpu()
+    return t.view(torch.int16).numpy() if t.dtype == torch.float16 else t.numpy()
+
+
+@torch.no_grad()
+def test_oracle_weights_are_the_library_weights_on_device(llama1b):
+    """The torch oracle on the GPU equals the numpy oracle, and the library's quantizer equals both."""
+    import int4_b200
+    from oracle import int4_oracle as orc
+    from oracle import int4_torch as ot
+
+    hf, _ = llama1b
+    for w in (hf.model.layers[0].self_attn.k_proj.weight, hf.model.layers[5].mlp.down_proj.weight):
+        got = ot.quantize_int4(w, GROUP)
+        want = orc.quantize_int4(w.cpu().view(torch.int16).numpy().view(np.uint16), GROUP, "bfloat16")
+        lib = int4_b200.quantize_int4(w.contiguous(), GROUP)
+        for a, b, c in zip(got, want, lib):
+            np.testing.assert_array_equal(_bits(a), b.view(np.int16) if b.dtype == np.float16 else b)
+            assert torch.equal(a, c)
+
+
+def _reference_steps(fake, ids, steps):
+    """The reference's decode: prompt into a StaticCache, then cached single-token steps on the greedy token.
+
+    Returns the tokens fed at each step and the reference logits [B, 1, V] (fp32) of each step."""
+    from transformers import StaticCache
+
+    B, S = ids.shape
+    cache = StaticCache(config=fake.config, max_cache_len=S + steps + 8)
+    out = fake(input_ids=ids, cache_position=torch.arange(S, device=ids.device), past_key_values=cache, use_cache=True)
+    tok = out.logits[:, -1:].argmax(-1)
+    toks, logits = [], []
+    for i in range(steps):
+        pos = torch.tensor([S + i], device=ids.device)
+        lg = fake(input_ids=tok, cache_position=pos, position_ids=pos[None].expand(B, 1), past_key_values=cache,
+                  use_cache=True).logits[:, -1:].float()
+        toks.append(tok)
+        logits.append(lg)
+        tok = lg[:, -1:].argmax(-1)
+    return toks, logits
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("B", [1, 2, 4])
+def test_w4_decode_logits_within_2e2_of_fake_quant_static_cache(llama1b, B):
+    from int4_b200 import _lib
+    from int4_b200.decode import LlamaTP
+
+    hf, fake = llama1b
+    S, steps = 300, 4
+    ids = _ids(B, S, 40 + B)
+    toks, ref = _reference_steps(fake, ids, steps)
+    errs = {}
+    for label, persistent in (("persistent", True), ("per-launch", False)):
+        m = LlamaTP(hf, w4=True, group_size=GROUP, max_seq=S + steps + 8, max_batch=B, persistent=persistent)
+        assert (m.persistent is not None) == persistent
+        m.prefill(ids)
+        e = []
+        for i in range(steps):
+            pos = torch.tensor([S + i], device="cuda")
+            got = m.decode_step(toks[i].contiguous(), pos).float()
+            e.append((got - ref[i]).abs().max().item())
+        errs[label] = e
+        m.close()
+        del m
+    print(f"B={B} max-abs logit error per step vs the fake-quant StaticCache step: {errs}")
+    for label, e in errs.items():
+        assert max(e) <= LOGIT_TOL, (label, e)
+    assert _lib.device_error_flags(0) == 0
+
+
+@torch.no_grad()
+def test_config4_mean_nll_matches_fake_quant_reference(llama1b):
+    """BASELINE config 4's quality check: mean token NLL over 8 random 2048-token sequences (W4 vs fake-quant)."""
+    import torch.nn.functional as F
+
+    from int4_b200 import _lib
+    from int4_b200.decode import LlamaTP
+
+    hf, fake = llama1b
+    seqlen, n = 2048, 8
+    ids = _ids(n, seqlen, 2024)
+    m = LlamaTP(hf, w4=True, group_size=GROUP, max_seq=seqlen, max_batch=1, persistent=False)
+    nll_w4, nll_ref = 0.0, 0.0
+    max_logit_err = 0.0
+    for i in range(n):
+        x = ids[i:i + 1]
+        lw = m.prefill(x, all_logits=True)[0, :-1].float()
+        lr = fake(x, use_cache=False).logits[0, :-1].float()
+        nll_w4 += F.cross_entropy(lw, x[0, 1:], reduction="sum").item()
+        nll_ref += F.cross_entropy(lr, x[0, 1:], reduction="sum").item()
+        max_logit_err = max(max_logit_err, (lw - lr).abs().max().item())
+        del lw, lr
+    m.close()
+    tokens = n * (seqlen - 1)
+    nll_w4, nll_ref = nll_w4 / tokens, nll_ref / tokens
+    print(f"mean NLL: W4 {nll_w4:.6f}, fake-quant reference {nll_ref:.6f}, |diff| {abs(nll_w4 - nll_ref):.2e}; "
+          f"max-abs logit difference over all prompt positions {max_logit_err:.3e}")
+    assert abs(nll_w4 - nll_ref) <= NLL_TOL
+    assert _lib.device_error_flags(0) == 0

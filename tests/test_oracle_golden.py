@@ -88,3 +88,65 @@ def test_oracle_gemm_matches_reference_expression(name, golden_arrays):
     ref = golden_arrays[f"{name}/y_ref"]
     # Same fp32 products; only the BLAS summation order differs from torch's.
     assert orc.rel_fro_error(y, ref) < 1e-6
+
+
+# ----------------------------------------------------------------------------- the torch restatement
+
+
+def _as_torch(a, dt):
+    import torch
+
+    if dt == "bfloat16":
+        return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+    if dt == "float16":
+        return torch.from_numpy(a.view(np.float16).copy())
+    return torch.from_numpy(np.ascontiguousarray(a))
+
+
+@pytest.mark.parametrize("name", cases.SMALL_QUANT)
+def test_torch_oracle_small_bit_exact(name, golden_arrays):
+    """oracle/int4_torch.py gives the reference-generated bits on the small fixtures."""
+    import torch
+
+    from oracle import int4_torch as ot
+
+    shape, dt, g, _seed, _frac = cases.QUANT_CASES[name]
+    w = _as_torch(golden_arrays[f"{name}/w"], dt)
+    qw, s, z = ot.quantize_int4(w, g)
+    np.testing.assert_array_equal(qw.numpy(), golden_arrays[f"{name}/qweight"])
+    np.testing.assert_array_equal(s.view(torch.int16).numpy().view(np.uint16), golden_arrays[f"{name}/scales"])
+    np.testing.assert_array_equal(z.view(torch.int16).numpy().view(np.uint16), golden_arrays[f"{name}/zeros"])
+    for odt, tdt in (("float32", torch.float32), ("float16", torch.float16), ("bfloat16", torch.bfloat16)):
+        d = ot.dequantize_int4(qw, s, z, tdt)
+        got = d.numpy() if odt == "float32" else d.view(torch.int16).numpy().view(np.uint16)
+        np.testing.assert_array_equal(got, golden_arrays[f"{name}/dequant_{odt}"], err_msg=f"dequant {odt}")
+
+
+@pytest.mark.parametrize("name", ["cfg1_2048x2048_g128_bfloat16", "block_gate_proj_g128", "sweep_down_proj_g32"])
+def test_torch_oracle_full_size_hashes(name, golden_meta):
+    from oracle import int4_torch as ot
+
+    shape, dt, g, _seed, _frac = cases.QUANT_CASES[name]
+    qw, s, z = ot.quantize_int4(cases.quant_input(name), g)
+    m = golden_meta["quant"][name]
+    assert cases.sha256(qw.numpy()) == m["qweight_sha256"]
+    assert cases.sha256(s.numpy()) == m["scales_sha256"]
+    assert cases.sha256(z.numpy()) == m["zeros_sha256"]
+
+
+def test_torch_oracle_fake_quantizes_the_selected_linears():
+    """fake_quantize_model_ replaces every decoder linear's weight by its INT4 round trip and skips lm_head."""
+    import torch
+
+    from oracle import int4_torch as ot
+
+    torch.manual_seed(0)
+    model = torch.nn.ModuleDict({"mlp": torch.nn.Linear(256, 64, bias=False), "lm_head": torch.nn.Linear(256, 32)})
+    model = model.to(torch.bfloat16)
+    before = {k: v.weight.detach().clone() for k, v in model.items()}
+    ot.fake_quantize_model_(model, 128)
+    w = before["mlp"]
+    qw, s, z = orc.quantize_int4(w.view(torch.int16).numpy().view(np.uint16), 128, "bfloat16")
+    want = orc.dequantize_int4(qw, s, z, "bfloat16")
+    np.testing.assert_array_equal(model["mlp"].weight.view(torch.int16).numpy().view(np.uint16), want)
+    assert torch.equal(model["lm_head"].weight, before["lm_head"])
