@@ -142,6 +142,14 @@ void i4b_set_pdl(int enable);
  * (which autotunes, int4_triton/gemm.py:51-56). */
 void i4b_set_skinny_override(int wn, int wk, int splits);
 
+/* Tuning hook for W4 M <= 8: kernel 0 = automatic (the register-streaming GEMV where it applies), 1 = the
+ * register-streaming GEMV, 2 = the shared-memory-staged small-M kernel, 3 = the staged kernel or, for very
+ * wide N, the streaming lm_head kernel (the choice before the register-streaming GEMV existed), 4 / 5 = the
+ * register-streaming GEMV with 4 / 8 steps of weights in flight per lane; wk and splits
+ * set the register-streaming GEMV's warps along K per CTA and its cluster split (0 = automatic).
+ * Process-wide.  No counterpart in the reference. */
+void i4b_set_w4_kernel_override(int kernel, int wk, int splits);
+
 /* Bytes of the scratch array built into the library for i4b_w4a16_matmul_noalloc. */
 #define I4B_NOALLOC_SCRATCH_BYTES (16u << 20)
 

@@ -150,6 +150,8 @@ void i4b_set_skinny_override(int wn, int wk, int splits) {
 
 void i4b_set_pdl(int enable) { g_pdl = enable != 0; }
 
+void i4b_set_w4_kernel_override(int kernel, int wk, int splits) { set_w4_kernel_override(kernel, wk, splits); }
+
 void i4b_set_gemm_override(int tile, int splits) { set_tc_override(tile, splits); }
 
 int i4b_quantize_int4(const void* w, int w_dtype, int64_t N, int64_t K, int64_t stride_wn, int64_t stride_wk,

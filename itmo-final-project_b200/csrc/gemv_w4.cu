@@ -74,6 +74,9 @@ struct W4SArgs {
   uint8_t* ar_buf[kArMaxRanks];
   int64_t ar_cap;
   int ar_world, ar_rank;
+  // w4_gemv_kernel: WN x WK warps per CTA (columns x K), KW k per warp, scale / zero rows staged per CTA
+  int WN, WK, KW;
+  int sz_rows;
 };
 
 enum { kProPlain = 0, kProRmsNorm = 1, kProSwiGlu = 2 };
@@ -188,6 +191,14 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
+// Packed weights are read once per call: 128-bit loads that do not allocate in L1.
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
 __device__ __forceinline__ void cp16(uint32_t dst, const void* src, uint32_t bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
@@ -213,6 +224,128 @@ __device__ __forceinline__ void cp_async_wait_upto(int pending) {
 }
 
 }  // namespace
+
+// Stages the activations of token rows 0..M-1, k in [k0, k0 + 8*nreal), in shared memory at s_x (row pitch
+// a.xpitch), each 8-k chunk permuted to the k order of the A fragments; chunks nreal..nch-1 are zero (padding).
+// With a prologue the activations are derived from the previous step's tensors (RMSNorm of x + delta, with
+// the full-row statistics computed here; or SwiGLU of a gate | up row).  s_inv: shared [32] floats.  All
+// threads of the CTA take part; the caller synchronises before reading.
+template <bool F16, int PRO>
+__device__ __forceinline__ void stage_activations(const W4SArgs& a, uint32_t s_x, int k0, int nch, int nreal,
+                                                  float* s_inv) {
+  constexpr int XB = 4;  // chunks per thread in flight
+  const int M = a.M;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nthr = blockDim.x, nwarps = nthr >> 5;
+  const int total = M * nch;
+  if constexpr (PRO == kProRmsNorm) {
+    // Full-row statistics of h' = bf16(h + delta) for every token (warp t % warps owns token t); CTA (0, 0)
+    // also writes h' to resid_out.  Rows are contiguous with K % 8 == 0 and 16-byte alignment.
+    const bool writer = a.resid_out && blockIdx.x == 0 && blockIdx.y == 0;
+    for (int t = warp; t < M; t += nwarps) {
+      const uint16_t* hr = a.x + int64_t(t) * a.sxm;
+      const uint16_t* dr = a.delta ? a.delta + int64_t(t) * a.sxm : nullptr;
+      float ss = 0.0f;
+      for (int c = lane * 8; c < a.K; c += 256) {
+        uint4 hv = __ldg(reinterpret_cast<const uint4*>(hr + c));
+        if (dr) {
+          const uint4 dv = __ldg(reinterpret_cast<const uint4*>(dr + c));
+          const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
+          const uint32_t* da = reinterpret_cast<const uint32_t*>(&dv);
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[i] = bfr(bfv(ha[i] & 0xFFFFu) + bfv(da[i] & 0xFFFFu)) |
+                   (bfr(bfv(ha[i] >> 16) + bfv(da[i] >> 16)) << 16);
+          hv = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        if (writer) *reinterpret_cast<uint4*>(a.resid_out + int64_t(t) * a.sxm + c) = hv;
+        const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float lo = bfv(ha[i] & 0xFFFFu), hi = bfv(ha[i] >> 16);
+          ss = fmaf(lo, lo, ss);
+          ss = fmaf(hi, hi, ss);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+      if (lane == 0) s_inv[t] = rsqrtf(ss / float(a.K) + a.eps);
+    }
+    __syncthreads();
+  }
+  for (int base = 0; base < total; base += XB * nthr) {
+    uint4 v[XB];
+#pragma unroll
+    for (int j = 0; j < XB; ++j) {
+      const int idx = base + j * nthr + tid;
+      const int t = idx / nch, ch = idx - t * nch;
+      v[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (idx < total && ch < nreal) {
+        const uint16_t* p = a.x + int64_t(t) * a.sxm + int64_t(k0 + 8 * ch) * a.sxk;
+        if constexpr (PRO == kProRmsNorm) {
+          // x = bf16(w * bf16(h' * inv)),  h' = bf16(h + delta)        (LlamaRMSNorm after the residual add)
+          const uint4 hv = __ldg(reinterpret_cast<const uint4*>(p));
+          const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0 + 8 * ch));
+          uint4 dv = make_uint4(0u, 0u, 0u, 0u);
+          if (a.delta) dv = __ldg(reinterpret_cast<const uint4*>(a.delta + int64_t(t) * a.sxm + k0 + 8 * ch));
+          const float inv = s_inv[t];
+          const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
+          const uint32_t* da = reinterpret_cast<const uint32_t*>(&dv);
+          const uint32_t* wa = reinterpret_cast<const uint32_t*>(&wv);
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t lo = ha[i] & 0xFFFFu, hi = ha[i] >> 16;
+            if (a.delta) {
+              lo = bfr(bfv(lo) + bfv(da[i] & 0xFFFFu));
+              hi = bfr(bfv(hi) + bfv(da[i] >> 16));
+            }
+            o[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(lo) * inv))) |
+                   (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(hi) * inv))) << 16);
+          }
+          v[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        } else if constexpr (PRO == kProSwiGlu) {
+          // x = bf16(bf16(silu(g)) * u),  g = row[k], u = row[K + k]                       (LlamaMLP)
+          const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p));
+          const uint4 uv = __ldg(reinterpret_cast<const uint4*>(p + a.K));
+          const uint32_t* ga = reinterpret_cast<const uint32_t*>(&gv);
+          const uint32_t* ua = reinterpret_cast<const uint32_t*>(&uv);
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float g0 = bfv(ga[i] & 0xFFFFu), g1 = bfv(ga[i] >> 16);
+            const float s0 = bfv(bfr(g0 / (1.0f + expf(-g0)))), s1 = bfv(bfr(g1 / (1.0f + expf(-g1))));
+            o[i] = bfr(s0 * bfv(ua[i] & 0xFFFFu)) | (bfr(s1 * bfv(ua[i] >> 16)) << 16);
+          }
+          v[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        } else if (a.vec_x) {
+          v[j] = __ldg(reinterpret_cast<const uint4*>(p));
+        } else {
+          uint16_t e[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) e[q] = __ldg(p + q * a.sxk);
+          v[j] = make_uint4(uint32_t(e[0]) | (uint32_t(e[1]) << 16), uint32_t(e[2]) | (uint32_t(e[3]) << 16),
+                            uint32_t(e[4]) | (uint32_t(e[5]) << 16), uint32_t(e[6]) | (uint32_t(e[7]) << 16));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < XB; ++j) {
+      const int idx = base + j * nthr + tid;
+      if (base + j * nthr >= total) break;  // uniform over the CTA
+      const int t = idx / nch, ch = idx - t * nch;
+      const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      if (idx < total) {
+        // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
+                     "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
+                     "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
+                     : "memory");
+      }
+    }
+  }
+}
 
 // Shared memory: weights [step][warp][lane] x 16 B | scales+zeros [segment][warp][r] x 16 B (s0..s3, z0..z3) |
 // activations [token][k/8] x 16 B (pre-permuted) | partial sums [token][128] fp32.  The K range of a CTA is
@@ -311,118 +444,8 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
   }
   {
     // Stage x in shared memory, each 8-k chunk permuted to the k order of the A fragments.
-    constexpr int XB = 4;  // chunks per thread in flight
-    const int nch = nstages * SPST * 4;  // chunks of 8 k, padded
-    const int nreal = a.KC / 8;
-    const int total = M * nch;
     __shared__ float s_inv[32];
-    if constexpr (PRO == kProRmsNorm) {
-      // Full-row statistics of h' = bf16(h + delta) for every token (warp t % 4 owns token t); CTA (0, 0)
-      // also writes h' to resid_out.  Rows are contiguous with K % 8 == 0 and 16-byte alignment.
-      const bool writer = a.resid_out && blockIdx.x == 0 && blockIdx.y == 0;
-      for (int t = warp; t < M; t += 4) {
-        const uint16_t* hr = a.x + int64_t(t) * a.sxm;
-        const uint16_t* dr = a.delta ? a.delta + int64_t(t) * a.sxm : nullptr;
-        float ss = 0.0f;
-        for (int c = lane * 8; c < a.K; c += 256) {
-          uint4 hv = __ldg(reinterpret_cast<const uint4*>(hr + c));
-          if (dr) {
-            const uint4 dv = __ldg(reinterpret_cast<const uint4*>(dr + c));
-            const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
-            const uint32_t* da = reinterpret_cast<const uint32_t*>(&dv);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              o[i] = bfr(bfv(ha[i] & 0xFFFFu) + bfv(da[i] & 0xFFFFu)) |
-                     (bfr(bfv(ha[i] >> 16) + bfv(da[i] >> 16)) << 16);
-            hv = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-          if (writer) *reinterpret_cast<uint4*>(a.resid_out + int64_t(t) * a.sxm + c) = hv;
-          const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float lo = bfv(ha[i] & 0xFFFFu), hi = bfv(ha[i] >> 16);
-            ss = fmaf(lo, lo, ss);
-            ss = fmaf(hi, hi, ss);
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-        if (lane == 0) s_inv[t] = rsqrtf(ss / float(a.K) + a.eps);
-      }
-      __syncthreads();
-    }
-    for (int base = 0; base < total; base += XB * 128) {
-      uint4 v[XB];
-#pragma unroll
-      for (int j = 0; j < XB; ++j) {
-        const int idx = base + j * 128 + tid;
-        const int t = idx / nch, ch = idx - t * nch;
-        v[j] = make_uint4(0u, 0u, 0u, 0u);
-        if (idx < total && ch < nreal) {
-          const uint16_t* p = a.x + int64_t(t) * a.sxm + int64_t(k0 + 8 * ch) * a.sxk;
-          if constexpr (PRO == kProRmsNorm) {
-            // x = bf16(w * bf16(h' * inv)),  h' = bf16(h + delta)        (LlamaRMSNorm after the residual add)
-            const uint4 hv = __ldg(reinterpret_cast<const uint4*>(p));
-            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(a.norm_w + k0 + 8 * ch));
-            uint4 dv = make_uint4(0u, 0u, 0u, 0u);
-            if (a.delta) dv = __ldg(reinterpret_cast<const uint4*>(a.delta + int64_t(t) * a.sxm + k0 + 8 * ch));
-            const float inv = s_inv[t];
-            const uint32_t* ha = reinterpret_cast<const uint32_t*>(&hv);
-            const uint32_t* da = reinterpret_cast<const uint32_t*>(&dv);
-            const uint32_t* wa = reinterpret_cast<const uint32_t*>(&wv);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint32_t lo = ha[i] & 0xFFFFu, hi = ha[i] >> 16;
-              if (a.delta) {
-                lo = bfr(bfv(lo) + bfv(da[i] & 0xFFFFu));
-                hi = bfr(bfv(hi) + bfv(da[i] >> 16));
-              }
-              o[i] = bfr(bfv(wa[i] & 0xFFFFu) * bfv(bfr(bfv(lo) * inv))) |
-                     (bfr(bfv(wa[i] >> 16) * bfv(bfr(bfv(hi) * inv))) << 16);
-            }
-            v[j] = make_uint4(o[0], o[1], o[2], o[3]);
-          } else if constexpr (PRO == kProSwiGlu) {
-            // x = bf16(bf16(silu(g)) * u),  g = row[k], u = row[K + k]                       (LlamaMLP)
-            const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p));
-            const uint4 uv = __ldg(reinterpret_cast<const uint4*>(p + a.K));
-            const uint32_t* ga = reinterpret_cast<const uint32_t*>(&gv);
-            const uint32_t* ua = reinterpret_cast<const uint32_t*>(&uv);
-            uint32_t o[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float g0 = bfv(ga[i] & 0xFFFFu), g1 = bfv(ga[i] >> 16);
-              const float s0 = bfv(bfr(g0 / (1.0f + expf(-g0)))), s1 = bfv(bfr(g1 / (1.0f + expf(-g1))));
-              o[i] = bfr(s0 * bfv(ua[i] & 0xFFFFu)) | (bfr(s1 * bfv(ua[i] >> 16)) << 16);
-            }
-            v[j] = make_uint4(o[0], o[1], o[2], o[3]);
-          } else if (a.vec_x) {
-            v[j] = __ldg(reinterpret_cast<const uint4*>(p));
-          } else {
-            uint16_t e[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) e[q] = __ldg(p + q * a.sxk);
-            v[j] = make_uint4(uint32_t(e[0]) | (uint32_t(e[1]) << 16), uint32_t(e[2]) | (uint32_t(e[3]) << 16),
-                              uint32_t(e[4]) | (uint32_t(e[5]) << 16), uint32_t(e[6]) | (uint32_t(e[7]) << 16));
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < XB; ++j) {
-        const int idx = base + j * 128 + tid;
-        if (base + j * 128 >= total) break;  // uniform over the CTA
-        const int t = idx / nch, ch = idx - t * nch;
-        const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-        if (idx < total) {
-          // (x0,x4) (x1,x5) (x2,x6) (x3,x7): the nibble-pair order of the A fragments
-          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(s_x + t * a.xpitch + ch * 16),
-                       "r"(__byte_perm(u[0], u[2], 0x5410)), "r"(__byte_perm(u[0], u[2], 0x7632)),
-                       "r"(__byte_perm(u[1], u[3], 0x5410)), "r"(__byte_perm(u[1], u[3], 0x7632))
-                       : "memory");
-        }
-      }
-    }
+    stage_activations<F16, PRO>(a, s_x, k0, nstages * SPST * 4, a.KC / 8, s_inv);
   }
   __syncthreads();
 
@@ -802,11 +825,171 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
   cp_async_wait<0>();
 }
 
+// ------------------------------------------------------------------ decode GEMV, M <= 8, weights in registers
+
+// Register-streaming form of the M <= 8 path.  grid = (ceil(N / (32 WN)), S), cluster (1, S, 1) when S > 1;
+// CTA = WN x WK warps.  Warp (wn, wk) owns columns n0 + 32 wn .. + 31 and the k range
+// [k0 + wk KW, k0 + (wk + 1) KW) of its CTA's K slice [k0, k0 + KC), KC = K / S.  Each lane streams its packed
+// words straight into a ring of D registers with 128-bit loads that bypass L1 (lane (r, c) reads the words
+// of columns 4r..4r+3 at k8 row 4 step + c: 4 x 128 contiguous bytes per warp and step), so no copy through
+// shared memory and no barrier sits between the weight stream and the math.  The ring's first D steps are
+// requested before griddepcontrol.wait.  Scales / zeros of the CTA's columns and groups are staged once in
+// shared memory (cp.async), the activations once per CTA (stage_activations).  Dequant and MMA are those of
+// w4_skinny_kernel.  The WK warp partials of a column add in shared memory in warp order; the S CTAs of a
+// cluster then add through distributed shared memory in rank order: results are identical from run to run.
+template <bool F16, int SPS, int PRO, int D>
+__global__ void __launch_bounds__(256) w4_gemv_kernel(const W4SArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float s_inv[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wn = warp % a.WN, wk = warp / a.WN;
+  const int r = lane >> 2, c = lane & 3;
+  const int BN = 32 * a.WN;
+  const int M = a.M;
+  const int64_t n0 = int64_t(blockIdx.x) * BN;
+  const int k0 = int(blockIdx.y) * a.KC;
+  const int kw0 = wk * a.KW;  // warp's first k inside the CTA slice
+  const int nsteps = a.KW / 32;
+  const int64_t n_lane = n0 + wn * 32 + 4 * r;
+  const bool n_in = n_lane < a.N;  // N % 8 == 0: a lane's 4 columns are all in or all out
+
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t s_sz = s_base + a.off_sz;  // scales [rows][BN] fp16, then zeros [rows][BN] fp16
+  const uint32_t s_x = s_base + a.off_x;
+  float* red = reinterpret_cast<float*>(smem + a.off_part);  // [WK][M][BN]
+
+  // ---- weights: the first D steps of this lane's stream, independent of the previous kernel
+  const uint32_t* wsrc = a.qw + int64_t((k0 + kw0) / 8 + c) * a.sqk + (n_in ? n_lane : 0);
+  const int64_t wstep = 4 * a.sqk;
+  uint4 wr[D];
+#pragma unroll
+  for (int i = 0; i < D; ++i)
+    wr[i] = (i < nsteps && n_in) ? ld_stream_u4(wsrc + i * wstep) : make_uint4(0u, 0u, 0u, 0u);
+  const int g_first = k0 / a.G;
+  // ---- scales / zeros of the CTA's groups and columns: 16-byte chunks of 8 columns
+  {
+    const int rows = min(a.sz_rows, a.K / a.G - g_first);  // group rows of this CTA's K slice
+    const int cpr = BN / 8;                                  // chunks per row
+    const int nchunk = 2 * a.sz_rows * cpr;
+    for (int i = tid; i < nchunk; i += blockDim.x) {
+      const int arr = i / (a.sz_rows * cpr), rem = i - arr * (a.sz_rows * cpr);
+      const int row = rem / cpr, ch = rem - row * cpr;
+      if (row >= rows) continue;
+      const int64_t n = n0 + 8 * ch;
+      const uint16_t* src = (arr ? a.zr : a.sc) + int64_t(g_first + row) * a.ssg + (n < a.N ? n : 0);
+      cp16(s_sz + uint32_t(arr * a.sz_rows * BN * 2 + row * BN * 2 + ch * 16), src, n < a.N ? 16u : 0u);
+    }
+    cp_async_commit();
+  }
+  // ---- activations: produced by the previous kernel of the stream
+  if (a.pdl) {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+  stage_activations<F16, PRO>(a, s_x, k0, a.KC / 8, a.KC / 8, s_inv);
+  cp_async_wait<0>();
+  __syncthreads();
+
+  const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
+  const uint32_t xl = s_x + min(r, M - 1) * a.xpitch + (kw0 / 8 + c) * 16;
+  const int L = 32 * SPS;
+  const uint32_t szl = s_sz + uint32_t((wn * 32 + 4 * r) * 2);
+  float acc[2][4], acc1[2][4];  // the k16 halves of each step accumulate separately (two MMA chains)
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[t][e] = acc1[t][e] = 0.0f;
+  DqParams dp[4];
+#pragma unroll 1
+  for (int base = 0; base < nsteps; base += D) {
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      const int step = base + i;
+      if (step >= nsteps) break;  // uniform over the CTA
+      if (step % SPS == 0) {      // a new segment: scale and zero of columns 4r .. 4r + 3
+        const int seg = (k0 + kw0) / L + step / SPS;
+        const int row = (a.gpl_shift >= 0 ? (seg >> a.gpl_shift) : seg / a.gpl) - g_first;
+        uint32_t sv0, sv1, zv0, zv1;
+        const uint32_t sa = szl + uint32_t(row * BN * 2), za = sa + uint32_t(a.sz_rows * BN * 2);
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(sv0), "=r"(sv1) : "r"(sa));
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(zv0), "=r"(zv1) : "r"(za));
+        dp[0] = dq_params<F16>(uint16_t(sv0 & 0xFFFFu), uint16_t(zv0 & 0xFFFFu));
+        dp[1] = dq_params<F16>(uint16_t(sv0 >> 16), uint16_t(zv0 >> 16));
+        dp[2] = dq_params<F16>(uint16_t(sv1 & 0xFFFFu), uint16_t(zv1 & 0xFFFFu));
+        dp[3] = dq_params<F16>(uint16_t(sv1 >> 16), uint16_t(zv1 >> 16));
+      }
+      const uint32_t wd[4] = {wr[i].x, wr[i].y, wr[i].z, wr[i].w};
+      if (step + D < nsteps && n_in) wr[i] = ld_stream_u4(wsrc + (step + D) * wstep);  // refill the slot
+      uint32_t af[2][2][4];  // [row tile][k16 half][reg]: the dequantized weights, rounded as the reference does
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          af[t][h][0] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * h, magic), dp[2 * t]);
+          af[t][h][1] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * h, magic), dp[2 * t + 1]);
+          af[t][h][2] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * h + 1, magic), dp[2 * t]);
+          af[t][h][3] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * h + 1, magic), dp[2 * t + 1]);
+        }
+      const uint4 b = lds128(xl + step * 64);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        mma_16816<F16>(acc[t], af[t][0], b.x, b.y);
+        mma_16816<F16>(acc1[t], af[t][1], b.z, b.w);
+      }
+    }
+  }
+  // ---- this warp's partials: acc[t][e] is (token 2c + (e & 1), column 32 wn + 4r + 2t + (e >> 1))
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int tok = 2 * c + (e & 1);
+      if (tok < M) red[(wk * M + tok) * BN + wn * 32 + 4 * r + 2 * t + (e >> 1)] = acc[t][e] + acc1[t][e];
+    }
+  __syncthreads();
+  const int nout = M * BN;
+  for (int idx = tid; idx < nout; idx += blockDim.x) {  // sum over the K warps, in warp order
+    float v = red[idx];
+    for (int q = 1; q < a.WK; ++q) v += red[q * nout + idx];
+    if (a.S == 1) {
+      const int tok = idx / BN;
+      const int64_t n = n0 + (idx - tok * BN);
+      if (n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
+    } else {
+      red[idx] = v;
+    }
+  }
+  if (a.S == 1) return;
+  // Cluster of S CTAs along K: rank q adds outputs q*blockDim + tid, ... over all ranks, in rank order.
+  cluster_sync();
+  const uint32_t rank = cluster_ctarank();
+  for (int idx = int(rank) * blockDim.x + tid; idx < nout; idx += a.S * blockDim.x) {
+    const uint32_t addr = smem_u32(red + idx);
+    float t[8];  // all S (<= 8) remote loads in flight, then added in rank order
+#pragma unroll
+    for (int q = 0; q < 8; ++q) t[q] = q < a.S ? ld_shared_cluster_f32(mapa_shared(addr, uint32_t(q))) : 0.0f;
+    float v = t[0];
+#pragma unroll
+    for (int q = 1; q < 8; ++q)
+      if (q < a.S) v += t[q];
+    const int tok = idx / BN;
+    const int64_t n = n0 + (idx - tok * BN);
+    if (n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
+  }
+  cluster_sync();  // no CTA leaves while others may still read its shared memory
+}
+
 // ------------------------------------------------------------------ planning
 
 static int g_w4_ovr_s = 0;
+static int g_w4_ovr_kernel = 0, g_w4_ovr_wk = 0, g_w4_ovr_gs = 0;
 
 void set_w4_split_override(int splits) { g_w4_ovr_s = splits; }
+void set_w4_kernel_override(int kernel, int wk, int splits) {
+  g_w4_ovr_kernel = kernel;
+  g_w4_ovr_wk = wk;
+  g_w4_ovr_gs = splits;
+}
 
 static int gcd_i(int a, int b) {
   while (b) {
@@ -957,6 +1140,108 @@ static cudaError_t launch_stream(bool f16, const W4SArgs& a, int sps, int num_sm
 #undef I4B_ST
 }
 
+// ---- register-streaming GEMV (M <= 8): plan and launch
+
+struct W4GPlan {
+  int WN, WK, S, KC, KW, sz_rows, D;
+  size_t smem;
+  bool ok;
+};
+
+// Shared memory of one CTA: scales + zeros [2][rows][32 WN] fp16 | activations [M][pitch] | partials [WK][M][32 WN].
+static size_t w4g_smem(int M, int WN, int WK, int KC, int sz_rows, int* xpitch, int* off_x, int* off_part) {
+  const int BN = 32 * WN;
+  const size_t sz = size_t(2) * sz_rows * BN * 2;
+  *xpitch = (KC / 8) % 8 == 0 ? KC * 2 + 64 : KC * 2;  // token rows 4 mod 8 16-byte units apart
+  *off_x = int((sz + 127) / 128 * 128);
+  *off_part = int((size_t(*off_x) + size_t(M) * *xpitch + 15) / 16 * 16);
+  return size_t(*off_part) + size_t(WK) * M * BN * 4;
+}
+
+// K is cut into segments of L = 32 * gcd(G / 32, 8) k; a warp owns KW = K / (S WK) consecutive k, a whole number
+// of segments.  The CTA has WK = 8 warps along K (fewer when K holds fewer segments); the cluster split S is the
+// smallest that gives every SM a CTA, as long as a warp keeps at least one segment.
+static W4GPlan plan_w4_gemv(int64_t M, int64_t N, int64_t K, int G, int sms) {
+  W4GPlan p{};
+  const int SPS = gcd_i(G / 32, 8);
+  const int64_t L = 32 * SPS;
+  const int64_t units = K / L;
+  const int64_t ncg = cdiv(N, 32);
+  p.WN = 1;
+  int WK = 8;
+  while (WK > 1 && units % WK) WK >>= 1;
+  if (g_w4_ovr_wk > 0 && g_w4_ovr_wk <= 8 && units % g_w4_ovr_wk == 0) WK = g_w4_ovr_wk;
+  int S = 1;
+  while (S < 8 && ncg * S < sms && units % (int64_t(2 * S) * WK) == 0) S *= 2;
+  if (g_w4_ovr_gs > 0 && g_w4_ovr_gs <= 8 && units % (int64_t(g_w4_ovr_gs) * WK) == 0) S = g_w4_ovr_gs;
+  p.WK = WK;
+  p.S = S;
+  p.KC = int(K / S);
+  p.KW = p.KC / WK;
+  p.sz_rows = p.KC >= G ? p.KC / G + 1 : 2;  // groups a K slice can touch
+  p.D = p.KW / 32 >= 8 ? 8 : 4;
+  if (g_w4_ovr_kernel == 4) p.D = 4;
+  if (g_w4_ovr_kernel == 5) p.D = 8;
+  int xp, ox, op;
+  p.smem = w4g_smem(int(M), p.WN, p.WK, p.KC, p.sz_rows, &xp, &ox, &op);
+  p.ok = M <= 8 && units % (int64_t(S) * WK) == 0 && p.smem <= 200 * 1024 && K <= INT32_MAX;
+  return p;
+}
+
+template <bool F16, int SPS, int PRO, int D>
+static cudaError_t launch_gemv_impl(const W4SArgs& a, const W4GPlan& p, cudaStream_t stream) {
+  auto kern = w4_gemv_kernel<F16, SPS, PRO, D>;
+  if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), p.smem)) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(cdiv(a.N, 32 * p.WN)), unsigned(p.S));
+  cfg.blockDim = dim3(unsigned(32 * p.WN * p.WK));
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (p.S > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = unsigned(p.S);
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (a.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <bool F16, int PRO, int D>
+static cudaError_t launch_gemv_sps(const W4SArgs& a, const W4GPlan& p, int sps, cudaStream_t stream) {
+  switch (sps) {
+    case 1: return launch_gemv_impl<F16, 1, PRO, D>(a, p, stream);
+    case 2: return launch_gemv_impl<F16, 2, PRO, D>(a, p, stream);
+    case 4: return launch_gemv_impl<F16, 4, PRO, D>(a, p, stream);
+    default: return launch_gemv_impl<F16, 8, PRO, D>(a, p, stream);
+  }
+}
+
+template <int D>
+static cudaError_t launch_gemv_d(bool f16, const W4SArgs& a, const W4GPlan& p, int sps, cudaStream_t stream) {
+  if (f16) return launch_gemv_sps<true, kProPlain, D>(a, p, sps, stream);
+  if (a.pro == kProRmsNorm) return launch_gemv_sps<false, kProRmsNorm, D>(a, p, sps, stream);
+  if (a.pro == kProSwiGlu) return launch_gemv_sps<false, kProSwiGlu, D>(a, p, sps, stream);
+  return launch_gemv_sps<false, kProPlain, D>(a, p, sps, stream);
+}
+
+// The register-streaming kernel takes M <= 8 without the tensor-parallel epilogue, with 16-byte aligned packed
+// words and scale / zero rows (N % 8 == 0).
+static bool gemv_eligible(const W4SArgs& a, const W4GPlan& p) {
+  const auto addr = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr); };
+  return p.ok && a.M <= 8 && a.ar_world <= 1 && a.N % 8 == 0 && a.vec_w && addr(a.sc) % 16 == 0 &&
+         addr(a.zr) % 16 == 0 && a.ssg % 8 == 0;
+}
+
 cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
                       int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
                       int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream, const W4Prologue* pro,
@@ -1008,7 +1293,27 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   }
   int sms = 0, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (sms > 0 && a.ar_world <= 1 && stream_eligible(a, p, sms)) return launch_stream(f16, a, p.SPS, sms, stream);
+  // kernel choice for M <= 8: the register-streaming GEMV, unless the tuning hook asks for another one
+  if (sms > 0 && g_w4_ovr_kernel != 2 && g_w4_ovr_kernel != 3) {
+    const W4GPlan gp = plan_w4_gemv(M, N, K, G, sms);
+    if (gemv_eligible(a, gp)) {
+      a.WN = gp.WN;
+      a.WK = gp.WK;
+      a.KW = gp.KW;
+      a.KC = gp.KC;
+      a.S = gp.S;
+      a.sz_rows = gp.sz_rows;
+      int xp, ox, op;
+      w4g_smem(a.M, gp.WN, gp.WK, gp.KC, gp.sz_rows, &xp, &ox, &op);
+      a.xpitch = xp;
+      a.off_sz = 0;
+      a.off_x = ox;
+      a.off_part = op;
+      return gp.D == 8 ? launch_gemv_d<8>(f16, a, gp, p.SPS, stream) : launch_gemv_d<4>(f16, a, gp, p.SPS, stream);
+    }
+  }
+  if (sms > 0 && a.ar_world <= 1 && g_w4_ovr_kernel != 2 && stream_eligible(a, p, sms))
+    return launch_stream(f16, a, p.SPS, sms, stream);
   const int spst = p.SPS > 4 ? p.SPS : 4;  // steps per stage, as in the kernel
   const int nsteps = p.KC / 32;
   a.nstages = (nsteps + spst - 1) / spst;

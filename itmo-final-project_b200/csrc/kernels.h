@@ -78,6 +78,11 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
                       int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream,
                       const W4Prologue* pro = nullptr, const W4AllReduce* ar = nullptr);
 void set_w4_split_override(int splits);
+// Tuning override of the M <= 8 kernel choice: kernel 0 automatic, 1 register-streaming GEMV, 2 the staged
+// small-M kernel, 3 the staged kernel or the streaming lm_head kernel, 4 / 5 the register-streaming GEMV with a
+// ring of 4 / 8 steps; wk / splits: warps along K per CTA and cluster split of the register-streaming GEMV
+// (0 automatic).
+void set_w4_kernel_override(int kernel, int wk, int splits);
 unsigned int read_w4_error(bool clear);
 // Greedy token of rows split over the ranks of a peer group (columns [offset, offset + n) on this rank).
 cudaError_t launch_argmax_allreduce(const uint16_t* x, int64_t rows, int64_t n, int64_t sx, int64_t offset,

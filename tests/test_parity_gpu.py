@@ -370,3 +370,51 @@ def test_shared_workspace_across_plans_stays_consistent(cuda_device):
         w4a16_matmul(xs, *q2)
         w4a16_matmul(xs[:, :2048], *q1)
         torch.testing.assert_close(w4a16_matmul(x1, *q1), first, rtol=0, atol=0)
+
+
+# ----------------------------------------------------------------------------- register-streaming GEMV (M <= 8)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("N,K,G", [(200, 2048, 128), (2048, 2048, 128), (3072, 2048, 64), (2048, 8192, 32),
+                                   (96, 384, 96), (16384, 2048, 128)])
+def test_register_gemv_every_plan_matches_oracle(N, K, G, M, dtype, cuda_device):
+    """The M <= 8 register-streaming GEMV under each warp split, cluster split and ring depth (tuning hook),
+    against the oracle, and run to run identical; the staged kernel it replaced agrees within the same bound."""
+    from int4_b200 import _lib, quantize_int4, w4a16_matmul
+
+    L = _lib.lib()
+    torch.manual_seed(N + K + M)
+    x = torch.randn(M, K, dtype=dtype, device=cuda_device)
+    w = torch.randn(N, K, dtype=torch.bfloat16, device=cuda_device) * 0.02
+    qw, s, z = quantize_int4(w, G)
+    ref = _oracle_mm(x, qw, s, z)
+    plans = [(0, 0, 0), (2, 0, 0), (3, 0, 0), (4, 0, 0), (5, 0, 0), (1, 2, 1), (1, 8, 2), (1, 4, 4), (1, 1, 8)]
+    try:
+        for kernel, wk, splits in plans:
+            L.i4b_set_w4_kernel_override(kernel, wk, splits)
+            out = w4a16_matmul(x, qw, s, z)
+            _assert_matches(out, ref)
+            torch.testing.assert_close(w4a16_matmul(x, qw, s, z), out, rtol=0, atol=0)
+    finally:
+        L.i4b_set_w4_kernel_override(0, 0, 0)
+
+
+def test_transposed_views_take_the_copy_path_above_the_small_m_switch(cuda_device):
+    """A transposed-view W16 weight at M = 32 and a qweight whose row stride is not a multiple of 4 words at
+    M = 48 (both tcgen05 GEMM) are copied by the Python wrappers instead of being rejected."""
+    from int4_b200 import quantize_int4, w16a16_matmul, w4a16_matmul
+
+    torch.manual_seed(5)
+    x = torch.randn(32, 512, device=cuda_device, dtype=torch.bfloat16)
+    wt = (torch.randn(512, 256, device=cuda_device, dtype=torch.bfloat16) * 0.02).t()  # [256, 512], stride_wk 256
+    ref = x.float() @ wt.float().t()
+    torch.testing.assert_close(w16a16_matmul(x, wt).float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+    w = torch.randn(256, 512, device=cuda_device, dtype=torch.bfloat16) * 0.02
+    qw, s, z = quantize_int4(w, 128)
+    qpad = torch.zeros(qw.shape[0], qw.shape[1] + 1, dtype=torch.int32, device=cuda_device)
+    qpad[:, :256] = qw
+    qv = qpad[:, :256]  # row stride 257 words
+    x2 = torch.randn(48, 512, device=cuda_device, dtype=torch.bfloat16)
+    _assert_matches(w4a16_matmul(x2, qv, s, z), _oracle_mm(x2, qw, s, z))
