@@ -322,27 +322,35 @@ def run_block(args, world, rank, local):
 
 
 def cpu_block_sample(M: int, threads: int, steps: int = 1) -> tuple[float, str]:
-    """Reference CPU path (oracle port) for the whole block at M tokens; seconds per block."""
+    """The reference's CPU path for the whole block at M tokens, seconds per block: each linear is
+    ``x.float() @ dequantize_int4_ref(qweight, scales, zeros, torch.float32).t()`` (the reference tests'
+    expression, ``tests/test_kernels.py:54-57``), its output rounded to bf16 for the next linear.  The helper is
+    the oracle's torch restatement of ``dequantize_int4_ref`` (``int4_triton/quantize.py:120-135``); torch runs
+    the matmuls on ``threads`` host threads.  Quantization (``quantize_int4_ref``) is set-up, not timed."""
     import cases
-    from oracle import int4_oracle as orc
+    from oracle import int4_torch as ot
 
+    torch.set_num_threads(threads)
     qs = []
     for li, (name, N, K, _) in enumerate(BLOCK):
-        w = cases.weight((N, K), "bfloat16", seed=100 + li, outlier_frac=1e-3)
-        qs.append(orc.quantize_int4(w.view(torch.int16).numpy().view(np.uint16), GROUP, "bfloat16"))
-    x = cases.activations(M, 2048, "bfloat16", seed=1).view(torch.int16).numpy().view(np.uint16)
+        qs.append(ot.quantize_int4(cases.weight((N, K), "bfloat16", seed=100 + li, outlier_frac=1e-3), GROUP))
+    x = cases.activations(M, 2048, "bfloat16", seed=1)
+
+    def lin(inp, i):
+        return (inp.float() @ ot.dequantize_int4(*qs[i], dtype=torch.float32).t()).to(torch.bfloat16)
+
     t0 = time.perf_counter()
     for _ in range(steps):
-        h = x
-        q = orc.w4a16_matmul_threaded(h, *qs[0], threads=threads)
-        orc.w4a16_matmul_threaded(h, *qs[1], threads=threads)
-        orc.w4a16_matmul_threaded(h, *qs[2], threads=threads)
-        o = orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(q), *qs[3], threads=threads)
-        gg = orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(o), *qs[4], threads=threads)
-        orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(o), *qs[5], threads=threads)
-        orc.w4a16_matmul_threaded(orc.f32_to_bf16_bits(gg), *qs[6], threads=threads)
+        q = lin(x, 0)
+        lin(x, 1)
+        lin(x, 2)
+        o = lin(q, 3)
+        gg = lin(o, 4)
+        lin(o, 5)
+        lin(gg, 6)
     dt = (time.perf_counter() - t0) / steps
-    return dt, f"{steps} full block step(s) at M={M}: 7 dequantize-then-matmul linears, numpy fp32"
+    return dt, (f"{steps} full block step(s) at M={M}: 7 x (dequantize_int4_ref to fp32, then x.float() @ W^T), "
+                f"torch on {threads} threads")
 
 
 # ----------------------------------------------------------------------------- model workload
@@ -440,11 +448,15 @@ def time_decode(m, B: int, prompt: int, steps: int, warmup: int, world: int, dev
     return res
 
 
-def run_model(args, world, rank, local):
+def run_model(args, world, rank, local, B=None, steps=None, nll=False):
+    """W4 (and, with --compare-bf16, bf16) decode of the Llama-3.2-1B-shaped model; optionally the config-4
+    mean-NLL check afterwards on the same random-init weights."""
     from int4_b200.decode import LlamaTP
 
     dev = torch.device("cuda", local)
-    B, prompt, steps = args.m, args.prompt, args.steps
+    B = args.m if B is None else B
+    steps = args.steps if steps is None else steps
+    prompt = args.prompt
     hf = build_llama(dev)
     res = {}
     for label, w4 in (("w4", True), ("bf16", False))[:2 if args.compare_bf16 else 1]:
@@ -475,26 +487,65 @@ def run_model(args, world, rank, local):
         res[label] = r
         del m
         torch.cuda.empty_cache()
+    if nll:
+        res["nll"] = model_nll(hf, world, rank, dev)
     del hf
     torch.cuda.empty_cache()
     return res
 
 
+NLL_SEQS, NLL_LEN = 8, 2048
+
+
+@torch.no_grad()
+def model_nll(hf, world: int, rank: int, dev) -> dict:
+    """BASELINE config 4's quality check: mean next-token NLL over 8 seeded random 2048-token sequences, the W4
+    model's prompt pass (this library, tensor-parallel when world > 1) against the fake-quant model
+    (``quantize_model_linears(fake=True)``: the same dequantized weights run by transformers with cuBLAS), as the
+    reference's ``eval_ppl`` computes it (``benchmarks/eval_llama.py:77-117``).  Random tokens on a random-init
+    model stand in for WikiText-2 and the checkpoint."""
+    import copy
+
+    import torch.nn.functional as F
+
+    import int4_b200 as ib
+    from int4_b200.decode import LlamaTP
+
+    g = torch.Generator().manual_seed(2024)
+    ids = torch.randint(0, LLAMA_1B["vocab_size"], (NLL_SEQS, NLL_LEN), generator=g).to(dev)
+    m = LlamaTP(hf, w4=True, group_size=GROUP, rank=rank, world=world, max_seq=NLL_LEN, max_batch=1, device=dev,
+                persistent=False)
+    nw4 = 0.0
+    for i in range(NLL_SEQS):
+        lw = m.prefill(ids[i:i + 1], all_logits=True)[0, :-1].float()
+        nw4 += F.cross_entropy(lw, ids[i, 1:], reduction="sum").item()
+        del lw
+    m.close()
+    del m
+    fake = copy.deepcopy(hf)
+    ib.quantize_model_linears(fake, GROUP, skip=("lm_head",), fake=True)
+    nref = 0.0
+    for i in range(NLL_SEQS):
+        lr = fake(ids[i:i + 1], use_cache=False).logits[0, :-1].float()
+        nref += F.cross_entropy(lr, ids[i, 1:], reduction="sum").item()
+        del lr
+    del fake
+    torch.cuda.empty_cache()
+    tok = NLL_SEQS * (NLL_LEN - 1)
+    return {"w4": nw4 / tok, "fake_quant_reference": nref / tok, "abs_diff": abs(nw4 - nref) / tok,
+            "sequences": NLL_SEQS, "seq_len": NLL_LEN, "tolerance": 1e-3}
+
+
 def cpu_model_sample(threads: int, B: int = 1, steps: int = 2) -> tuple[float, str]:
-    """The reference's model-level CPU path: fake-quant Llama-3.2-1B (bf16 dequantized W4 weights, G=128,
-    oracle quantizer) in transformers on the host cores; seconds per decode step after a 32-token prompt."""
-    import cases  # noqa: F401
-    from oracle import int4_oracle as orc
+    """The reference's model-level CPU path: the fake-quant Llama-3.2-1B (decoder linears replaced by their
+    dequantized INT4 round trip, G=128, ``quantize_model_linears(fake=True)`` semantics restated by the oracle's
+    torch helpers) in transformers on the host cores; seconds per decode step after a 32-token prompt."""
+    from oracle import int4_torch as ot
 
     torch.set_num_threads(threads)
     hf = build_llama("cpu")
     with torch.no_grad():
-        for mod in hf.model.layers.modules():
-            if isinstance(mod, torch.nn.Linear):
-                w = mod.weight.data
-                qw, s, z = orc.quantize_int4(w.view(torch.int16).numpy().view(np.uint16), GROUP, "bfloat16")
-                mod.weight.data.copy_(torch.from_numpy(orc.dequantize_int4(qw, s, z, "bfloat16").view(np.int16))
-                                      .view(torch.bfloat16))
+        ot.fake_quantize_model_(hf, GROUP, skip=("lm_head",))
         ids = torch.randint(0, LLAMA_1B["vocab_size"], (B, 32), generator=torch.Generator().manual_seed(7))
         out = hf(ids, use_cache=True)
         past = out.past_key_values
@@ -558,6 +609,145 @@ def main_model(args, world, rank, local, threads):
     print(json.dumps(line), flush=True)
 
 
+def decode_summary(args, dec: dict, world: int) -> dict:
+    """The config-4 decode numbers measured inside the block run (W4 tokens/s is BASELINE's lead metric)."""
+    if "error" in dec:
+        return {"metric": MODEL_METRIC, "error": dec["error"]}
+    pk = peaks()
+    w4, bf = dec["w4"], dec.get("bf16")
+    steps = args.decode_steps
+    step_s = w4["decode_s"] / steps
+    achieved = w4["bytes_per_step_rank"] / step_s / 1e9
+    out = {
+        "metric": MODEL_METRIC, "tokens_per_s": steps / w4["decode_s"], "unit": "tokens/s", "steps": steps,
+        "ms_per_token": step_s * 1e3, "batch": 1, "prompt": args.prompt,
+        "bf16_tokens_per_s": steps / bf["decode_s"] if bf else None,
+        "w4_over_bf16": bf["decode_s"] / w4["decode_s"] if bf else None,
+        "e2e_tokens_per_s": steps / w4["e2e_s"],
+        "prefill_ms": {"w4": w4["prefill_ms"], "bf16": bf["prefill_ms"] if bf else None},
+        "decode": "one launch for all layers (i4b_decode_layers)" if w4["persistent"] else
+                  "one launch per projection / glue op",
+        "tp_sum": w4["tp_sum"], "greedy": w4["greedy"], "lm_head": "bf16 (cuBLAS)",
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"],
+                     "kernel": "whole decode step: projection weights + lm_head + KV cache bytes per rank / step time"},
+        "clocks": w4["clocks"],
+    }
+    if "nll" in dec:
+        out["nll"] = dec["nll"]
+    return out
+
+
+COMPARE_M = (1, 8, 32, 128, 1024)
+
+
+def main_compare(args, world, rank, local, threads):
+    """BASELINE config 2 as the reference's benchmark tabulates it (``benchmarks/bench_gemm.py:46-60``): device
+    time of the block's seven linears per M, W4 (this library) next to torch bf16 (cuBLAS) and W16 (this library's
+    full-precision path), weights rotated past L2; one JSON line per M on rank 0 (one GPU: no tensor parallelism)."""
+    import cases
+    import int4_b200 as ib
+    import torch.nn.functional as F
+
+    dev = torch.device("cuda", local)
+    lin = []
+    for li, (name, N, K, _) in enumerate(BLOCK):
+        w = cases.weight((N, K), "bfloat16", seed=100 + li, outlier_frac=1e-3).to(dev)
+        lin.append((name, N, K, w, ib.quantize_int4(w, GROUP)))
+    pk = peaks()
+    for M in COMPARE_M:
+        x = {K: torch.randn(M, K, device=dev).to(torch.bfloat16) for K in (2048, 8192)}
+        res = {}
+        for label, fn in (("w4", lambda xx, l: ib.w4a16_matmul(xx, *l[4])), ("bf16", lambda xx, l: F.linear(xx, l[3])),
+                          ("w16", lambda xx, l: ib.w16a16_matmul(xx, l[3]))):
+            wbytes = sum((l[1] * l[2] // 2 + 4 * l[1] * l[2] // GROUP) if label == "w4" else 2 * l[1] * l[2]
+                         for l in lin)
+            copies = max(1, math.ceil(2 * L2_BYTES / wbytes))
+            sets = [lin] + [[(l[0], l[1], l[2], l[3].clone() if label != "w4" else l[3],
+                              tuple(t.clone() for t in l[4]) if label == "w4" else l[4]) for l in lin]
+                            for _ in range(copies - 1)]
+            reps = 20
+
+            def run(i):
+                for l in sets[i % copies]:
+                    fn(x[l[2]], l)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for i in range(3):
+                    run(i)
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=side):
+                for i in range(reps):
+                    run(i)
+            gr.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            flops = sum(2 * M * l[1] * l[2] for l in lin)
+            res[label] = {"us": us, "GB/s": (wbytes + sum(2 * M * (l[1] + l[2]) for l in lin)) / us / 1e3,
+                          "TFLOP/s": flops / us / 1e6}
+            del gr, sets
+            torch.cuda.empty_cache()
+        if rank == 0:
+            print(json.dumps({"workload": "compare (BASELINE config 2)", "M": M, "G": GROUP, "block_us": res,
+                              "w4_over_bf16": res["bf16"]["us"] / res["w4"]["us"],
+                              "peaks": {"hbm_gbs": pk["hbm_gbs"], "bf16_tflops": pk["bf16_tflops"]}}), flush=True)
+
+
+SWEEP = [("gate_proj", 8192, 2048), ("down_proj", 2048, 8192)]
+
+
+def main_sweep(args, world, rank, local, threads):
+    """gate_proj and down_proj, G in {32, 64, 128}, M in {1, 2, 16, 64}; device time per
+    matmul and HBM GB/s of its algorithmic bytes (weights rotated past L2); one JSON line per case."""
+    import cases
+    import int4_b200 as ib
+
+    dev = torch.device("cuda", local)
+    pk = peaks()
+    for li, (name, N, K) in enumerate(SWEEP):
+        w = cases.weight((N, K), "bfloat16", seed=300 + li, outlier_frac=1e-3).to(dev)
+        for G in (32, 64, 128):
+            q = ib.quantize_int4(w, G)
+            nb = N * K // 2 + 4 * N * K // G
+            copies = max(2, math.ceil(2 * L2_BYTES / nb))
+            qs = [q] + [tuple(t.clone() for t in q) for _ in range(copies - 1)]
+            for M in (1, 2, 16, 64):
+                x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+                reps = 60
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    for i in range(3):
+                        ib.w4a16_matmul(x, *qs[i % copies])
+                torch.cuda.synchronize()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=side):
+                    for i in range(reps):
+                        ib.w4a16_matmul(x, *qs[i % copies])
+                gr.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                gr.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps
+                gbs = alg_bytes(M, N, K, G) / us / 1e3
+                if rank == 0:
+                    print(json.dumps({"workload": "sweep (BASELINE config 3)", "layer": name, "N": N, "K": K, "G": G,
+                                      "M": M, "us": us, "GB/s": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"]}), flush=True)
+                del gr
+            del qs
+            torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -565,7 +755,14 @@ def main():
                     help="timed steps (default 20000 block steps, 256 decode steps for the model workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "model"], default="block")
+    ap.add_argument("--workload", choices=["block", "model", "compare", "sweep"], default="block",
+                    help="block: BASELINE config 2 at --m tokens (default; the same run also times config 4's "
+                         "decode and checks its NLL); model: configs 4/5 decode; compare: config 2's W4 / cuBLAS "
+                         "bf16 / W16 block table over M; sweep: config 3's group-size x M table")
+    ap.add_argument("--decode-steps", type=int, default=64,
+                    help="block workload: greedy decode steps of the config-4 model timed in the same run "
+                         "(0 skips the decode section)")
+    ap.add_argument("--nll", type=int, default=1, help="block workload: config-4 mean-NLL check after the decode")
     ap.add_argument("--prompt", type=int, default=512, help="model workload: prompt tokens before decoding")
     ap.add_argument("--lm-head-w4", type=int, default=0, help="model workload: quantize the lm_head too")
     ap.add_argument("--m", type=int, default=1, help="tokens per step")
@@ -638,14 +835,22 @@ def main():
         _lib.set_pdl(True)
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
-    if args.workload == "model":
-        main_model(args, world, rank, local, threads)
+    if args.workload in ("model", "compare", "sweep"):
+        {"model": main_model, "compare": main_compare, "sweep": main_sweep}[args.workload](args, world, rank, local,
+                                                                                          threads)
         if world > 1:
             import torch.distributed as dist
 
             dist.destroy_process_group()
         return
     r = run_block(args, world, rank, local)
+    dec = None
+    if args.decode_steps > 0:
+        # BASELINE config 4 in the same run: W4 decode tokens/s next to bf16 in the same loop, batch 1
+        try:
+            dec = run_model(args, world, rank, local, B=1, steps=args.decode_steps, nll=bool(args.nll))
+        except Exception as ex:  # reported in the line; the block number stands on its own
+            dec = {"error": f"{type(ex).__name__}: {ex}"}
     pk = peaks()
     us = r["us_per_step"]
     achieved = r["bytes_per_step_rank"] / (us * 1e-6) / 1e9  # per rank, GB/s
@@ -667,7 +872,8 @@ def main():
             "block_gbs_per_gpu": achieved, "block_us_l2_hot": r["hot_us"],
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": prof_traffic,
-                         "kernel": "w4_skinny_kernel (decode GEMV), the 4 launches of a step (q|k|v, o, gate|up, down)",
+                         "kernel": "w4_gemv_kernel (register-streaming decode GEMV), the 4 launches of a step "
+                                   "(q|k|v, o, gate|up, down)",
                          "peak_source": pk["source"]},
             "cpu_baseline": cpu,
             "e2e": {"value": r["e2e_us"], "unit": "us", "h2d_bytes_per_step": r["h2d"],
@@ -675,6 +881,8 @@ def main():
             "gpu_launches": r["launches_per_step"] * args.steps,
             "clocks": r["clocks"], "device_error_flags": r["device_error_flags"],
         }
+        if dec is not None:
+            line["decode"] = decode_summary(args, dec, world)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -113,6 +113,22 @@ int i4b_w4a16_matmul_prologue(int prologue, const void* src, const void* delta, 
                               int64_t stride_sg, int group_size, void* y, int64_t stride_ym, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* Greedy choice fused into the W4 lm_head GEMV, for 1 <= M <= 8 rows:
+ * out[m] = index of the first maximum of row m of x @ W_hat^T, the logits compared as rounded to x's dtype
+ * (what torch.argmax(-1) sees on the stored logits; NaN never compares greater).  y, when not NULL, also
+ * receives the logits (y element (m, n) at y + m*stride_ym + n).  Replaces the lm_head matmul followed by the
+ * greedy choice of the reference's decode loop (benchmarks/eval_llama.py:121-183, logits[:, -1:].argmax(-1))
+ * with one launch: each CTA keeps its columns' candidate, the last CTA to finish (atomic ticket, no spinning)
+ * compares them.  x rows contiguous (stride_xm >= K); N % 8 == 0; qweight, scales and zeros 16-byte aligned
+ * with stride_qk % 4 == 0 and stride_sg % 8 == 0 (else I4B_ERR_LAYOUT).  Workspace: zero-filled before first
+ * use, left zero by every call, i4b_w4a16_argmax_workspace_size bytes (0: sizes not supported); calls sharing
+ * it must not overlap in time. */
+size_t i4b_w4a16_argmax_workspace_size(int64_t M, int64_t N, int64_t K, int group_size);
+int i4b_w4a16_matmul_argmax(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm,
+                            const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales,
+                            const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
+                            int64_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Workspace bytes for i4b_w16a16_matmul (same zero-fill rule as above). */
 size_t i4b_w16a16_workspace_size(int64_t M, int64_t N, int64_t K);
 

@@ -261,6 +261,43 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
   return e == cudaSuccess ? I4B_OK : fail_cuda(e);
 }
 
+size_t i4b_w4a16_argmax_workspace_size(int64_t M, int64_t N, int64_t K, int group_size) {
+  if (M <= 0 || M > 8 || N <= 0 || K <= 0 || group_size <= 0 || group_size % 32 != 0 || K % group_size != 0)
+    return 0;
+  DevInfo d;
+  if (current_device_info(&d) != I4B_OK) d.sms = 148;
+  return w4_argmax_workspace_bytes(M, N, K, group_size, d.sms);
+}
+
+int i4b_w4a16_matmul_argmax(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm,
+                            const int32_t* qweight, int64_t N, int64_t stride_qk, const uint16_t* scales,
+                            const uint16_t* zeros, int64_t stride_sg, int group_size, void* y, int64_t stride_ym,
+                            int64_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (x_dtype != I4B_F16 && x_dtype != I4B_BF16) return I4B_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return I4B_ERR_INVALID_ARG;
+  if (M > 8 || K % 8 != 0) return I4B_ERR_SHAPE;
+  const int G = group_size;
+  if (G <= 0 || G % 32 != 0 || K % G != 0) return I4B_ERR_GROUP;
+  if (M == 0) return I4B_OK;
+  if (N == 0 || K == 0) return I4B_ERR_SHAPE;  // no column to choose
+  if (!x || !qweight || !scales || !zeros || !out) return I4B_ERR_INVALID_ARG;
+  if (N > INT32_MAX || K > INT32_MAX) return I4B_ERR_SHAPE;
+  if (stride_qk < N || stride_sg < N || (y && stride_ym < N) || stride_xm < K) return I4B_ERR_LAYOUT;
+  if (N % 8 != 0 || !aligned16(qweight) || stride_qk % 4 != 0 || !aligned16(scales) || !aligned16(zeros) ||
+      stride_sg % 8 != 0)
+    return I4B_ERR_LAYOUT;
+  DevInfo d;
+  if (int st = current_device_info(&d)) return st;
+  const size_t need = w4_argmax_workspace_bytes(M, N, K, G, d.sms);
+  if (need == 0) return I4B_ERR_SHAPE;
+  if (!workspace || workspace_bytes < need) return I4B_ERR_WORKSPACE;
+  const cudaError_t e = launch_w4_argmax(x_dtype == I4B_F16, x, M, K, stride_xm, qweight, N, stride_qk, scales, zeros,
+                                         stride_sg, G, y, stride_ym, out, workspace, g_pdl, d.sms,
+                                         static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidConfiguration) return I4B_ERR_LAYOUT;
+  return e == cudaSuccess ? I4B_OK : fail_cuda(e);
+}
+
 int i4b_w4a16_matmul_prologue(int prologue, const void* src, const void* delta, const void* norm_weight, float eps,
                               void* resid_out, int64_t M, int64_t K, int64_t stride_src, const int32_t* qweight,
                               int64_t N, int64_t stride_qk, const uint16_t* scales, const uint16_t* zeros,

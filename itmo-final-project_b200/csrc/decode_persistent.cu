@@ -609,7 +609,6 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
         h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(sum))));
       }
     }
-    if (tp_out) __threadfence_system();  // the pushes reach every rank before the counters below
   }
   cbar();
   stamp(P, l, st_id, 4);
@@ -618,6 +617,9 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
     // release: the CTA's output stores (ordered before by the barrier) are visible before the count
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.ctr + l * C_LAYER + st_id), "r"(unsigned(n))
                  : "memory");
+    // the barrier above ordered every thread's pushes before this fence; the fence (cumulative) orders them
+    // before the counters of the other ranks, once per CTA
+    if (tp_out) __threadfence_system();
     if (tp_out)
       for (int p = 0; p < P.tp_world; ++p)
         if (p != P.tp_rank)

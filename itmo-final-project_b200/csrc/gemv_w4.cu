@@ -77,6 +77,9 @@ struct W4SArgs {
   // w4_gemv_kernel: WN x WK warps per CTA (columns x K), KW k per warp, scale / zero rows staged per CTA
   int WN, WK, KW;
   int sz_rows;
+  // fused greedy choice (w4_gemv_kernel with ARG): candidates [tiles][M] of (value, column), out [M]
+  float2* cand;
+  int64_t* amax_out;
 };
 
 enum { kProPlain = 0, kProRmsNorm = 1, kProSwiGlu = 2 };
@@ -129,11 +132,12 @@ __device__ __forceinline__ float ar_sum(const A& a, uint32_t slot, int64_t off) 
   return v;
 }
 // After every thread of the CTA has pushed: raise this CTA's flag in every other rank's buffer, then wait
-// (bounded) for the same CTA of every other rank.  A wait that gives up sets I4B_DEVERR_PEER_TIMEOUT; once
-// set, later waits on this device return at once.
+// (bounded) for the same CTA of every other rank.  The CTA barrier orders every thread's pushes before
+// thread 0's system-scope fence, and that fence (cumulative) before its release stores of the flags, so one
+// fence per CTA suffices -- the pattern of a grid-wide barrier.  A wait that gives up sets
+// I4B_DEVERR_PEER_TIMEOUT; once set, later waits on this device return at once.
 template <class A>
 __device__ __forceinline__ void ar_publish_wait(const A& a, uint32_t ep, int cta) {
-  __threadfence_system();  // this thread's pushes reach every rank before the flags below
   __syncthreads();
   const uint32_t slot = ep & 1u;
   if (threadIdx.x == 0) {
@@ -825,6 +829,65 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
   cp_async_wait<0>();
 }
 
+// ------------------------------------------------------------------ greedy choice fused into the GEMV
+
+// First maximum among (value, column) candidates in increasing column order: a strictly greater value wins, an
+// equal one only at a lower column (NaN never compares greater, as in block_row_argmax).
+__device__ __forceinline__ void first_max(float& best, int64_t& bi, float v, int64_t i) {
+  if (v > best || (v == best && i < bi)) {
+    best = v;
+    bi = i;
+  }
+}
+
+// Greedy token of every row, fused after the logits of the tile are final (vals[tok * BN + col]: the logits as
+// stored, -inf past N).  Warp t finds token t's first maximum in the tile and stores it as the tile's candidate;
+// the last CTA to finish (atomic ticket, no spinning) compares the candidates of all tiles in tile order --
+// i.e. column order -- and writes the index of the first maximum of the row (0 when no logit exceeds -inf),
+// then resets the ticket.
+__device__ __forceinline__ void greedy_epilogue(const W4SArgs& a, const float* vals, int nout, int BN, int64_t n0) {
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  __syncthreads();
+  for (int t = warp; t < a.M; t += nwarps) {
+    float best = -INFINITY;
+    int64_t bi = INT64_MAX;
+    for (int col = lane; col < BN; col += 32) first_max(best, bi, vals[t * BN + col], n0 + col);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      first_max(best, bi, ob, oi);
+    }
+    if (lane == 0)
+      a.cand[int64_t(blockIdx.x) * a.M + t] = make_float2(best, __int_as_float(bi == INT64_MAX ? -1 : int(bi)));
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(a.tickets, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int t = warp; t < a.M; t += nwarps) {
+    float best = -INFINITY;
+    int64_t bi = INT64_MAX;
+    for (int tile = lane; tile < int(gridDim.x); tile += 32) {
+      const float2 c = __ldcg(a.cand + int64_t(tile) * a.M + t);
+      const int i = __float_as_int(c.y);
+      if (i >= 0) first_max(best, bi, c.x, i);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      first_max(best, bi, ob, oi);
+    }
+    if (lane == 0) a.amax_out[t] = bi == INT64_MAX ? 0 : bi;
+  }
+  if (tid == 0) atomicExch(a.tickets, 0u);
+}
+
 // ------------------------------------------------------------------ decode GEMV, M <= 8, weights in registers
 
 // Register-streaming form of the M <= 8 path.  grid = (ceil(N / (32 WN)), S), cluster (1, S, 1) when S > 1;
@@ -837,7 +900,7 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
 // shared memory (cp.async), the activations once per CTA (stage_activations).  Dequant and MMA are those of
 // w4_skinny_kernel.  The WK warp partials of a column add in shared memory in warp order; the S CTAs of a
 // cluster then add through distributed shared memory in rank order: results are identical from run to run.
-template <bool F16, int SPS, int PRO, int D>
+template <bool F16, int SPS, int PRO, int D, bool ARG>
 __global__ void __launch_bounds__(256) w4_gemv_kernel(const W4SArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float s_inv[32];
@@ -954,10 +1017,19 @@ __global__ void __launch_bounds__(256) w4_gemv_kernel(const W4SArgs a) {
     if (a.S == 1) {
       const int tok = idx / BN;
       const int64_t n = n0 + (idx - tok * BN);
-      if (n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
+      const uint16_t bits = f2h_bits<F16>(v);
+      if (n < a.N && a.y) a.y[int64_t(tok) * a.sym + n] = bits;
+      if constexpr (ARG) {  // the logit as stored, or -inf past N; the warp-order sum above has read red[idx]
+        const float r = F16 ? __half2float(__ushort_as_half(bits)) : __uint_as_float(uint32_t(bits) << 16);
+        red[idx] = n < a.N ? r : -INFINITY;
+      }
     } else {
       red[idx] = v;
     }
+  }
+  if constexpr (ARG) {
+    greedy_epilogue(a, red, nout, BN, n0);
+    return;
   }
   if (a.S == 1) return;
   // Cluster of S CTAs along K: rank q adds outputs q*blockDim + tid, ... over all ranks, in rank order.
@@ -1188,9 +1260,9 @@ static W4GPlan plan_w4_gemv(int64_t M, int64_t N, int64_t K, int G, int sms) {
   return p;
 }
 
-template <bool F16, int SPS, int PRO, int D>
+template <bool F16, int SPS, int PRO, int D, bool ARG = false>
 static cudaError_t launch_gemv_impl(const W4SArgs& a, const W4GPlan& p, cudaStream_t stream) {
-  auto kern = w4_gemv_kernel<F16, SPS, PRO, D>;
+  auto kern = w4_gemv_kernel<F16, SPS, PRO, D, ARG>;
   if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), p.smem)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(cdiv(a.N, 32 * p.WN)), unsigned(p.S));
@@ -1216,13 +1288,13 @@ static cudaError_t launch_gemv_impl(const W4SArgs& a, const W4GPlan& p, cudaStre
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <bool F16, int PRO, int D>
+template <bool F16, int PRO, int D, bool ARG = false>
 static cudaError_t launch_gemv_sps(const W4SArgs& a, const W4GPlan& p, int sps, cudaStream_t stream) {
   switch (sps) {
-    case 1: return launch_gemv_impl<F16, 1, PRO, D>(a, p, stream);
-    case 2: return launch_gemv_impl<F16, 2, PRO, D>(a, p, stream);
-    case 4: return launch_gemv_impl<F16, 4, PRO, D>(a, p, stream);
-    default: return launch_gemv_impl<F16, 8, PRO, D>(a, p, stream);
+    case 1: return launch_gemv_impl<F16, 1, PRO, D, ARG>(a, p, stream);
+    case 2: return launch_gemv_impl<F16, 2, PRO, D, ARG>(a, p, stream);
+    case 4: return launch_gemv_impl<F16, 4, PRO, D, ARG>(a, p, stream);
+    default: return launch_gemv_impl<F16, 8, PRO, D, ARG>(a, p, stream);
   }
 }
 
@@ -1333,6 +1405,78 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
     case 2: return f16 ? launch_w4_sps<2, true>(a, p, smem, stream) : launch_w4_sps<2, false>(a, p, smem, stream);
     default: return f16 ? launch_w4_sps<4, true>(a, p, smem, stream) : launch_w4_sps<4, false>(a, p, smem, stream);
   }
+}
+
+// ---- greedy choice fused into the M <= 8 GEMV (the lm_head of a greedy decode step)
+
+static W4GPlan plan_w4_argmax(int64_t M, int64_t N, int64_t K, int G, int sms) {
+  W4GPlan p = plan_w4_gemv(M, N, K, G, sms);
+  if (p.S != 1) {  // one CTA owns all of K for its columns, so each tile's logits are final in that CTA
+    p.S = 1;
+    p.KC = int(K);
+    p.KW = p.KC / p.WK;
+    p.sz_rows = p.KC >= G ? p.KC / G + 1 : 2;
+    p.D = p.KW / 32 >= 8 ? 8 : 4;
+    int xp, ox, op;
+    p.smem = w4g_smem(int(M), p.WN, p.WK, p.KC, p.sz_rows, &xp, &ox, &op);
+    p.ok = p.ok && p.smem <= 200 * 1024;
+  }
+  return p;
+}
+
+size_t w4_argmax_workspace_bytes(int64_t M, int64_t N, int64_t K, int G, int sms) {
+  const W4GPlan p = plan_w4_argmax(M, N, K, G, sms);
+  if (!p.ok) return 0;
+  return kTicketBytes + size_t(cdiv(N, 32 * p.WN)) * size_t(M) * sizeof(float2);
+}
+
+cudaError_t launch_w4_argmax(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, const int32_t* qw, int64_t N,
+                             int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
+                             int64_t sym, int64_t* out, void* ws, bool pdl, int sms, cudaStream_t stream) {
+  const W4GPlan p = plan_w4_argmax(M, N, K, G, sms);
+  W4SArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.sxm = sxm;
+  a.sxk = 1;
+  a.qw = reinterpret_cast<const uint32_t*>(qw);
+  a.sqk = sqk;
+  a.sc = sc;
+  a.zr = zr;
+  a.ssg = ssg;
+  a.y = static_cast<uint16_t*>(y);
+  a.sym = sym;
+  a.M = int(M);
+  a.N = int(N);
+  a.K = int(K);
+  a.G = G;
+  a.pdl = pdl ? 1 : 0;
+  const auto addr = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr); };
+  a.vec_w = addr(qw) % 16 == 0 && sqk % 4 == 0 && N % 4 == 0;
+  a.vec_x = addr(x) % 16 == 0 && (sxm % 8 == 0 || M == 1);
+  const int SPS = gcd_i(G / 32, 8);
+  a.gpl = G / (32 * SPS);
+  a.gpl_shift = (a.gpl & (a.gpl - 1)) == 0 ? __builtin_ctz(unsigned(a.gpl)) : -1;
+  if (!gemv_eligible(a, p)) return cudaErrorInvalidConfiguration;
+  a.WN = p.WN;
+  a.WK = p.WK;
+  a.KW = p.KW;
+  a.KC = p.KC;
+  a.S = 1;
+  a.sz_rows = p.sz_rows;
+  int xp, ox, op;
+  w4g_smem(a.M, p.WN, p.WK, p.KC, p.sz_rows, &xp, &ox, &op);
+  a.xpitch = xp;
+  a.off_sz = 0;
+  a.off_x = ox;
+  a.off_part = op;
+  a.tickets = static_cast<unsigned int*>(ws);
+  a.cand = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + kTicketBytes);
+  a.amax_out = out;
+  if (p.D == 8)
+    return f16 ? launch_gemv_sps<true, kProPlain, 8, true>(a, p, SPS, stream)
+               : launch_gemv_sps<false, kProPlain, 8, true>(a, p, SPS, stream);
+  return f16 ? launch_gemv_sps<true, kProPlain, 4, true>(a, p, SPS, stream)
+             : launch_gemv_sps<false, kProPlain, 4, true>(a, p, SPS, stream);
 }
 
 // ------------------------------------------------------------------ greedy token over tensor-parallel ranks

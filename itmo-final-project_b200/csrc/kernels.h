@@ -83,6 +83,12 @@ void set_w4_split_override(int splits);
 // ring of 4 / 8 steps; wk / splits: warps along K per CTA and cluster split of the register-streaming GEMV
 // (0 automatic).
 void set_w4_kernel_override(int kernel, int wk, int splits);
+// Greedy choice fused into the M <= 8 GEMV: out[m] = first column of row m's maximum logit (as rounded to x's
+// dtype); y (may be null) receives the logits.  Workspace: w4_argmax_workspace_bytes (0 = sizes not supported).
+size_t w4_argmax_workspace_bytes(int64_t M, int64_t N, int64_t K, int G, int sms);
+cudaError_t launch_w4_argmax(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, const int32_t* qw, int64_t N,
+                             int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
+                             int64_t sym, int64_t* out, void* ws, bool pdl, int sms, cudaStream_t stream);
 unsigned int read_w4_error(bool clear);
 // Greedy token of rows split over the ranks of a peer group (columns [offset, offset + n) on this rank).
 cudaError_t launch_argmax_allreduce(const uint16_t* x, int64_t rows, int64_t n, int64_t sx, int64_t offset,

@@ -34,6 +34,9 @@ _SIGNATURES = {
     "i4b_w4a16_matmul_prologue": (_c_int, [_c_int, _c_vp, _c_vp, _c_vp, ctypes.c_float, _c_vp, _c_i64, _c_i64, _c_i64,
                                            _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp,
                                            _c_size, _c_vp]),
+    "i4b_w4a16_argmax_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int]),
+    "i4b_w4a16_matmul_argmax": (_c_int, [_c_vp, _c_int, _c_i64, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp,
+                                         _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_vp, _c_size, _c_vp]),
     "i4b_w16a16_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "i4b_w16a16_matmul": (_c_int, [_c_vp, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64,
                                    _c_vp, _c_i64, _c_vp, _c_size, _c_vp]),

@@ -33,7 +33,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .gemm import w4a16_matmul
+from .gemm import w4a16_matmul, w4a16_matmul_argmax
 from .peer import argmax_allreduce, w4a16_matmul_allreduce
 from .quantize import quantize_int4
 
@@ -528,6 +528,9 @@ class LlamaTP:
         as ``logits[:, -1].argmax(-1)`` in the reference's decode loop).  Under tensor parallelism with the peer
         all-reduce, each rank picks the first maximum of its vocabulary shard and the ranks exchange those
         candidates (``argmax_allreduce``) instead of all-gathering the logits."""
+        if self.world == 1 and self.fused and self.lm_head.q is not None and ids.shape[0] <= 8:
+            # W4 lm_head on one GPU: the greedy choice runs inside the lm_head GEMV (no logits round trip)
+            return w4a16_matmul_argmax(self._decode_hidden(ids, pos), *self.lm_head.q)
         local = self._decode_local(ids, pos)
         if self.world > 1 and self.peers is not None:
             return argmax_allreduce(self.peers, local, self.rank * local.shape[-1])
@@ -535,14 +538,9 @@ class LlamaTP:
 
     def _decode_local(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """This rank's logits [B, V / world] of one decode step."""
+        if self.persistent is not None or self.fused:
+            return self.lm_head(self._decode_hidden(ids, pos))
         B = ids.shape[0]
-        if self.persistent is not None and B <= self.max_batch:
-            h = self.persistent.run(ids, pos)
-            x = torch.empty_like(h)
-            add_rmsnorm(h, None, self.norm, x, self.eps)
-            return self.lm_head(x)
-        if self.fused:
-            return self._decode_step_fused(ids, pos)
         h = F.embedding(ids, self.embed)
         cos = self.cos.index_select(0, pos)
         sin = self.sin.index_select(0, pos)
@@ -550,6 +548,17 @@ class LlamaTP:
         for i in range(len(self.layers)):
             h = self._layer(i, h, cos, sin, pos, mask)
         return self.lm_head(rms_norm(h, self.norm, self.eps)).view(B, -1)
+
+    def _decode_hidden(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """The final-normed hidden state [B, H] of one decode step (the lm_head's input); fused kernels only."""
+        B = ids.shape[0]
+        if self.persistent is not None and B <= self.max_batch:
+            h = self.persistent.run(ids, pos)
+            x = torch.empty_like(h)
+            add_rmsnorm(h, None, self.norm, x, self.eps)
+            return x
+        assert self.fused, "the unfused decode step has no separate hidden-state form"
+        return self._decode_step_fused(ids, pos)
 
     def _decode_step_fused(self, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         B = ids.shape[0]
@@ -594,4 +603,4 @@ class LlamaTP:
                 silu_mul(L["gu"](x), act)
                 delta = self._all_reduce(L["down"](act))
         add_rmsnorm(cur, delta, self.norm, x, self.eps)
-        return self.lm_head(x)
+        return x

@@ -63,6 +63,35 @@ def w4a16_matmul(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, z
     return y.reshape(*x.shape[:-1], N)
 
 
+def w4a16_matmul_argmax(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+                        logits: bool = False):
+    """Greedy choice fused into the W4 matmul (an lm_head): index of the first maximum of each row of
+    x[M, K] @ W^T (1 <= M <= 8), as ``(x @ W^T).argmax(-1, keepdim=True)`` on the stored logits.  Returns the
+    int64 indices [M, 1], and the logits [M, N] too when ``logits`` is true.  No counterpart in ``int4_triton``."""
+    assert x.dtype in (torch.bfloat16, torch.float16) and x.dim() == 2
+    if not x.is_cuda:
+        raise ValueError("int4_b200 computes on the GPU only: x must be a CUDA tensor")
+    M, K = x.shape
+    N = qweight.shape[1]
+    G = K // scales.shape[0]
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    out = torch.empty((M, 1), dtype=torch.long, device=x.device)
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device) if logits else None
+    L = _lib.lib()
+    dev = x.device
+    stream = _lib.stream_handle(dev)
+    with torch.cuda.device(dev):
+        need = L.i4b_w4a16_argmax_workspace_size(M, N, K, G)
+        ws_ptr, ws_size = _lib.workspace(dev, stream, need)
+        st = L.i4b_w4a16_matmul_argmax(x.data_ptr(), _lib.DTYPE_CODE[x.dtype], M, K, x.stride(0), qweight.data_ptr(), N,
+                                       qweight.stride(0), scales.data_ptr(), zeros.data_ptr(), scales.stride(0), G,
+                                       None if y is None else y.data_ptr(), N, out.data_ptr(), ws_ptr, ws_size,
+                                       stream)
+    _lib.check(st, "w4a16_matmul_argmax")
+    return (out, y) if logits else out
+
+
 def w16a16_matmul(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """x[..., K] @ w[N, K]^T with full-precision weights: the same kernel structure as the W4 path."""
     assert x.dtype == w.dtype and x.dtype in (torch.bfloat16, torch.float16)
