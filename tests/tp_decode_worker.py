@@ -40,12 +40,21 @@ def main() -> int:
     from int4_b200.decode import LlamaTP
     from test_decode_gpu import build_hf, tiny_config
 
-    def mid_config():
-        """Widths at which the tensor-parallel shards still run the persistent decode (per-rank q width and
-        intermediate of at least 512 at two ranks)."""
+    def small_config():
+        """The tiny model, widened just enough that every rank holds whole heads and quantization groups."""
         c = tiny_config()
-        c.hidden_size, c.intermediate_size, c.num_hidden_layers = 1024, 2048, 3
-        c.num_attention_heads, c.num_key_value_heads = 16, 4
+        if world > 2:
+            c.num_attention_heads, c.num_key_value_heads = 2 * world, world
+            c.intermediate_size = max(c.intermediate_size, 128 * world)
+        return c
+
+    def mid_config():
+        """Llama-3.2-1B widths (hidden 2048, 32 / 8 heads, intermediate 8192), two layers: the shards run the
+        persistent decode where the per-rank q width is at least 512 (two and four ranks), the per-projection
+        decode beyond (eight ranks: 256-wide o_proj shards)."""
+        c = tiny_config()
+        c.hidden_size, c.intermediate_size, c.num_hidden_layers = 2048, 8192, 2
+        c.num_attention_heads, c.num_key_value_heads = 32, 8
         return c
 
     from int4_b200 import _lib
@@ -53,16 +62,19 @@ def main() -> int:
     graph_diff, greedy_bad = 0.0, 0
     excess, report = -1.0, []  # max over runs of (difference - bound); per-run "difference / bound"
     with torch.no_grad():
-        hf_tiny = build_hf(0)
+        hf_tiny = build_hf(0, small_config())
         hf_mid = build_hf(0, mid_config())
+        mid_persistent = 32 // world * 64 >= 512
         g = torch.Generator().manual_seed(3)
         ids = torch.randint(0, 512, (1, 24), generator=g).to(dev)
         # (model, quantized lm_head, peer all-reduce, persistent decode expected)
         runs = ((hf_tiny, False, True, False), (hf_tiny, True, True, False), (hf_tiny, False, False, False),
-                (hf_mid, False, True, True))
+                (hf_mid, False, True, mid_persistent))
         for hf, lm_w4, peer, persistent in runs:
+            # the fused sums inside the matmuls need every CTA of a matmul resident at once; the wide model's
+            # per-projection path (eight ranks) keeps NCCL's all-reduce, as LlamaTP does by default
             tp = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=rank, world=world, max_seq=64, device=dev,
-                         peer_allreduce=peer, matmul_allreduce=peer)
+                         peer_allreduce=peer, matmul_allreduce=peer and hf is hf_tiny)
             assert (tp.peers is not None) == peer
             assert (tp.persistent is not None) == persistent
             one = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev)
