@@ -426,8 +426,9 @@ def test_transposed_views_take_the_copy_path_above_the_small_m_switch(cuda_devic
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("M,N,K,G", [(1, 128256, 2048, 128), (4, 2056, 512, 64), (8, 4096, 1024, 32)])
 def test_matmul_argmax_is_the_first_maximum_of_the_stored_logits(M, N, K, G, dtype, cuda_device):
-    """w4a16_matmul_argmax: the logits equal w4a16_matmul's bit for bit and the index is torch.argmax of them
-    (first maximum); ties planted across tiles and within a tile go to the lower column."""
+    """w4a16_matmul_argmax: the index is torch.argmax (first maximum) of the logits the call returns, which match
+    the oracle like any W4 matmul (where the plain matmul splits K over a cluster the summation order differs);
+    ties planted in two other tiles go to the lowest column."""
     from int4_b200 import quantize_int4, w4a16_matmul, w4a16_matmul_argmax
 
     torch.manual_seed(M + N)
@@ -435,10 +436,9 @@ def test_matmul_argmax_is_the_first_maximum_of_the_stored_logits(M, N, K, G, dty
     w = torch.randn(N, K, dtype=torch.bfloat16, device=cuda_device) * 0.02
     qw, s, z = quantize_int4(w, G)
     idx, y = w4a16_matmul_argmax(x, qw, s, z, logits=True)
-    ref = w4a16_matmul(x, qw, s, z)
-    assert torch.equal(y, ref)
-    assert torch.equal(idx, ref.argmax(-1, keepdim=True))
+    assert torch.equal(idx, y.argmax(-1, keepdim=True))
     _assert_matches(y, _oracle_mm(x, qw, s, z))
+    _assert_matches(w4a16_matmul(x, qw, s, z), _oracle_mm(x, qw, s, z))
     assert torch.equal(w4a16_matmul_argmax(x, qw, s, z), idx)  # without logits, and a second call on the workspace
     # ties: duplicate the winning weight column at a lower and at a higher column, in another tile
     dup = w.clone()
@@ -447,5 +447,5 @@ def test_matmul_argmax_is_the_first_maximum_of_the_stored_logits(M, N, K, G, dty
     dup[lo] = w[win]
     dup[hi] = w[win]
     q2 = quantize_int4(dup, G)
-    i2 = w4a16_matmul_argmax(x, *q2)
-    assert torch.equal(i2, w4a16_matmul(x, *q2).argmax(-1, keepdim=True))
+    i2, y2 = w4a16_matmul_argmax(x, *q2, logits=True)
+    assert torch.equal(i2, y2.argmax(-1, keepdim=True))
