@@ -1051,6 +1051,194 @@ __global__ void __launch_bounds__(256) w4_gemv_kernel(const W4SArgs a) {
   cluster_sync();  // no CTA leaves while others may still read its shared memory
 }
 
+// ------------------------------------------------------------------ slab-streaming GEMV (M <= 8), K split over P warps
+
+// The streaming kernel above, generalised to any width: a persistent grid of CTAs of 4 warps; the warps of a
+// CTA form 4 / P groups of P warps, and a group takes the CTA's slabs (32 columns x all of K) one after the
+// other, its P warps splitting each slab's K into P consecutive parts.  Each warp streams its part of slab
+// after slab through its own cp.async ring (RING stages of SPST 32-k steps), so the weight stream does not
+// stop between slabs and the per-warp fixed work (ring fill, activation staging) is paid once per launch.
+// The activations (any prologue) are staged once per CTA.  For P > 1 the warps of a group write their
+// partial sums of a slab into a double-buffered shared array, meet at a named barrier of the group, and
+// warp 0 of the group adds the P partials in part order: results are identical from run to run.
+template <bool F16, int SPS, int PRO, int P>
+__global__ void __launch_bounds__(128) w4_slab_kernel(const W4SArgs a) {
+  constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;  // 32-k steps per ring stage
+  constexpr int SEGST = SPST / SPS;
+  constexpr int RING = kStreamRing;
+  constexpr int WSTAGE = SPST * 512;    // weight bytes of a stage (32 lanes x 16 B per step)
+  constexpr int SZSTAGE = SEGST * 128;  // scale / zero bytes of a stage (8 records of 16 B per segment)
+  constexpr int GPC = 4 / P;            // slab groups per CTA
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float s_inv[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = lane >> 2, c = lane & 3;
+  const int part = warp % P, grp = warp / P;
+  const int M = a.M;
+  const int KP = a.K / P;  // k per warp and slab
+  const int kp0 = part * KP;
+  const int L = 32 * SPS;
+  const int stages_slab = KP / (32 * SPST);
+  const int nslabs = (a.N + 31) / 32;
+  const int G_total = int(gridDim.x) * GPC;
+  const int gg = int(blockIdx.x) * GPC + grp;
+  const int my_slabs = gg < nslabs ? (nslabs - gg + G_total - 1) / G_total : 0;  // same for the group's warps
+  const int total = my_slabs * stages_slab;
+
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t s_x = s_base;                                            // [M][xpitch]
+  float* partials = reinterpret_cast<float*>(smem + a.off_part);         // [2][GPC][P][8 tokens][32 columns]
+  const uint32_t s_w = s_base + a.off_sz + warp * RING * (WSTAGE + SZSTAGE);  // this warp's ring
+
+  // Issue cursor: the next stage of this warp's stream, as running pointers (no division per stage).
+  const int64_t row4 = 4 * a.sqk;  // words between the k8 rows of consecutive 32-k steps
+  const int g_row0 = kp0 / a.G;    // first scale row of this warp's part
+  const int gcnt0 = (kp0 / L) % a.gpl;
+  int is_left = total, is_st = 0, is_slot = 0;
+  int64_t is_n = int64_t(gg) * 32 + 4 * r;
+  const uint32_t* const w_part = a.qw + int64_t(kp0 / 8 + c) * a.sqk;
+  const uint32_t* is_w = w_part + is_n;
+  const uint16_t* const sz0 = (c < 2 ? a.sc : a.zr) + 2 * (c & 1) + int64_t(g_row0) * a.ssg;
+  const uint16_t* is_sz = sz0 + is_n;
+  int is_gcnt = gcnt0;
+  auto issue_next = [&]() {
+    if (is_left > 0) {
+      const bool n_in = is_n < a.N;
+      const uint32_t dst = s_w + is_slot * (WSTAGE + SZSTAGE);
+      if (n_in) {
+        const uint32_t* src = is_w;
+#pragma unroll
+        for (int i = 0; i < SPST; ++i) {
+          cp16(dst + i * 512 + lane * 16, src, 16u);
+          src += row4;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < SPST; ++i) cp16(dst + i * 512 + lane * 16, a.qw, 0u);  // columns past N: zeros
+      }
+#pragma unroll
+      for (int j = 0; j < SEGST; ++j) {
+        cp4(dst + WSTAGE + j * 128 + r * 16 + 4 * c, n_in ? is_sz : a.sc, n_in ? 4u : 0u);
+        if (++is_gcnt == a.gpl) {
+          is_gcnt = 0;
+          is_sz += a.ssg;
+        }
+      }
+      --is_left;
+      is_slot = is_slot == RING - 1 ? 0 : is_slot + 1;
+      if (++is_st == stages_slab) {  // next slab of this group
+        is_st = 0;
+        is_n += int64_t(G_total) * 32;
+        is_w = w_part + is_n;
+        is_sz = sz0 + is_n;
+        is_gcnt = gcnt0;
+      } else {
+        is_w += SPST * row4;
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll 1
+  for (int g = 0; g < RING; ++g) issue_next();
+
+  if (a.pdl) {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+  stage_activations<F16, PRO>(a, s_x, 0, a.K / 8, a.K / 8, s_inv);
+  __syncthreads();
+
+  const uint32_t magic = F16 ? 0x64006400u : 0x43004300u;
+  const uint32_t xl0 = s_x + min(r, M - 1) * a.xpitch + (kp0 / 8 + c) * 16;
+  float acc[2][4], acc1[2][4];  // the k16 halves of each step accumulate separately (two MMA chains)
+  int st = 0, slot = 0, sl = 0;
+  int64_t n_slab = int64_t(gg) * 32;
+  uint32_t xl = xl0;
+  DqParams dp[4];
+#pragma unroll 1
+  for (int g = 0; g < total; ++g) {
+    if (st == 0) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[t][e] = acc1[t][e] = 0.0f;
+    }
+    cp_async_wait<RING - 1>();
+    __syncwarp();
+    const uint32_t sb = s_w + slot * (WSTAGE + SZSTAGE);
+#pragma unroll
+    for (int i = 0; i < SPST; ++i) {
+      if (i % SPS == 0) {  // a new segment: scale and zero of columns 4r .. 4r + 3
+        const uint4 sz = lds128(sb + WSTAGE + (i / SPS) * 128 + r * 16);
+        dp[0] = dq_params<F16>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.z & 0xFFFFu));
+        dp[1] = dq_params<F16>(uint16_t(sz.x >> 16), uint16_t(sz.z >> 16));
+        dp[2] = dq_params<F16>(uint16_t(sz.y & 0xFFFFu), uint16_t(sz.w & 0xFFFFu));
+        dp[3] = dq_params<F16>(uint16_t(sz.y >> 16), uint16_t(sz.w >> 16));
+      }
+      const uint4 w4 = lds128(sb + i * 512 + lane * 16);
+      const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
+      uint32_t af[2][2][4];  // the dequantized weights, rounded as the reference does
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          af[t][h][0] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * h, magic), dp[2 * t]);
+          af[t][h][1] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * h, magic), dp[2 * t + 1]);
+          af[t][h][2] = dq_pair<F16>(nib_pair(wd[2 * t], 2 * h + 1, magic), dp[2 * t]);
+          af[t][h][3] = dq_pair<F16>(nib_pair(wd[2 * t + 1], 2 * h + 1, magic), dp[2 * t + 1]);
+        }
+      const uint4 b = lds128(xl + i * 64);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        mma_16816<F16>(acc[t], af[t][0], b.x, b.y);
+        mma_16816<F16>(acc1[t], af[t][1], b.z, b.w);
+      }
+    }
+    __syncwarp();  // every lane is done with the slot before it is refilled
+    issue_next();
+    slot = slot == RING - 1 ? 0 : slot + 1;
+    xl += SPST * 64;
+    if (++st == stages_slab) {  // slab complete: acc[t][e] is (token 2c + (e & 1), column 4r + 2t + (e >> 1))
+      if constexpr (P == 1) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tok = 2 * c + (e & 1);
+            const int64_t n = n_slab + 4 * r + 2 * t + (e >> 1);
+            if (tok < M && n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(acc[t][e] + acc1[t][e]);
+          }
+      } else {
+        float* pb = partials + ((sl & 1) * GPC + grp) * (P * 256);
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tok = 2 * c + (e & 1);
+            if (tok < M) pb[part * 256 + tok * 32 + 4 * r + 2 * t + (e >> 1)] = acc[t][e] + acc1[t][e];
+          }
+        // the group's P warps meet; warp 0 of the group adds the parts in order (the next slab's barrier
+        // keeps the other buffer from being rewritten before it has been read)
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(32 * P) : "memory");
+        if (part == 0) {
+          const int64_t n = n_slab + lane;
+          for (int tok = 0; tok < M; ++tok) {
+            float v = pb[tok * 32 + lane];
+#pragma unroll
+            for (int q = 1; q < P; ++q) v += pb[q * 256 + tok * 32 + lane];
+            if (n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(v);
+          }
+        }
+      }
+      st = 0;
+      ++sl;
+      n_slab += int64_t(G_total) * 32;
+      xl = xl0;
+    }
+  }
+  cp_async_wait<0>();
+}
+
 // ------------------------------------------------------------------ planning
 
 static int g_w4_ovr_s = 0;
@@ -1314,6 +1502,92 @@ static bool gemv_eligible(const W4SArgs& a, const W4GPlan& p) {
          addr(a.zr) % 16 == 0 && a.ssg % 8 == 0;
 }
 
+// ---- slab-streaming GEMV (M <= 8): plan and launch
+
+struct W4SlabPlan {
+  int P, per_sm, grid;
+  size_t smem;
+  bool ok;
+};
+
+// P: the smallest split that gives every SM at least kSlabWarpsPerSm busy warps (1, 2 or 4); the grid covers
+// the slab groups, at most per_sm CTAs per SM (shared memory and registers).
+constexpr int kSlabWarpsPerSm = 8;
+
+static W4SlabPlan plan_w4_slab(const W4SArgs& a, int sps, int sms) {
+  W4SlabPlan p{};
+  const int spst = sps > kStreamSteps ? sps : kStreamSteps;
+  const int64_t slabs = cdiv(a.N, 32);
+  p.P = 4;
+  for (int P : {1, 2, 4})
+    if (slabs * P >= int64_t(kSlabWarpsPerSm) * sms) {
+      p.P = P;
+      break;
+    }
+  if (g_w4_ovr_kernel == 6 && (g_w4_ovr_wk == 1 || g_w4_ovr_wk == 2 || g_w4_ovr_wk == 4)) p.P = g_w4_ovr_wk;
+  const int xpitch = (a.K / 8) % 8 == 0 ? a.K * 2 + 64 : a.K * 2;
+  const size_t x_bytes = (size_t(a.M) * xpitch + 127) / 128 * 128;
+  const size_t part_bytes = p.P > 1 ? size_t(2) * 4 * 256 * 4 : 0;
+  p.smem = x_bytes + part_bytes + 4 * kStreamRing * (size_t(spst) * 512 + (spst / sps) * 128);
+  int per_sm = int((227 * 1024) / (p.smem + 1024));
+  p.per_sm = per_sm < 1 ? 1 : (per_sm > 6 ? 6 : per_sm);  // 6 x 128 threads at <= 80 registers
+  const int64_t groups = cdiv(slabs, 4 / p.P);
+  p.grid = int(std::min<int64_t>(int64_t(sms) * p.per_sm, groups));
+  p.ok = a.M <= 8 && a.ar_world <= 1 && a.vec_w && a.vec_s && a.K % (p.P * 32 * spst) == 0 &&
+         p.smem <= 200 * 1024;
+  return p;
+}
+
+template <bool F16, int SPS, int PRO, int P>
+static cudaError_t launch_slab_impl(const W4SArgs& a, const W4SlabPlan& p, cudaStream_t stream) {
+  auto kern = w4_slab_kernel<F16, SPS, PRO, P>;
+  if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), p.smem)) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(p.grid));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (a.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <bool F16, int PRO, int P>
+static cudaError_t launch_slab_sps(const W4SArgs& a, const W4SlabPlan& p, int sps, cudaStream_t stream) {
+  switch (sps) {
+    case 1: return launch_slab_impl<F16, 1, PRO, P>(a, p, stream);
+    case 2: return launch_slab_impl<F16, 2, PRO, P>(a, p, stream);
+    case 4: return launch_slab_impl<F16, 4, PRO, P>(a, p, stream);
+    default: return launch_slab_impl<F16, 8, PRO, P>(a, p, stream);
+  }
+}
+
+template <int P>
+static cudaError_t launch_slab_p(bool f16, const W4SArgs& a, const W4SlabPlan& p, int sps, cudaStream_t stream) {
+  if (f16) return launch_slab_sps<true, kProPlain, P>(a, p, sps, stream);
+  if (a.pro == kProRmsNorm) return launch_slab_sps<false, kProRmsNorm, P>(a, p, sps, stream);
+  if (a.pro == kProSwiGlu) return launch_slab_sps<false, kProSwiGlu, P>(a, p, sps, stream);
+  return launch_slab_sps<false, kProPlain, P>(a, p, sps, stream);
+}
+
+static cudaError_t launch_slab(bool f16, W4SArgs a, const W4SlabPlan& p, int sps, cudaStream_t stream) {
+  a.xpitch = (a.K / 8) % 8 == 0 ? a.K * 2 + 64 : a.K * 2;
+  a.off_part = int((size_t(a.M) * a.xpitch + 127) / 128 * 128);
+  a.off_sz = a.off_part + (p.P > 1 ? 2 * 4 * 256 * 4 : 0);  // start of the rings
+  switch (p.P) {
+    case 1: return launch_slab_p<1>(f16, a, p, sps, stream);
+    case 2: return launch_slab_p<2>(f16, a, p, sps, stream);
+    default: return launch_slab_p<4>(f16, a, p, sps, stream);
+  }
+}
+
 cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, int64_t sxk, const int32_t* qw,
                       int64_t N, int64_t sqk, const uint16_t* sc, const uint16_t* zr, int64_t ssg, int G, void* y,
                       int64_t sym, void* ws, const W4Plan& p, bool pdl, cudaStream_t stream, const W4Prologue* pro,
@@ -1365,8 +1639,14 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   }
   int sms = 0, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // kernel choice for M <= 8: the register-streaming GEMV, unless the tuning hook asks for another one
-  if (sms > 0 && g_w4_ovr_kernel != 2 && g_w4_ovr_kernel != 3) {
+  // kernel choice for M <= 8: the slab-streaming GEMV, else the register-streaming one, unless the tuning hook
+  // asks for another
+  const bool ovr_reg = g_w4_ovr_kernel == 1 || g_w4_ovr_kernel == 4 || g_w4_ovr_kernel == 5;
+  if (sms > 0 && (g_w4_ovr_kernel == 0 || g_w4_ovr_kernel == 6)) {
+    const W4SlabPlan sp = plan_w4_slab(a, p.SPS, sms);
+    if (sp.ok) return launch_slab(f16, a, sp, p.SPS, stream);
+  }
+  if (sms > 0 && (g_w4_ovr_kernel == 0 || ovr_reg)) {
     const W4GPlan gp = plan_w4_gemv(M, N, K, G, sms);
     if (gemv_eligible(a, gp)) {
       a.WN = gp.WN;
