@@ -700,6 +700,43 @@ def main_compare(args, world, rank, local, threads):
                               "peaks": {"hbm_gbs": pk["hbm_gbs"], "bf16_tflops": pk["bf16_tflops"]}}), flush=True)
 
 
+GEMV_SHAPES = {"qkv": (3072, 2048), "o_proj": (2048, 2048), "gate_up": (16384, 2048), "down_proj": (2048, 8192),
+               "lm_head": (128256, 2048), "gate_proj": (8192, 2048)}
+
+
+def main_gemv(args, world, rank, local, threads):
+    """A fixed number of launches of one W4 matmul (a --layer shape of the Llama-3.2-1B block, G=128, --m tokens),
+    for profiler captures: --launches launches of each --kernel choice, after two warm-up launches each, plus
+    the quantizer (quantize_pow2_kernel) once per weight.  Prints the device time of the last launch of each."""
+    import int4_b200 as ib
+    from int4_b200 import _lib
+
+    dev = torch.device("cuda", local)
+    N, K = GEMV_SHAPES[args.layer]
+    g = torch.Generator().manual_seed(5)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    q = ib.quantize_int4(w, GROUP)
+    x = torch.randn(args.m, K, generator=g).to(torch.bfloat16).to(dev)
+    L = _lib.lib()
+    out = {}
+    for kernel in [int(k) for k in args.kernel.split(",")]:
+        L.i4b_set_w4_kernel_override(kernel, 0, 0)
+        for _ in range(2):
+            ib.w4a16_matmul(x, *q)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(args.launches):
+            e0.record()
+            ib.w4a16_matmul(x, *q)
+            e1.record()
+        torch.cuda.synchronize()
+        out[kernel] = e0.elapsed_time(e1) * 1e3
+    L.i4b_set_w4_kernel_override(0, 0, 0)
+    assert _lib.device_error_flags(local) == 0
+    if rank == 0:
+        print(json.dumps({"workload": "gemv", "layer": args.layer, "N": N, "K": K, "M": args.m,
+                          "last_launch_us": out}), flush=True)
+
+
 SWEEP = [("gate_proj", 8192, 2048), ("down_proj", 2048, 8192)]
 
 
@@ -755,7 +792,12 @@ def main():
                     help="timed steps (default 20000 block steps, 256 decode steps for the model workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "model", "compare", "sweep"], default="block",
+    ap.add_argument("--layer", choices=sorted(GEMV_SHAPES), default="gate_up", help="gemv workload: the shape")
+    ap.add_argument("--kernel", default="0", help="gemv workload: comma-separated W4 kernel choices "
+                    "(i4b_set_w4_kernel_override: 0 automatic, 1 register-streaming, 2 staged, 3 staged / lm_head "
+                    "streaming, 6 slab-streaming)")
+    ap.add_argument("--launches", type=int, default=3, help="gemv workload: launches per kernel choice")
+    ap.add_argument("--workload", choices=["block", "model", "compare", "sweep", "gemv"], default="block",
                     help="block: BASELINE config 2 at --m tokens (default; the same run also times config 4's "
                          "decode and checks its NLL); model: configs 4/5 decode; compare: config 2's W4 / cuBLAS "
                          "bf16 / W16 block table over M; sweep: config 3's group-size x M table")
@@ -818,6 +860,11 @@ def main():
         ref_steps = min(args.steps, 5)
         dt, sample = cpu_block_sample(args.m, threads, ref_steps)
         v = dt * 1e6
+        dec = None
+        if args.decode_steps > 0:  # config 4's decode on the host cores: the fake-quant model in transformers
+            dts, dsample = cpu_model_sample(threads, 1, 2)
+            dec = {"metric": MODEL_METRIC, "tokens_per_s": 1.0 / dts, "unit": "tokens/s", "ms_per_token": dts * 1e3,
+                   "cores": threads, "kind": "port", "sample": dsample}
         print(json.dumps({
             "impl": "reference", "metric": metric, "value": v, "unit": "us", "n_gpus": world,
             "steps": ref_steps, "steps_requested": args.steps, "warmup": 0, "ms_per_step": dt * 1e3,
@@ -825,6 +872,7 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "w4a16-bf16", "data": "synthetic", "config": config,
             "cpu_baseline": {"value": v, "unit": "us", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "decode": dec,
         }), flush=True)
         return
 
@@ -835,9 +883,9 @@ def main():
         _lib.set_pdl(True)
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
-    if args.workload in ("model", "compare", "sweep"):
-        {"model": main_model, "compare": main_compare, "sweep": main_sweep}[args.workload](args, world, rank, local,
-                                                                                          threads)
+    if args.workload in ("model", "compare", "sweep", "gemv"):
+        {"model": main_model, "compare": main_compare, "sweep": main_sweep, "gemv": main_gemv}[args.workload](
+            args, world, rank, local, threads)
         if world > 1:
             import torch.distributed as dist
 
