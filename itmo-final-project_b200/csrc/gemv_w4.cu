@@ -176,6 +176,24 @@ __device__ __forceinline__ void ar_finish(const A& a, uint32_t ep) {
   }
 }
 
+// The dequantization constants of columns 4r .. 4r + 3 from their 16-byte scale / zero record
+// (s0 s1 | s2 s3 | z0 z1 | z2 z3): lane c (of the four lanes with the same r) converts column 4r + c only and
+// the four lanes exchange the results by shuffle, instead of each lane converting all four.
+template <bool F16>
+__device__ __forceinline__ void dq_params_shared(const uint4& sz, int c, DqParams (&dp)[4]) {
+  const uint32_t sw = c < 2 ? sz.x : sz.y, zw = c < 2 ? sz.z : sz.w;
+  const int sh = (c & 1) * 16;
+  const DqParams mine = dq_params<F16>(uint16_t(sw >> sh), uint16_t(zw >> sh));
+  const int base = (threadIdx.x & 31) & ~3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    dp[j].zz = __shfl_sync(0xFFFFFFFFu, mine.zz, base + j);
+    dp[j].shi = __shfl_sync(0xFFFFFFFFu, mine.shi, base + j);
+    if constexpr (!F16) dp[j].slo = __shfl_sync(0xFFFFFFFFu, mine.slo, base + j);
+    else dp[j].slo = 0u;
+  }
+}
+
 __device__ __forceinline__ float bfv(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 __device__ __forceinline__ uint32_t bfr(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
 
@@ -976,10 +994,7 @@ __global__ void __launch_bounds__(256) w4_gemv_kernel(const W4SArgs a) {
         const uint32_t sa = szl + uint32_t(row * BN * 2), za = sa + uint32_t(a.sz_rows * BN * 2);
         asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(sv0), "=r"(sv1) : "r"(sa));
         asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(zv0), "=r"(zv1) : "r"(za));
-        dp[0] = dq_params<F16>(uint16_t(sv0 & 0xFFFFu), uint16_t(zv0 & 0xFFFFu));
-        dp[1] = dq_params<F16>(uint16_t(sv0 >> 16), uint16_t(zv0 >> 16));
-        dp[2] = dq_params<F16>(uint16_t(sv1 & 0xFFFFu), uint16_t(zv1 & 0xFFFFu));
-        dp[3] = dq_params<F16>(uint16_t(sv1 >> 16), uint16_t(zv1 >> 16));
+        dq_params_shared<F16>(make_uint4(sv0, sv1, zv0, zv1), c, dp);
       }
       const uint32_t wd[4] = {wr[i].x, wr[i].y, wr[i].z, wr[i].w};
       if (step + D < nsteps && n_in) wr[i] = ld_stream_u4(wsrc + (step + D) * wstep);  // refill the slot
@@ -1062,13 +1077,14 @@ __global__ void __launch_bounds__(256) w4_gemv_kernel(const W4SArgs a) {
 // partial sums of a slab into a double-buffered shared array, meet at a named barrier of the group, and
 // warp 0 of the group adds the P partials in part order: results are identical from run to run.
 template <bool F16, int SPS, int PRO, int P>
-__global__ void __launch_bounds__(128) w4_slab_kernel(const W4SArgs a) {
+__global__ void __launch_bounds__(32 * (P > 4 ? P : 4)) w4_slab_kernel(const W4SArgs a) {
   constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;  // 32-k steps per ring stage
   constexpr int SEGST = SPST / SPS;
   constexpr int RING = kStreamRing;
   constexpr int WSTAGE = SPST * 512;    // weight bytes of a stage (32 lanes x 16 B per step)
   constexpr int SZSTAGE = SEGST * 128;  // scale / zero bytes of a stage (8 records of 16 B per segment)
-  constexpr int GPC = 4 / P;            // slab groups per CTA
+  constexpr int NW = P > 4 ? P : 4;     // warps per CTA
+  constexpr int GPC = NW / P;           // slab groups per CTA
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float s_inv[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1169,11 +1185,7 @@ __global__ void __launch_bounds__(128) w4_slab_kernel(const W4SArgs a) {
 #pragma unroll
     for (int i = 0; i < SPST; ++i) {
       if (i % SPS == 0) {  // a new segment: scale and zero of columns 4r .. 4r + 3
-        const uint4 sz = lds128(sb + WSTAGE + (i / SPS) * 128 + r * 16);
-        dp[0] = dq_params<F16>(uint16_t(sz.x & 0xFFFFu), uint16_t(sz.z & 0xFFFFu));
-        dp[1] = dq_params<F16>(uint16_t(sz.x >> 16), uint16_t(sz.z >> 16));
-        dp[2] = dq_params<F16>(uint16_t(sz.y & 0xFFFFu), uint16_t(sz.w & 0xFFFFu));
-        dp[3] = dq_params<F16>(uint16_t(sz.y >> 16), uint16_t(sz.w >> 16));
+        dq_params_shared<F16>(lds128(sb + WSTAGE + (i / SPS) * 128 + r * 16), c, dp);
       }
       const uint4 w4 = lds128(sb + i * 512 + lane * 16);
       const uint32_t wd[4] = {w4.x, w4.y, w4.z, w4.w};
@@ -1505,36 +1517,40 @@ static bool gemv_eligible(const W4SArgs& a, const W4GPlan& p) {
 // ---- slab-streaming GEMV (M <= 8): plan and launch
 
 struct W4SlabPlan {
-  int P, per_sm, grid;
+  int P, per_sm, grid, sms;
   size_t smem;
   bool ok;
 };
 
-// P: the smallest split that gives every SM at least kSlabWarpsPerSm busy warps (1, 2 or 4); the grid covers
-// the slab groups, at most per_sm CTAs per SM (shared memory and registers).
-constexpr int kSlabWarpsPerSm = 8;
+// Wide matrices only (at least two slabs per SM; narrower ones go to the register-streaming GEMV, whose
+// cluster split spreads few slabs over all SMs).  P: the smallest split (1, 2, 4 or 8) giving kSlabWarpsPerSm
+// busy warps per SM; the grid covers the slab groups, at most as many CTAs as are resident at once.
+constexpr int kSlabWarpsPerSm = 32;
 
 static W4SlabPlan plan_w4_slab(const W4SArgs& a, int sps, int sms) {
   W4SlabPlan p{};
   const int spst = sps > kStreamSteps ? sps : kStreamSteps;
   const int64_t slabs = cdiv(a.N, 32);
-  p.P = 4;
-  for (int P : {1, 2, 4})
+  p.P = 8;
+  for (int P : {1, 2, 4, 8})
     if (slabs * P >= int64_t(kSlabWarpsPerSm) * sms) {
       p.P = P;
       break;
     }
-  if (g_w4_ovr_kernel == 6 && (g_w4_ovr_wk == 1 || g_w4_ovr_wk == 2 || g_w4_ovr_wk == 4)) p.P = g_w4_ovr_wk;
+  if (g_w4_ovr_kernel == 6 && (g_w4_ovr_wk == 1 || g_w4_ovr_wk == 2 || g_w4_ovr_wk == 4 || g_w4_ovr_wk == 8))
+    p.P = g_w4_ovr_wk;
+  const int NW = p.P > 4 ? p.P : 4;
   const int xpitch = (a.K / 8) % 8 == 0 ? a.K * 2 + 64 : a.K * 2;
   const size_t x_bytes = (size_t(a.M) * xpitch + 127) / 128 * 128;
-  const size_t part_bytes = p.P > 1 ? size_t(2) * 4 * 256 * 4 : 0;
-  p.smem = x_bytes + part_bytes + 4 * kStreamRing * (size_t(spst) * 512 + (spst / sps) * 128);
+  const size_t part_bytes = p.P > 1 ? size_t(2) * NW * 256 * 4 : 0;
+  p.smem = x_bytes + part_bytes + NW * kStreamRing * (size_t(spst) * 512 + (spst / sps) * 128);
   int per_sm = int((227 * 1024) / (p.smem + 1024));
-  p.per_sm = per_sm < 1 ? 1 : (per_sm > 6 ? 6 : per_sm);  // 6 x 128 threads at <= 80 registers
-  const int64_t groups = cdiv(slabs, 4 / p.P);
+  p.per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
+  const int64_t groups = cdiv(slabs, NW / p.P);
   p.grid = int(std::min<int64_t>(int64_t(sms) * p.per_sm, groups));
+  p.sms = sms;
   p.ok = a.M <= 8 && a.ar_world <= 1 && a.vec_w && a.vec_s && a.K % (p.P * 32 * spst) == 0 &&
-         p.smem <= 200 * 1024;
+         p.smem <= 200 * 1024 && (slabs >= 2 * int64_t(sms) || g_w4_ovr_kernel == 6);
   return p;
 }
 
@@ -1542,9 +1558,14 @@ template <bool F16, int SPS, int PRO, int P>
 static cudaError_t launch_slab_impl(const W4SArgs& a, const W4SlabPlan& p, cudaStream_t stream) {
   auto kern = w4_slab_kernel<F16, SPS, PRO, P>;
   if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), p.smem)) return e;
+  // a persistent grid: no more CTAs than can be resident at once (registers and shared memory)
+  constexpr int NW = P > 4 ? P : 4;
+  int per_sm = 0;
+  if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * NW, p.smem)) return e;
+  per_sm = std::max(1, std::min(per_sm, p.per_sm));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(p.grid));
-  cfg.blockDim = dim3(128);
+  cfg.gridDim = dim3(unsigned(std::min<int64_t>(int64_t(p.grid), int64_t(p.sms) * per_sm)));
+  cfg.blockDim = dim3(32 * NW);
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1580,11 +1601,13 @@ static cudaError_t launch_slab_p(bool f16, const W4SArgs& a, const W4SlabPlan& p
 static cudaError_t launch_slab(bool f16, W4SArgs a, const W4SlabPlan& p, int sps, cudaStream_t stream) {
   a.xpitch = (a.K / 8) % 8 == 0 ? a.K * 2 + 64 : a.K * 2;
   a.off_part = int((size_t(a.M) * a.xpitch + 127) / 128 * 128);
-  a.off_sz = a.off_part + (p.P > 1 ? 2 * 4 * 256 * 4 : 0);  // start of the rings
+  const int NW = p.P > 4 ? p.P : 4;
+  a.off_sz = a.off_part + (p.P > 1 ? 2 * NW * 256 * 4 : 0);  // start of the rings
   switch (p.P) {
     case 1: return launch_slab_p<1>(f16, a, p, sps, stream);
     case 2: return launch_slab_p<2>(f16, a, p, sps, stream);
-    default: return launch_slab_p<4>(f16, a, p, sps, stream);
+    case 4: return launch_slab_p<4>(f16, a, p, sps, stream);
+    default: return launch_slab_p<8>(f16, a, p, sps, stream);
   }
 }
 

@@ -380,8 +380,8 @@ def test_shared_workspace_across_plans_stays_consistent(cuda_device):
 @pytest.mark.parametrize("N,K,G", [(200, 2048, 128), (2048, 2048, 128), (3072, 2048, 64), (2048, 8192, 32),
                                    (96, 384, 96), (16384, 2048, 128)])
 def test_register_gemv_every_plan_matches_oracle(N, K, G, M, dtype, cuda_device):
-    """The M <= 8 kernels under every choice of the tuning hook -- the slab-streaming GEMV with K split over 1, 2
-    or 4 warps, the register-streaming GEMV with its warp / cluster splits and ring depths, the staged and the
+    """The M <= 8 kernels under every choice of the tuning hook -- the slab-streaming GEMV with K split over 1, 2,
+    4 or 8 warps, the register-streaming GEMV with its warp / cluster splits and ring depths, the staged and the
     lm_head streaming kernels -- against the oracle, and run to run identical."""
     from int4_b200 import _lib, quantize_int4_ref, w4a16_matmul
 
@@ -392,7 +392,7 @@ def test_register_gemv_every_plan_matches_oracle(N, K, G, M, dtype, cuda_device)
     qw, s, z = quantize_int4_ref(w, G)  # any multiple of 8 dividing K, e.g. G = 96
     ref = _oracle_mm(x, qw, s, z)
     plans = [(0, 0, 0), (2, 0, 0), (3, 0, 0), (4, 0, 0), (5, 0, 0), (1, 2, 1), (1, 8, 2), (1, 4, 4), (1, 1, 8),
-             (6, 1, 0), (6, 2, 0), (6, 4, 0)]
+             (6, 1, 0), (6, 2, 0), (6, 4, 0), (6, 8, 0)]
     try:
         for kernel, wk, splits in plans:
             L.i4b_set_w4_kernel_override(kernel, wk, splits)
