@@ -1665,6 +1665,9 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
   // kernel choice for M <= 8: the slab-streaming GEMV, else the register-streaming one, unless the tuning hook
   // asks for another
   const bool ovr_reg = g_w4_ovr_kernel == 1 || g_w4_ovr_kernel == 4 || g_w4_ovr_kernel == 5;
+  // one token over a very wide matrix (an lm_head): the one-warp-per-slab stream measured fastest
+  if (sms > 0 && g_w4_ovr_kernel == 0 && a.M == 1 && a.ar_world <= 1 && stream_eligible(a, p, sms))
+    return launch_stream(f16, a, p.SPS, sms, stream);
   if (sms > 0 && (g_w4_ovr_kernel == 0 || g_w4_ovr_kernel == 6)) {
     const W4SlabPlan sp = plan_w4_slab(a, p.SPS, sms);
     if (sp.ok) return launch_slab(f16, a, sp, p.SPS, stream);

@@ -1,19 +1,22 @@
-"""One rank of the two-GPU tensor-parallel decode check (launched by tests/test_decode_gpu.py via torchrun).
+"""One rank of the tensor-parallel decode check (tests/test_decode_gpu.py launches it on two GPUs via torchrun;
+it runs on any number of ranks that divides the heads).
 
-Every rank builds the same seeded Llama, runs its ``LlamaTP`` shard for a
+Every rank builds the same seeded Llamas, runs its ``LlamaTP`` shard for a
 prompt and three cached decode steps, and compares with a one-rank ``LlamaTP``
 of the same weights.  The row-parallel o/down outputs of the decode steps are
 summed inside the W4 matmuls through peer exchange buffers
 (``w4a16_matmul_allreduce``), by an NCCL all-reduce (``peer_allreduce=False``),
-or -- for the wider model, whose shards qualify -- inside the persistent decode
-launch, which exchanges the partials itself; the prompt always uses NCCL; the
-vocab-parallel logits are all-gathered, and the greedy token computed without
-that all-gather (``decode_greedy``) must be their first maximum.  With the fused sums, three more steps
-replayed from one CUDA graph must equal the eager steps bit for bit.  Exit
-status 0 only if every rank stays within 2e-2 max-abs (for the wider,
-persistent model: max(2e-2, twice the noise floor of a cached step at that
-width, measured in the run between two one-rank W4 decoders that differ only in
-summation order), and no kernel's bounded wait expired.
+or -- for the Llama-3.2-1B-width model where its shards qualify (two and four
+ranks) -- inside the persistent decode launch, which exchanges the partials
+itself; the prompt always uses NCCL; the vocab-parallel logits are
+all-gathered, and the greedy token computed without that all-gather
+(``decode_greedy``) must be their first maximum.  With the peer exchange, three
+more steps replayed from one CUDA graph must equal the eager steps bit for bit.
+Exit status 0 only if the small models stay within 2e-2 max-abs of one rank;
+the Llama-1B-width model is held to the exact fp32 run of its fake-quant
+weights -- no farther from it than the one-rank decoder (x1.25), or 2e-2 --
+because one bf16 ulp of its larger logits already exceeds 2e-2; and no
+kernel's bounded wait expired.
 """
 from __future__ import annotations
 
@@ -59,6 +62,29 @@ def main() -> int:
 
     from int4_b200 import _lib
 
+    def exact_logits(hf, ids, toks):
+        """Logits (fp32) of the fake-quant model in exact fp32 arithmetic: all prompt positions, then one cached
+        step per token of ``toks`` (StaticCache, as the reference's decode loop runs it)."""
+        import copy
+
+        from transformers import StaticCache
+
+        from oracle import int4_torch as ot
+
+        exact = copy.deepcopy(hf)
+        ot.fake_quantize_model_(exact, 128, skip=("lm_head",))
+        exact = exact.float()
+        S = ids.shape[1]
+        cache = StaticCache(config=exact.config, max_cache_len=S + len(toks) + 8)
+        out = [exact(input_ids=ids, cache_position=torch.arange(S, device=dev), past_key_values=cache,
+                     use_cache=True).logits.float()]
+        for i, t in enumerate(toks):
+            pos = torch.tensor([S + i], device=dev)
+            out.append(exact(input_ids=t, cache_position=pos, position_ids=pos[None], past_key_values=cache,
+                             use_cache=True).logits.float())
+        del exact
+        return out
+
     graph_diff, greedy_bad = 0.0, 0
     excess, report = -1.0, []  # max over runs of (difference - bound); per-run "difference / bound"
     with torch.no_grad():
@@ -78,24 +104,16 @@ def main() -> int:
             assert (tp.peers is not None) == peer
             assert (tp.persistent is not None) == persistent
             one = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev)
-            # Noise floor of a cached step at this width: two one-rank W4 decoders whose only difference is
-            # the fp32 summation order (the persistent launch against the per-projection launches).  Where
-            # the tensor-parallel model runs the persistent decode its bound is max(2e-2, twice that floor).
-            floor_ref = LlamaTP(hf, w4=True, quantize_lm_head=lm_w4, rank=0, world=1, max_seq=64, device=dev,
-                                persistent=False) if persistent else None
             a, b = tp.prefill(ids, all_logits=True), one.prefill(ids, all_logits=True)
-            worst = (a.float() - b.float()).abs().max().item()
-            floor = 0.0
-            if floor_ref is not None:
-                floor_ref.prefill(ids)
+            tp_logits, one_logits = [a.float()], [b.float()]
             tok = b[:, -1].argmax(-1, keepdim=True)
-            eager = []
+            toks, eager = [], []
             for step in range(3):
                 pos = torch.tensor([24 + step], device=dev)
                 a, b = tp.decode_step(tok, pos), one.decode_step(tok, pos)
-                worst = max(worst, (a.float() - b.float()).abs().max().item())
-                if floor_ref is not None:
-                    floor = max(floor, (floor_ref.decode_step(tok, pos).float() - b.float()).abs().max().item())
+                tp_logits.append(a.float())
+                one_logits.append(b.float())
+                toks.append(tok)
                 eager.append(a.clone())
                 # the same step again (same position, same cache writes), choosing the token without the
                 # logits all-gather: the first maximum of the gathered logits
@@ -103,6 +121,18 @@ def main() -> int:
                 if not torch.equal(greedy, a[:, -1].float().argmax(-1, keepdim=True)):
                     greedy_bad += 1
                 tok = b[:, -1].argmax(-1, keepdim=True)
+            worst = max((x - y).abs().max().item() for x, y in zip(tp_logits, one_logits))
+            if hf is hf_mid:
+                # At the Llama-1B widths one bf16 ulp of a logit of 4 is 0.031, so two correct decoders differ
+                # by more than 2e-2.  Judge both against the exact model instead: the same fake-quant weights
+                # run by transformers in fp32 (prompt, then the same cached steps); the tensor-parallel
+                # logits must be no farther from it than the one-rank logits are (x1.25), or 2e-2.
+                ref = exact_logits(hf, ids, toks)
+                e_tp = max((x - y).abs().max().item() for x, y in zip(tp_logits, ref))
+                e_one = max((x - y).abs().max().item() for x, y in zip(one_logits, ref))
+                worst, bound = e_tp, max(2e-2, 1.25 * e_one)
+            else:
+                bound = 2e-2
             if peer:
                 # the same three steps replayed from one captured step: identical logits
                 first = one.prefill(ids)[:, -1].argmax(-1, keepdim=True)
@@ -123,7 +153,6 @@ def main() -> int:
                 torch.cuda.synchronize()
                 del graph
             tp.close()
-            bound = max(2e-2, 2 * floor)
             excess = max(excess, worst - bound)
             report.append(f"{worst:.3e}/{bound:.1e}")
     flags = _lib.device_error_flags(local)
@@ -132,7 +161,8 @@ def main() -> int:
     torch.cuda.synchronize()
     dist.destroy_process_group()
     if rank == 0:
-        print(f"max |logits(tp{world}) - logits(tp1)| / bound per run: {', '.join(report)}; "
+        print(f"max-abs logit difference / bound per run (small models: tp{world} vs one rank; Llama-1B widths: "
+              f"tp{world} vs the exact fp32 model): {', '.join(report)}; "
               f"graph vs eager {t[1].item():.3e}, device error flags {'set' if t[2].item() else 'clear'}, "
               f"greedy mismatches {int(t[3].item())}")
     return 0 if t[0].item() <= 0.0 and t[1].item() == 0.0 and t[2].item() == 0.0 and t[3].item() == 0 else 1
