@@ -313,10 +313,12 @@ typedef struct i4b_decode_model {
   void* h_out;           /* bf16 [batch, hidden]: the residual stream after the last layer */
   /* Tensor parallelism: NULL (or world 1) for one rank.  Otherwise heads, kv_heads and intermediate are
    * this rank's shares, the weights its shards (q/k/v and gate/up split along N, o and down along K) and
-   * the caches hold its kv heads.  The o / down epilogues then store their fp32 partial outputs into
-   * every rank's exchange buffer (each of at least i4b_decode_peer_capacity outputs, used by no other
-   * call), and the stages that consume the residual stream add the ranks' partials in rank order: every
-   * rank ends with the same h_out.  All ranks must make the same sequence of calls on one group. */
+   * the caches hold its kv heads.  The o / down epilogues store each fp32 partial output, together with a
+   * tag naming the step and stage, as one 64-bit word into every rank's exchange buffer (each of at least
+   * i4b_decode_peer_capacity outputs, used by no other call); the stages that consume the residual stream
+   * poll those words until the tags match (bounded) and add the ranks' partials in rank order: every rank
+   * ends with the same h_out, and no fence or flag is needed between ranks.  All ranks must make the same
+   * sequence of calls on one group. */
   const i4b_peer_group* peers;
 } i4b_decode_model;
 

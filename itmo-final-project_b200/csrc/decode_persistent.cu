@@ -175,36 +175,56 @@ __device__ bool wait_counter(const unsigned int* c, unsigned int target, const u
 }
 
 // ---- tensor parallelism: exchange buffer of rank p (i4b_peer_group), as this launch uses it:
-//   [epoch u32 | 256 B][counters u32 [layers][2]: o_proj, down_proj partials received from the other ranks]
-//   [fp32 partial outputs [layers][2][world][kMaxTok][hidden], at kArDataOff]
-// The counters only grow: step e (the epoch) waits for (e + 1) * (world - 1) * slabs of the stage.
-__device__ __forceinline__ float* xdata(const DkHot& P, int p, int l, int s, int src) {
-  return reinterpret_cast<float*>(P.xb[p] + kArDataOff) +
+//   [epoch u32 | 256 B] ... [tagged partial outputs u64 [layers][2][world][kMaxTok][hidden], at kArDataOff]
+// Each exchanged fp32 partial travels with its tag in ONE 64-bit store (value in the low word, tag in the
+// high word), and the reader polls the words it needs until every tag is the one it expects: the data is its
+// own flag, so neither a memory fence nor a counter sits between a producer and its readers (a system-scope
+// fence would wait for everything the SM has in flight, the weight prefetch included).  The tag of
+// (step e, layer l, o_proj / down_proj s) is e * 2L + 2l + s + 1: never 0 (the zero-filled buffer), and
+// different from every earlier use of the same words.
+__device__ __forceinline__ uint64_t* xword(const DkHot& P, int p, int l, int s, int src) {
+  return reinterpret_cast<uint64_t*>(P.xb[p] + kArDataOff) +
          int64_t((l * 2 + s) * P.tp_world + src) * kMaxTok * P.m.hidden;
 }
-__device__ __forceinline__ unsigned int* xctr(const DkHot& P, int p, int l, int s) {
-  return reinterpret_cast<unsigned int*>(P.xb[p] + kArCtlBytes) + l * 2 + s;
+__device__ __forceinline__ unsigned int xtag(unsigned int ep, int l, int s, int layers) {
+  return ep * unsigned(2 * layers) + unsigned(2 * l + s) + 1u;
 }
-__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-// Wait until the counter another GPU raises reaches target (wrap-around order; acquire at system scope).
-__device__ bool wait_counter_sys(const unsigned int* c, unsigned int target, const unsigned int* abort_word) {
-  const uint64_t t0 = globaltimer_ns();
+__device__ __forceinline__ void ld_relaxed_sys_u64x2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// The 8 partials (token t, columns 8ch..8ch+7) of source rank `src` for update u, once all carry `tag`.
+// Bounded: false after I4B_WAIT_LIMIT_NS or when another CTA aborted.
+__device__ __forceinline__ bool poll_partials(const DkHot& P, int u, int src, int t, int ch, unsigned int tag,
+                                              const unsigned int* abort_word, float (&v)[8]) {
+  const uint64_t* d = xword(P, P.tp_rank, u >> 1, u & 1, src) + int64_t(t) * P.m.hidden + 8 * ch;
+  uint64_t w[8];
+  uint64_t t0 = 0;
   for (uint32_t i = 1;; ++i) {
-    if (int(ld_acquire_sys_u32(c) - target) >= 0) return true;
-    if ((i & 31u) == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ld_relaxed_sys_u64x2(d + 2 * j, w[2 * j], w[2 * j + 1]);
+    bool ready = true;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ready = ready && unsigned(w[j] >> 32) == tag;
+    if (ready) break;
+    if (i == 1) t0 = globaltimer_ns();
+    if ((i & 15u) == 0) {
       if (ld_relaxed_u32(abort_word)) return false;
       if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
     }
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(unsigned(w[j]));
+  return true;
 }
 // Eight residual values (token t, columns 8ch..8ch+7) after update u: bf16(h_{u-1} + bf16(sum over ranks,
 // in rank order, of their fp32 partials)) -- the one-rank epilogue's rounding, bf16(h + bf16(sum)).
-// h_{-1} is the token's embedding row.
-__device__ __forceinline__ uint4 residual_chunk(const DkHot& P, int u, int t, int ch) {
+// h_{-1} is the token's embedding row.  The partials are polled until they carry this step's tag; a wait
+// that gives up clears *ok.
+__device__ __forceinline__ uint4 residual_chunk(const DkHot& P, int u, int t, int ch, unsigned int ep,
+                                                const unsigned int* abort_word, bool* ok) {
   const i4b_decode_model& m = P.m;
   const int H = m.hidden;
   uint4 hv;
@@ -216,11 +236,15 @@ __device__ __forceinline__ uint4 residual_chunk(const DkHot& P, int u, int t, in
     hv = ldcg128(P.hbuf[(u - 1) & 1] + int64_t(t) * H + 8 * ch);
   }
   float sm[8];
+  const unsigned int tag = xtag(ep, u >> 1, u & 1, m.layers);
 #pragma unroll 1
   for (int r = 0; r < P.tp_world; ++r) {
-    const float* d = xdata(P, P.tp_rank, u >> 1, u & 1, r) + int64_t(t) * H + 8 * ch;
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(d)), b = __ldcg(reinterpret_cast<const float4*>(d + 4));
-    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float v[8];
+    if (!poll_partials(P, u, r, t, ch, tag, abort_word, v)) {
+      *ok = false;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) sm[i] = r == 0 ? v[i] : sm[i] + v[i];
   }
@@ -359,13 +383,16 @@ __device__ __noinline__ void stage_x(int g, int l, int K) {
     // one CTA also stores them for the next update
     const int u = g == G_GU ? 2 * l : 2 * l - 1;
     uint16_t* hout = int(blockIdx.x) == P.writer[g] ? P.hbuf[u & 1] : nullptr;
+    const unsigned int* abort_word = P.ctr + P.i_abort;
+    bool ok = true;
 #pragma unroll 1
     for (int idx = tid; idx < total; idx += kCT) {
       const int t = idx >> lg, ch = idx & (nch - 1);
-      const uint4 v = residual_chunk(P, u, t, ch);
+      const uint4 v = residual_chunk(P, u, t, ch, S.ep, abort_word, &ok);
       *reinterpret_cast<uint4*>(sx + t * P.xpitch + ch * 16) = v;
       if (hout) *reinterpret_cast<uint4*>(hout + int64_t(t) * H + 8 * ch) = v;
     }
+    if (!ok) S.flag = 0;  // a partial that never arrived: the stage fails (checked after the barrier)
     cbar();
   } else {
 #pragma unroll 1
@@ -467,18 +494,14 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
       c = P.ctr + l * C_LAYER + C_GU, target = unsigned(P.nslab[G_GU]);
     }
     if (c != nullptr && !wait_counter(c, target, abort_word)) S.flag = 0;  // sticky: errors are never cleared
-    if (TP && S.flag && (g == G_GU || (g == G_QKV && l > 0))) {
-      const int lu = g == G_GU ? l : l - 1, su = g == G_GU ? 0 : 1;
-      const unsigned int xt = (S.ep + 1u) * unsigned(P.tp_world - 1) * unsigned(P.nslab[su ? G_DOWN : G_O]);
-      if (!wait_counter_sys(xctr(P, P.tp_rank, lu, su), xt, abort_word)) S.flag = 0;
-    }
   }
   cbar();
   if (!S.flag) return false;
   stamp(P, l, st_id, 1);
   const int K = g == G_DOWN ? m.intermediate : (g == G_O ? P.q_n : m.hidden);
-  stage_x<TP>(g, l, K);
+  stage_x<TP>(g, l, K);  // under tensor parallelism it also waits for the other ranks' partials
   cbar();
+  if (!S.flag) return false;
   stamp(P, l, st_id, 2);
   // residual inputs of the o_proj / down_proj epilogue: loaded here, consumed after the pieces
   uint16_t* h = static_cast<uint16_t*>(m.h_out);
@@ -602,9 +625,10 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
       const int64_t nn = int64_t(S.slab[ib + i]) * kSlabW + col;
       if (g == G_QKV) {
         P.qkv[int64_t(b) * P.qkv_n + nn] = uint16_t(bfr(sum));
-      } else if (tp_out) {  // this rank's fp32 partial, into every rank's buffer
+      } else if (tp_out) {  // this rank's fp32 partial with its tag, into every rank's buffer: one 64-bit store
         const int s2 = g == G_O ? 0 : 1;
-        for (int p = 0; p < P.tp_world; ++p) xdata(P, p, l, s2, P.tp_rank)[int64_t(b) * H + nn] = sum;
+        const uint64_t word = (uint64_t(xtag(S.ep, l, s2, m.layers)) << 32) | __float_as_uint(sum);
+        for (int p = 0; p < P.tp_world; ++p) st_relaxed_sys_u64(xword(P, p, l, s2, P.tp_rank) + int64_t(b) * H + nn, word);
       } else {
         h[int64_t(b) * H + nn] = uint16_t(bfr(bfv(res[k]) + bfv(bfr(sum))));
       }
@@ -617,15 +641,7 @@ __device__ __noinline__ bool gemv_stage(int g, int l) {
     // release: the CTA's output stores (ordered before by the barrier) are visible before the count
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.ctr + l * C_LAYER + st_id), "r"(unsigned(n))
                  : "memory");
-    // the barrier above ordered every thread's pushes before this fence; the fence (cumulative) orders them
-    // before the counters of the other ranks, once per CTA
-    if (tp_out) __threadfence_system();
-    if (tp_out)
-      for (int p = 0; p < P.tp_world; ++p)
-        if (p != P.tp_rank)
-          asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(xctr(P, p, l, g == G_O ? 0 : 1)),
-                       "r"(unsigned(n))
-                       : "memory");
+    // (the partials sent to the other ranks carry their own tags: nothing to publish for them)
   }
   stamp(P, l, st_id, 6);
   return true;
@@ -882,21 +898,21 @@ __device__ __noinline__ bool tp_finalize() {
   const int tid = threadIdx.x, L = m.layers, H = m.hidden;
   const unsigned int* abort_word = P.ctr + P.i_abort;
   if (tid == 0) {
-    const unsigned int xt = (S.ep + 1u) * unsigned(P.tp_world - 1) * unsigned(P.nslab[G_DOWN]);
-    if (!wait_counter(P.ctr + (L - 1) * C_LAYER + C_DOWN, unsigned(P.nslab[G_DOWN]), abort_word) ||
-        !wait_counter_sys(xctr(P, P.tp_rank, L - 1, 1), xt, abort_word))
-      S.flag = 0;
+    if (!wait_counter(P.ctr + (L - 1) * C_LAYER + C_DOWN, unsigned(P.nslab[G_DOWN]), abort_word)) S.flag = 0;
   }
   cbar();
   if (!S.flag) return false;
   uint16_t* out = static_cast<uint16_t*>(m.h_out);
   const int nch = H / 8;
+  bool ok = true;
 #pragma unroll 1
   for (int idx = tid; idx < m.batch * nch; idx += kCT) {
     const int t = idx / nch, ch = idx - t * nch;
-    *reinterpret_cast<uint4*>(out + int64_t(t) * H + 8 * ch) = residual_chunk(P, 2 * L - 1, t, ch);
+    *reinterpret_cast<uint4*>(out + int64_t(t) * H + 8 * ch) = residual_chunk(P, 2 * L - 1, t, ch, S.ep, abort_word, &ok);
   }
-  return true;
+  if (!ok) S.flag = 0;
+  cbar();
+  return S.flag != 0;
 }
 
 template <int SPS, int GS, bool TP>
@@ -1185,9 +1201,10 @@ cudaError_t launch_dk_s(const DkParams& p, int grid, size_t smem, cudaStream_t s
 }  // namespace
 
 int64_t decode_peer_capacity(int layers, int world, int hidden) {
-  // fp32 partials [layers][2][world][kMaxTok][hidden] in the 2 x kArMaxRanks x capacity data area
-  const int64_t floats = int64_t(layers) * 2 * world * kMaxTok * hidden;
-  return (floats + 2 * kArMaxRanks - 1) / (2 * kArMaxRanks);
+  // tagged partials (8 bytes each) [layers][2][world][kMaxTok][hidden] in the 2 x kArMaxRanks x capacity fp32
+  // data area
+  const int64_t words = int64_t(layers) * 2 * world * kMaxTok * hidden * 2;
+  return (words + 2 * kArMaxRanks - 1) / (2 * kArMaxRanks);
 }
 
 size_t tile_w4_bytes(int64_t N, int64_t K, int G) {

@@ -14,7 +14,7 @@ all-gathered, and the greedy token computed without that all-gather
 more steps replayed from one CUDA graph must equal the eager steps bit for bit.
 Exit status 0 only if the small models stay within 2e-2 max-abs of one rank;
 the Llama-1B-width model is held to the exact fp32 run of its fake-quant
-weights -- no farther from it than the one-rank decoder (x1.25), or 2e-2 --
+weights -- no farther from it than the one-rank decoder (x1.5), or 2e-2 --
 because one bf16 ulp of its larger logits already exceeds 2e-2; and no
 kernel's bounded wait expired.
 """
@@ -126,11 +126,12 @@ def main() -> int:
                 # At the Llama-1B widths one bf16 ulp of a logit of 4 is 0.031, so two correct decoders differ
                 # by more than 2e-2.  Judge both against the exact model instead: the same fake-quant weights
                 # run by transformers in fp32 (prompt, then the same cached steps); the tensor-parallel
-                # logits must be no farther from it than the one-rank logits are (x1.25), or 2e-2.
+                # logits must be no farther from it than the one-rank logits are (x1.5: a few steps of a
+                # different summation order are a small sample of that noise), or 2e-2.
                 ref = exact_logits(hf, ids, toks)
                 e_tp = max((x - y).abs().max().item() for x, y in zip(tp_logits, ref))
                 e_one = max((x - y).abs().max().item() for x, y in zip(one_logits, ref))
-                worst, bound = e_tp, max(2e-2, 1.25 * e_one)
+                worst, bound = e_tp, max(2e-2, 1.5 * e_one)
             else:
                 bound = 2e-2
             if peer:
