@@ -193,10 +193,10 @@ int i4b_w4a16_matmul_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, i
  * The reference runs on one GPU.  Its tensor-parallel form shards o_proj and down_proj along K
  * (row-parallel): every rank computes a partial product over its slice of K and the ranks' partials
  * are summed.  i4b_w4a16_matmul_allreduce does that sum inside the matmul's epilogue. Each CTA:
- *   - stores its fp32 partial outputs into every rank's exchange buffer (plain stores through
- *     CUDA-IPC mappings);
- *   - raises one flag per rank;
- *   - waits, bounded, for the same CTA of every other rank;
+ *   - stores each fp32 partial output, with a tag naming the call, as one 64-bit word into every rank's
+ *     exchange buffer (plain stores through CUDA-IPC mappings);
+ *   - polls, bounded, the words of the same outputs from every other rank until their tags match (the data
+ *     is its own flag: no fence, no separate flag);
  *   - adds the ranks' partials in rank order and writes y.
  * It replaces w4a16_matmul (int4_triton/gemm.py:303-309) followed by a separate all-reduce launch.
  * Every rank ends with bit-identical y.  All ranks must make the same sequence of calls on one

@@ -1201,9 +1201,9 @@ cudaError_t launch_dk_s(const DkParams& p, int grid, size_t smem, cudaStream_t s
 }  // namespace
 
 int64_t decode_peer_capacity(int layers, int world, int hidden) {
-  // tagged partials (8 bytes each) [layers][2][world][kMaxTok][hidden] in the 2 x kArMaxRanks x capacity fp32
-  // data area
-  const int64_t words = int64_t(layers) * 2 * world * kMaxTok * hidden * 2;
+  // tagged partials (8 bytes each) [layers][2][world][kMaxTok][hidden] in the 2 x kArMaxRanks x capacity data
+  // area of 8-byte words
+  const int64_t words = int64_t(layers) * 2 * world * kMaxTok * hidden;
   return (words + 2 * kArMaxRanks - 1) / (2 * kArMaxRanks);
 }
 

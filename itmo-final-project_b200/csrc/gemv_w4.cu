@@ -88,24 +88,17 @@ __device__ unsigned int g_w4_err = 0;
 
 // ---- fused all-reduce over peer exchange buffers (layout in kernels.h).  The helpers take any argument
 // struct with the fields ar_buf, ar_cap, ar_world and ar_rank.
+//
+// Each exchanged fp32 value travels with its tag -- the call's epoch + 1 -- in ONE 64-bit store (value in the
+// low word, tag in the high word), and the reader polls the words it needs until their tags match: the data
+// is its own flag, so no memory fence and no per-CTA flag sit between the ranks.  Two slots (epoch & 1)
+// alternate: a rank starts call e + 2, which rewrites call e's slot, only after every rank's data of call
+// e + 1 reached it, i.e. after every rank finished call e.
 
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// fp32 outputs of source rank `src` in rank p's buffer
+// tagged outputs of source rank `src` in rank p's buffer
 template <class A>
-__device__ __forceinline__ float* ar_data(const A& a, int p, uint32_t slot, int src) {
-  return reinterpret_cast<float*>(a.ar_buf[p] + kArDataOff) + (int64_t(slot) * kArMaxRanks + src) * a.ar_cap;
-}
-template <class A>
-__device__ __forceinline__ unsigned int* ar_flag(const A& a, int p, uint32_t slot, int src, int cta) {
-  return reinterpret_cast<unsigned int*>(a.ar_buf[p] + kArCtlBytes) + (int(slot) * kArMaxRanks + src) * kArMaxCtas +
-         cta;
+__device__ __forceinline__ uint64_t* ar_data(const A& a, int p, uint32_t slot, int src) {
+  return reinterpret_cast<uint64_t*>(a.ar_buf[p] + kArDataOff) + (int64_t(slot) * kArMaxRanks + src) * a.ar_cap;
 }
 // The call's epoch, read once per CTA (after the previous kernel of the stream has completed).
 template <class A>
@@ -114,53 +107,45 @@ __device__ __forceinline__ uint32_t ar_epoch(const A& a, uint32_t* s_ep) {
   __syncthreads();
   return *s_ep;
 }
-// Push one output (offset tok * N + n) to every rank's buffer, slot of this epoch, region of this rank.
+// Push one output (offset tok * N + n) with the call's tag to every rank's buffer, slot of this epoch, region
+// of this rank.
 template <class A>
-__device__ __forceinline__ void ar_push(const A& a, uint32_t slot, int64_t off, float v) {
-  for (int p = 0; p < a.ar_world; ++p) ar_data(a, p, slot, a.ar_rank)[off] = v;
+__device__ __forceinline__ void ar_push(const A& a, uint32_t ep, int64_t off, float v) {
+  const uint64_t word = (uint64_t(ep + 1u) << 32) | __float_as_uint(v);
+  for (int p = 0; p < a.ar_world; ++p)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ar_data(a, p, ep & 1u, a.ar_rank) + off), "l"(word)
+                 : "memory");
 }
-// Sum over source ranks, in rank order, of one output in this rank's buffer.
+// One output of source rank q once it carries the call's tag.  Bounded: a wait that gives up sets
+// I4B_DEVERR_PEER_TIMEOUT and yields 0; once that bit is set, later waits on this device return at once.
 template <class A>
-__device__ __forceinline__ float ar_sum(const A& a, uint32_t slot, int64_t off) {
-  float t[kArMaxRanks];
-#pragma unroll
-  for (int q = 0; q < kArMaxRanks; ++q) t[q] = q < a.ar_world ? __ldcg(ar_data(a, a.ar_rank, slot, q) + off) : 0.0f;
-  float v = t[0];
-#pragma unroll
-  for (int q = 1; q < kArMaxRanks; ++q)
-    if (q < a.ar_world) v += t[q];
-  return v;
-}
-// After every thread of the CTA has pushed: raise this CTA's flag in every other rank's buffer, then wait
-// (bounded) for the same CTA of every other rank.  The CTA barrier orders every thread's pushes before
-// thread 0's system-scope fence, and that fence (cumulative) before its release stores of the flags, so one
-// fence per CTA suffices -- the pattern of a grid-wide barrier.  A wait that gives up sets
-// I4B_DEVERR_PEER_TIMEOUT; once set, later waits on this device return at once.
-template <class A>
-__device__ __forceinline__ void ar_publish_wait(const A& a, uint32_t ep, int cta) {
-  __syncthreads();
-  const uint32_t slot = ep & 1u;
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < a.ar_world; ++p)
-      if (p != a.ar_rank) st_release_sys(ar_flag(a, p, slot, a.ar_rank, cta), ep + 1);
-  }
-  const int src = int(threadIdx.x);
-  if (src < a.ar_world && src != a.ar_rank) {
-    const unsigned int* f = ar_flag(a, a.ar_rank, slot, src, cta);
-    const uint64_t t0 = globaltimer_ns();
-    uint32_t it = 0;
-    while (int(ld_acquire_sys(f) - (ep + 1)) < 0) {
-      if ((++it & 255u) == 0) {
-        if (*reinterpret_cast<volatile unsigned int*>(&g_w4_err) & I4B_DEVERR_PEER_TIMEOUT) break;
-        if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) {
-          atomicOr(&g_w4_err, I4B_DEVERR_PEER_TIMEOUT);
-          break;
-        }
+__device__ __forceinline__ float ar_take(const A& a, uint32_t ep, int q, int64_t off) {
+  const uint64_t* w = ar_data(a, a.ar_rank, ep & 1u, q) + off;
+  uint64_t v;
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
+    if (uint32_t(v >> 32) == ep + 1u) return __uint_as_float(uint32_t(v));
+    if (it == 1) t0 = globaltimer_ns();
+    if ((it & 63u) == 0) {
+      if (*reinterpret_cast<volatile unsigned int*>(&g_w4_err) & I4B_DEVERR_PEER_TIMEOUT) return 0.0f;
+      if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) {
+        atomicOr(&g_w4_err, I4B_DEVERR_PEER_TIMEOUT);
+        return 0.0f;
       }
     }
   }
-  __syncthreads();
+}
+// Sum over source ranks, in rank order, of one output in this rank's buffer (a value that has already arrived
+// costs one load).
+template <class A>
+__device__ __forceinline__ float ar_sum(const A& a, uint32_t ep, int64_t off) {
+  float v = 0.0f;
+  for (int q = 0; q < a.ar_world; ++q) {
+    const float t = ar_take(a, ep, q, off);
+    v = q == 0 ? t : v + t;
+  }
+  return v;
 }
 // The last CTA of the call advances this rank's epoch (read by the next call on the group).
 template <class A>
@@ -541,7 +526,6 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
   if (a.ar_world > 1 && a.mode == 0) {
     // Tensor-parallel sum of the ranks' outputs: push, publish, wait for the other ranks, add in rank order.
     const uint32_t ep = ar_epoch(a, &s_ep);
-    const uint32_t slot = ep & 1u;
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -550,9 +534,8 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
         for (int e = 0; e < 4; ++e) {
           const int tok = mt * 8 + 2 * c + (e & 1);
           const int64_t n = n_lane + 2 * t + (e >> 1);
-          if (tok < M && n < a.N) ar_push(a, slot, int64_t(tok) * a.N + n, acc[t][mt][e]);
+          if (tok < M && n < a.N) ar_push(a, ep, int64_t(tok) * a.N + n, acc[t][mt][e]);
         }
-    ar_publish_wait(a, ep, int(blockIdx.y * gridDim.x + blockIdx.x));
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -561,7 +544,7 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
         for (int e = 0; e < 4; ++e) {
           const int tok = mt * 8 + 2 * c + (e & 1);
           const int64_t n = n_lane + 2 * t + (e >> 1);
-          if (tok < M && n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(ar_sum(a, slot, int64_t(tok) * a.N + n));
+          if (tok < M && n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(ar_sum(a, ep, int64_t(tok) * a.N + n));
         }
     ar_finish(a, ep);
     return;
@@ -595,7 +578,6 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
     const uint32_t rank = cluster_ctarank();
     if (a.ar_world > 1) {
       // The cluster's sums are this rank's partials: push them, then the tensor-parallel sum as in mode 0.
-      const uint32_t slot = ep & 1u;
       for (int idx = int(rank) * kBN + tid; idx < M * kBN; idx += a.S * kBN) {
         const uint32_t addr = smem_u32(sP + idx);
         float t[8];
@@ -607,14 +589,13 @@ __global__ void __launch_bounds__(128) w4_skinny_kernel(const W4SArgs a) {
           if (q < a.S) v += t[q];
         const int tok = idx / kBN;
         const int64_t n = n0 + idx % kBN;
-        if (n < a.N) ar_push(a, slot, int64_t(tok) * a.N + n, v);
+        if (n < a.N) ar_push(a, ep, int64_t(tok) * a.N + n, v);
       }
       cluster_sync();  // remote shared-memory reads done before any CTA of the cluster moves on
-      ar_publish_wait(a, ep, int(blockIdx.y * gridDim.x + blockIdx.x));
       for (int idx = int(rank) * kBN + tid; idx < M * kBN; idx += a.S * kBN) {
         const int tok = idx / kBN;
         const int64_t n = n0 + idx % kBN;
-        if (n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(ar_sum(a, slot, int64_t(tok) * a.N + n));
+        if (n < a.N) y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(ar_sum(a, ep, int64_t(tok) * a.N + n));
       }
       ar_finish(a, ep);
       return;
@@ -1807,19 +1788,17 @@ __global__ void __launch_bounds__(1024) argmax_allreduce_kernel(const ArgmaxArAr
   int64_t bi;
   block_row_argmax(a.x + int64_t(row) * a.sx, a.n, &best, &bi);
   const uint32_t ep = ar_epoch(a, &s_ep);
-  const uint32_t slot = ep & 1u;
   if (threadIdx.x == 0) {
     const int gi = bi < a.n ? int(a.offset + bi) : -1;  // -1: nothing above -inf on this rank
-    ar_push(a, slot, 2 * int64_t(row), best);
-    ar_push(a, slot, 2 * int64_t(row) + 1, __int_as_float(gi));
+    ar_push(a, ep, 2 * int64_t(row), best);
+    ar_push(a, ep, 2 * int64_t(row) + 1, __int_as_float(gi));
   }
-  ar_publish_wait(a, ep, row);
   if (threadIdx.x == 0) {
     float bv = 0.0f;
     int gi = -1;
     for (int q = 0; q < a.ar_world; ++q) {
-      const float v = __ldcg(ar_data(a, a.ar_rank, slot, q) + 2 * row);
-      const int i = __float_as_int(__ldcg(ar_data(a, a.ar_rank, slot, q) + 2 * row + 1));
+      const float v = ar_take(a, ep, q, 2 * int64_t(row));
+      const int i = __float_as_int(ar_take(a, ep, q, 2 * int64_t(row) + 1));
       if (i >= 0 && (gi < 0 || v > bv)) {
         bv = v;
         gi = i;

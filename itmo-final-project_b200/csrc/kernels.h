@@ -58,15 +58,15 @@ struct W4Prologue {
   float eps;
 };
 // Peer exchange buffer of the fused tensor-parallel all-reduce (i4b_peer_group), per rank:
-//   [control: epoch u32, done-ticket u32 | 256 B][flags u32 [2 slots][8 source ranks][kArMaxCtas]]
-//   [data fp32 [2 slots][8 source ranks][capacity]]
-// A call of epoch e uses slot e & 1 and raises flags to e + 1.
+//   [control: epoch u32, done-ticket u32 | 256 B][reserved | kArDataOff]
+//   [data: tagged values u64 [2 slots][8 source ranks][capacity]]
+// A call of epoch e uses slot e & 1; each value is stored with the tag e + 1 in its high word.
 constexpr size_t kArCtlBytes = 256;
 constexpr int kArMaxRanks = 8;
 constexpr int kArMaxCtas = 1024;
 constexpr size_t kArDataOff = kArCtlBytes + size_t(2) * kArMaxRanks * kArMaxCtas * 4;
 inline size_t ar_buffer_bytes(int64_t capacity) {
-  return kArDataOff + size_t(2) * kArMaxRanks * size_t(capacity) * 4;
+  return kArDataOff + size_t(2) * kArMaxRanks * size_t(capacity) * 8;
 }
 struct W4AllReduce {
   void* buffers[kArMaxRanks];

@@ -92,7 +92,8 @@ def test_fused_allreduce_validation_before_any_device_call(L):
     assert call(grp(2, 0, 64, [fake[0], fake[1] + 16])) == 1  # buffers are 256-byte aligned allocations
     assert call(grp(2, 0, 64, fake), M=0) == 0        # empty: no-op
     assert L.i4b_peer_buffer_bytes(0) == 256 + 2 * 8 * 1024 * 4
-    assert L.i4b_peer_buffer_bytes(1000) == 256 + 2 * 8 * 1024 * 4 + 2 * 8 * 1000 * 4
+    # control, reserved, then 2 slots x 8 source ranks x capacity tagged 64-bit values
+    assert L.i4b_peer_buffer_bytes(1000) == 256 + 2 * 8 * 1024 * 4 + 2 * 8 * 1000 * 8
     assert L.i4b_ipc_get_handle(None, None) == 1 and L.i4b_ipc_open_handle(None, None) == 1
 
 
