@@ -1528,7 +1528,7 @@ static W4SlabPlan plan_w4_slab(const W4SArgs& a, int sps, int sms) {
   int per_sm = int((227 * 1024) / (p.smem + 1024));
   p.per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
   const int64_t groups = cdiv(slabs, NW / p.P);
-  p.grid = int(std::min<int64_t>(int64_t(sms) * p.per_sm, groups));
+  p.grid = int(groups);  // slab groups; the launch caps the grid at what is resident and balances it
   p.sms = sms;
   p.ok = a.M <= 8 && a.ar_world <= 1 && a.vec_w && a.vec_s && a.K % (p.P * 32 * spst) == 0 &&
          p.smem <= 200 * 1024 && (slabs >= 2 * int64_t(sms) || g_w4_ovr_kernel == 6);
@@ -1544,8 +1544,13 @@ static cudaError_t launch_slab_impl(const W4SArgs& a, const W4SlabPlan& p, cudaS
   int per_sm = 0;
   if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * NW, p.smem)) return e;
   per_sm = std::max(1, std::min(per_sm, p.per_sm));
+  // Balanced: every CTA takes the same number of slab groups (a ragged last round would cost a whole
+  // group-time for a few CTAs), unless the tuning hook asks for every resident CTA (splits == 1).
+  const int64_t resident = int64_t(p.sms) * per_sm, groups = p.grid;
+  int64_t grid = std::min(groups, resident);
+  if (!(g_w4_ovr_kernel == 6 && g_w4_ovr_gs == 1)) grid = cdiv(groups, cdiv(groups, resident));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(std::min<int64_t>(int64_t(p.grid), int64_t(p.sms) * per_sm)));
+  cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(32 * NW);
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = stream;
