@@ -179,6 +179,15 @@ __device__ __forceinline__ void dq_params_shared(const uint4& sz, int c, DqParam
   }
 }
 
+// First maximum among (value, column) candidates in increasing column order: a strictly greater value wins, an
+// equal one only at a lower column (NaN never compares greater, as in block_row_argmax).
+__device__ __forceinline__ void first_max(float& best, int64_t& bi, float v, int64_t i) {
+  if (v > best || (v == best && i < bi)) {
+    best = v;
+    bi = i;
+  }
+}
+
 __device__ __forceinline__ float bfv(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 __device__ __forceinline__ uint32_t bfr(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
 
@@ -669,7 +678,7 @@ constexpr int kStreamSteps = I4B_STREAM_STEPS;  // 32-k steps per stage (at leas
 // the weight stream never stops between slabs.  The activations (M <= 8 rows x K) are staged once per
 // CTA.  No K split, hence no cross-CTA reduction; the dequant / MMA / segment
 // arithmetic is that of w4_skinny_kernel.
-template <bool F16, int SPS, bool ONE>
+template <bool F16, int SPS, bool ONE, bool ARG = false>
 __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
   constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;  // 32-k steps per ring stage
   constexpr int SEGST = SPST / SPS;
@@ -765,6 +774,8 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
   float acc[2][4], acc1[2][4];  // the k16 halves of each step accumulate separately (two MMA chains)
   int st = 0, slot = 0;
   int64_t n_base = int64_t(gw) * 32 + 4 * r;
+  float gbest[2] = {-INFINITY, -INFINITY};  // fused greedy choice: this lane's first maxima of tokens 2c, 2c+1
+  int64_t gidx[2] = {INT64_MAX, INT64_MAX};
   uint32_t xl = xl0;
   DqParams dp[4];
 #pragma unroll 1
@@ -818,7 +829,14 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
           if (ONE && (e & 1)) continue;
           const int tok = 2 * c + (e & 1);
           const int64_t n = n_base + 2 * t + (e >> 1);
-          if (tok < M && n < a.N) a.y[int64_t(tok) * a.sym + n] = f2h_bits<F16>(acc[t][e] + acc1[t][e]);
+          const uint16_t bits = f2h_bits<F16>(acc[t][e] + acc1[t][e]);
+          if (tok < M && n < a.N) {
+            if (!ARG || a.y) a.y[int64_t(tok) * a.sym + n] = bits;
+            if constexpr (ARG) {
+              const float v = F16 ? __half2float(__ushort_as_half(bits)) : __uint_as_float(uint32_t(bits) << 16);
+              first_max(gbest[e & 1], gidx[e & 1], v, n);
+            }
+          }
         }
       st = 0;
       n_base += int64_t(W) * 32;
@@ -826,18 +844,53 @@ __global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
     }
   }
   cp_async_wait<0>();
+  if constexpr (ARG) {
+    // lanes with the same c hold the same two tokens: reduce over r, then one candidate per warp and token
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const float ob = __shfl_xor_sync(0xFFFFFFFFu, gbest[h], o);
+        const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, gidx[h], o);
+        first_max(gbest[h], gidx[h], ob, oi);
+      }
+    if (r == 0)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int tok = 2 * c + h;
+        if (tok < M)
+          a.cand[int64_t(gw) * M + tok] = make_float2(gbest[h], __int_as_float(gidx[h] == INT64_MAX ? -1 : int(gidx[h])));
+      }
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.tickets, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int nwarps_total = int(gridDim.x) * 4;
+    for (int t = warp; t < M; t += 4) {
+      float best = -INFINITY;
+      int64_t bi = INT64_MAX;
+      for (int w = lane; w < nwarps_total; w += 32) {
+        const float2 cnd = __ldcg(a.cand + int64_t(w) * M + t);
+        const int i = __float_as_int(cnd.y);
+        if (i >= 0) first_max(best, bi, cnd.x, i);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        first_max(best, bi, ob, oi);
+      }
+      if (lane == 0) a.amax_out[t] = bi == INT64_MAX ? 0 : bi;
+    }
+    if (tid == 0) atomicExch(a.tickets, 0u);
+  }
 }
 
 // ------------------------------------------------------------------ greedy choice fused into the GEMV
 
-// First maximum among (value, column) candidates in increasing column order: a strictly greater value wins, an
-// equal one only at a lower column (NaN never compares greater, as in block_row_argmax).
-__device__ __forceinline__ void first_max(float& best, int64_t& bi, float v, int64_t i) {
-  if (v > best || (v == best && i < bi)) {
-    best = v;
-    bi = i;
-  }
-}
 
 // Greedy token of every row, fused after the logits of the tile are final (vals[tok * BN + col]: the logits as
 // stored, -inf past N).  Warp t finds token t's first maximum in the tile and stores it as the tile's candidate;
@@ -1347,16 +1400,18 @@ static bool stream_eligible(const W4SArgs& a, const W4Plan& p, int num_sms) {
          int64_t(a.M) * (2 * int64_t(a.K) + 64) <= 48 * 1024 && slabs >= int64_t(num_sms) * 12 * 2;
 }
 
-template <bool F16, int SPS, bool ONE>
+template <bool F16, int SPS, bool ONE, bool ARG = false>
 static cudaError_t launch_stream_impl(W4SArgs a, int num_sms, cudaStream_t stream) {
-  auto kern = w4_stream_kernel<F16, SPS, ONE>;
+  auto kern = w4_stream_kernel<F16, SPS, ONE, ARG>;
   constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;
   constexpr int SEGST = SPST / SPS;
   a.xpitch = (a.K / 8) % 8 == 0 ? a.K * 2 + 64 : a.K * 2;
   a.off_sz = int((size_t(a.M) * a.xpitch + 127) / 128 * 128);  // start of the rings
   const size_t smem = size_t(a.off_sz) + 4 * kStreamRing * (SPST * 512 + SEGST * 128);
   if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem)) return e;
-  int per_sm = int((227 * 1024) / (smem + 1024));
+  // a persistent grid: as many CTAs as are resident at once (shared memory and registers), at most 8 per SM
+  int per_sm = 0;
+  if (cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem)) return e;
   per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(num_sms * per_sm));
@@ -1375,13 +1430,14 @@ static cudaError_t launch_stream_impl(W4SArgs a, int num_sms, cudaStream_t strea
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+template <bool ARG = false>
 static cudaError_t launch_stream(bool f16, const W4SArgs& a, int sps, int num_sms, cudaStream_t stream) {
 #define I4B_ST(F, O) \
   switch (sps) { \
-    case 1: return launch_stream_impl<F, 1, O>(a, num_sms, stream); \
-    case 2: return launch_stream_impl<F, 2, O>(a, num_sms, stream); \
-    case 4: return launch_stream_impl<F, 4, O>(a, num_sms, stream); \
-    default: return launch_stream_impl<F, 8, O>(a, num_sms, stream); \
+    case 1: return launch_stream_impl<F, 1, O, ARG>(a, num_sms, stream); \
+    case 2: return launch_stream_impl<F, 2, O, ARG>(a, num_sms, stream); \
+    case 4: return launch_stream_impl<F, 4, O, ARG>(a, num_sms, stream); \
+    default: return launch_stream_impl<F, 8, O, ARG>(a, num_sms, stream); \
   }
   const bool one = a.M == 1;
   if (f16) {
@@ -1392,6 +1448,9 @@ static cudaError_t launch_stream(bool f16, const W4SArgs& a, int sps, int num_sm
   I4B_ST(false, false);
 #undef I4B_ST
 }
+
+// Upper bound of the stream kernel's warps (its grid is SMs x at most 8 CTAs of 4 warps).
+static int64_t stream_max_warps(int sms) { return int64_t(sms) * 8 * 4; }
 
 // ---- register-streaming GEMV (M <= 8): plan and launch
 
@@ -1719,7 +1778,9 @@ static W4GPlan plan_w4_argmax(int64_t M, int64_t N, int64_t K, int G, int sms) {
 size_t w4_argmax_workspace_bytes(int64_t M, int64_t N, int64_t K, int G, int sms) {
   const W4GPlan p = plan_w4_argmax(M, N, K, G, sms);
   if (!p.ok) return 0;
-  return kTicketBytes + size_t(cdiv(N, 32 * p.WN)) * size_t(M) * sizeof(float2);
+  // candidates: one per column tile (register-streaming form) or per warp (streaming form), whichever is more
+  const int64_t cands = std::max<int64_t>(cdiv(N, 32 * p.WN), stream_max_warps(sms));
+  return kTicketBytes + size_t(cands) * size_t(M) * sizeof(float2);
 }
 
 cudaError_t launch_w4_argmax(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm, const int32_t* qw, int64_t N,
@@ -1748,6 +1809,16 @@ cudaError_t launch_w4_argmax(bool f16, const void* x, int64_t M, int64_t K, int6
   const int SPS = gcd_i(G / 32, 8);
   a.gpl = G / (32 * SPS);
   a.gpl_shift = (a.gpl & (a.gpl - 1)) == 0 ? __builtin_ctz(unsigned(a.gpl)) : -1;
+  a.tickets = static_cast<unsigned int*>(ws);
+  a.cand = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + kTicketBytes);
+  a.amax_out = out;
+  {  // a very wide head: the streaming kernel (the fastest form there), greedy choice in its epilogue
+    const auto addr = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr); };
+    a.vec_s = addr(sc) % 4 == 0 && addr(zr) % 4 == 0 && ssg % 2 == 0 && N % 4 == 0;
+    W4Plan wp{};
+    wp.SPS = SPS;
+    if (g_w4_ovr_kernel != 1 && stream_eligible(a, wp, sms)) return launch_stream<true>(f16, a, SPS, sms, stream);
+  }
   if (!gemv_eligible(a, p)) return cudaErrorInvalidConfiguration;
   a.WN = p.WN;
   a.WK = p.WK;
@@ -1761,9 +1832,6 @@ cudaError_t launch_w4_argmax(bool f16, const void* x, int64_t M, int64_t K, int6
   a.off_sz = 0;
   a.off_x = ox;
   a.off_part = op;
-  a.tickets = static_cast<unsigned int*>(ws);
-  a.cand = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + kTicketBytes);
-  a.amax_out = out;
   if (p.D == 8)
     return f16 ? launch_gemv_sps<true, kProPlain, 8, true>(a, p, SPS, stream)
                : launch_gemv_sps<false, kProPlain, 8, true>(a, p, SPS, stream);
