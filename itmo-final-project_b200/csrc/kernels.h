@@ -80,8 +80,8 @@ cudaError_t launch_w4(bool f16, const void* x, int64_t M, int64_t K, int64_t sxm
 void set_w4_split_override(int splits);
 // Tuning override of the M <= 8 kernel choice: kernel 0 automatic, 1 register-streaming GEMV, 2 the staged
 // small-M kernel, 3 the staged kernel or the streaming lm_head kernel, 4 / 5 the register-streaming GEMV with a
-// ring of 4 / 8 steps, 6 the slab-streaming GEMV (wk = its K split P: 1, 2, 4 or 8; splits = 1: every resident
-// CTA instead of a balanced grid); wk / splits otherwise: warps along K per CTA and cluster split of the
+// ring of 4 / 8 steps, 6 the slab-streaming GEMV (wk = its K split P: 1, 2, 4 or 8; splits = 2: a balanced grid
+// instead of every resident CTA); wk / splits otherwise: warps along K per CTA and cluster split of the
 // register-streaming GEMV (0 automatic).
 void set_w4_kernel_override(int kernel, int wk, int splits);
 // Greedy choice fused into the M <= 8 GEMV: out[m] = first column of row m's maximum logit (as rounded to x's
