@@ -920,8 +920,8 @@ def main():
             "block_gbs_per_gpu": achieved, "block_us_l2_hot": r["hot_us"],
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": prof_traffic,
-                         "kernel": "w4_gemv_kernel (register-streaming decode GEMV), the 4 launches of a step "
-                                   "(q|k|v, o, gate|up, down)",
+                         "kernel": "the 4 decode GEMV launches of a step: w4_slab_kernel (q|k|v, o, gate|up) and "
+                                   "w4_gemv_kernel (down)",
                          "peak_source": pk["source"]},
             "cpu_baseline": cpu,
             "e2e": {"value": r["e2e_us"], "unit": "us", "h2d_bytes_per_step": r["h2d"],

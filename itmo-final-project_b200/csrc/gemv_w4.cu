@@ -1590,8 +1590,14 @@ static W4SlabPlan plan_w4_slab(const W4SArgs& a, int sps, int sms) {
   const int64_t groups = cdiv(slabs, NW / p.P);
   p.grid = int(groups);  // slab groups; the launch caps the grid at what is resident and balances it
   p.sms = sms;
+  // Wide matrices (two slabs per SM or more) stream best as slabs; so do short ones (K <= 2048: a warp's
+  // share of a slab is at most 256 columns of K at P = 8) as long as there are slabs for half the SMs, or one
+  // or two tokens.  Measured at M = 1 (us): qkv 3072x2048 4.1 against 5.2 for the register kernel, o
+  // 2048x2048 3.8 against 4.2; at M = 8 the register kernel keeps o (4.8 against 5.7) and long K (down
+  // 2048x8192: 7.5 against 11.2 at M = 1).
+  const bool shape_ok = slabs >= 2 * int64_t(sms) || (a.K <= 2048 && (a.M <= 2 || 2 * slabs >= sms));
   p.ok = a.M <= 8 && a.ar_world <= 1 && a.vec_w && a.vec_s && a.K % (p.P * 32 * spst) == 0 &&
-         p.smem <= 200 * 1024 && (slabs >= 2 * int64_t(sms) || g_w4_ovr_kernel == 6);
+         p.smem <= 200 * 1024 && (shape_ok || g_w4_ovr_kernel == 6);
   return p;
 }
 
