@@ -351,10 +351,17 @@ int i4b_decode_layers(const i4b_decode_model* model, void* workspace, size_t wor
  * fence done, ticket taken, combined and published.  Process-wide; null turns it off. */
 void i4b_set_decode_trace(void* buffer, size_t bytes);
 
-/* Tuning hook for the M > 32 tcgen05 GEMM: tile (1: 128x128, 2: 256x128, 3: 128x256, 4: 256x256) and
- * K splits (1..4); 0 keeps the automatic choice.  Process-wide.  Changes the workspace size a later
+/* Tuning hook for the tcgen05 GEMMs (W4 above the register-dequant range, W16 M > 16): tile 1..4 = the
+ * shared-memory-operand kernel (1: 128x128, 2: 256x128, 3: 128x256, 4: 256x256; K splits 1, 2 or 4), tile
+ * 5..8 = INT4 only, the TMEM-weight kernel with 128 weight rows x 256 / 128 / 64 / 32 tokens per CTA (K
+ * splits 1, 2, 4 or 8); 0 keeps the automatic choice.  Process-wide.  Changes the workspace size a later
  * i4b_w4a16_workspace_size / i4b_w16a16_workspace_size reports.  No counterpart in the reference. */
 void i4b_set_gemm_override(int tile, int splits);
+
+/* Tuning hook: the largest M (8..32) for which i4b_w4a16_matmul runs the register-dequant kernels rather
+ * than the tcgen05 GEMM; any other value restores the default.  Process-wide; changes the workspace size a
+ * later i4b_w4a16_workspace_size reports.  No counterpart in the reference. */
+void i4b_set_w4_small_m_override(int max_m);
 
 /* Device-side error flags raised by kernels of this library on `device`
  * (a bounded wait that expired sets bit 0; a wait for another rank of a peer

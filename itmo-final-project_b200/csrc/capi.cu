@@ -74,7 +74,7 @@ size_t tc_w4_workspace(int64_t M, int64_t N, int64_t K, int G, int sms) {
     const int64_t Np = round_up(N, 8);
     b += align256(size_t(K / 8) * Np * 4) + 2 * align256(size_t(K / G) * Np * 2);
   }
-  return b + align256(tc_partial_bytes(tc_plan(M, N, K, sms), M, N));
+  return b + align256(tc_partial_bytes(tc_plan_w4(M, N, K, sms), M, N));
 }
 
 size_t tc_w16_workspace(int64_t M, int64_t N, int64_t K, int sms) {
@@ -88,6 +88,10 @@ size_t tc_w16_workspace(int64_t M, int64_t N, int64_t K, int sms) {
 // SMALL_M = 64, gemm.py:17; measured on B200 the tcgen05 GEMM wins from 33 tokens on):
 // INT4 kW4MaxM = 32, W16 kSkinnyMaxM = 16.
 constexpr int64_t kSmallM = kSkinnyMaxM;
+
+// INT4 M up to which the register-dequant kernels run instead of the tcgen05 GEMM (tuning hook: 8..32)
+int64_t g_w4_small_max = kW4MaxM;
+int64_t w4_small_max_m() { return g_w4_small_max; }
 
 }  // namespace
 
@@ -154,6 +158,8 @@ void i4b_set_w4_kernel_override(int kernel, int wk, int splits) { set_w4_kernel_
 
 void i4b_set_gemm_override(int tile, int splits) { set_tc_override(tile, splits); }
 
+void i4b_set_w4_small_m_override(int max_m) { g_w4_small_max = (max_m >= 8 && max_m <= kW4MaxM) ? max_m : kW4MaxM; }
+
 int i4b_quantize_int4(const void* w, int w_dtype, int64_t N, int64_t K, int64_t stride_wn, int64_t stride_wk,
                       int group_size, int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream) {
   if (w_dtype != I4B_F16 && w_dtype != I4B_BF16 && w_dtype != I4B_F32) return I4B_ERR_INVALID_ARG;
@@ -190,7 +196,7 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
   if (M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || group_size % 32 != 0 || K % group_size != 0) return 0;
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
-  if (M <= kW4MaxM) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
+  if (M <= w4_small_max_m()) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
   return tc_w4_workspace(M, N, K, group_size, d.sms);
 }
 
@@ -212,7 +218,7 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool f16 = x_dtype == I4B_F16;
 
-  if (M <= kW4MaxM) {
+  if (M <= w4_small_max_m()) {
     const W4Plan p = plan_w4(M, N, K, G, d.sms);
     if (p.mode == 3) return I4B_ERR_SHAPE;
     if (w4_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;
@@ -253,7 +259,7 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
     o.zr = reinterpret_cast<const uint16_t*>(zc);
     o.ssg = Np;
   }
-  const TcPlan plan = tc_plan(M, N, K, d.sms);
+  const TcPlan plan = tc_plan_w4(M, N, K, d.sms);
   uint8_t* part = static_cast<uint8_t*>(workspace) + tc_w4_workspace(M, N, K, G, d.sms) -
                   align256(tc_partial_bytes(plan, M, N));
   e = launch_tc(true, f16, o, M, N, K, G, static_cast<uint16_t*>(y), stride_ym, plan, reinterpret_cast<float*>(part),
@@ -590,7 +596,7 @@ int i4b_device_error_flags(int device, int clear) {
   if (cudaSetDevice(device) != cudaSuccess) return -1;
   int flags = -1;
   if (cudaDeviceSynchronize() == cudaSuccess) {
-    flags = int(read_quant_error(clear != 0) | read_tc_error(clear != 0) | read_dk_error(clear != 0) |
+    flags = int(read_quant_error(clear != 0) | read_tc_error(clear != 0) | read_w4t_error(clear != 0) | read_dk_error(clear != 0) |
                 read_w4_error(clear != 0));
   }
   cudaSetDevice(prev);

@@ -461,7 +461,7 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // 2-D row-major tensor: `inner` contiguous elements per row, `rows` rows `row_bytes` apart.
-static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
                      uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
@@ -482,17 +482,17 @@ static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int
   using C = TcCfg<INT4, BN, BMT>;
   const CUtensorMapDataType act = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap mx{}, mw{}, ms{}, mz{};
-  bool ok = make_map(&mx, act, o.x, uint64_t(K), uint64_t(M), uint64_t(o.sxm) * 2, 64, C::BM,
+  bool ok = make_tma_map_2d(&mx, act, o.x, uint64_t(K), uint64_t(M), uint64_t(o.sxm) * 2, 64, C::BM,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if constexpr (INT4) {
-    ok = ok && make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, o.w, uint64_t(N), uint64_t(K / 8), uint64_t(o.sw) * 4, BN,
+    ok = ok && make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, o.w, uint64_t(N), uint64_t(K / 8), uint64_t(o.sw) * 4, BN,
                         8, CU_TENSOR_MAP_SWIZZLE_NONE);
-    ok = ok && make_map(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.sc, uint64_t(N), uint64_t(K / G), uint64_t(o.ssg) * 2,
+    ok = ok && make_tma_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.sc, uint64_t(N), uint64_t(K / G), uint64_t(o.ssg) * 2,
                         BN, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
-    ok = ok && make_map(&mz, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.zr, uint64_t(N), uint64_t(K / G), uint64_t(o.ssg) * 2,
+    ok = ok && make_tma_map_2d(&mz, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.zr, uint64_t(N), uint64_t(K / G), uint64_t(o.ssg) * 2,
                         BN, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
   } else {
-    ok = ok && make_map(&mw, act, o.w, uint64_t(K), uint64_t(N), uint64_t(o.sw) * 2, 64, BN,
+    ok = ok && make_tma_map_2d(&mw, act, o.w, uint64_t(K), uint64_t(N), uint64_t(o.sw) * 2, 64, BN,
                         CU_TENSOR_MAP_SWIZZLE_128B);
     ms = mw;
     mz = mw;
@@ -522,8 +522,8 @@ static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int
 static int g_tc_ovr_tile = 0, g_tc_ovr_splits = 0;
 
 void set_tc_override(int tile, int splits) {
-  g_tc_ovr_tile = tile >= 1 && tile <= 4 ? tile : 0;
-  g_tc_ovr_splits = splits >= 1 && splits <= 4 ? splits : 0;
+  g_tc_ovr_tile = tile >= 1 && tile <= 8 ? tile : 0;
+  g_tc_ovr_splits = (splits == 1 || splits == 2 || splits == 4 || splits == 8) ? splits : 0;
 }
 
 static int64_t tc_tiles(int tile, int64_t M, int64_t N) {
@@ -548,12 +548,13 @@ TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
   const int64_t kb = cdiv(K, 64);
   TcPlan best{1, 1};
   double best_t = 1e30;
+  const int ovr_tile = g_tc_ovr_tile <= 4 ? g_tc_ovr_tile : 0, ovr_splits = g_tc_ovr_splits <= 4 ? g_tc_ovr_splits : 0;
   for (int tile : {4, 2, 1}) {
     if (I4B_TC_FORCE && tile != I4B_TC_FORCE) continue;
-    if (g_tc_ovr_tile && tile != g_tc_ovr_tile) continue;
+    if (ovr_tile && tile != ovr_tile) continue;
     if (tile != 1 && M <= 128) continue;  // a 256-row tile would be half empty
     for (int splits : {1, 2, 4}) {
-      if (g_tc_ovr_splits && splits != g_tc_ovr_splits) continue;
+      if (ovr_splits && splits != ovr_splits) continue;
       if (splits > 1 && (tc_tiles(tile, M, N) > kMaxTickets || kb < 4 * splits)) continue;
       const double t = tc_cost(tile, splits, M, N, kb, num_sms);
       if (t < best_t) {
@@ -563,7 +564,46 @@ TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
     }
   }
   if (I4B_TC_FORCE && best_t >= 1e30) best = TcPlan{I4B_TC_FORCE, 1};
-  if (g_tc_ovr_tile && best_t >= 1e30) best = TcPlan{g_tc_ovr_tile, 1};
+  if (ovr_tile && best_t >= 1e30) best = TcPlan{ovr_tile, 1};
+  return best;
+}
+
+// INT4: the TMEM-weight kernel (gemm_w4t.cu), tile code 5..8 = 256, 128, 64 or 32 tokens per CTA, unless the
+// tuning hook asks for one of the shared-memory tiles above (codes 1..4).  Cost model (us) in the form of the
+// one above: a wave of CTAs costs F + c_NT * (k-blocks per CTA); a K split adds its fp32 partials' round trip
+// through L2.  c_NT is the larger of the tensor time of a 128 x NT x 64 k-block and the dequant time of its
+// 128 x 64 weights (the floor for small NT).
+static double w4t_cost(int nt, int splits, int64_t M, int64_t N, int64_t kb, int num_sms) {
+  const double F = 3.0;
+  const double c = nt == 256 ? 0.32 : nt == 128 ? 0.18 : 0.11;
+  const int64_t tiles = cdiv(N, 128) * cdiv(M, int64_t(nt));
+  const int64_t waves = cdiv(tiles * splits, int64_t(num_sms));
+  double t = double(waves) * (F + c * double(cdiv(kb, int64_t(splits))));
+  if (splits > 1) t += 2.0 + double(splits) * double(M) * double(N) * 8.0 / 3.0e6;
+  return t;
+}
+
+TcPlan tc_plan_w4(int64_t M, int64_t N, int64_t K, int num_sms) {
+  if (g_tc_ovr_tile >= 1 && g_tc_ovr_tile <= 4) return tc_plan(M, N, K, num_sms);
+  const int64_t kb = cdiv(K, 64);
+  TcPlan best{6, 1};
+  double best_t = 1e30;
+  for (int tile : {5, 6, 7, 8}) {
+    if (g_tc_ovr_tile && tile != g_tc_ovr_tile) continue;
+    const int nt = w4t_token_tile(tile);
+    if (nt > 32 && M <= nt / 2) continue;  // more than half of the tile would be padding
+    for (int splits : {1, 2, 4, 8}) {
+      if (g_tc_ovr_splits && splits != g_tc_ovr_splits) continue;
+      if (splits > 1 && (cdiv(N, 128) * cdiv(M, int64_t(nt)) > kMaxTickets || kb < 2 * splits || N % 4 != 0))
+        continue;
+      const double t = w4t_cost(nt, splits, M, N, kb, num_sms);
+      if (t < best_t) {
+        best_t = t;
+        best = TcPlan{tile, splits};
+      }
+    }
+  }
+  if (best_t >= 1e30 && g_tc_ovr_tile) best = TcPlan{g_tc_ovr_tile, 1};
   return best;
 }
 
@@ -574,7 +614,11 @@ size_t tc_partial_bytes(const TcPlan& p, int64_t M, int64_t N) {
 cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                       int64_t sym, const TcPlan& plan, float* partials, unsigned int* tickets, cudaStream_t stream) {
   const int bn = plan.tile, ks = plan.splits;
-  // bn: tile code, ks: K splits (from tc_plan)
+  // bn: tile code, ks: K splits (from tc_plan / tc_plan_w4)
+  if (bn >= 5) {
+    if (!int4 || (ks > 1 && N % 4 != 0)) return cudaErrorInvalidValue;
+    return launch_w4t(f16, o, M, N, K, G, y, sym, bn, ks, partials, tickets, stream);
+  }
 #define I4B_TC(I, F) \
   return bn == 4   ? launch_tc_impl<I, F, 256, 2>(o, M, N, K, G, y, sym, ks, partials, tickets, stream) \
          : bn == 2 ? launch_tc_impl<I, F, 128, 2>(o, M, N, K, G, y, sym, ks, partials, tickets, stream) \

@@ -1,0 +1,387 @@
+// W4A16 GEMM on the 5th-generation tensor cores with the dequantized weights held in TMEM.
+//
+// Replaces the reference's large-M Triton path _matmul_kernel (int4_triton/gemm.py:74-157, launched at
+// gemm.py:270-296) and, from 9 tokens on, its split-K small-M path (gemm.py:160-260).
+// y[M, N] = x[M, K] @ W_hat[N, K]^T with W_hat = bf16_rn((q - z) * s) (int4_triton/gemm.py:137-140).
+//
+// The MMA is computed transposed, y^T tile = W_hat tile (A) x x^T tile (B):
+//   A  128 weight rows x 16 k per instruction, read from TMEM (tcgen05.mma ... [a-tmem]): the dequant
+//      warps write each 128 x 64 k-block of W_hat straight into a 4-slot TMEM ring with tcgen05.st, so
+//      dequantized weights never pass through shared memory;
+//   B  NT tokens x 16 k from shared memory (the TMA-loaded activation tile, K-major, 128-byte swizzle);
+//   D  128 x NT fp32 accumulator in TMEM (lane = weight row, column = token).
+// Shared-memory traffic per k-block is the activation tile written by TMA and read once by the MMAs plus
+// the 4 KB of packed weights; keeping the bf16 weight tile out of shared memory is what lets the tensor pipe
+// run instead of waiting on shared-memory bandwidth (which an A/B-from-shared design saturates first).
+//
+// One CTA computes a 128-weight-row x NT-token tile over k-blocks [kb0, kb1) (a K split when ksplit > 1).
+// 18 warps:
+//   warp 0      TMA producer: per 64-wide k-block the activation tile (NT x 64), the packed words
+//               (8 k8-rows x 128 int32) and two group rows of scales and zeros;
+//   warp 1      allocates TMEM (accumulator + A ring) and, from one thread, issues four
+//               tcgen05.mma.kind::f16 per k-block, then tcgen05.commit frees the stage and the A slot;
+//   warps 2..17 dequantize: warp w owns TMEM lane quarter w % 4 (weight rows 32 (w % 4) + lane) and packed
+//               words 2h, 2h + 1 of each k-block (h = (w - 2) / 4); then read the accumulator back with
+//               tcgen05.ld and store y (or fp32 partials of the K split).
+// Every wait is bounded; on expiry the kernel records I4B_DEVERR_WAIT_TIMEOUT, drains its own TMA copies,
+// frees TMEM and returns.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace i4b {
+
+static __device__ unsigned int g_w4t_err = 0;
+
+template <int NT>
+struct W4tCfg {
+  static constexpr int BF = 128, BK = 64;  // weight rows (the MMA's M) and k per k-block
+  static constexpr int DQ_WARPS = 16;
+  static constexpr int THREADS = 64 + 32 * DQ_WARPS;
+  static constexpr int X_BYTES = NT * BK * 2;     // activation tile: NT rows of 128 B
+  static constexpr int P_BYTES = 8 * BF * 4;      // packed words of one k-block
+  static constexpr int SZ_BYTES = 2 * 2 * BF * 2; // scales + zeros, two group rows
+  static constexpr int STAGE_BYTES = X_BYTES + P_BYTES + SZ_BYTES;  // a multiple of 1024
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 12 ? 12 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int NA = 4;                    // A slots (k-blocks) in TMEM
+  static constexpr int A_COL = NT < 32 ? 32 : NT; // first TMEM column of the A ring
+  static constexpr int A_SLOT_COLS = BK / 2;      // 64 16-bit values per row = 32 columns
+  static constexpr int TMEM_COLS = (A_COL + NA * A_SLOT_COLS) <= 256 ? 256 : 512;
+  static constexpr int BAR_BYTES = (2 * STAGES + 2 * NA + 1) * 8 + 8;
+  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + BAR_BYTES;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+  static_assert(STAGES >= 3, "at least three pipeline stages");
+  static_assert(A_COL + NA * A_SLOT_COLS <= TMEM_COLS && TMEM_COLS <= 512, "TMEM budget");
+  static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N for M = 128");
+};
+
+// 8 nibbles of one packed word -> 8 dequantized 16-bit values in k order, packed two per 32 bits
+// (low half = even k): exactly the TMEM layout of one A row over 8 k.
+template <bool F16>
+__device__ __forceinline__ uint4 w4t_dequant_word(uint32_t w, const DqParams& p) {
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t q = and_or(w >> (4 * i), 0x000F000Fu, F16 ? 0x64006400u : 0x43004300u);  // (q_i, q_{i+4})
+    uint32_t d;
+    if constexpr (F16) {
+      asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(q), "r"(p.zz));
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[i]) : "r"(d), "r"(p.shi));
+    } else {
+      uint32_t pl;
+      asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(q), "r"(p.zz));
+      asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(pl) : "r"(d), "r"(p.slo));
+      asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r[i]) : "r"(d), "r"(p.shi), "r"(pl));
+    }
+  }
+  return make_uint4(__byte_perm(r[0], r[1], 0x5410), __byte_perm(r[2], r[3], 0x5410),
+                    __byte_perm(r[0], r[1], 0x7632), __byte_perm(r[2], r[3], 0x7632));
+}
+
+// 32 lanes x 32 bit, 8 consecutive columns from this thread's registers (the warp's lane quarter).
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint4& a, const uint4& b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (bf16 or fp16 operands, fp32 accumulator).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <bool F16, int NT>
+__global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
+    w4t_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z, int M, int N,
+                    int K, int G, uint16_t* __restrict__ y, int64_t sym, int ksplit, float* __restrict__ partials,
+                    unsigned int* __restrict__ tickets) {
+  using C = W4tCfg<NT>;
+  constexpr int S = C::STAGES, NA = C::NA;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  // [S stages: X | P | SZ] [barriers]
+  uint8_t* stage0 = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage0 + S * C::STAGE_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* aready = empty + S;  // A slot dequantized into TMEM (one arrival per dequant warp)
+  uint64_t* afree = aready + NA;  // A slot no longer read by the MMAs
+  uint64_t* tfull = afree + NA;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  auto sX = [&](int s) { return stage0 + s * C::STAGE_BYTES; };
+  auto sP = [&](int s) { return stage0 + s * C::STAGE_BYTES + C::X_BYTES; };
+  auto sSZ = [&](int s) { return stage0 + s * C::STAGE_BYTES + C::X_BYTES + C::P_BYTES; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * C::BF, m0 = blockIdx.y * NT;
+  const int KBT = (K + C::BK - 1) / C::BK;
+  const int kb0 = int((int64_t(blockIdx.z) * KBT) / ksplit), kb1 = int((int64_t(blockIdx.z + 1) * KBT) / ksplit);
+  const int KB = kb1 - kb0;
+  __shared__ int s_last;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < NA; ++b) {
+      mbar_init(&aready[b], C::DQ_WARPS);
+      mbar_init(&afree[b], 1);
+    }
+    mbar_init(tfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_s);
+    tma_prefetch_desc(&tm_z);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kp = kb0 + S; kp < kb0 + 2 * S && kp < kb1; ++kp) {  // the first S k-blocks are loaded right away
+        tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
+        tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
+        tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
+      }
+      for (int kbl = 0; kbl < KB; ++kbl) {
+        const int kb = kb0 + kbl;
+        const int s = kbl % S, u = kbl / S;
+        if (kbl >= S && !mbar_wait(&empty[s], (u - 1) & 1)) { ok = false; break; }
+        // pull the packed weights of k-block kb + 2S into L2 now: their loads, S k-blocks from now, then
+        // find them there (the activation rows are shared by every CTA of the row and stay in L2)
+        const int kp = kb + 2 * S;
+        if (kp < kb1) {
+          tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
+          tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
+          tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
+        }
+        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+        const int g_lo = (kb * C::BK) / G;
+        tma_load_2d(sX(s), &tm_x, &full[s], kb * C::BK, m0);
+        tma_load_2d(sP(s), &tm_w, &full[s], n0, kb * 8);
+        tma_load_2d(sSZ(s), &tm_s, &full[s], n0, g_lo);
+        tma_load_2d(sSZ(s) + 2 * C::BF * 2, &tm_z, &full[s], n0, g_lo);
+        ++issued;
+      }
+      // Never leave a bulk copy in flight: wait for the last use of every stage.
+      for (int s = 0; s < S && s < issued; ++s) {
+        const int last = ((issued - 1 - s) / S) * S + s;
+        if (!mbar_wait(&full[s], (last / S) & 1)) ok = false;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(F16 ? 0 : 1, C::BF, NT);
+      for (int kbl = 0; kbl < KB; ++kbl) {
+        const int s = kbl % S, u = kbl / S, b = kbl % NA;
+        if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
+        if (!mbar_wait(&aready[b], (kbl / NA) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t bdesc = umma_desc_sw128(smem_u32(sX(s)));
+        const uint32_t acol = tmem + uint32_t(C::A_COL + b * C::A_SLOT_COLS);
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk)
+          umma_f16_ts(tmem, acol + uint32_t(8 * kk), bdesc + 2 * kk, idesc, (kbl | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[s]);
+        umma_commit(&afree[b]);
+      }
+      umma_commit(tfull);  // also on the error path: completes once the issued MMAs are done
+    }
+  } else {
+    // dequant warp: TMEM lane quarter q (rows 32 q + lane), packed words 2h and 2h + 1 of each k-block
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    const int nl = 32 * q + lane;
+    const uint32_t lane_base = uint32_t(32 * q) << 16;
+    int g_lo = (kb0 * C::BK) / G, g_end = (g_lo + 1) * G;
+    int g_cached = -1;
+    DqParams pc{};
+    for (int kbl = 0; kbl < KB && ok; ++kbl) {
+      const int s = kbl % S, u = kbl / S, b = kbl % NA;
+      const int k_begin = (kb0 + kbl) * C::BK;
+      while (k_begin >= g_end) {
+        ++g_lo;
+        g_end += G;
+      }
+      if (!mbar_wait_sleep(&full[s], u & 1)) { ok = false; break; }
+      if (kbl >= NA) {
+        if (!mbar_wait_sleep(&afree[b], ((kbl / NA) - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+      }
+      const uint32_t* P = reinterpret_cast<const uint32_t*>(sP(s));
+      const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ(s));
+      const uint16_t* Zs = Ss + 2 * C::BF;
+      if (g_cached != g_lo) {
+        pc = dq_params<F16>(Ss[nl], Zs[nl]);
+        g_cached = g_lo;
+      }
+      const DqParams p0 = pc;
+      const int jsplit = (g_end - k_begin) >> 3;  // words of this k-block inside group g_lo (>= 1)
+      DqParams p1 = p0;
+      if (jsplit < 8) {
+        p1 = dq_params<F16>(Ss[C::BF + nl], Zs[C::BF + nl]);
+        pc = p1;
+        g_cached = g_lo + 1;
+      }
+      const int j0 = 2 * h;
+      const uint4 v0 = w4t_dequant_word<F16>(P[j0 * C::BF + nl], j0 >= jsplit ? p1 : p0);
+      const uint4 v1 = w4t_dequant_word<F16>(P[(j0 + 1) * C::BF + nl], j0 + 1 >= jsplit ? p1 : p0);
+      tmem_st_32x32b_x8(tmem + lane_base + uint32_t(C::A_COL + b * C::A_SLOT_COLS + 4 * j0), v0, v1);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aready[b]);
+    }
+    // ---- epilogue: the sixteen warps read the accumulator in 16-token chunks: warp (q, h) takes chunks
+    // h, h + 4, ... of lane quarter q.  Thread = weight row n; per token, a warp stores 32 consecutive
+    // outputs (64 bytes of y, or 128 bytes of fp32 partials).
+    if (!mbar_wait_sleep(tfull, 0)) ok = false;
+    tc_fence_after();
+    const int n = n0 + nl;
+#pragma unroll 1
+    for (int c0 = 16 * h; c0 < NT; c0 += 64) {
+      uint32_t v[16];
+      tmem_ld_32x32b_x16(tmem + lane_base + uint32_t(c0), v);  // the whole warp, every iteration
+      tmem_ld_wait();
+      const int rows = min(16, M - (m0 + c0));
+      if (n < N && ksplit > 1) {
+        float* dst = partials + (int64_t(blockIdx.z) * M + m0 + c0) * N + n;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < rows) dst[int64_t(i) * N] = __uint_as_float(v[i]);
+      } else if (n < N) {
+        uint16_t* dst = y + int64_t(m0 + c0) * sym + n;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float a = __uint_as_float(v[i]);
+          if (i < rows)
+            dst[int64_t(i) * sym] =
+                F16 ? __half_as_ushort(__float2half_rn(a)) : __bfloat16_as_ushort(__float2bfloat16_rn(a));
+        }
+      }
+      __syncwarp();
+    }
+  }
+  if (!ok) atomicOr(&g_w4t_err, I4B_DEVERR_WAIT_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (ksplit > 1) {
+    // The last CTA of this output tile (atomic ticket, no spinning) adds the ksplit fp32 partials in split
+    // order and writes y; then it resets the ticket for the next call.
+    const unsigned int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(tickets + tile, 1u) == unsigned(ksplit - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int64_t stride_z = int64_t(M) * N;
+    // items of 4 consecutive outputs of one token (N % 8 == 0 on this path); 32 threads cover a token's 128
+    constexpr int NQ = C::BF / 4;
+    for (int idx = threadIdx.x; idx < NT * NQ; idx += blockDim.x) {
+      const int m = m0 + idx / NQ, nn = n0 + 4 * (idx % NQ);
+      if (m >= M || nn >= N) continue;
+      const float* src = partials + int64_t(m) * N + nn;
+      float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+      for (int z = 1; z < ksplit; ++z) {  // split order
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(src + z * stride_z));
+        a.x += t.x;
+        a.y += t.y;
+        a.z += t.z;
+        a.w += t.w;
+      }
+      uint16_t* dst = y + int64_t(m) * sym + nn;
+      if constexpr (F16) {
+        dst[0] = __half_as_ushort(__float2half_rn(a.x));
+        dst[1] = __half_as_ushort(__float2half_rn(a.y));
+        dst[2] = __half_as_ushort(__float2half_rn(a.z));
+        dst[3] = __half_as_ushort(__float2half_rn(a.w));
+      } else {
+        dst[0] = __bfloat16_as_ushort(__float2bfloat16_rn(a.x));
+        dst[1] = __bfloat16_as_ushort(__float2bfloat16_rn(a.y));
+        dst[2] = __bfloat16_as_ushort(__float2bfloat16_rn(a.z));
+        dst[3] = __bfloat16_as_ushort(__float2bfloat16_rn(a.w));
+      }
+    }
+    if (threadIdx.x == 0) atomicExch(tickets + tile, 0u);
+  }
+}
+
+// ------------------------------------------------------------------ launch
+
+template <bool F16, int NT>
+static cudaError_t launch_w4t_impl(const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
+                                   int64_t sym, int ksplit, float* partials, unsigned int* tickets,
+                                   cudaStream_t stream) {
+  using C = W4tCfg<NT>;
+  const CUtensorMapDataType act = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap mx{}, mw{}, ms{}, mz{};
+  bool ok = make_tma_map_2d(&mx, act, o.x, uint64_t(K), uint64_t(M), uint64_t(o.sxm) * 2, 64, NT,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  ok = ok && make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, o.w, uint64_t(N), uint64_t(K / 8),
+                             uint64_t(o.sw) * 4, C::BF, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+  ok = ok && make_tma_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.sc, uint64_t(N), uint64_t(K / G),
+                             uint64_t(o.ssg) * 2, C::BF, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  ok = ok && make_tma_map_2d(&mz, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.zr, uint64_t(N), uint64_t(K / G),
+                             uint64_t(o.ssg) * 2, C::BF, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) return cudaErrorInvalidValue;
+  auto kern = w4t_gemm_kernel<F16, NT>;
+  if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), C::SMEM)) return e;
+  dim3 grid(unsigned(cdiv(N, C::BF)), unsigned(cdiv(M, NT)), unsigned(ksplit));
+  kern<<<grid, C::THREADS, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym, ksplit, partials,
+                                               tickets);
+  return cudaGetLastError();
+}
+
+int w4t_token_tile(int tile) { return tile == 5 ? 256 : tile == 6 ? 128 : tile == 7 ? 64 : tile == 8 ? 32 : 0; }
+
+cudaError_t launch_w4t(bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
+                       int64_t sym, int tile, int ksplit, float* partials, unsigned int* tickets,
+                       cudaStream_t stream) {
+#define I4B_W4T(F)                                                                                   \
+  switch (w4t_token_tile(tile)) {                                                                    \
+    case 256: return launch_w4t_impl<F, 256>(o, M, N, K, G, y, sym, ksplit, partials, tickets, stream); \
+    case 128: return launch_w4t_impl<F, 128>(o, M, N, K, G, y, sym, ksplit, partials, tickets, stream); \
+    case 64: return launch_w4t_impl<F, 64>(o, M, N, K, G, y, sym, ksplit, partials, tickets, stream);   \
+    case 32: return launch_w4t_impl<F, 32>(o, M, N, K, G, y, sym, ksplit, partials, tickets, stream);   \
+    default: return cudaErrorInvalidValue;                                                           \
+  }
+  if (f16) I4B_W4T(true);
+  I4B_W4T(false);
+#undef I4B_W4T
+}
+
+unsigned int read_w4t_error(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_w4t_err, sizeof(v));
+  if (clear) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_w4t_err, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace i4b

@@ -1,6 +1,7 @@
 // Host-side declarations of the kernel launchers shared between the .cu files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -112,17 +113,27 @@ struct TcOperands {
   int64_t ssg;
 };
 struct TcPlan {
-  int tile;    // 1: 128 x 128, 2: 256 x 128, 3: 128 x 256, 4: 256 x 256
+  int tile;    // 1: 128 x 128, 2: 256 x 128, 3: 128 x 256, 4: 256 x 256 (shared-memory operands);
+               // INT4 only, weights in TMEM: 5..8 = 128 weight rows x 256 / 128 / 64 / 32 tokens
   int splits;  // K splits (fp32 partials in the workspace when > 1)
 };
-TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int num_sms);
+TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int num_sms);     // W16 (and INT4 tiles 1..4)
+TcPlan tc_plan_w4(int64_t M, int64_t N, int64_t K, int num_sms);  // INT4
 void set_tc_override(int tile, int splits);  // tuning: 0 keeps the automatic choice
+bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
 size_t tc_partial_bytes(const TcPlan& p, int64_t M, int64_t N);
 cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                       int64_t sym, const TcPlan& plan, float* partials, unsigned int* tickets, cudaStream_t stream);
 cudaError_t launch_repack(const void* in, int esize, int64_t rows, int64_t cols_in, int64_t sr, int64_t sc, void* out,
                           int64_t cols_out, cudaStream_t stream);
 unsigned int read_tc_error(bool clear);
+
+// gemm_w4t.cu (INT4, weights dequantized into TMEM; tile codes 5..8 of TcPlan)
+int w4t_token_tile(int tile);
+cudaError_t launch_w4t(bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
+                       int64_t sym, int tile, int ksplit, float* partials, unsigned int* tickets, cudaStream_t stream);
+unsigned int read_w4t_error(bool clear);
 
 // decode_ops.cu (decode-step glue of a Llama layer)
 cudaError_t launch_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, uint16_t* out, int rows, int H,

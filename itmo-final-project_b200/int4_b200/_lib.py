@@ -49,6 +49,7 @@ _SIGNATURES = {
     "i4b_argmax_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp]),
     "i4b_set_pdl": (None, [_c_int]),
     "i4b_set_w4_kernel_override": (None, [_c_int, _c_int, _c_int]),
+    "i4b_set_w4_small_m_override": (None, [_c_int]),
     "i4b_set_skinny_override": (None, [_c_int, _c_int, _c_int]),
     "i4b_set_gemm_override": (None, [_c_int, _c_int]),
     "i4b_device_error_flags": (_c_int, [_c_int, _c_int]),

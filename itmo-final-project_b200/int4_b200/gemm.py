@@ -44,7 +44,7 @@ def w4a16_matmul(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, z
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     if M == 0 or N == 0:
         return y.reshape(*x.shape[:-1], N)
-    tma = M > _W4_SMALL_M
+    tma = M > 8  # above the GEMV range the tcgen05 GEMM may run (TMA operands)
     qweight = _unit_n_stride(qweight, tma)
     scales = _unit_n_stride(scales, tma)
     zeros = _unit_n_stride(zeros, tma)
