@@ -34,6 +34,18 @@ namespace i4b {
 
 static __device__ unsigned int g_w4t_err = 0;
 
+// Build-time tuning knobs: A slots in TMEM, whether the dequant warps wait with a suspend hint, and whether
+// the producer prefetches packed weights into L2 ahead of their loads.
+#ifndef I4B_W4T_NA
+#define I4B_W4T_NA 4
+#endif
+#ifndef I4B_W4T_SLEEP
+#define I4B_W4T_SLEEP 1
+#endif
+#ifndef I4B_W4T_L2PF
+#define I4B_W4T_L2PF 1
+#endif
+
 template <int NT>
 struct W4tCfg {
   static constexpr int BF = 128, BK = 64;  // weight rows (the MMA's M) and k per k-block
@@ -44,7 +56,7 @@ struct W4tCfg {
   static constexpr int SZ_BYTES = 2 * 2 * BF * 2; // scales + zeros, two group rows
   static constexpr int STAGE_BYTES = X_BYTES + P_BYTES + SZ_BYTES;  // a multiple of 1024
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 12 ? 12 : (200 * 1024) / STAGE_BYTES;
-  static constexpr int NA = 4;                    // A slots (k-blocks) in TMEM
+  static constexpr int NA = I4B_W4T_NA;           // A slots (k-blocks) in TMEM
   static constexpr int A_COL = NT < 32 ? 32 : NT; // first TMEM column of the A ring
   static constexpr int A_SLOT_COLS = BK / 2;      // 64 16-bit values per row = 32 columns
   static constexpr int TMEM_COLS = (A_COL + NA * A_SLOT_COLS) <= 256 ? 256 : 512;
@@ -158,11 +170,12 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
-      for (int kp = kb0 + S; kp < kb0 + 2 * S && kp < kb1; ++kp) {  // the first S k-blocks are loaded right away
-        tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
-        tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
-        tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
-      }
+      if (I4B_W4T_L2PF)
+        for (int kp = kb0 + S; kp < kb0 + 2 * S && kp < kb1; ++kp) {  // the first S k-blocks load right away
+          tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
+          tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
+          tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
+        }
       for (int kbl = 0; kbl < KB; ++kbl) {
         const int kb = kb0 + kbl;
         const int s = kbl % S, u = kbl / S;
@@ -170,7 +183,7 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
         // pull the packed weights of k-block kb + 2S into L2 now: their loads, S k-blocks from now, then
         // find them there (the activation rows are shared by every CTA of the row and stay in L2)
         const int kp = kb + 2 * S;
-        if (kp < kb1) {
+        if (I4B_W4T_L2PF && kp < kb1) {
           tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
           tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
           tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
@@ -222,9 +235,10 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
         ++g_lo;
         g_end += G;
       }
-      if (!mbar_wait_sleep(&full[s], u & 1)) { ok = false; break; }
+      if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&full[s], u & 1) : mbar_wait(&full[s], u & 1))) { ok = false; break; }
       if (kbl >= NA) {
-        if (!mbar_wait_sleep(&afree[b], ((kbl / NA) - 1) & 1)) { ok = false; break; }
+        const uint32_t par = ((kbl / NA) - 1) & 1;
+        if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&afree[b], par) : mbar_wait(&afree[b], par))) { ok = false; break; }
         tc_fence_after();
       }
       const uint32_t* P = reinterpret_cast<const uint32_t*>(sP(s));
