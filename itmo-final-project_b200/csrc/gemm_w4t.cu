@@ -20,9 +20,9 @@
 //               (8 k8-rows x 128 int32) and two group rows of scales and zeros;
 //   warp 1      allocates TMEM (accumulator + A ring) and, from one thread, issues four
 //               tcgen05.mma.kind::f16 per k-block, then tcgen05.commit frees the stage and the A slot;
-//   warps 2..17 dequantize: warp w owns TMEM lane quarter w % 4 (weight rows 32 (w % 4) + lane) and packed
-//               words 2h, 2h + 1 of each k-block (h = (w - 2) / 4); then read the accumulator back with
-//               tcgen05.ld and store y (or fp32 partials of the K split).
+//   warps 2..17 dequantize in four groups of four: group h = (w - 2) / 4 takes every fourth k-block, and warp
+//               w of it owns TMEM lane quarter w % 4 (weight rows 32 (w % 4) + lane); then all sixteen read
+//               the accumulator back with tcgen05.ld and store y (or fp32 partials of the K split).
 // Every wait is bounded; on expiry the kernel records I4B_DEVERR_WAIT_TIMEOUT, drains its own TMA copies,
 // frees TMEM and returns.
 #include <algorithm>
@@ -37,13 +37,13 @@ static __device__ unsigned int g_w4t_err = 0;
 // Build-time tuning knobs: A slots in TMEM, whether the dequant warps wait with a suspend hint, and whether
 // the producer prefetches packed weights into L2 ahead of their loads.
 #ifndef I4B_W4T_NA
-#define I4B_W4T_NA 4
+#define I4B_W4T_NA 8
 #endif
 #ifndef I4B_W4T_SLEEP
 #define I4B_W4T_SLEEP 1
 #endif
 #ifndef I4B_W4T_L2PF
-#define I4B_W4T_L2PF 1
+#define I4B_W4T_L2PF 0
 #endif
 
 template <int NT>
@@ -64,6 +64,7 @@ struct W4tCfg {
   static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + BAR_BYTES;
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
   static_assert(STAGES >= 3, "at least three pipeline stages");
+  static_assert(NA % 4 == 0, "each of the four dequant groups owns NA / 4 slots");
   static_assert(A_COL + NA * A_SLOT_COLS <= TMEM_COLS && TMEM_COLS <= 512, "TMEM budget");
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N for M = 128");
 };
@@ -91,11 +92,15 @@ __device__ __forceinline__ uint4 w4t_dequant_word(uint32_t w, const DqParams& p)
                     __byte_perm(r[0], r[1], 0x7632), __byte_perm(r[2], r[3], 0x7632));
 }
 
-// 32 lanes x 32 bit, 8 consecutive columns from this thread's registers (the warp's lane quarter).
-__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint4& a, const uint4& b) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-               "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
-               : "memory");
+// 32 lanes x 32 bit, 16 consecutive columns from this thread's registers (the warp's lane quarter).
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint4& a, const uint4& b, const uint4& c,
+                                                   const uint4& d) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w), "r"(c.x), "r"(c.y), "r"(c.z),
+      "r"(c.w), "r"(d.x), "r"(d.y), "r"(d.z), "r"(d.w)
+      : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -145,7 +150,7 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < NA; ++b) {
-      mbar_init(&aready[b], C::DQ_WARPS);
+      mbar_init(&aready[b], 4);  // the four warps (lane quarters) of the group that dequantizes the slot
       mbar_init(&afree[b], 1);
     }
     mbar_init(tfull, 1);
@@ -221,14 +226,15 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
       umma_commit(tfull);  // also on the error path: completes once the issued MMAs are done
     }
   } else {
-    // dequant warp: TMEM lane quarter q (rows 32 q + lane), packed words 2h and 2h + 1 of each k-block
+    // Dequant warps in four groups of four: group h takes k-blocks h, h + 4, h + 8, ... (so four k-blocks are
+    // dequantized at once: one warp's pass -- wait, dequantize, tcgen05.st, wait::st, arrive -- is a latency
+    // chain several times longer than a k-block's MMAs); within a group, warp q owns TMEM lane quarter q
+    // (weight rows 32 q + lane) and all eight packed words of the row.
     const int q = warp & 3, h = (warp - 2) >> 2;
     const int nl = 32 * q + lane;
     const uint32_t lane_base = uint32_t(32 * q) << 16;
-    int g_lo = (kb0 * C::BK) / G, g_end = (g_lo + 1) * G;
-    int g_cached = -1;
-    DqParams pc{};
-    for (int kbl = 0; kbl < KB && ok; ++kbl) {
+    int g_lo = ((kb0 + h) * C::BK) / G, g_end = (g_lo + 1) * G;
+    for (int kbl = h; kbl < KB && ok; kbl += 4) {
       const int s = kbl % S, u = kbl / S, b = kbl % NA;
       const int k_begin = (kb0 + kbl) * C::BK;
       while (k_begin >= g_end) {
@@ -244,22 +250,18 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
       const uint32_t* P = reinterpret_cast<const uint32_t*>(sP(s));
       const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ(s));
       const uint16_t* Zs = Ss + 2 * C::BF;
-      if (g_cached != g_lo) {
-        pc = dq_params<F16>(Ss[nl], Zs[nl]);
-        g_cached = g_lo;
-      }
-      const DqParams p0 = pc;
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = P[j * C::BF + nl];
+      const DqParams p0 = dq_params<F16>(Ss[nl], Zs[nl]);
       const int jsplit = (g_end - k_begin) >> 3;  // words of this k-block inside group g_lo (>= 1)
-      DqParams p1 = p0;
-      if (jsplit < 8) {
-        p1 = dq_params<F16>(Ss[C::BF + nl], Zs[C::BF + nl]);
-        pc = p1;
-        g_cached = g_lo + 1;
-      }
-      const int j0 = 2 * h;
-      const uint4 v0 = w4t_dequant_word<F16>(P[j0 * C::BF + nl], j0 >= jsplit ? p1 : p0);
-      const uint4 v1 = w4t_dequant_word<F16>(P[(j0 + 1) * C::BF + nl], j0 + 1 >= jsplit ? p1 : p0);
-      tmem_st_32x32b_x8(tmem + lane_base + uint32_t(C::A_COL + b * C::A_SLOT_COLS + 4 * j0), v0, v1);
+      const DqParams p1 = jsplit < 8 ? dq_params<F16>(Ss[C::BF + nl], Zs[C::BF + nl]) : p0;
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = w4t_dequant_word<F16>(w[j], j >= jsplit ? p1 : p0);
+      const uint32_t col = tmem + lane_base + uint32_t(C::A_COL + b * C::A_SLOT_COLS);
+      tmem_st_32x32b_x16(col, v[0], v[1], v[2], v[3]);
+      tmem_st_32x32b_x16(col + 16u, v[4], v[5], v[6], v[7]);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
