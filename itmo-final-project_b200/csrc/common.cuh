@@ -202,6 +202,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+// 3-D tiled load global -> shared (box stored densely, innermost dimension first), completion on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t* bar, int32_t c0, int32_t c1,
+                                            int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
 // Fire-and-forget prefetch of a 2-D tensor tile into L2 (no shared memory, no completion to wait for).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const void* map, int32_t c0, int32_t c1) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(c0), "r"(c1)

@@ -475,6 +475,21 @@ bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
 
 
 
+// 3-D tensor: `d0` contiguous elements, then `d1` rows `stride1` bytes apart, then `d2` planes `stride2`
+// bytes apart.
+bool make_tma_map_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                     uint64_t d2, uint64_t stride1, uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2,
+                     CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1, stride2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <bool INT4, bool F16, int BN, int BMT>
 static cudaError_t launch_tc_impl(const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                                   int64_t sym, int ksplit, float* partials, unsigned int* tickets,
@@ -617,7 +632,12 @@ cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64
   // bn: tile code, ks: K splits (from tc_plan / tc_plan_w4)
   if (bn >= 5) {
     if (!int4 || (ks > 1 && N % 4 != 0)) return cudaErrorInvalidValue;
-    return launch_w4t(f16, o, M, N, K, G, y, sym, bn, ks, partials, tickets, stream);
+    const cudaError_t e = launch_w4t(f16, o, M, N, K, G, y, sym, bn, ks, partials, tickets, stream);
+    if (e != cudaErrorNotSupported) return e;
+    // scales / zeros whose tensor maps cannot be encoded as one 3-D box (e.g. interleaved views): the
+    // shared-memory-operand kernel, one 128 x 128 tile per CTA, no K split (no workspace needed)
+    return f16 ? launch_tc_impl<true, true, 128, 1>(o, M, N, K, G, y, sym, 1, partials, tickets, stream)
+               : launch_tc_impl<true, false, 128, 1>(o, M, N, K, G, y, sym, 1, partials, tickets, stream);
   }
 #define I4B_TC(I, F) \
   return bn == 4   ? launch_tc_impl<I, F, 256, 2>(o, M, N, K, G, y, sym, ks, partials, tickets, stream) \

@@ -34,36 +34,35 @@ namespace i4b {
 
 static __device__ unsigned int g_w4t_err = 0;
 
-// Build-time tuning knobs: A slots in TMEM, whether the dequant warps wait with a suspend hint, and whether
-// the producer prefetches packed weights into L2 ahead of their loads.
+// Build-time tuning knobs: A slots in TMEM, and whether the dequant warps wait with a suspend hint.
 #ifndef I4B_W4T_NA
 #define I4B_W4T_NA 8
 #endif
 #ifndef I4B_W4T_SLEEP
 #define I4B_W4T_SLEEP 1
 #endif
-#ifndef I4B_W4T_L2PF
-#define I4B_W4T_L2PF 0
-#endif
 
 template <int NT>
 struct W4tCfg {
   static constexpr int BF = 128, BK = 64;  // weight rows (the MMA's M) and k per k-block
   static constexpr int DQ_WARPS = 16;
-  static constexpr int THREADS = 64 + 32 * DQ_WARPS;
-  static constexpr int X_BYTES = NT * BK * 2;     // activation tile: NT rows of 128 B
-  static constexpr int P_BYTES = 8 * BF * 4;      // packed words of one k-block
-  static constexpr int SZ_BYTES = 2 * 2 * BF * 2; // scales + zeros, two group rows
-  static constexpr int STAGE_BYTES = X_BYTES + P_BYTES + SZ_BYTES;  // a multiple of 1024
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 12 ? 12 : (200 * 1024) / STAGE_BYTES;
-  static constexpr int NA = I4B_W4T_NA;           // A slots (k-blocks) in TMEM
-  static constexpr int A_COL = NT < 32 ? 32 : NT; // first TMEM column of the A ring
-  static constexpr int A_SLOT_COLS = BK / 2;      // 64 16-bit values per row = 32 columns
+  static constexpr int THREADS = 32 * (3 + DQ_WARPS);  // X producer, MMA, 16 dequant warps, W producer
+  static constexpr int X_BYTES = NT * BK * 2;          // activation tile: NT rows of 128 B
+  // weight stage: two k-blocks (128 k) of packed words, and scales + zeros of up to 4 groups
+  static constexpr int P_BYTES = 16 * BF * 4;
+  static constexpr int SZ_ROWS = 4;
+  static constexpr int SZ_BYTES = 2 * SZ_ROWS * BF * 2;
+  static constexpr int W_BYTES = P_BYTES + SZ_BYTES;
+  static constexpr int SX = NT >= 256 ? 4 : NT >= 128 ? 6 : NT >= 64 ? 10 : 12;  // activation stages
+  static constexpr int SW = NT >= 256 ? 6 : NT >= 128 ? 8 : NT >= 64 ? 10 : 12;  // weight stages
+  static constexpr int NA = I4B_W4T_NA;                // A slots (k-blocks) in TMEM
+  static constexpr int A_COL = NT < 32 ? 32 : NT;      // first TMEM column of the A ring
+  static constexpr int A_SLOT_COLS = BK / 2;           // 64 16-bit values per row = 32 columns
   static constexpr int TMEM_COLS = (A_COL + NA * A_SLOT_COLS) <= 256 ? 256 : 512;
-  static constexpr int BAR_BYTES = (2 * STAGES + 2 * NA + 1) * 8 + 8;
-  static constexpr size_t SMEM = 1024 + size_t(STAGES) * STAGE_BYTES + BAR_BYTES;
-  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
-  static_assert(STAGES >= 3, "at least three pipeline stages");
+  static constexpr int BAR_BYTES = (2 * SX + 2 * SW + 2 * NA + 1) * 8 + 8;
+  static constexpr size_t SMEM = 1024 + size_t(SX) * X_BYTES + size_t(SW) * W_BYTES + BAR_BYTES;
+  static_assert(X_BYTES % 1024 == 0, "activation stages keep the 1024-byte swizzle alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(NA % 4 == 0, "each of the four dequant groups owns NA / 4 slots");
   static_assert(A_COL + NA * A_SLOT_COLS <= TMEM_COLS && TMEM_COLS <= 512, "TMEM budget");
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N for M = 128");
@@ -118,49 +117,55 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 template <bool F16, int NT>
 __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
     w4t_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z, int M, int N,
-                    int K, int G, uint16_t* __restrict__ y, int64_t sym, int ksplit, float* __restrict__ partials,
+                    const __grid_constant__ CUtensorMap tm_sz, int sz_swap, int M, int N, int K, int G,
+                    uint16_t* __restrict__ y, int64_t sym, int ksplit, float* __restrict__ partials,
                     unsigned int* __restrict__ tickets) {
   using C = W4tCfg<NT>;
-  constexpr int S = C::STAGES, NA = C::NA;
+  constexpr int SX = C::SX, SW = C::SW, NA = C::NA;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  // [S stages: X | P | SZ] [barriers]
-  uint8_t* stage0 = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage0 + S * C::STAGE_BYTES);
-  uint64_t* empty = full + S;
-  uint64_t* aready = empty + S;  // A slot dequantized into TMEM (one arrival per dequant warp)
-  uint64_t* afree = aready + NA;  // A slot no longer read by the MMAs
+  // [SX activation stages][SW weight stages: P | scales and zeros][barriers]
+  uint8_t* xring = smem;
+  uint8_t* wring = xring + SX * C::X_BYTES;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(wring + SW * C::W_BYTES);
+  uint64_t* xempty = xfull + SX;   // MMA commit: the activation stage is read
+  uint64_t* wfull = xempty + SX;
+  uint64_t* wempty = wfull + SW;   // dequant arrivals: the weight stage is read
+  uint64_t* aready = wempty + SW;  // A slot dequantized into TMEM (the four warps of a group)
+  uint64_t* afree = aready + NA;   // A slot no longer read by the MMAs
   uint64_t* tfull = afree + NA;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
-  auto sX = [&](int s) { return stage0 + s * C::STAGE_BYTES; };
-  auto sP = [&](int s) { return stage0 + s * C::STAGE_BYTES + C::X_BYTES; };
-  auto sSZ = [&](int s) { return stage0 + s * C::STAGE_BYTES + C::X_BYTES + C::P_BYTES; };
+  auto sX = [&](int s) { return xring + s * C::X_BYTES; };
+  auto sW = [&](int s) { return wring + s * C::W_BYTES; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * C::BF, m0 = blockIdx.y * NT;
   const int KBT = (K + C::BK - 1) / C::BK;
   const int kb0 = int((int64_t(blockIdx.z) * KBT) / ksplit), kb1 = int((int64_t(blockIdx.z + 1) * KBT) / ksplit);
-  const int KB = kb1 - kb0;
+  const int KB = kb1 - kb0;  // k-blocks of this CTA; weight stage j holds its k-blocks 2j and 2j + 1
+  const int NWS = (KB + 1) / 2;
   __shared__ int s_last;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < SX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 8);  // the two dequant groups (four warps each) of its two k-blocks
     }
     for (int b = 0; b < NA; ++b) {
-      mbar_init(&aready[b], 4);  // the four warps (lane quarters) of the group that dequantizes the slot
+      mbar_init(&aready[b], 4);
       mbar_init(&afree[b], 1);
     }
     mbar_init(tfull, 1);
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_x);
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_x);
+  if (warp == 2 + C::DQ_WARPS && lane == 0) {
     tma_prefetch_desc(&tm_w);
-    tma_prefetch_desc(&tm_s);
-    tma_prefetch_desc(&tm_z);
+    tma_prefetch_desc(&tm_sz);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -173,46 +178,46 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
   bool ok = true;
 
   if (warp == 0) {
+    // activation producer: one 64-k tile per k-block
     if (lane == 0) {
       int issued = 0;
-      if (I4B_W4T_L2PF)
-        for (int kp = kb0 + S; kp < kb0 + 2 * S && kp < kb1; ++kp) {  // the first S k-blocks load right away
-          tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
-          tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
-          tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
-        }
       for (int kbl = 0; kbl < KB; ++kbl) {
-        const int kb = kb0 + kbl;
-        const int s = kbl % S, u = kbl / S;
-        if (kbl >= S && !mbar_wait(&empty[s], (u - 1) & 1)) { ok = false; break; }
-        // pull the packed weights of k-block kb + 2S into L2 now: their loads, S k-blocks from now, then
-        // find them there (the activation rows are shared by every CTA of the row and stay in L2)
-        const int kp = kb + 2 * S;
-        if (I4B_W4T_L2PF && kp < kb1) {
-          tma_prefetch_l2_2d(&tm_w, n0, kp * 8);
-          tma_prefetch_l2_2d(&tm_s, n0, (kp * C::BK) / G);
-          tma_prefetch_l2_2d(&tm_z, n0, (kp * C::BK) / G);
-        }
-        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-        const int g_lo = (kb * C::BK) / G;
-        tma_load_2d(sX(s), &tm_x, &full[s], kb * C::BK, m0);
-        tma_load_2d(sP(s), &tm_w, &full[s], n0, kb * 8);
-        tma_load_2d(sSZ(s), &tm_s, &full[s], n0, g_lo);
-        tma_load_2d(sSZ(s) + 2 * C::BF * 2, &tm_z, &full[s], n0, g_lo);
+        const int s = kbl % SX, u = kbl / SX;
+        if (kbl >= SX && !mbar_wait(&xempty[s], (u - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
+        tma_load_2d(sX(s), &tm_x, &xfull[s], (kb0 + kbl) * C::BK, m0);
         ++issued;
       }
-      // Never leave a bulk copy in flight: wait for the last use of every stage.
-      for (int s = 0; s < S && s < issued; ++s) {
-        const int last = ((issued - 1 - s) / S) * S + s;
-        if (!mbar_wait(&full[s], (last / S) & 1)) ok = false;
+      for (int s = 0; s < SX && s < issued; ++s) {  // never leave a bulk copy in flight
+        const int last = ((issued - 1 - s) / SX) * SX + s;
+        if (!mbar_wait(&xfull[s], (last / SX) & 1)) ok = false;
+      }
+    }
+  } else if (warp == 2 + C::DQ_WARPS) {
+    // weight producer: per weight stage the packed words of 128 k (16 rows) and one 3-D box of scales and
+    // zeros (SZ_ROWS group rows of both tensors)
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < NWS; ++j) {
+        const int s = j % SW, u = j / SW;
+        if (j >= SW && !mbar_wait(&wempty[s], (u - 1) & 1)) { ok = false; break; }
+        const int k_begin = (kb0 + 2 * j) * C::BK;
+        mbar_arrive_expect_tx(&wfull[s], C::W_BYTES);
+        tma_load_2d(sW(s), &tm_w, &wfull[s], n0, k_begin / 8);
+        tma_load_3d(sW(s) + C::P_BYTES, &tm_sz, &wfull[s], n0, k_begin / G, 0);
+        ++issued;
+      }
+      for (int s = 0; s < SW && s < issued; ++s) {
+        const int last = ((issued - 1 - s) / SW) * SW + s;
+        if (!mbar_wait(&wfull[s], (last / SW) & 1)) ok = false;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(F16 ? 0 : 1, C::BF, NT);
       for (int kbl = 0; kbl < KB; ++kbl) {
-        const int s = kbl % S, u = kbl / S, b = kbl % NA;
-        if (!mbar_wait(&full[s], u & 1)) { ok = false; break; }
+        const int s = kbl % SX, u = kbl / SX, b = kbl % NA;
+        if (!mbar_wait(&xfull[s], u & 1)) { ok = false; break; }
         if (!mbar_wait(&aready[b], (kbl / NA) & 1)) { ok = false; break; }
         tc_fence_after();
         const uint64_t bdesc = umma_desc_sw128(smem_u32(sX(s)));
@@ -220,45 +225,50 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < C::BK / 16; ++kk)
           umma_f16_ts(tmem, acol + uint32_t(8 * kk), bdesc + 2 * kk, idesc, (kbl | kk) != 0 ? 1u : 0u);
-        umma_commit(&empty[s]);
+        umma_commit(&xempty[s]);
         umma_commit(&afree[b]);
       }
       umma_commit(tfull);  // also on the error path: completes once the issued MMAs are done
     }
   } else {
-    // Dequant warps in four groups of four: group h takes k-blocks h, h + 4, h + 8, ... (so four k-blocks are
-    // dequantized at once: one warp's pass -- wait, dequantize, tcgen05.st, wait::st, arrive -- is a latency
-    // chain several times longer than a k-block's MMAs); within a group, warp q owns TMEM lane quarter q
-    // (weight rows 32 q + lane) and all eight packed words of the row.
+    // Dequant warps in four groups of four: group h takes k-blocks h, h + 4, h + 8, ... (four dequant passes
+    // in flight: one warp's pass -- wait, dequantize, tcgen05.st, wait::st, arrive -- is a latency chain
+    // longer than a k-block's MMAs); within a group, warp q owns TMEM lane quarter q (weight rows
+    // 32 q + lane) and all eight packed words of the row.
     const int q = warp & 3, h = (warp - 2) >> 2;
     const int nl = 32 * q + lane;
     const uint32_t lane_base = uint32_t(32 * q) << 16;
-    int g_lo = ((kb0 + h) * C::BK) / G, g_end = (g_lo + 1) * G;
+    const int zoff = sz_swap ? 0 : C::SZ_ROWS * C::BF, soff = sz_swap ? C::SZ_ROWS * C::BF : 0;
     for (int kbl = h; kbl < KB && ok; kbl += 4) {
-      const int s = kbl % S, u = kbl / S, b = kbl % NA;
+      const int j = kbl >> 1, ws = j % SW, b = kbl % NA;
       const int k_begin = (kb0 + kbl) * C::BK;
-      while (k_begin >= g_end) {
-        ++g_lo;
-        g_end += G;
+      if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&wfull[ws], (j / SW) & 1) : mbar_wait(&wfull[ws], (j / SW) & 1))) {
+        ok = false;
+        break;
       }
-      if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&full[s], u & 1) : mbar_wait(&full[s], u & 1))) { ok = false; break; }
       if (kbl >= NA) {
         const uint32_t par = ((kbl / NA) - 1) & 1;
         if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&afree[b], par) : mbar_wait(&afree[b], par))) { ok = false; break; }
         tc_fence_after();
       }
-      const uint32_t* P = reinterpret_cast<const uint32_t*>(sP(s));
-      const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sSZ(s));
-      const uint16_t* Zs = Ss + 2 * C::BF;
+      const uint32_t* P = reinterpret_cast<const uint32_t*>(sW(ws)) + (kbl & 1) * 8 * C::BF;
+      const uint16_t* SZ = reinterpret_cast<const uint16_t*>(sW(ws) + C::P_BYTES);
       uint32_t w[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) w[j] = P[j * C::BF + nl];
-      const DqParams p0 = dq_params<F16>(Ss[nl], Zs[nl]);
+      for (int jw = 0; jw < 8; ++jw) w[jw] = P[jw * C::BF + nl];
+      // group rows of the stage's scale / zero box: the stage starts at group (k of its first k-block) / G
+      const int g_stage = ((kb0 + 2 * j) * C::BK) / G;
+      const int g_lo = k_begin / G, g_end = (g_lo + 1) * G;
+      const int r_lo = g_lo - g_stage;
+      const DqParams p0 = dq_params<F16>(SZ[soff + r_lo * C::BF + nl], SZ[zoff + r_lo * C::BF + nl]);
       const int jsplit = (g_end - k_begin) >> 3;  // words of this k-block inside group g_lo (>= 1)
-      const DqParams p1 = jsplit < 8 ? dq_params<F16>(Ss[C::BF + nl], Zs[C::BF + nl]) : p0;
+      const DqParams p1 =
+          jsplit < 8 ? dq_params<F16>(SZ[soff + (r_lo + 1) * C::BF + nl], SZ[zoff + (r_lo + 1) * C::BF + nl]) : p0;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[ws]);  // the words and parameters are in registers
       uint4 v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = w4t_dequant_word<F16>(w[j], j >= jsplit ? p1 : p0);
+      for (int jw = 0; jw < 8; ++jw) v[jw] = w4t_dequant_word<F16>(w[jw], jw >= jsplit ? p1 : p0);
       const uint32_t col = tmem + lane_base + uint32_t(C::A_COL + b * C::A_SLOT_COLS);
       tmem_st_32x32b_x16(col, v[0], v[1], v[2], v[3]);
       tmem_st_32x32b_x16(col + 16u, v[4], v[5], v[6], v[7]);
@@ -354,21 +364,26 @@ static cudaError_t launch_w4t_impl(const TcOperands& o, int64_t M, int64_t N, in
                                    cudaStream_t stream) {
   using C = W4tCfg<NT>;
   const CUtensorMapDataType act = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  CUtensorMap mx{}, mw{}, ms{}, mz{};
+  CUtensorMap mx{}, mw{}, msz{};
   bool ok = make_tma_map_2d(&mx, act, o.x, uint64_t(K), uint64_t(M), uint64_t(o.sxm) * 2, 64, NT,
                             CU_TENSOR_MAP_SWIZZLE_128B);
   ok = ok && make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, o.w, uint64_t(N), uint64_t(K / 8),
-                             uint64_t(o.sw) * 4, C::BF, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
-  ok = ok && make_tma_map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.sc, uint64_t(N), uint64_t(K / G),
-                             uint64_t(o.ssg) * 2, C::BF, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
-  ok = ok && make_tma_map_2d(&mz, CU_TENSOR_MAP_DATA_TYPE_UINT16, o.zr, uint64_t(N), uint64_t(K / G),
-                             uint64_t(o.ssg) * 2, C::BF, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (!ok) return cudaErrorInvalidValue;
+                             uint64_t(o.sw) * 4, C::BF, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+  // scales and zeros as the two planes of one 3-D tensor (the lower address first), so that one box brings
+  // both; the planes are 16-byte aligned allocations, so their distance is a multiple of 16 bytes
+  const uintptr_t ps = reinterpret_cast<uintptr_t>(o.sc), pz = reinterpret_cast<uintptr_t>(o.zr);
+  const int swap = pz < ps ? 1 : 0;
+  const uint16_t* lo = swap ? o.zr : o.sc;
+  const uint64_t dist = swap ? uint64_t(ps - pz) : uint64_t(pz - ps);
+  if (dist == 0 || dist % 16 != 0) return cudaErrorNotSupported;
+  ok = ok && make_tma_map_3d(&msz, CU_TENSOR_MAP_DATA_TYPE_UINT16, lo, uint64_t(N), uint64_t(K / G), 2,
+                             uint64_t(o.ssg) * 2, dist, C::BF, C::SZ_ROWS, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) return cudaErrorNotSupported;  // the caller falls back to the shared-memory-operand kernel
   auto kern = w4t_gemm_kernel<F16, NT>;
   if (cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), C::SMEM)) return e;
   dim3 grid(unsigned(cdiv(N, C::BF)), unsigned(cdiv(M, NT)), unsigned(ksplit));
-  kern<<<grid, C::THREADS, C::SMEM, stream>>>(mx, mw, ms, mz, int(M), int(N), int(K), G, y, sym, ksplit, partials,
-                                               tickets);
+  kern<<<grid, C::THREADS, C::SMEM, stream>>>(mx, mw, msz, swap, int(M), int(N), int(K), G, y, sym, ksplit,
+                                               partials, tickets);
   return cudaGetLastError();
 }
 

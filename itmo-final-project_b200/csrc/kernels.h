@@ -122,6 +122,9 @@ TcPlan tc_plan_w4(int64_t M, int64_t N, int64_t K, int num_sms);  // INT4
 void set_tc_override(int tile, int splits);  // tuning: 0 keeps the automatic choice
 bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
                      uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
+bool make_tma_map_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                     uint64_t d2, uint64_t stride1, uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2,
+                     CUtensorMapSwizzle swz);
 size_t tc_partial_bytes(const TcPlan& p, int64_t M, int64_t N);
 cudaError_t launch_tc(bool int4, bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                       int64_t sym, const TcPlan& plan, float* partials, unsigned int* tickets, cudaStream_t stream);
