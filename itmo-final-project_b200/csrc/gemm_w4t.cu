@@ -114,6 +114,19 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// One lane of a converged warp (elect.sync).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\telect.sync r|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+// Bounded wait by a whole warp, with one verdict for all its lanes.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
 template <bool F16, int NT>
 __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
     w4t_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -177,59 +190,66 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
+  // The control warps (activation producer, weight producer, MMA) run their loops on all 32 lanes, so that
+  // stage indices, coordinates and descriptors are warp-uniform values, and issue each TMA / tcgen05
+  // instruction from one elected lane.
   if (warp == 0) {
     // activation producer: one 64-k tile per k-block
-    if (lane == 0) {
-      int issued = 0;
-      for (int kbl = 0; kbl < KB; ++kbl) {
-        const int s = kbl % SX, u = kbl / SX;
-        if (kbl >= SX && !mbar_wait(&xempty[s], (u - 1) & 1)) { ok = false; break; }
+    int issued = 0;
+    for (int kbl = 0; kbl < KB; ++kbl) {
+      const int s = kbl % SX, u = kbl / SX;
+      if (kbl >= SX && !warp_wait(&xempty[s], (u - 1) & 1)) { ok = false; break; }
+      if (elect_one()) {
         mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
         tma_load_2d(sX(s), &tm_x, &xfull[s], (kb0 + kbl) * C::BK, m0);
-        ++issued;
       }
-      for (int s = 0; s < SX && s < issued; ++s) {  // never leave a bulk copy in flight
-        const int last = ((issued - 1 - s) / SX) * SX + s;
-        if (!mbar_wait(&xfull[s], (last / SX) & 1)) ok = false;
-      }
+      __syncwarp();
+      ++issued;
+    }
+    for (int s = 0; s < SX && s < issued; ++s) {  // never leave a bulk copy in flight
+      const int last = ((issued - 1 - s) / SX) * SX + s;
+      if (!warp_wait(&xfull[s], (last / SX) & 1)) ok = false;
     }
   } else if (warp == 2 + C::DQ_WARPS) {
     // weight producer: per weight stage the packed words of 128 k (16 rows) and one 3-D box of scales and
     // zeros (SZ_ROWS group rows of both tensors)
-    if (lane == 0) {
-      int issued = 0;
-      for (int j = 0; j < NWS; ++j) {
-        const int s = j % SW, u = j / SW;
-        if (j >= SW && !mbar_wait(&wempty[s], (u - 1) & 1)) { ok = false; break; }
-        const int k_begin = (kb0 + 2 * j) * C::BK;
+    int issued = 0;
+    for (int j = 0; j < NWS; ++j) {
+      const int s = j % SW, u = j / SW;
+      if (j >= SW && !warp_wait(&wempty[s], (u - 1) & 1)) { ok = false; break; }
+      const int k_begin = (kb0 + 2 * j) * C::BK;
+      if (elect_one()) {
         mbar_arrive_expect_tx(&wfull[s], C::W_BYTES);
         tma_load_2d(sW(s), &tm_w, &wfull[s], n0, k_begin / 8);
         tma_load_3d(sW(s) + C::P_BYTES, &tm_sz, &wfull[s], n0, k_begin / G, 0);
-        ++issued;
       }
-      for (int s = 0; s < SW && s < issued; ++s) {
-        const int last = ((issued - 1 - s) / SW) * SW + s;
-        if (!mbar_wait(&wfull[s], (last / SW) & 1)) ok = false;
-      }
+      __syncwarp();
+      ++issued;
+    }
+    for (int s = 0; s < SW && s < issued; ++s) {
+      const int last = ((issued - 1 - s) / SW) * SW + s;
+      if (!warp_wait(&wfull[s], (last / SW) & 1)) ok = false;
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(F16 ? 0 : 1, C::BF, NT);
-      for (int kbl = 0; kbl < KB; ++kbl) {
-        const int s = kbl % SX, u = kbl / SX, b = kbl % NA;
-        if (!mbar_wait(&xfull[s], u & 1)) { ok = false; break; }
-        if (!mbar_wait(&aready[b], (kbl / NA) & 1)) { ok = false; break; }
-        tc_fence_after();
-        const uint64_t bdesc = umma_desc_sw128(smem_u32(sX(s)));
-        const uint32_t acol = tmem + uint32_t(C::A_COL + b * C::A_SLOT_COLS);
+    constexpr uint32_t idesc = umma_idesc_f16(F16 ? 0 : 1, C::BF, NT);
+    for (int kbl = 0; kbl < KB; ++kbl) {
+      const int s = kbl % SX, u = kbl / SX, b = kbl % NA;
+      if (!warp_wait(&xfull[s], u & 1)) { ok = false; break; }
+      if (!warp_wait(&aready[b], (kbl / NA) & 1)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t bdesc = umma_desc_sw128(smem_u32(sX(s)));
+      const uint32_t acol = tmem + uint32_t(C::A_COL + b * C::A_SLOT_COLS);
+      if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < C::BK / 16; ++kk)
           umma_f16_ts(tmem, acol + uint32_t(8 * kk), bdesc + 2 * kk, idesc, (kbl | kk) != 0 ? 1u : 0u);
         umma_commit(&xempty[s]);
         umma_commit(&afree[b]);
       }
-      umma_commit(tfull);  // also on the error path: completes once the issued MMAs are done
+      __syncwarp();
     }
+    if (elect_one()) umma_commit(tfull);  // also on the error path: completes once the issued MMAs are done
+    __syncwarp();
   } else {
     // Dequant warps in four groups of four: group h takes k-blocks h, h + 4, h + 8, ... (four dequant passes
     // in flight: one warp's pass -- wait, dequantize, tcgen05.st, wait::st, arrive -- is a latency chain
