@@ -156,13 +156,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity; false after I4B_WAIT_LIMIT_NS.
+// Bounded wait for the phase with the given parity; false once I4B_WAIT_LIMIT_NS have passed since the
+// 256th probe.  The global timer is read only every 256 probes: a read costs hundreds of cycles, which a
+// pipeline stage waiting a few hundred cycles for its data would otherwise pay on every wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0 && globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
+    if ((i & 255u) == 255u) {
+      const uint64_t t = globaltimer_ns();
+      if (i == 255u) t0 = t;
+      else if (t - t0 > I4B_WAIT_LIMIT_NS) return false;
+    }
   }
 }
 
@@ -180,11 +185,14 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait_sleep(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > I4B_WAIT_LIMIT_NS) return false;
+    if ((i & 15u) == 15u) {  // each probe may sleep up to ~1 us: the timer every 16 probes
+      const uint64_t t = globaltimer_ns();
+      if (i == 15u) t0 = t;
+      else if (t - t0 > I4B_WAIT_LIMIT_NS) return false;
+    }
   }
 }
 
