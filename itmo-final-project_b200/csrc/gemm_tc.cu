@@ -592,7 +592,7 @@ static double w4t_cost(int nt, int splits, int64_t M, int64_t N, int64_t kb, int
   const double F = 3.0;
   const double c = nt == 256 ? 0.32 : nt == 128 ? 0.18 : 0.11;
   const int64_t tiles = cdiv(N, 128) * cdiv(M, int64_t(nt));
-  const int64_t waves = cdiv(tiles * splits, int64_t(num_sms));
+  const int64_t waves = cdiv(tiles * splits, int64_t(num_sms) * w4t_ctas_per_sm(nt == 256 ? 5 : 6));
   double t = double(waves) * (F + c * double(cdiv(kb, int64_t(splits))));
   if (splits > 1) t += 2.0 + double(splits) * double(M) * double(N) * 8.0 / 3.0e6;
   return t;

@@ -20,9 +20,11 @@
 //               (8 k8-rows x 128 int32) and two group rows of scales and zeros;
 //   warp 1      allocates TMEM (accumulator + A ring) and, from one thread, issues four
 //               tcgen05.mma.kind::f16 per k-block, then tcgen05.commit frees the stage and the A slot;
-//   warps 2..17 dequantize in four groups of four: group h = (w - 2) / 4 takes every fourth k-block, and warp
-//               w of it owns TMEM lane quarter w % 4 (weight rows 32 (w % 4) + lane); then all sixteen read
-//               the accumulator back with tcgen05.ld and store y (or fp32 partials of the K split).
+//   warps 2..    dequantize in groups of four (four groups for 256-token tiles, two otherwise): group
+//               h = (w - 2) / 4 takes every GROUPS-th k-block, and warp w of it owns TMEM lane quarter w % 4
+//               (weight rows 32 (w % 4) + lane); then all of them read the accumulator back with
+//               tcgen05.ld and store y (or fp32 partials of the K split);
+//   last warp   weight producer: per two k-blocks the packed words and one box of scales and zeros.
 // Every wait is bounded; on expiry the kernel records I4B_DEVERR_WAIT_TIMEOUT, drains its own TMA copies,
 // frees TMEM and returns.
 #include <algorithm>
@@ -45,25 +47,31 @@ static __device__ unsigned int g_w4t_err = 0;
 template <int NT>
 struct W4tCfg {
   static constexpr int BF = 128, BK = 64;  // weight rows (the MMA's M) and k per k-block
-  static constexpr int DQ_WARPS = 16;
-  static constexpr int THREADS = 32 * (3 + DQ_WARPS);  // X producer, MMA, 16 dequant warps, W producer
+  // Token tiles up to 128 run two CTAs per SM (each with two dequant groups, 256 TMEM columns and at most
+  // 113 KB of shared memory): a pipeline step of the control warps costs a few hundred cycles whatever its
+  // size, so two independent pipelines per SM double the steps in flight.  256-token tiles need all of TMEM.
+  static constexpr int CPS = NT <= 128 ? 2 : 1;        // CTAs per SM
+  static constexpr int GROUPS = CPS == 2 ? 2 : 4;      // dequant groups of four warps
+  static constexpr int DQ_WARPS = 4 * GROUPS;
+  static constexpr int THREADS = 32 * (3 + DQ_WARPS);  // X producer, MMA, dequant warps, W producer
   static constexpr int X_BYTES = NT * BK * 2;          // activation tile: NT rows of 128 B
   // weight stage: two k-blocks (128 k) of packed words, and scales + zeros of up to 4 groups
   static constexpr int P_BYTES = 16 * BF * 4;
   static constexpr int SZ_ROWS = 4;
   static constexpr int SZ_BYTES = 2 * SZ_ROWS * BF * 2;
   static constexpr int W_BYTES = P_BYTES + SZ_BYTES;
-  static constexpr int SX = NT >= 256 ? 4 : NT >= 128 ? 6 : NT >= 64 ? 10 : 12;  // activation stages
-  static constexpr int SW = NT >= 256 ? 6 : NT >= 128 ? 8 : NT >= 64 ? 10 : 12;  // weight stages
-  static constexpr int NA = I4B_W4T_NA;                // A slots (k-blocks) in TMEM
+  static constexpr int SX = NT >= 256 ? 4 : NT >= 128 ? 4 : NT >= 64 ? 6 : 8;  // activation stages
+  static constexpr int SW = NT >= 256 ? 6 : NT >= 128 ? 4 : NT >= 64 ? 5 : 7;  // weight stages
+  static constexpr int NA = CPS == 2 ? 4 : I4B_W4T_NA;  // A slots (k-blocks) in TMEM
   static constexpr int A_COL = NT < 32 ? 32 : NT;      // first TMEM column of the A ring
   static constexpr int A_SLOT_COLS = BK / 2;           // 64 16-bit values per row = 32 columns
   static constexpr int TMEM_COLS = (A_COL + NA * A_SLOT_COLS) <= 256 ? 256 : 512;
   static constexpr int BAR_BYTES = (2 * SX + 2 * SW + 2 * NA + 1) * 8 + 8;
   static constexpr size_t SMEM = 1024 + size_t(SX) * X_BYTES + size_t(SW) * W_BYTES + BAR_BYTES;
   static_assert(X_BYTES % 1024 == 0, "activation stages keep the 1024-byte swizzle alignment");
-  static_assert(SMEM <= 227 * 1024, "shared memory");
-  static_assert(NA % 4 == 0, "each of the four dequant groups owns NA / 4 slots");
+  static_assert(SMEM <= (CPS == 2 ? 113 * 1024 : 227 * 1024), "shared memory");
+  static_assert(NA % GROUPS == 0, "each dequant group owns NA / GROUPS slots");
+  static_assert(CPS == 1 || TMEM_COLS == 256, "two CTAs per SM share TMEM");
   static_assert(A_COL + NA * A_SLOT_COLS <= TMEM_COLS && TMEM_COLS <= 512, "TMEM budget");
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N for M = 128");
 };
@@ -128,7 +136,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 }
 
 template <bool F16, int NT>
-__global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
+__global__ void __launch_bounds__(W4tCfg<NT>::THREADS, W4tCfg<NT>::CPS)
     w4t_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_sz, int sz_swap, int M, int N, int K, int G,
                     uint16_t* __restrict__ y, int64_t sym, int ksplit, float* __restrict__ partials,
@@ -251,15 +259,15 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
     if (elect_one()) umma_commit(tfull);  // also on the error path: completes once the issued MMAs are done
     __syncwarp();
   } else {
-    // Dequant warps in four groups of four: group h takes k-blocks h, h + 4, h + 8, ... (four dequant passes
-    // in flight: one warp's pass -- wait, dequantize, tcgen05.st, wait::st, arrive -- is a latency chain
-    // longer than a k-block's MMAs); within a group, warp q owns TMEM lane quarter q (weight rows
+    // Dequant warps in GROUPS groups of four: group h takes k-blocks h, h + GROUPS, ... (several dequant
+    // passes in flight: one warp's pass -- wait, dequantize, tcgen05.st, wait::st, arrive -- is a latency
+    // chain longer than a k-block's MMAs); within a group, warp q owns TMEM lane quarter q (weight rows
     // 32 q + lane) and all eight packed words of the row.
     const int q = warp & 3, h = (warp - 2) >> 2;
     const int nl = 32 * q + lane;
     const uint32_t lane_base = uint32_t(32 * q) << 16;
     const int zoff = sz_swap ? 0 : C::SZ_ROWS * C::BF, soff = sz_swap ? C::SZ_ROWS * C::BF : 0;
-    for (int kbl = h; kbl < KB && ok; kbl += 4) {
+    for (int kbl = h; kbl < KB && ok; kbl += C::GROUPS) {
       const int j = kbl >> 1, ws = j % SW, b = kbl % NA;
       const int k_begin = (kb0 + kbl) * C::BK;
       if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&wfull[ws], (j / SW) & 1) : mbar_wait(&wfull[ws], (j / SW) & 1))) {
@@ -297,14 +305,14 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&aready[b]);
     }
-    // ---- epilogue: the sixteen warps read the accumulator in 16-token chunks: warp (q, h) takes chunks
-    // h, h + 4, ... of lane quarter q.  Thread = weight row n; per token, a warp stores 32 consecutive
+    // ---- epilogue: the dequant warps read the accumulator in 16-token chunks: warp (q, h) takes chunks
+    // h, h + GROUPS, ... of lane quarter q.  Thread = weight row n; per token, a warp stores 32 consecutive
     // outputs (64 bytes of y, or 128 bytes of fp32 partials).
     if (!mbar_wait_sleep(tfull, 0)) ok = false;
     tc_fence_after();
     const int n = n0 + nl;
 #pragma unroll 1
-    for (int c0 = 16 * h; c0 < NT; c0 += 64) {
+    for (int c0 = 16 * h; c0 < NT; c0 += 16 * C::GROUPS) {
       uint32_t v[16];
       tmem_ld_32x32b_x16(tmem + lane_base + uint32_t(c0), v);  // the whole warp, every iteration
       tmem_ld_wait();
@@ -406,6 +414,8 @@ static cudaError_t launch_w4t_impl(const TcOperands& o, int64_t M, int64_t N, in
                                                partials, tickets);
   return cudaGetLastError();
 }
+
+int w4t_ctas_per_sm(int tile) { return tile == 5 ? W4tCfg<256>::CPS : W4tCfg<128>::CPS; }
 
 int w4t_token_tile(int tile) { return tile == 5 ? 256 : tile == 6 ? 128 : tile == 7 ? 64 : tile == 8 ? 32 : 0; }
 

@@ -134,6 +134,7 @@ unsigned int read_tc_error(bool clear);
 
 // gemm_w4t.cu (INT4, weights dequantized into TMEM; tile codes 5..8 of TcPlan)
 int w4t_token_tile(int tile);
+int w4t_ctas_per_sm(int tile);
 cudaError_t launch_w4t(bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
                        int64_t sym, int tile, int ksplit, float* partials, unsigned int* tickets, cudaStream_t stream);
 unsigned int read_w4t_error(bool clear);
