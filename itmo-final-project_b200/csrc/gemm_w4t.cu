@@ -130,27 +130,9 @@ __device__ __forceinline__ bool elect_one() {
       : "=r"(pred));
   return pred != 0;
 }
-// Bounded wait by a whole warp: lane 0 polls the barrier (one probe per poll instead of 32), then the verdict is
-// broadcast and __syncwarp orders the other lanes' later accesses after lane 0's acquire.
-#ifndef I4B_W4T_LANE0_POLL
-#define I4B_W4T_LANE0_POLL 1
-#endif
+// Bounded wait by a whole warp, with one verdict for all its lanes.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  if (!I4B_W4T_LANE0_POLL) return __all_sync(0xffffffffu, mbar_wait(bar, parity));
-  bool r = true;
-  if ((threadIdx.x & 31) == 0) r = mbar_wait(bar, parity);
-  r = __shfl_sync(0xffffffffu, r, 0);
-  __syncwarp();
-  return r;
-}
-__device__ __forceinline__ bool warp_wait_sleep(uint64_t* bar, uint32_t parity) {
-  if (!I4B_W4T_LANE0_POLL) return __all_sync(0xffffffffu, I4B_W4T_SLEEP ? mbar_wait_sleep(bar, parity)
-                                                                         : mbar_wait(bar, parity));
-  bool r = true;
-  if ((threadIdx.x & 31) == 0) r = I4B_W4T_SLEEP ? mbar_wait_sleep(bar, parity) : mbar_wait(bar, parity);
-  r = __shfl_sync(0xffffffffu, r, 0);
-  __syncwarp();
-  return r;
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
 
 template <bool F16, int NT>
@@ -288,9 +270,13 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, W4tCfg<NT>::CPS)
     for (int kbl = h; kbl < KB && ok; kbl += C::GROUPS) {
       const int j = kbl >> 1, ws = j % SW, b = kbl % NA;
       const int k_begin = (kb0 + kbl) * C::BK;
-      if (!warp_wait_sleep(&wfull[ws], (j / SW) & 1)) { ok = false; break; }
+      if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&wfull[ws], (j / SW) & 1) : mbar_wait(&wfull[ws], (j / SW) & 1))) {
+        ok = false;
+        break;
+      }
       if (kbl >= NA) {
-        if (!warp_wait_sleep(&afree[b], ((kbl / NA) - 1) & 1)) { ok = false; break; }
+        const uint32_t par = ((kbl / NA) - 1) & 1;
+        if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&afree[b], par) : mbar_wait(&afree[b], par))) { ok = false; break; }
         tc_fence_after();
       }
       const uint32_t* P = reinterpret_cast<const uint32_t*>(sW(ws)) + (kbl & 1) * 8 * C::BF;
@@ -322,7 +308,7 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, W4tCfg<NT>::CPS)
     // ---- epilogue: the dequant warps read the accumulator in 16-token chunks: warp (q, h) takes chunks
     // h, h + GROUPS, ... of lane quarter q.  Thread = weight row n; per token, a warp stores 32 consecutive
     // outputs (64 bytes of y, or 128 bytes of fp32 partials).
-    if (!warp_wait_sleep(tfull, 0)) ok = false;
+    if (!mbar_wait_sleep(tfull, 0)) ok = false;
     tc_fence_after();
     const int n = n0 + nl;
 #pragma unroll 1
