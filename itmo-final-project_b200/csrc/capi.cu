@@ -84,14 +84,22 @@ size_t tc_w16_workspace(int64_t M, int64_t N, int64_t K, int sms) {
   return b + align256(tc_partial_bytes(tc_plan(M, N, Kp, sms), M, N));
 }
 
-// Up to these M the register-dequant kernels run (the reference switches paths at
-// SMALL_M = 64, gemm.py:17; measured on B200 the tcgen05 GEMM wins from 33 tokens on):
-// INT4 kW4MaxM = 32, W16 kSkinnyMaxM = 16.
+// The reference switches from its split-K small-M path to the tiled GEMM at SMALL_M = 64 (gemm.py:17).
+// Here: W16 runs the register kernel up to kSkinnyMaxM = 16; INT4 up to kW4MaxM = 32 at most, by the rule of
+// w4_register_path below.
 constexpr int64_t kSmallM = kSkinnyMaxM;
 
-// INT4 M up to which the register-dequant kernels run instead of the tcgen05 GEMM (tuning hook: 8..32)
-int64_t g_w4_small_max = kW4MaxM;
-int64_t w4_small_max_m() { return g_w4_small_max; }
+// INT4 routing between the register-dequant kernels (M <= 32) and the tcgen05 GEMM.  Measured on B200 at
+// M = 16..32 (Llama-3.2-1B block): the GEMM's fixed cost per launch (~10 us) loses to the register kernels on
+// matrices under ~12 M weights (q|k|v 7.8 against 10.9 us, o), and wins on larger ones (gate|up 17.4 against
+// 18.1 us, down_proj 14.9 against 18.1 us at M = 16; ~15 against 65 us at M = 32).  The tuning hook sets a
+// plain M threshold (8..32) instead.
+int64_t g_w4_small_max = 0;  // 0: the shape rule above
+bool w4_register_path(int64_t M, int64_t N, int64_t K) {
+  if (g_w4_small_max) return M <= g_w4_small_max;
+  if (M <= 8) return true;
+  return M <= kW4MaxM && N * K < (int64_t(12) << 20);
+}
 
 }  // namespace
 
@@ -158,7 +166,7 @@ void i4b_set_w4_kernel_override(int kernel, int wk, int splits) { set_w4_kernel_
 
 void i4b_set_gemm_override(int tile, int splits) { set_tc_override(tile, splits); }
 
-void i4b_set_w4_small_m_override(int max_m) { g_w4_small_max = (max_m >= 8 && max_m <= kW4MaxM) ? max_m : kW4MaxM; }
+void i4b_set_w4_small_m_override(int max_m) { g_w4_small_max = (max_m >= 8 && max_m <= kW4MaxM) ? max_m : 0; }
 
 int i4b_quantize_int4(const void* w, int w_dtype, int64_t N, int64_t K, int64_t stride_wn, int64_t stride_wk,
                       int group_size, int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream) {
@@ -196,7 +204,7 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
   if (M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || group_size % 32 != 0 || K % group_size != 0) return 0;
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
-  if (M <= w4_small_max_m()) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
+  if (w4_register_path(M, N, K)) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
   return tc_w4_workspace(M, N, K, group_size, d.sms);
 }
 
@@ -218,7 +226,7 @@ int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool f16 = x_dtype == I4B_F16;
 
-  if (M <= w4_small_max_m()) {
+  if (w4_register_path(M, N, K)) {
     const W4Plan p = plan_w4(M, N, K, G, d.sms);
     if (p.mode == 3) return I4B_ERR_SHAPE;
     if (w4_workspace_bytes(p) > workspace_bytes || (p.mode == 2 && !workspace)) return I4B_ERR_WORKSPACE;

@@ -585,12 +585,13 @@ TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int num_sms) {
 
 // INT4: the TMEM-weight kernel (gemm_w4t.cu), tile code 5..8 = 256, 128, 64 or 32 tokens per CTA, unless the
 // tuning hook asks for one of the shared-memory tiles above (codes 1..4).  Cost model (us) in the form of the
-// one above: a wave of CTAs costs F + c_NT * (k-blocks per CTA); a K split adds its fp32 partials' round trip
-// through L2.  c_NT is the larger of the tensor time of a 128 x NT x 64 k-block and the dequant time of its
-// 128 x 64 weights (the floor for small NT).
+// one above, fitted to B200 sweeps of the Llama-3.2-1B block shapes at M = 16..1024: a wave of CTAs (one per
+// SM for 256-token tiles, two per SM otherwise) costs F + c_NT * (k-blocks per CTA), where a k-block's cost is
+// set by the fixed latency of a pipeline step more than by its MMA work; a K split adds its fp32 partials'
+// round trip through L2.
 static double w4t_cost(int nt, int splits, int64_t M, int64_t N, int64_t kb, int num_sms) {
   const double F = 3.0;
-  const double c = nt == 256 ? 0.32 : nt == 128 ? 0.18 : 0.11;
+  const double c = nt == 256 ? 0.60 : 0.65;
   const int64_t tiles = cdiv(N, 128) * cdiv(M, int64_t(nt));
   const int64_t waves = cdiv(tiles * splits, int64_t(num_sms) * w4t_ctas_per_sm(nt == 256 ? 5 : 6));
   double t = double(waves) * (F + c * double(cdiv(kb, int64_t(splits))));

@@ -2,11 +2,11 @@
 
 Same public functions as ``int4_triton.gemm`` (``gemm.py:303-317``).  The
 dispatch on M happens inside ``libint4_b200.so`` (``i4b_w4a16_matmul``):
-M <= 32 runs the register-dequant tensor-core kernel with its in-kernel
-deterministic split-K reduction (M == 1 is the decode GEMV), M > 32 runs the
-TMA + tcgen05/TMEM GEMM (the reference switches at M = 64; on B200 the tcgen05
-GEMM is the faster one from 33 tokens on).  ``w16a16_matmul`` switches at
-M = 16.  Launches are asynchronous on the current stream and
+M <= 8 runs the register-dequant decode GEMVs, 9 <= M <= 32 runs the
+register-dequant kernel with its in-kernel deterministic split-K reduction on
+matrices under 12 Mi weights, and everything larger runs the TMA + tcgen05 GEMM
+that dequantizes the weights into TMEM (the reference switches at M = 64; here
+the measured faster kernel runs).  ``w16a16_matmul`` switches at M = 16.  Launches are asynchronous on the current stream and
 capture into CUDA graphs (no host synchronisation, no allocation outside torch).
 """
 from __future__ import annotations
@@ -16,9 +16,9 @@ import torch
 from . import _lib
 
 
-# Above these M the C side runs the TMA + tcgen05 GEMM, whose operands need 16-byte aligned bases and
-# row strides (capi.cu: kW4MaxM, kSkinnyMaxM).
-_W4_SMALL_M, _W16_SMALL_M = 32, 16
+# Above these M the C side may run the TMA + tcgen05 GEMM, whose operands need 16-byte aligned bases and
+# row strides (capi.cu: w4_register_path, kSkinnyMaxM).
+_W4_GEMV_M, _W16_SMALL_M = 8, 16
 
 
 def _tma_ok(t: torch.Tensor) -> bool:
@@ -44,7 +44,7 @@ def w4a16_matmul(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, z
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     if M == 0 or N == 0:
         return y.reshape(*x.shape[:-1], N)
-    tma = M > 8  # above the GEMV range the tcgen05 GEMM may run (TMA operands)
+    tma = M > _W4_GEMV_M
     qweight = _unit_n_stride(qweight, tma)
     scales = _unit_n_stride(scales, tma)
     zeros = _unit_n_stride(zeros, tma)
