@@ -72,7 +72,8 @@ int i4b_quantize_int4(const void* w, int w_dtype, int64_t N, int64_t K, int64_t 
 int i4b_dequantize_int4(const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros, int64_t N, int64_t K,
                         int group_size, int out_dtype, void* out, void* stream);
 
-/* Bytes of workspace i4b_w4a16_matmul needs for these sizes (0 is possible).
+/* Bytes of workspace i4b_w4a16_matmul needs for these sizes (0 is possible); for M <= 32 also enough for
+ * i4b_w4a16_matmul_prologue and i4b_w4a16_matmul_allreduce.
  * The workspace must be zero-filled before its first use; every call leaves
  * its counter area zero again, so a workspace kept per stream needs no
  * further clearing.  Calls that share a workspace must not overlap in time. */

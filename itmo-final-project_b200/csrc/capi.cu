@@ -204,8 +204,11 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
   if (M <= 0 || N <= 0 || K <= 0 || group_size <= 0 || group_size % 32 != 0 || K % group_size != 0) return 0;
   DevInfo d;
   if (current_device_info(&d) != I4B_OK) d.sms = 148;
-  if (w4_register_path(M, N, K)) return w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms));
-  return tc_w4_workspace(M, N, K, group_size, d.sms);
+  // Up to M = 32 the size covers the register-dequant plan as well, which the prologue and all-reduce entry
+  // points (sized by this query) always run.
+  const size_t small = M <= kW4MaxM ? w4_workspace_bytes(plan_w4(M, N, K, group_size, d.sms)) : 0;
+  if (w4_register_path(M, N, K)) return small;
+  return std::max(small, tc_w4_workspace(M, N, K, group_size, d.sms));
 }
 
 int i4b_w4a16_matmul(const void* x, int x_dtype, int64_t M, int64_t K, int64_t stride_xm, int64_t stride_xk,
