@@ -155,4 +155,14 @@ def test_matmul_with_swiglu_prologue_matches_silu_mul_then_matmul(cuda_device, M
     y = w4a16_matmul_prologue(PROLOGUE_SWIGLU, gu, *q)
     act = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
     silu_mul(gu, act)
-    assert torch.equal(y, int4_b200.w4a16_matmul(act, *q))  # same activations, same kernel: same bits
+    from int4_b200 import _lib
+
+    L = _lib.lib()
+    L.i4b_set_w4_small_m_override(32)  # the prologue entry runs the register kernels: compare with those
+    try:
+        same_kernel = int4_b200.w4a16_matmul(act, *q)
+    finally:
+        L.i4b_set_w4_small_m_override(0)
+    assert torch.equal(y, same_kernel)  # same activations, same kernel: same bits
+    routed = int4_b200.w4a16_matmul(act, *q)  # M = 32 on 16 Mi weights: the tcgen05 GEMM
+    assert ((routed.float() - y.float()).norm() / y.float().norm()).item() < 1e-3
