@@ -600,7 +600,9 @@ static double w4t_cost(int nt, int splits, int64_t M, int64_t N, int64_t kb, int
 }
 
 TcPlan tc_plan_w4(int64_t M, int64_t N, int64_t K, int num_sms) {
-  if (g_tc_ovr_tile >= 1 && g_tc_ovr_tile <= 4) return tc_plan(M, N, K, num_sms);
+  // The TMEM-weight kernel runs only when the tuning hook asks for it (tile 5..8): an illegal memory access
+  // under back-to-back graph replay at M = 128 is not yet explained.
+  if (g_tc_ovr_tile < 5) return tc_plan(M, N, K, num_sms);
   const int64_t kb = cdiv(K, 64);
   TcPlan best{6, 1};
   double best_t = 1e30;
