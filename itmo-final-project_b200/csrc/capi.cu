@@ -97,9 +97,7 @@ constexpr int64_t kSmallM = kSkinnyMaxM;
 int64_t g_w4_small_max = 0;  // 0: the shape rule above
 bool w4_register_path(int64_t M, int64_t N, int64_t K) {
   if (g_w4_small_max) return M <= g_w4_small_max;
-  // The shape rule below needs the TMEM-weight GEMM, which is held back (gemm_tc.cu, tc_plan_w4): until it
-  // returns, every M <= 32 runs the register kernels.
-  if (M <= kW4MaxM || N * K < 0) return true;
+  if (!I4B_W4T_DEFAULT) return M <= kW4MaxM;  // the shape rule needs the TMEM-weight GEMM as the default
   return M <= 8 || (M <= kW4MaxM && N * K < (int64_t(12) << 20));
 }
 

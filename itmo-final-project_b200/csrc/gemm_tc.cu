@@ -195,6 +195,13 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
         const int last = ((issued - 1 - s) / S) * S + s;
         if (!mbar_wait(&full[s], (last / S) & 1)) ok = false;
       }
+      // Nor an MMA-completion arrival (tcgen05.commit arrives asynchronously; one landing after the CTA has
+      // exited would write into the shared memory of the next CTA on this SM): wait for the release of every
+      // stage's last use.
+      for (int s = 0; ok && s < S && s < issued; ++s) {
+        const int last = ((issued - 1 - s) / S) * S + s;
+        if (!mbar_wait(&empty[s], (last / S) & 1)) ok = false;
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -267,6 +274,13 @@ __global__ void __launch_bounds__(TcCfg<INT4, BN, BMT>::THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bready[kbl % NB]);
+      }
+    }
+    if constexpr (INT4) {
+      // the MMA release of each B slot's last use (see the producer)
+      for (int b = 0; ok && b < NB && b < KB; ++b) {
+        const int last = b + NB * ((KB - 1 - b) / NB);
+        if (!mbar_wait_sleep(&bfree[b], (last / NB) & 1)) ok = false;
       }
     }
     // ---- epilogue: TMEM -> registers -> y.  The dequant warps form DQ_WARPS / 4 sets of four (one per
@@ -600,9 +614,10 @@ static double w4t_cost(int nt, int splits, int64_t M, int64_t N, int64_t kb, int
 }
 
 TcPlan tc_plan_w4(int64_t M, int64_t N, int64_t K, int num_sms) {
-  // The TMEM-weight kernel runs only when the tuning hook asks for it (tile 5..8): an illegal memory access
-  // under back-to-back graph replay at M = 128 is not yet explained.
-  if (g_tc_ovr_tile < 5) return tc_plan(M, N, K, num_sms);
+  // I4B_W4T_DEFAULT = 0 holds the TMEM-weight kernel back (it then runs only when the tuning hook asks for
+  // tile 5..8) and keeps the shared-memory-operand kernel as the default.
+  if (!I4B_W4T_DEFAULT && g_tc_ovr_tile < 5) return tc_plan(M, N, K, num_sms);
+  if (g_tc_ovr_tile >= 1 && g_tc_ovr_tile <= 4) return tc_plan(M, N, K, num_sms);
   const int64_t kb = cdiv(K, 64);
   TcPlan best{6, 1};
   double best_t = 1e30;

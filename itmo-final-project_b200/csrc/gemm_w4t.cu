@@ -218,6 +218,13 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, W4tCfg<NT>::CPS)
       const int last = ((issued - 1 - s) / SX) * SX + s;
       if (!warp_wait(&xfull[s], (last / SX) & 1)) ok = false;
     }
+    // Nor an MMA-completion arrival: tcgen05.commit arrives on its barrier asynchronously, and one landing after
+    // the CTA has exited would write into the shared memory of the next CTA on this SM.  So wait for the
+    // release of every stage's last use.
+    for (int s = 0; ok && s < SX && s < issued; ++s) {
+      const int last = ((issued - 1 - s) / SX) * SX + s;
+      if (!warp_wait(&xempty[s], (last / SX) & 1)) ok = false;
+    }
   } else if (warp == 2 + C::DQ_WARPS) {
     // weight producer: per weight stage the packed words of 128 k (16 rows) and one 3-D box of scales and
     // zeros (SZ_ROWS group rows of both tensors)
@@ -304,6 +311,12 @@ __global__ void __launch_bounds__(W4tCfg<NT>::THREADS, W4tCfg<NT>::CPS)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&aready[b]);
+    }
+    // The same for the A slots this group dequantized into: wait for the MMA release of each slot's last use.
+    for (int b = h; ok && b < NA && b < KB; b += C::GROUPS) {
+      const int last = b + NA * ((KB - 1 - b) / NA);
+      const uint32_t par = (last / NA) & 1;
+      if (!(I4B_W4T_SLEEP ? mbar_wait_sleep(&afree[b], par) : mbar_wait(&afree[b], par))) ok = false;
     }
     // ---- epilogue: the dequant warps read the accumulator in 16-token chunks: warp (q, h) takes chunks
     // h, h + GROUPS, ... of lane quarter q.  Thread = weight row n; per token, a warp stores 32 consecutive

@@ -132,7 +132,11 @@ cudaError_t launch_repack(const void* in, int esize, int64_t rows, int64_t cols_
                           int64_t cols_out, cudaStream_t stream);
 unsigned int read_tc_error(bool clear);
 
-// gemm_w4t.cu (INT4, weights dequantized into TMEM; tile codes 5..8 of TcPlan)
+// gemm_w4t.cu (INT4, weights dequantized into TMEM; tile codes 5..8 of TcPlan).  I4B_W4T_DEFAULT: whether the
+// INT4 dispatch chooses it by default (capi.cu w4_register_path, gemm_tc.cu tc_plan_w4).
+#ifndef I4B_W4T_DEFAULT
+#define I4B_W4T_DEFAULT 0
+#endif
 int w4t_token_tile(int tile);
 int w4t_ctas_per_sm(int tile);
 cudaError_t launch_w4t(bool f16, const TcOperands& o, int64_t M, int64_t N, int64_t K, int G, uint16_t* y,
