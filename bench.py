@@ -485,7 +485,8 @@ def run_model(args, world, rank, local, B=None, steps=None, nll=False):
     for label, w4 in (("w4", True), ("bf16", False))[:2 if args.compare_bf16 else 1]:
         persistent = None if args.persistent < 0 else bool(args.persistent) and w4
         m = LlamaTP(hf, w4=w4, quantize_lm_head=w4 and args.lm_head_w4, rank=rank, world=world, persistent=persistent,
-                    peer_allreduce=args.peer_allreduce != 0, matmul_allreduce=args.peer_allreduce == 1,
+                    peer_allreduce=args.peer_allreduce != 0,
+                    matmul_allreduce=args.peer_allreduce == 1 or (args.peer_allreduce < 0 and B <= 8),
                     max_seq=prompt + steps + args.warmup + 8, max_batch=B, device=dev)
         with ClockSampler(local) as clk:
             r = time_decode(m, B, prompt, steps, args.warmup, world, dev, LLAMA_1B["vocab_size"],
@@ -856,8 +857,10 @@ def main():
     ap.add_argument("--peer-allreduce", type=int, default=-1,
                     help="tensor-parallel runs: 1 = sum the row-parallel outputs inside every W4 matmul through peer "
                          "exchange buffers; 0 = NCCL all-reduces only; -1 (default) = what measured fastest: the "
-                         "block sums inside its o/down matmuls (4 ranks: 24.1 against 44.4 us with NCCL), the "
-                         "decode sums inside its persistent launch, and the greedy token by peer exchange")
+                         "block sums inside its o/down matmuls (4 ranks: 24.1 against 44.4 us with NCCL; 8 ranks: "
+                         "28.8 against 65.0), the decode inside its persistent launch or, where that does not fit "
+                         "(8 ranks), inside the per-launch o/down matmuls for batches up to 8 (whose grids are "
+                         "resident at once), and the greedy token by peer exchange")
     ap.add_argument("--pdl", type=int, default=1,
                     help="programmatic dependent launch for the small-M kernels (weights fetched before the wait)")
     args = ap.parse_args()
