@@ -84,7 +84,14 @@ class DecodeModel(ctypes.Structure):
 
 
 class Int4B200Error(RuntimeError):
-    """A C-ABI call returned a non-zero status."""
+    """A C-ABI call returned a non-zero status (``status``: the ``i4b_status`` code)."""
+
+    def __init__(self, message: str, status: int = 0):
+        super().__init__(message)
+        self.status = status
+
+
+STATUS_SHAPE = 2  # I4B_ERR_SHAPE
 
 
 def lib() -> ctypes.CDLL:
@@ -112,7 +119,7 @@ def check(status: int, what: str) -> None:
         msg = L.i4b_status_string(status).decode()
         if status == 6:  # I4B_ERR_CUDA
             msg += f" (cudaError {L.i4b_last_cuda_error()})"
-        raise Int4B200Error(f"{what}: {msg} [status {status}]")
+        raise Int4B200Error(f"{what}: {msg} [status {status}]", status)
 
 
 def stream_handle(device: torch.device) -> int:

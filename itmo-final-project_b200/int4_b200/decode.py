@@ -348,8 +348,10 @@ class LlamaTP:
     and ``decode_greedy`` exchanges the ranks' best tokens instead of
     all-gathering the logits.  ``matmul_allreduce`` additionally sums the o /
     down outputs of the per-launch decode (<= 32 tokens) inside those matmuls
-    (``i4b_w4a16_matmul_allreduce``) instead of an NCCL all-reduce; it is off by
-    default because, measured at two ranks, NCCL's all-reduce is faster there.
+    (``i4b_w4a16_matmul_allreduce``) instead of an NCCL all-reduce: measured at
+    two ranks, batch 1, 1231 against 977 tokens/s; a shape whose grid cannot be
+    resident at once falls back to NCCL on every rank.  It is off by default
+    (the persistent decode sums inside its own launch where it runs).
     """
 
     def __init__(self, hf_model, *, w4: bool = True, group_size: int = 128, quantize_lm_head: bool = False,
@@ -459,6 +461,22 @@ class LlamaTP:
         if self.world > 1:
             torch.distributed.all_reduce(x, group=self.group)
         return x
+
+    def _matmul_allreduce_or_none(self, x: torch.Tensor, q, prologue: int = 0):
+        """The row-parallel matmul with the ranks' sum inside it, or None when the library refuses the shape
+        (the fused sum needs its whole grid resident at once).  The refusal comes from the host-side plan, the
+        same on every rank, so all ranks then take NCCL's all-reduce together, for this and later steps."""
+        from ._lib import STATUS_SHAPE, Int4B200Error
+
+        try:
+            if prologue:
+                return w4a16_matmul_allreduce(self.peers, x, *q, prologue=prologue)
+            return w4a16_matmul_allreduce(self.peers, x, *q)
+        except Int4B200Error as e:
+            if e.status != STATUS_SHAPE:
+                raise
+            self.matmul_allreduce = False
+            return None
 
     def _gather_vocab(self, logits: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -587,16 +605,16 @@ class LlamaTP:
             decode_attention(q, kc, vc, pos, att, nq, nkv, hd ** -0.5)
             fused_ar = fold and self.peers is not None and self.matmul_allreduce
             if fused_ar:
-                o = w4a16_matmul_allreduce(self.peers, att, *L["o"].q)
-            else:
+                o = self._matmul_allreduce_or_none(att, L["o"].q)
+                fused_ar = o is not None
+            if not fused_ar:
                 o = self._all_reduce(L["o"](att))
             if fold:
                 gu = w4a16_matmul_prologue(PROLOGUE_RMSNORM, cur, *L["gu"].q, delta=o, norm_weight=L["ln2"],
                                            eps=self.eps, resid_out=other)
                 cur, other = other, cur
-                if fused_ar:
-                    delta = w4a16_matmul_allreduce(self.peers, gu, *L["down"].q, prologue=PROLOGUE_SWIGLU)
-                else:
+                delta = self._matmul_allreduce_or_none(gu, L["down"].q, PROLOGUE_SWIGLU) if fused_ar else None
+                if delta is None:
                     delta = self._all_reduce(w4a16_matmul_prologue(PROLOGUE_SWIGLU, gu, *L["down"].q))
             else:
                 add_rmsnorm(cur, o, L["ln2"], x, self.eps)
