@@ -110,3 +110,44 @@ def test_argmax_allreduce_validation_before_any_device_call(L):
     assert call(ctypes.byref(grp), 0x1000, 9, 100, 100, 0, 0x2000, None) == 2  # 2 * rows beyond capacity
     assert call(ctypes.byref(grp), None, 4, 100, 100, 0, 0x2000, None) == 1
     assert call(ctypes.byref(grp), 0x1000, 0, 100, 100, 0, 0x2000, None) == 0   # no rows: no-op
+
+
+def test_w4_workspace_query_covers_the_register_plan_and_the_tuning_hooks(L):
+    """Up to M = 32 the size query covers the register-dequant plan, which the prologue and all-reduce entry
+    points (sized by the same query) always run; the tuning hooks only ever move the answer between the
+    two paths' needs and are restored by their reset values."""
+    try:
+        sizes = {}
+        for small in (0, 8, 32):  # 0: default routing
+            L.i4b_set_w4_small_m_override(small)
+            sizes[small] = [L.i4b_w4a16_workspace_size(M, 2048, 8192, 128) for M in (1, 16, 32, 48)]
+        # forcing the register path up to 32 never asks for more than the default covers at M <= 32
+        assert all(d >= r for d, r in zip(sizes[0][:3], sizes[32][:3]))
+        # M = 48 is always the tcgen05 GEMM
+        assert sizes[0][3] == sizes[8][3] == sizes[32][3] > 0
+        L.i4b_set_gemm_override(6, 2)  # tuning: a K split of the TMEM-weight tile adds fp32 partials
+        split = L.i4b_w4a16_workspace_size(48, 2048, 8192, 128)
+        L.i4b_set_gemm_override(0, 0)
+        assert split >= 2 * 48 * 2048 * 4
+        assert L.i4b_w4a16_workspace_size(48, 2048, 8192, 128) == sizes[0][3]
+    finally:
+        L.i4b_set_w4_small_m_override(0)
+        L.i4b_set_gemm_override(0, 0)
+
+
+def test_bench_stdout_is_one_json_line_per_run():
+    """The driver parses bench.py's stdout: the reference arm prints exactly one JSON line there, whatever
+    native libraries write to file descriptor 1."""
+    import json
+    import subprocess
+    import sys
+
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "3", "--decode-steps", "0"], capture_output=True, text=True, timeout=600,
+                         cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1, out.stdout[:2000]
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["steps"] == 1 and line["warmup"] == 1
+    assert line["cpu_baseline"]["kind"] == "port" and line["e2e"]["h2d_bytes_per_step"] == 0
