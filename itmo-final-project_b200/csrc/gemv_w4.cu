@@ -678,11 +678,8 @@ constexpr int kStreamSteps = I4B_STREAM_STEPS;  // 32-k steps per stage (at leas
 // the weight stream never stops between slabs.  The activations (M <= 8 rows x K) are staged once per
 // CTA.  No K split, hence no cross-CTA reduction; the dequant / MMA / segment
 // arithmetic is that of w4_skinny_kernel.
-// The greedy-choice variant is held to six resident CTAs per SM (80 registers, no spills at one token): its
-// epilogue otherwise takes 93 registers, one CTA fewer per SM on the oversubscribed grid, and measured
-// 72 us (cold, ncu) against 56 us for the plain stream on the 128256 x 2048 head.
 template <bool F16, int SPS, bool ONE, bool ARG = false>
-__global__ void __launch_bounds__(128, ARG ? 6 : 1) w4_stream_kernel(const W4SArgs a) {
+__global__ void __launch_bounds__(128) w4_stream_kernel(const W4SArgs a) {
   constexpr int SPST = SPS > kStreamSteps ? SPS : kStreamSteps;  // 32-k steps per ring stage
   constexpr int SEGST = SPST / SPS;
   constexpr int RING = kStreamRing;
