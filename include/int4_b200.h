@@ -81,11 +81,12 @@ size_t i4b_w4a16_workspace_size(int64_t M, int64_t N, int64_t K, int group_size)
 
 /* y[M, N] = x[M, K] @ W_hat^T in x's dtype (fp32 accumulation).
  * Replaces int4_triton.w4a16_matmul (int4_triton/gemm.py:303-309, dispatch
- * gemm.py:234-300): M <= 8 (decode) runs the register-dequant GEMV kernels, and
- * so does 9 <= M <= 32 on matrices of fewer than 12 Mi weights (deterministic
- * in-kernel split-K reduction); larger M and larger matrices run the TMA +
- * tcgen05 GEMM that dequantizes the weights into TMEM (the reference switches
- * at M = 64; on B200 the choice is the measured faster one).
+ * gemm.py:234-300): M <= 32 runs the register-dequant kernels (M <= 8: the
+ * decode GEMVs; 9..32: deterministic in-kernel split-K reduction), larger M the
+ * TMA + tcgen05/TMEM GEMM (the reference switches at M = 64; on B200 the tcgen05
+ * GEMM wins from 33 tokens on).  A library built with -DI4B_W4T_DEFAULT=1 routes
+ * instead by shape to the GEMM that dequantizes the weights into TMEM (from 9
+ * tokens on matrices of 12 Mi weights or more).
  * When the tcgen05 GEMM runs, qweight, scales and zeros must meet the TMA rules
  * (16-byte aligned bases and row strides) unless N % 8 != 0 (then they are
  * copied into the workspace); otherwise I4B_ERR_LAYOUT.
@@ -361,9 +362,9 @@ void i4b_set_decode_trace(void* buffer, size_t bytes);
 void i4b_set_gemm_override(int tile, int splits);
 
 /* Tuning hook: the largest M (8..32) for which i4b_w4a16_matmul runs the register-dequant kernels rather
- * than the tcgen05 GEMM; any other value restores the default (register kernels for M <= 8, and for
- * M <= 32 on matrices of fewer than 12 Mi weights).  Process-wide; changes the workspace size a later
- * i4b_w4a16_workspace_size reports.  No counterpart in the reference. */
+ * than the tcgen05 GEMM; any other value restores the default routing (see i4b_w4a16_matmul).
+ * Process-wide; changes the workspace size a later i4b_w4a16_workspace_size reports.  No counterpart in
+ * the reference. */
 void i4b_set_w4_small_m_override(int max_m);
 
 /* Device-side error flags raised by kernels of this library on `device`

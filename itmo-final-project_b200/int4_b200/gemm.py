@@ -2,11 +2,10 @@
 
 Same public functions as ``int4_triton.gemm`` (``gemm.py:303-317``).  The
 dispatch on M happens inside ``libint4_b200.so`` (``i4b_w4a16_matmul``):
-M <= 8 runs the register-dequant decode GEMVs, 9 <= M <= 32 runs the
-register-dequant kernel with its in-kernel deterministic split-K reduction on
-matrices under 12 Mi weights, and everything larger runs the TMA + tcgen05 GEMM
-that dequantizes the weights into TMEM (the reference switches at M = 64; here
-the measured faster kernel runs).  ``w16a16_matmul`` switches at M = 16.  Launches are asynchronous on the current stream and
+M <= 8 runs the register-dequant decode GEMVs, 9 <= M <= 32 the
+register-dequant kernel with its in-kernel deterministic split-K reduction, and
+larger M the TMA + tcgen05/TMEM GEMM (the reference switches at M = 64; on B200
+the tcgen05 GEMM wins from 33 tokens on).  ``w16a16_matmul`` switches at M = 16.  Launches are asynchronous on the current stream and
 capture into CUDA graphs (no host synchronisation, no allocation outside torch).
 """
 from __future__ import annotations
