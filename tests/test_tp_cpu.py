@@ -109,3 +109,41 @@ def test_row_shard_rejects_uneven_splits():
         row_shard(w, 0, 4)
     with pytest.raises(AssertionError):
         column_shard(w, 0, 4)
+
+
+def test_fused_row_parallel_sum_falls_back_to_nccl_only_on_a_refused_shape(monkeypatch):
+    """``LlamaTP``'s per-launch decode sums the o / down outputs inside the matmul; when the library refuses
+    the shape (its grid cannot be resident at once: I4B_ERR_SHAPE, decided on the host from the plan, the same
+    on every rank) it answers None and turns the fused sums off for later steps, so every rank takes NCCL's
+    all-reduce together.  Any other failure propagates.  The library call is replaced by a fake here."""
+    from types import SimpleNamespace
+
+    from int4_b200 import decode
+    from int4_b200._lib import STATUS_SHAPE, Int4B200Error
+
+    calls = []
+
+    def fake(peers, x, qw, s, z, *, prologue=0):
+        calls.append(prologue)
+        if fake.mode == "ok":
+            return x + 1
+        raise Int4B200Error("w4a16_matmul_allreduce: refused", fake.status)
+
+    monkeypatch.setattr(decode, "w4a16_matmul_allreduce", fake)
+    helper = decode.LlamaTP._matmul_allreduce_or_none
+    me = SimpleNamespace(peers=object(), matmul_allreduce=True)
+    x = torch.zeros(1, 4)
+    q = (None, None, None)
+
+    fake.mode, fake.status = "ok", 0
+    assert torch.equal(helper(me, x, q), x + 1) and me.matmul_allreduce
+    assert torch.equal(helper(me, x, q, decode.PROLOGUE_SWIGLU), x + 1) and calls == [0, decode.PROLOGUE_SWIGLU]
+
+    fake.mode, fake.status = "refuse", STATUS_SHAPE
+    assert helper(me, x, q) is None and me.matmul_allreduce is False
+
+    me.matmul_allreduce = True
+    fake.status = 6  # a CUDA error is not a refusal
+    with pytest.raises(Int4B200Error):
+        helper(me, x, q)
+    assert me.matmul_allreduce is True
