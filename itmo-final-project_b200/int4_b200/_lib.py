@@ -131,19 +131,25 @@ def stream_handle(device: torch.device) -> int:
 _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
 
 
+_WS_LOCK = threading.Lock()
+
+
 def workspace(device: torch.device, stream: int, nbytes: int) -> tuple[int, int]:
-    """(pointer, size) of a workspace of at least ``nbytes`` for this device and stream."""
+    """(pointer, size) of a workspace of at least ``nbytes`` for this device and stream.  Growing it
+    replaces the buffer: the old one returns to torch's allocator in the stream's order, so launches already
+    queued on this stream still find it intact."""
     if nbytes == 0:
         return 0, 0
     key = (device.index, stream)
-    ws = _WORKSPACES.get(key)
-    if ws is None or ws.numel() < nbytes:
-        size = max(nbytes, 1 << 20)
-        if ws is not None:
-            size = max(size, 2 * ws.numel())
-        ws = torch.zeros(size, dtype=torch.uint8, device=device)
-        _WORKSPACES[key] = ws
-    return ws.data_ptr(), ws.numel()
+    with _WS_LOCK:
+        ws = _WORKSPACES.get(key)
+        if ws is None or ws.numel() < nbytes:
+            size = max(nbytes, 1 << 20)
+            if ws is not None:
+                size = max(size, 2 * ws.numel())
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            _WORKSPACES[key] = ws
+        return ws.data_ptr(), ws.numel()
 
 
 def device_error_flags(device: int = 0, clear: bool = True) -> int:
